@@ -1,0 +1,328 @@
+"""Benchmark: ResNet-18 bf16 inference images/s on 1..8 B200s (BASELINE.json metric).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl ours|reference]
+
+Workload ("resnet18_bf16_b256"): the config-0 ResNet-18 architecture (random
+Kaiming weights, random BN statistics, BN folded by the pass pipeline), bf16
+activations and weights with fp32 accumulation, B = 256 images per GPU of
+3x224x224 N(0,1) synthetic input. One step = one forward of the whole batch.
+Weak scaling: every rank runs its own B-image shard (batch-sharded inference,
+weights replicated, no collective on the hot path).
+
+Reported line (rank 0):
+* ``value``   images/s of the whole job with inputs resident in HBM (CUDA events
+  on each rank's stream, max over ranks);
+* ``e2e``     the same through the public zero-copy host API
+  (``Executable.run_pinned``): every step copies the fp32 NCHW input from
+  pinned host memory and reads the logits back;
+* ``roofline`` of the dominant kernel (the tcgen05 implicit-GEMM conv):
+  algorithmic conv FLOPs per launch / average launch time, from CUDA events
+  recorded around every conv launch inside the timed region, against the
+  measured bf16 tensor peak in MEASURED_PEAKS.json;
+* ``cpu_baseline`` the NumPy oracle (same algorithm as the reference executor,
+  single-threaded einsum) on a bounded sample of b=1 forwards.
+
+``--impl reference`` times the reference's CPU implementation of the path (the
+NumPy oracle restatement, one process per host core) on the same workload.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, ROOT)
+
+METRIC = "ResNet-18 images/s (b=256, 1/2/4/8 B200)"
+WORKLOAD = "resnet18_bf16_b256"
+GFLOP_PER_IMAGE = 3.628  # conv + FC, 1.8141 GMAC per 224x224 image
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["bf16_tflops"], p["hbm_gbs"], "measured"
+    except Exception:
+        return 1590.0, 6650.0, "fallback"
+
+
+class ClockSampler:
+    """nvidia-smi sampling of SM clocks and throttle reasons during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.proc = None
+        self.gpu = gpu_index
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={gpu_index}", f"--query-gpu={self.Q}", "--format=csv,noheader,nounits",
+                 "-lms", "100"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except Exception:
+            self.proc = None
+
+    def stop(self):
+        if self.proc is None:
+            return None
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except Exception:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        rows = [r.split(",") for r in out.strip().splitlines() if r.count(",") >= 8]
+        if not rows:
+            return None
+        sm = [float(r[1]) for r in rows if r[1].strip().replace(".", "").isdigit()]
+        smax = max(float(r[2]) for r in rows)
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[5 + i].strip() == "Active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": smax,
+                "reasons": reasons, "samples": len(rows)}
+
+
+def conv_flops(exe):
+    """Algorithmic FLOPs of each conv step (2*N*OH*OW*K*C/g*R*S) for one shard."""
+    out = []
+    for c in exe.devices[0].calls:
+        if c[0] == "conv":
+            d = c[1]
+            out.append(2.0 * d.n * d.oh * d.ow * d.k * (d.c // d.groups) * d.r * d.s)
+    return out
+
+
+def timed_steps(exe, steps, per_kernel=False):
+    """Issue `steps` forwards between CUDA events on the device stream; with
+    per_kernel, also record events around every conv launch."""
+    dev = exe.devices[0]
+    ctx = dev.ctx
+    slot = 2
+    conv_slots = []
+    ctx.event_record(0)
+    for _ in range(steps):
+        if not per_kernel:
+            dev.issue_forward()
+            continue
+        dev.issue_inputs()
+        for c in dev.calls:
+            if c[0] == "conv":
+                _, d, x, w, b, r, y, epi, cfg = c
+                ctx.event_record(slot)
+                ctx.conv2d(d, x, w, b, r, y, epi, cfg)
+                ctx.event_record(slot + 1)
+                conv_slots.append((slot, slot + 1))
+                slot += 2
+            elif c[0] == "pool":
+                ctx.pool2d(c[1], c[2], c[3])
+            else:
+                ctx.eltwise(c[1], c[2], c[3])
+        dev.issue_outputs()
+    ctx.event_record(1)
+    ctx.sync()
+    total = ctx.event_elapsed(0, 1)
+    conv_ms = sum(ctx.event_elapsed(a, b) for a, b in conv_slots)
+    return total, conv_ms, len(conv_slots)
+
+
+def cpu_baseline_sample(images=8, seed=0):
+    """Oracle (reference algorithm) b=1 forwards on the host; returns img/s."""
+    from mdlc_b200 import builders, passes
+    from oracle import reference as oref
+    g = passes.default_pipeline(builders.resnet18(batch=1, seed=seed))
+    rng = np.random.default_rng(1)
+    x = rng.standard_normal((1, 3, 224, 224)).astype(np.float32)
+    oref.run(g, {"input": x})   # warm-up
+    t0 = time.perf_counter()
+    for _ in range(images):
+        oref.run(g, {"input": x})
+    dt = time.perf_counter() - t0
+    return images / dt, dt
+
+
+def _ref_worker(args):
+    images, seed = args
+    ips, dt = cpu_baseline_sample(images, seed)
+    return images, dt
+
+
+def run_reference_arm(args, rank, world):
+    """Reference's CPU implementation of the path on all host cores."""
+    if rank != 0:
+        return 0
+    import multiprocessing as mp
+    cores = os.cpu_count() or 1
+    per_proc = 2
+    total_imgs, wall = 0, []
+    ctx = mp.get_context("spawn")
+    with ctx.Pool(cores) as pool:
+        pool.map(_ref_worker, [(1, 0)] * cores)            # warm-up: imports + one forward each
+        for _ in range(max(1, args.warmup)):
+            pass
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            res = pool.map(_ref_worker, [(per_proc, 0)] * cores)
+            wall.append(time.perf_counter() - t0)
+            total_imgs += sum(r[0] for r in res)
+    value = total_imgs / sum(wall)
+    line = {"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "images/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(1e3 * sum(wall) / args.steps, 3), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": WORKLOAD, "model": "resnet18", "per_step_sample": f"{cores * per_proc} images",
+                       "parallelism": f"{cores} host processes"},
+            "cpu_baseline": {"value": round(value, 3), "unit": "images/s", "cores": cores, "kind": "port",
+                             "sample": f"{cores} processes x {per_proc} b=1 forwards per step, "
+                                       f"{args.steps} steps (NumPy oracle, reference algorithm)"},
+            "e2e": {"value": round(value, 3), "unit": "images/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def main() -> int:
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=100)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--batch", type=int, default=256, help="images per GPU")
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--cpu-sample", type=int, default=12, help="b=1 oracle forwards for cpu_baseline")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import datetime
+        import torch
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+
+    if args.impl == "reference":
+        rc = run_reference_arm(args, rank, world)
+        if dist is not None:
+            dist.destroy_process_group()
+        return rc
+
+    from mdlc_b200 import builders, passes
+    from mdlc_b200.compiler import compile as mdlc_compile
+
+    g = passes.default_pipeline(builders.resnet18(batch=args.batch, seed=0))
+    exe = mdlc_compile(g, dtype="bf16", devices=[local])
+    dev = exe.devices[0]
+    ins, outs = exe.pinned_inputs(), exe.pinned_outputs()
+    rng = np.random.default_rng(1234 + rank)
+    ins["input"][...] = rng.standard_normal(ins["input"].shape, dtype=np.float32)
+    exe.run_pinned()                       # stage the input once (resident for `value`)
+    flops = conv_flops(exe)
+
+    def barrier():
+        if dist is not None:
+            import torch
+            torch.cuda.synchronize()
+            dist.barrier()
+
+    def max_over_ranks(v):
+        if dist is None:
+            return v
+        import torch
+        t = torch.tensor([v], dtype=torch.float64, device="cuda")
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item())
+
+    # ---- warm-up
+    for _ in range(args.warmup):
+        dev.issue_forward()
+    exe.sync()
+
+    # ---- timed: device-resident inputs
+    barrier()
+    sampler = ClockSampler(local) if rank == 0 else None
+    launches0 = dev.ctx.launch_count()
+    total_ms, conv_ms, nconv = timed_steps(exe, args.steps, per_kernel=True)
+    launches = dev.ctx.launch_count() - launches0
+    clocks = sampler.stop() if sampler else None
+    barrier()
+    total_ms = max_over_ranks(total_ms)
+    ms_per_step = total_ms / args.steps
+    value = world * args.batch / (ms_per_step / 1e3)
+
+    # ---- e2e through the public host API (pinned H2D of inputs + D2H of logits every step)
+    for _ in range(2):
+        exe.run_pinned()
+    barrier()
+    dev.ctx.event_record(2)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        exe.run_pinned(sync=False)
+    dev.ctx.event_record(3)
+    exe.sync()
+    e2e_wall = time.perf_counter() - t0
+    e2e_ms = max_over_ranks(dev.ctx.event_elapsed(2, 3)) / args.steps
+    barrier()
+    e2e_value = world * args.batch / (e2e_ms / 1e3)
+    logits = outs["logits"]
+    assert np.isfinite(logits).all()
+
+    if rank == 0:
+        peak_tf, _, peak_kind = _peaks()
+        conv_flops_step = sum(flops)
+        avg_launch_ms = conv_ms / nconv
+        achieved_tf = (conv_flops_step / len(flops)) / (avg_launch_ms / 1e3) / 1e12
+        cpu = None
+        if world == 1 and args.cpu_sample > 0:
+            ips, dt = cpu_baseline_sample(args.cpu_sample)
+            cpu = {"value": round(ips, 4), "unit": "images/s", "cores": 1, "kind": "port",
+                   "sample": f"{args.cpu_sample} ResNet-18 b=1 forwards ({dt:.1f} s), NumPy oracle "
+                             "(reference algorithm: im2col + single-threaded einsum)"}
+        in_bytes = int(np.prod(g.value_info["input"].shape)) * 4
+        line = {
+            "metric": METRIC, "value": round(value, 1), "unit": "images/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (N(0,1) 3x224x224 images, random Kaiming weights)",
+            "config": {"workload": WORKLOAD, "model": "resnet18", "per_gpu_batch": args.batch,
+                       "global_batch": args.batch * world, "image": 224, "parallelism": f"dp{world}",
+                       "l2": "working set > 126 MB L2 (input 154 MB fp32 + activations), no flush needed"},
+            "e2e": {"value": round(e2e_value, 1), "unit": "images/s", "h2d_bytes_per_step": in_bytes,
+                    "d2h_bytes_per_step": int(np.prod(logits.shape)) * 4,
+                    "wall_s": round(e2e_wall, 4)},
+            "roofline": {"kernel": "conv_tc_kernel (tcgen05 implicit GEMM)", "bound": "tensor",
+                         "achieved": round(achieved_tf, 1),
+                         "peak": peak_tf, "unit": "TFLOP/s", "frac": round(achieved_tf / peak_tf, 4),
+                         "peak_kind": f"{peak_kind} bf16 (burst)", "traffic": None,
+                         "conv_share_of_step": round(conv_ms / total_ms, 4) if total_ms else None,
+                         "flops_per_launch": round(conv_flops_step / len(flops)),
+                         "avg_launch_ms": round(avg_launch_ms, 5)},
+            "gpu_launches": launches,
+            "network_tflops": round(world * args.batch * GFLOP_PER_IMAGE / (ms_per_step / 1e3) / 1e3, 1),
+        }
+        if clocks:
+            line["clocks"] = clocks
+        if cpu:
+            line["cpu_baseline"] = cpu
+        print(json.dumps(line), flush=True)
+    exe.close()
+    if dist is not None:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())

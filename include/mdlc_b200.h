@@ -1,0 +1,229 @@
+/*
+ * mdlc_b200 — C ABI of the B200 (sm_100a) execution library for mdlc graphs.
+ *
+ * This library replaces the reference compiler's code generation + GPU runtime
+ * hot path: NVRTC compilation of generated CUDA C (mdlc/codegen/cuda/
+ * nvrtc_runtime.py:97-159), the per-launch argument marshalling of the GPU
+ * executor (mdlc/codegen/cuda/gpu_executor.py:38-98) and its host fallbacks
+ * (gpu_executor.py:100-114). Every kernel is prebuilt for sm_100a; there is no
+ * JIT and no host fallback.
+ *
+ * Conventions
+ *   - Every function returns MDLC_OK (0) or a negative MDLC_ERR_* status; no
+ *     C++ exception or abort crosses this boundary. mdlc_last_error() gives
+ *     the message of the last failure on a context.
+ *   - Pointers are device pointers unless named host_*. Kernels never free or
+ *     retain caller pointers.
+ *   - Activations are NHWC. A tensor's channel stride (c_stride / k_stride) is
+ *     its channel count rounded up to a multiple of 8 (16 for 8-bit types);
+ *     padding channels hold zeros and kernels keep them zero.
+ *   - One context per device and host thread; calls on different contexts are
+ *     independent. All work is issued on the context's stream.
+ *   - Device-side waits are bounded (~2 s); on expiry a kernel records an error
+ *     code in the context's device error word (read with mdlc_check_flag),
+ *     releases its tensor memory and returns instead of hanging.
+ */
+#ifndef MDLC_B200_H
+#define MDLC_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct mdlc_ctx mdlc_ctx;
+
+/* ---- status codes ------------------------------------------------------ */
+#define MDLC_OK 0
+#define MDLC_ERR_INVALID (-1)     /* bad argument / shape / alignment */
+#define MDLC_ERR_CUDA (-2)        /* a CUDA runtime call failed */
+#define MDLC_ERR_UNSUPPORTED (-3) /* valid request this build does not implement */
+#define MDLC_ERR_TIMEOUT (-4)     /* host-side wait exceeded its limit */
+#define MDLC_ERR_DEVICE (-5)      /* a kernel reported a device-side error */
+#define MDLC_ERR_NOMEM (-6)
+
+/* device-side error word values (mdlc_check_flag) */
+#define MDLC_DEVERR_NONE 0
+#define MDLC_DEVERR_WAIT_TIMEOUT 1 /* an mbarrier wait ran out of time */
+#define MDLC_DEVERR_BOUNDS 2       /* a checked index was out of range */
+#define MDLC_DEVERR_INJECTED 3     /* raised by mdlc_debug_timeout_probe */
+
+/* ---- element types ----------------------------------------------------- */
+enum { MDLC_F32 = 0, MDLC_BF16 = 1, MDLC_S8 = 2, MDLC_U8 = 3, MDLC_S32 = 4 };
+
+/* ---- epilogue activations (reference: mdlc/codegen/cuda/templates.py:24-51,
+ *      mdlc/runtime/reference.py:19-38; GELU is an extension) ------------- */
+enum {
+  MDLC_ACT_NONE = 0,
+  MDLC_ACT_RELU = 1,
+  MDLC_ACT_CLIP = 2,
+  MDLC_ACT_SIGMOID = 3,
+  MDLC_ACT_TANH = 4,
+  MDLC_ACT_LEAKY_RELU = 5,
+  MDLC_ACT_HARD_SIGMOID = 6,
+  MDLC_ACT_HARD_SWISH = 7,
+  MDLC_ACT_GELU = 8
+};
+
+/* Fused epilogue applied to every conv / GEMM output element:
+ *   float path: y = act(acc + bias[k] (+ residual))
+ *   int8 path : y = clamp(out_zp + requant(acc + bias32[k], rq_mult[k], rq_shift[k])
+ *                         + requant(residual - res_zp, res_mult, res_shift), qmin, qmax)
+ *               (gemmlowp fixed point; bias is int32 for the int8 path)
+ *   int8 path with out_type F32: y = deq_scale[k] * (acc + bias32[k]) + deq_bias[k]  */
+typedef struct {
+  int32_t act;
+  float alpha;    /* LeakyRelu slope / HardSigmoid alpha */
+  float beta;     /* HardSigmoid beta */
+  float clip_lo;  /* Clip bounds (use +-INFINITY for one-sided) */
+  float clip_hi;
+  const int32_t* rq_mult;  /* [k] Q31 multipliers (int8 path) */
+  const int32_t* rq_shift; /* [k] right shifts >= 0 (int8 path) */
+  int32_t out_zp, qmin, qmax;
+  int32_t res_zp, res_mult, res_shift;
+  const float* deq_scale; /* [k] (int8 path, float output) */
+  const float* deq_bias;  /* [k] (int8 path, float output) */
+} mdlc_epilogue;
+
+/* 2-D convolution over NHWC tensors (groups == 1: implicit GEMM; groups == c
+ * == k: depthwise). A GEMM y[M,N] = x[M,K] * W[N,K]^T is the 1x1 conv with
+ * n = M, h = w = 1. Reference semantics: mdlc/runtime/ops.py:56-81. */
+typedef struct {
+  int32_t n, h, w, c, c_stride; /* input */
+  int32_t k, k_stride;          /* output channels and output channel stride */
+  int32_t r, s;                 /* filter height / width */
+  int32_t stride_h, stride_w;
+  int32_t pad_t, pad_l;         /* top / left padding (bottom/right follow from oh/ow) */
+  int32_t dil_h, dil_w;
+  int32_t oh, ow;
+  int32_t groups;
+  int32_t in_type, out_type;    /* MDLC_BF16 -> MDLC_BF16|MDLC_F32; MDLC_F32 -> MDLC_F32;
+                                   MDLC_U8|MDLC_S8 -> MDLC_U8|MDLC_S8|MDLC_F32 */
+  int32_t res_stride;           /* residual channel stride (0: same as k_stride) */
+  int32_t in_zp;                /* 8-bit input zero point: padded taps read this value */
+} mdlc_conv_desc;
+
+/* Tile configuration for the tensor-core implicit GEMM (0 = library default). */
+typedef struct {
+  int32_t bn;     /* output channels per CTA: 64, 128 or 256 */
+  int32_t stages; /* shared-memory pipeline depth: 2..8 */
+  int32_t flags;  /* reserved, 0 */
+} mdlc_tile_cfg;
+
+/* Pooling over NHWC (reference: ops.py:109-150). kind: 0 max, 1 average,
+ * 2 global average (kernel/stride/pad ignored). */
+typedef struct {
+  int32_t kind;
+  int32_t n, h, w, c, c_stride;
+  int32_t kh, kw, stride_h, stride_w, pad_t, pad_l, oh, ow;
+  int32_t count_include_pad;
+  int32_t dtype; /* MDLC_F32 | MDLC_BF16 | MDLC_U8 | MDLC_S8 */
+  /* int8 average pooling requantisation (ignored for float types) */
+  int32_t in_zp, out_zp, rq_mult, rq_shift;
+} mdlc_pool_desc;
+
+/* Fused elementwise program (reference: FusedElementwise groups,
+ * mdlc/passes/fuse_elementwise.py:111-118, evaluated per element like
+ * mdlc/codegen/cuda/templates.py:209-269 but interpreted, not generated).
+ * Registers 0..n_inputs-1 are preloaded with the inputs; each instruction
+ * writes register dst = op(src0, src1) or op(src0) or src0 `op` imm. */
+enum {
+  MDLC_EW_ADD = 0, MDLC_EW_SUB, MDLC_EW_MUL, MDLC_EW_DIV,
+  MDLC_EW_ADDI, MDLC_EW_SUBI, MDLC_EW_RSUBI, MDLC_EW_MULI, MDLC_EW_DIVI, MDLC_EW_RDIVI,
+  MDLC_EW_RELU, MDLC_EW_CLIP, MDLC_EW_SIGMOID, MDLC_EW_TANH, MDLC_EW_LEAKY_RELU,
+  MDLC_EW_HARD_SIGMOID, MDLC_EW_HARD_SWISH, MDLC_EW_ERF, MDLC_EW_GELU, MDLC_EW_MAX, MDLC_EW_MIN
+};
+#define MDLC_EW_MAX_INPUTS 4
+#define MDLC_EW_MAX_OUTPUTS 2
+#define MDLC_EW_MAX_INSTR 24
+/* input broadcast modes over an NHWC output of shape [n, hw, c] */
+enum { MDLC_BC_FULL = 0, MDLC_BC_NC = 1, MDLC_BC_C = 2, MDLC_BC_SCALAR = 3 };
+
+typedef struct {
+  int8_t op, dst, src0, src1;
+  float imm0, imm1;
+} mdlc_ew_instr;
+
+typedef struct {
+  int32_t n, hw, c, c_stride; /* output geometry; every tensor uses c_stride */
+  int32_t dtype;              /* MDLC_F32 | MDLC_BF16 */
+  int32_t n_inputs, n_outputs, n_instr;
+  int32_t bcast[MDLC_EW_MAX_INPUTS];
+  int32_t out_reg[MDLC_EW_MAX_OUTPUTS];
+  mdlc_ew_instr code[MDLC_EW_MAX_INSTR];
+} mdlc_ew_prog;
+
+/* ---- library / context ------------------------------------------------- */
+int mdlc_version(void);
+int mdlc_device_count(int* count);
+int mdlc_ctx_create(int device, mdlc_ctx** out);
+int mdlc_ctx_destroy(mdlc_ctx* ctx);
+const char* mdlc_last_error(mdlc_ctx* ctx);
+int mdlc_get_stream(mdlc_ctx* ctx, void** stream); /* cudaStream_t of the context */
+
+/* ---- memory (the C side owns device and pinned host allocations) ------- */
+int mdlc_alloc(mdlc_ctx* ctx, size_t bytes, void** dev);
+int mdlc_free(mdlc_ctx* ctx, void* dev);
+int mdlc_host_alloc(mdlc_ctx* ctx, size_t bytes, void** host);
+int mdlc_host_free(mdlc_ctx* ctx, void* host);
+int mdlc_upload(mdlc_ctx* ctx, void* dev, const void* host, size_t bytes);      /* async on the stream */
+int mdlc_download(mdlc_ctx* ctx, void* host, const void* dev, size_t bytes);    /* async on the stream */
+int mdlc_memset(mdlc_ctx* ctx, void* dev, int value, size_t bytes);
+int mdlc_sync(mdlc_ctx* ctx, int timeout_ms);
+int mdlc_check_flag(mdlc_ctx* ctx, int* flag); /* reads and clears the device error word */
+
+/* ---- kernels (all asynchronous on the context stream) ------------------ */
+/* Replaces conv lowering (mdlc/codegen/cuda/emit.py:159-209: im2col + gemm),
+ * Gemm/MatMul lowering (emit.py:211-244) and grouped-conv host fallback
+ * (emit.py:175-180). Weights must be packed with mdlc_pack_conv_weights. */
+int mdlc_conv2d(mdlc_ctx* ctx, const mdlc_conv_desc* desc, const void* x, const void* w_packed,
+                const void* bias, const void* residual, void* y, const mdlc_epilogue* epi,
+                const mdlc_tile_cfg* cfg);
+/* Size in bytes of the packed weight buffer for desc (host helper). */
+int mdlc_conv_weight_bytes(const mdlc_conv_desc* desc, size_t* bytes);
+/* Pack OIHW fp32 weights (reference layout, mdlc/runtime/ops.py:57) into the
+ * layout the kernel for desc reads; int8 paths take already-quantised int8
+ * values stored as float. Host-only. */
+int mdlc_pack_conv_weights(const mdlc_conv_desc* desc, const float* host_w_oihw, void* host_out);
+/* Replaces the MaxPool / AveragePool / GlobalAveragePool host fallbacks
+ * (emit.py:32-35, ops.py:109-150). */
+int mdlc_pool2d(mdlc_ctx* ctx, const mdlc_pool_desc* desc, const void* x, void* y);
+/* Replaces the generated elementwise kernel (emit.py:246-278, templates.py:209-269). */
+int mdlc_eltwise(mdlc_ctx* ctx, const mdlc_ew_prog* prog, const void* const* inputs,
+                 void* const* outputs);
+
+/* Graph-boundary layout conversion (the reference stages feeds and reads
+ * outputs as NCHW fp32, gpu_executor.py:48-55,94). to_nhwc converts an NCHW
+ * fp32 tensor to NHWC with channel stride cs (pad channels zeroed) in dtype;
+ * for 8-bit dtypes q = clamp(rint(x * inv_scale) + zp). to_nchw is the
+ * inverse (8-bit: x = (q - zp) * scale, with scale = 1 / inv_scale given). */
+int mdlc_nchw_to_nhwc(mdlc_ctx* ctx, const float* x, int n, int c, int h, int w, void* y, int cs,
+                      int dtype, float inv_scale, int zp);
+int mdlc_nhwc_to_nchw(mdlc_ctx* ctx, const void* x, int n, int c, int h, int w, int cs, int dtype,
+                      float* y, float scale, int zp);
+
+/* ---- CUDA graph capture of a whole run (b=1 latency) ------------------- */
+int mdlc_graph_begin(mdlc_ctx* ctx);
+int mdlc_graph_end(mdlc_ctx* ctx);    /* instantiates the captured graph */
+int mdlc_graph_launch(mdlc_ctx* ctx);
+int mdlc_graph_reset(mdlc_ctx* ctx);
+
+/* ---- timing on the context stream (replaces nvrtc_runtime.py:211-225) -- */
+int mdlc_event_record(mdlc_ctx* ctx, int slot); /* slot in [0, 4096) */
+int mdlc_event_elapsed(mdlc_ctx* ctx, int start_slot, int stop_slot, float* ms);
+/* number of kernels this context has launched (including graph replays) */
+int mdlc_launch_count(mdlc_ctx* ctx, long long* count);
+
+/* ---- fault handling self-test ----------------------------------------- */
+/* Launches a one-thread kernel that waits on an mbarrier nothing will ever
+ * complete, with the given time limit in microseconds; the wait gives up, the
+ * kernel records MDLC_DEVERR_WAIT_TIMEOUT in the error word and returns. Used
+ * to test the bounded-wait path without faulting or hanging the GPU. */
+int mdlc_debug_timeout_probe(mdlc_ctx* ctx, int limit_us);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* MDLC_B200_H */

@@ -1,0 +1,396 @@
+"""``compile(graph) -> Executable``: the drop-in for mdlc's codegen + GPU runtime.
+
+Reference surface replaced (``mdlc/compiler.py:64-95`` builds ``Compiled``
+with a ``CudaModule`` from ``emit_cuda_module`` (``codegen/cuda/emit.py:292``)
+that ``GpuExecutor(module).run(feeds, timing)`` executes
+(``codegen/cuda/gpu_executor.py:38-98``)). Here:
+
+    exe = compile(graph, dtype="bf16", batch=256, devices=8)
+    out = exe.run({"input": x})          # dict name -> np.ndarray (fp32, reference layout)
+    exe.report(); exe.fallbacks() == []  # no host fallbacks, ever
+    exe.time_ms(iters=50, warmup=10)     # CUDA-event timing (nvrtc_runtime.py:211-225)
+
+``graph`` is the passes-optimised IR — the reference's own ``Graph`` from
+``default_pipeline()`` works by duck typing, as does
+:class:`mdlc_b200.ir.Graph` from :func:`mdlc_b200.passes.default_pipeline`.
+``schedule_fn`` (the reference codegen hook, ``emit.py:27,100``) is accepted
+as ``tuner``: a callable ``tuner(kind, geom) -> (bn, stages) | None``.
+
+Multi-GPU: ``devices=G`` shards the batch into G contiguous slices, one per
+GPU, with weights replicated and no collective; each device runs its slice
+on its own stream from its own host thread and the outputs are gathered on
+the host.
+"""
+
+from __future__ import annotations
+
+import ctypes as C
+import threading
+from dataclasses import dataclass
+
+import numpy as np
+
+from mdlc_b200 import _lib as L
+from mdlc_b200 import lowering, memory
+from mdlc_b200 import shapes as S
+
+DTYPES = {"bf16": L.BF16, "fp32": L.F32, "f32": L.F32}
+
+
+def _has_static_shapes(graph) -> bool:
+    vi = graph.value_info
+    for n in graph.nodes:
+        for o in n.outputs:
+            if o and (o not in vi or not all(isinstance(d, (int, np.integer)) and d >= 0
+                                             for d in vi[o].shape)):
+                return False
+    return True
+
+
+@dataclass
+class _ConvCall:
+    desc: L.ConvDesc
+    x: str
+    y: str
+    res: str
+    weight: str
+    epi: L.Epilogue
+    cfg: L.TileCfg
+
+
+class _Device:
+    """Per-GPU state: context, weights, arena, staging buffers, prepared calls."""
+
+    def __init__(self, exe: "Executable", device: int, batch: int):
+        self.exe = exe
+        self.ctx = L.Context(device)
+        self.batch = batch
+        lo = exe._lowered_for(batch)
+        self.lo = lo
+        self.plan = memory.plan_arena(lo.steps, lo.tensors, lo.inputs, lo.outputs)
+        self.arena = self.ctx.alloc(max(self.plan.total_bytes, 256))
+        self.addr = {name: self.arena + off for name, off in self.plan.offsets.items()}
+        # weights (packed on the host by the library's packer, uploaded once)
+        self.wbuf, self.bbuf = {}, {}
+        for wname, (geom, wt, bias) in lo.weights.items():
+            desc = self._desc(geom, lo)
+            packed = L.pack_weights(desc, wt)
+            self.wbuf[wname] = self.ctx.to_device(packed)
+            self.bbuf[wname] = self.ctx.to_device(bias)
+        self.cbuf = {name: self.ctx.to_device(arr) for name, arr in lo.consts.items()}
+        # staging: fp32 NCHW feeds / outputs on device and pinned on the host
+        self.in_dev, self.in_host, self.out_dev, self.out_host = {}, {}, {}, {}
+        for name in lo.inputs:
+            nbytes = int(np.prod(lo.shapes[name])) * 4
+            self.in_dev[name] = self.ctx.alloc(nbytes)
+            self.in_host[name] = self.ctx.host_alloc(nbytes)
+        for name in lo.outputs:
+            nbytes = int(np.prod(lo.shapes[name])) * 4
+            t = lo.tensors[name]
+            direct = t.dtype == L.F32 and t.cs == t.c and t.h * t.w == 1
+            self.out_dev[name] = None if direct else self.ctx.alloc(nbytes)
+            self.out_host[name] = self.ctx.host_alloc(nbytes)
+        self.calls = self._prepare()
+        self.graph_ready = False
+
+    def ptr(self, name):
+        return self.addr[memory.storage_of(self.lo.tensors, name)]
+
+    def _desc(self, geom, lo):
+        k = geom["k"]
+        return L.ConvDesc(n=geom["n"], h=geom["h"], w=geom["w"], c=geom["c"],
+                          c_stride=lowering.round_up(geom["c"], 8), k=k, k_stride=lowering.round_up(k, 8),
+                          r=geom["r"], s=geom["s"], stride_h=geom["sh"], stride_w=geom["sw"],
+                          pad_t=geom["pt"], pad_l=geom["pl"], dil_h=geom["dh"], dil_w=geom["dw"],
+                          oh=geom["oh"], ow=geom["ow"], groups=geom["groups"], in_type=lo.dtype,
+                          out_type=lo.dtype, res_stride=0, in_zp=0)
+
+    def _prepare(self):
+        lo, calls = self.lo, []
+        for st in lo.steps:
+            if st.kind == "conv":
+                geom, _, _ = lo.weights[st.params["weight"]]
+                d = self._desc(geom, lo)
+                yt = lo.tensors[st.outputs[0]]
+                d.out_type = yt.dtype
+                a = st.params["attrs"]
+                act = st.params["act"]
+                epi = L.Epilogue(act=lowering.ACT_CODES[act], alpha=float(a.get("alpha", 0.01)),
+                                 beta=float(a.get("beta", 0.5)),
+                                 clip_lo=-np.inf if a.get("clip_min") is None else float(a["clip_min"]),
+                                 clip_hi=np.inf if a.get("clip_max") is None else float(a["clip_max"]))
+                if act == "HardSigmoid":
+                    epi.alpha = float(a.get("alpha", 0.2))
+                cfg = None
+                if self.exe.tuner is not None:
+                    choice = self.exe.tuner("conv", dict(geom, dtype=lo.dtype))
+                    if choice:
+                        cfg = L.TileCfg(bn=choice[0], stages=choice[1], flags=0)
+                calls.append(("conv", d, self.ptr(st.inputs[0]), self.wbuf[st.params["weight"]],
+                              self.bbuf[st.params["weight"]],
+                              self.ptr(st.params["residual"]) if st.params["residual"] else 0,
+                              self.ptr(st.outputs[0]), epi, cfg))
+            elif st.kind == "pool":
+                xt, yt = lo.tensors[st.inputs[0]], lo.tensors[st.outputs[0]]
+                p = st.params
+                d = L.PoolDesc(kind=p["kind"], n=xt.n, h=xt.h, w=xt.w, c=xt.c, c_stride=xt.cs,
+                               kh=p.get("kh", 1), kw=p.get("kw", 1), stride_h=p.get("sh", 1),
+                               stride_w=p.get("sw", 1), pad_t=p.get("pt", 0), pad_l=p.get("pl", 0),
+                               oh=p.get("oh", 1), ow=p.get("ow", 1), count_include_pad=p.get("cip", 0),
+                               dtype=xt.dtype)
+                calls.append(("pool", d, self.ptr(st.inputs[0]), self.ptr(st.outputs[0])))
+            else:
+                yt = lo.tensors[st.outputs[0]]
+                p = st.params
+                prog = L.EwProg(n=yt.n, hw=yt.h * yt.w, c=yt.c, c_stride=yt.cs, dtype=yt.dtype,
+                                n_inputs=len(p["operands"]), n_outputs=len(st.outputs),
+                                n_instr=len(p["code"]))
+                for i, m in enumerate(p["bcast"]):
+                    prog.bcast[i] = m
+                for i, r in enumerate(p["out_regs"]):
+                    prog.out_reg[i] = r
+                for i, (op, dst, s0, s1, f0, f1) in enumerate(p["code"]):
+                    prog.code[i] = L.EwInstr(op=op, dst=dst, src0=s0, src1=s1, imm0=f0, imm1=f1)
+                ins = [self.cbuf[o] if o in self.cbuf else self.ptr(o) for o in p["operands"]]
+                calls.append(("eltwise", prog, ins, [self.ptr(o) for o in st.outputs]))
+        return calls
+
+    # -------------------------------------------------------------- execution
+    def issue_steps(self):
+        ctx = self.ctx
+        for c in self.calls:
+            if c[0] == "conv":
+                _, d, x, w, b, r, y, epi, cfg = c
+                ctx.conv2d(d, x, w, b, r, y, epi, cfg)
+            elif c[0] == "pool":
+                ctx.pool2d(c[1], c[2], c[3])
+            else:
+                ctx.eltwise(c[1], c[2], c[3])
+
+    def issue_inputs(self):
+        for name in self.lo.inputs:
+            t = self.lo.tensors[name]
+            self.ctx.to_nhwc(self.in_dev[name], t.n, t.c, t.h, t.w, self.ptr(name), t.cs, t.dtype)
+
+    def issue_outputs(self):
+        for name in self.lo.outputs:
+            t = self.lo.tensors[name]
+            if self.out_dev[name] is not None:
+                self.ctx.to_nchw(self.ptr(name), t.n, t.c, t.h, t.w, t.cs, t.dtype, self.out_dev[name])
+
+    def out_src(self, name):
+        return self.out_dev[name] if self.out_dev[name] is not None else self.ptr(name)
+
+    def issue_forward(self):
+        """Device-resident forward: layout-in, every step, layout-out."""
+        self.issue_inputs()
+        self.issue_steps()
+        self.issue_outputs()
+
+    def capture(self):
+        self.ctx.graph_begin()
+        try:
+            self.issue_forward()
+        finally:
+            self.ctx.graph_end()
+        self.graph_ready = True
+
+    def forward(self, use_graph):
+        if use_graph:
+            if not self.graph_ready:
+                self.capture()
+            self.ctx.graph_launch()
+        else:
+            self.issue_forward()
+
+    def run_host(self, feeds_slice, use_graph=False):
+        """Pinned H2D of the feeds, forward, D2H of the outputs (all on the stream)."""
+        lo = self.lo
+        for name in lo.inputs:
+            arr = np.ascontiguousarray(feeds_slice[name], dtype=np.float32)
+            host = np.ctypeslib.as_array((C.c_float * arr.size).from_address(self.in_host[name]))
+            host[:] = arr.reshape(-1)
+            self.ctx.upload_async(self.in_dev[name], self.in_host[name], arr.nbytes)
+        self.forward(use_graph)
+        outs = {}
+        for name in lo.outputs:
+            n = int(np.prod(lo.shapes[name]))
+            self.ctx.download_async(self.out_host[name], self.out_src(name), n * 4)
+        self.ctx.sync()
+        for name in lo.outputs:
+            n = int(np.prod(lo.shapes[name]))
+            host = np.ctypeslib.as_array((C.c_float * n).from_address(self.out_host[name]))
+            outs[name] = host.copy().reshape(lo.shapes[name])
+        return outs
+
+    def pinned_views(self):
+        lo = self.lo
+        ins = {n: np.ctypeslib.as_array((C.c_float * int(np.prod(lo.shapes[n]))).from_address(
+            self.in_host[n])).reshape(lo.shapes[n]) for n in lo.inputs}
+        outs = {n: np.ctypeslib.as_array((C.c_float * int(np.prod(lo.shapes[n]))).from_address(
+            self.out_host[n])).reshape(lo.shapes[n]) for n in lo.outputs}
+        return ins, outs
+
+    def issue_pinned(self, use_graph=False):
+        """H2D from the pinned feed buffers, forward, D2H into the pinned output buffers."""
+        lo = self.lo
+        for name in lo.inputs:
+            self.ctx.upload_async(self.in_dev[name], self.in_host[name], int(np.prod(lo.shapes[name])) * 4)
+        self.forward(use_graph)
+        for name in lo.outputs:
+            self.ctx.download_async(self.out_host[name], self.out_src(name), int(np.prod(lo.shapes[name])) * 4)
+
+    def close(self):
+        self.ctx.close()
+
+
+class Executable:
+    """A compiled graph bound to one or more B200s."""
+
+    def __init__(self, graph, *, dtype="bf16", batch=None, devices=1, tuner=None, mem_plan=None):
+        if dtype not in DTYPES:
+            raise ValueError(f"dtype must be one of {sorted(DTYPES)}")
+        self.graph = graph
+        self.dtype_name = dtype
+        self.dtype = DTYPES[dtype]
+        self.tuner = tuner
+        self.ref_mem_plan = mem_plan
+        base = S.infer(graph, batch)
+        self.batch = int(batch if batch is not None else base[graph.runtime_inputs[0]][0])
+        if _has_static_shapes(graph) and batch is None:
+            for n in graph.nodes:
+                for o in n.outputs:
+                    if o and tuple(graph.value_info[o].shape) != tuple(base[o]):
+                        raise ValueError(f"recorded shape of {o!r} disagrees with the shape rules")
+        if isinstance(devices, int):
+            ndev = devices
+            devs = list(range(devices))
+        else:
+            devs = list(devices)
+            ndev = len(devs)
+        if ndev < 1 or self.batch % ndev:
+            raise ValueError(f"batch {self.batch} must split evenly over {ndev} devices")
+        self.shard = self.batch // ndev
+        self._lowered = {}
+        self.lowered = self._lowered_for(self.shard)   # validates the graph (raises on gaps)
+        self.devices = [_Device(self, d, self.shard) for d in devs]
+
+    def _lowered_for(self, batch):
+        if batch not in self._lowered:
+            shp = S.infer(self.graph, batch)
+            lo = lowering.lower(self.graph, shp, self.dtype)
+            for o in lo.outputs:      # dense-conv graph outputs are written as fp32 directly
+                prod = [st for st in lo.steps if o in st.outputs]
+                if prod and prod[0].kind == "conv" and lo.weights[prod[0].params["weight"]][0]["groups"] == 1:
+                    lo.tensors[o].dtype = L.F32
+            self._lowered[batch] = lo
+        return self._lowered[batch]
+
+    # ------------------------------------------------------------------ API
+    def run(self, feeds: dict, *, use_graph: bool = False) -> dict:
+        """Run on host numpy feeds; returns fp32 outputs in the reference layout."""
+        names = self.lowered.inputs
+        missing = [n for n in names if n not in feeds]
+        if missing:
+            raise KeyError(f"missing feeds: {missing}")
+        slices = []
+        for i, _ in enumerate(self.devices):
+            lo, hi = i * self.shard, (i + 1) * self.shard
+            slices.append({n: np.asarray(feeds[n])[lo:hi] for n in names})
+        if len(self.devices) == 1:
+            results = [self.devices[0].run_host(slices[0], use_graph)]
+        else:
+            results = [None] * len(self.devices)
+            errors = []
+
+            def work(i):
+                try:
+                    results[i] = self.devices[i].run_host(slices[i], use_graph)
+                except BaseException as e:   # noqa: BLE001 - re-raised below
+                    errors.append(e)
+
+            threads = [threading.Thread(target=work, args=(i,)) for i in range(len(self.devices))]
+            for t in threads:
+                t.start()
+            for t in threads:
+                t.join()
+            if errors:
+                raise errors[0]
+        return {o: np.concatenate([r[o] for r in results], axis=0) if len(results) > 1 else results[0][o]
+                for o in self.lowered.outputs}
+
+    def pinned_inputs(self, device: int = 0) -> dict:
+        """Numpy views of a device's pinned feed buffers (fill them, then ``run_pinned``)."""
+        return self.devices[device].pinned_views()[0]
+
+    def pinned_outputs(self, device: int = 0) -> dict:
+        """Numpy views of a device's pinned output buffers (valid after ``run_pinned`` + ``sync``)."""
+        return self.devices[device].pinned_views()[1]
+
+    def run_pinned(self, use_graph: bool = False, sync: bool = True) -> None:
+        """Zero-copy host API: pinned H2D of the feeds, forward, D2H of the outputs."""
+        for d in self.devices:
+            d.issue_pinned(use_graph)
+        if sync:
+            self.sync()
+
+    def forward_device(self, use_graph: bool = False) -> None:
+        """Issue one forward on every device with inputs already resident."""
+        for d in self.devices:
+            d.forward(use_graph)
+
+    def sync(self) -> None:
+        for d in self.devices:
+            d.ctx.sync()
+
+    def time_ms(self, iters: int = 50, warmup: int = 10, use_graph: bool = False) -> float:
+        """Device time per forward (CUDA events on each device's stream; max over devices)."""
+        for _ in range(warmup):
+            self.forward_device(use_graph)
+        self.sync()
+        for d in self.devices:
+            d.ctx.event_record(0)
+        for _ in range(iters):
+            self.forward_device(use_graph)
+        for d in self.devices:
+            d.ctx.event_record(1)
+        self.sync()
+        return max(d.ctx.event_elapsed(0, 1) for d in self.devices) / iters
+
+    def fallbacks(self) -> list:
+        """Host-executed operations: always none (``emit.py:57-72`` lists them in the reference)."""
+        return []
+
+    def launches_per_forward(self) -> int:
+        return len(self.lowered.steps) + len(self.lowered.inputs) + sum(
+            1 for o in self.lowered.outputs if self.devices[0].out_dev[o] is not None)
+
+    def report(self) -> str:
+        lo = self.lowered
+        kinds = {}
+        for st in lo.steps:
+            kinds[st.kind] = kinds.get(st.kind, 0) + 1
+        lines = ["== mdlc_b200 executable ==",
+                 f"dtype {self.dtype_name}, batch {self.batch} over {len(self.devices)} device(s) "
+                 f"({self.shard} per device)",
+                 f"steps: {len(lo.steps)} (" + ", ".join(f"{k}x{v}" for k, v in sorted(kinds.items())) + ")",
+                 f"kernel launches per forward: {self.launches_per_forward()}",
+                 "host fallbacks: none",
+                 self.devices[0].plan.report()]
+        w = sum(L.weight_bytes(self.devices[0]._desc(g, lo)) for g, _, _ in lo.weights.values())
+        lines.append(f"packed weights: {w / 2**20:.3f} MB per device")
+        for st in lo.steps:
+            lines.append(f"  {st.label()}: {', '.join(st.inputs)} -> {', '.join(st.outputs)}")
+        return "\n".join(lines)
+
+    def close(self) -> None:
+        for d in self.devices:
+            d.close()
+        self.devices = []
+
+
+def compile(graph, *, mem_plan=None, dtype: str = "bf16", batch=None, devices=1, tuner=None,
+            schedule_fn=None) -> Executable:
+    """Compile a post-pass Graph IR for B200 execution (see module docstring)."""
+    return Executable(graph, dtype=dtype, batch=batch, devices=devices, tuner=tuner or schedule_fn,
+                      mem_plan=mem_plan)

@@ -1,0 +1,242 @@
+// Device-side helpers shared by the sm_100a kernels: inline PTX wrappers for
+// mbarriers, cp.async, TMA tile loads and tcgen05 (TMEM alloc, UMMA issue,
+// commit, TMEM->register loads), bounded waits, activation math and bf16
+// packing. Written against the PTX ISA for sm_100a; no CUTLASS types.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "mdlc_b200.h"
+
+#define MDLC_DEV __device__ __forceinline__
+
+namespace mdlc {
+
+// ------------------------------------------------------------ error word
+// Each context owns one int in device memory; kernels record the first
+// device-side failure with atomicCAS so the first cause is kept.
+MDLC_DEV void record_error(int* err, int code) {
+  if (err) atomicCAS(err, 0, code);
+}
+
+MDLC_DEV uint64_t globaltimer_ns() {
+  uint64_t t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+
+MDLC_DEV uint32_t smem_u32(const void* p) {
+  return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+// ------------------------------------------------------------ mbarrier
+MDLC_DEV void mbar_init(uint32_t bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(bar), "r"(count) : "memory");
+}
+MDLC_DEV void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+MDLC_DEV void mbar_arrive(uint32_t bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(bar) : "memory");
+}
+MDLC_DEV void mbar_arrive_expect_tx(uint32_t bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(bar), "r"(bytes)
+               : "memory");
+}
+MDLC_DEV bool mbar_try_wait(uint32_t bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(bar), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait for the phase with the given parity to complete. Gives up when
+// another role of the CTA has already given up (*abort != 0) or after
+// limit_ns; on time-out it records MDLC_DEVERR_WAIT_TIMEOUT and raises *abort.
+// Returns true when the phase completed.
+MDLC_DEV bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort, int* err,
+                        uint64_t limit_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = globaltimer_ns();
+  for (uint32_t i = 1;; ++i) {
+    if (mbar_try_wait(bar, parity)) return true;
+    if ((i & 63u) == 0) {
+      if (abort && *abort) return false;
+      if (globaltimer_ns() - t0 > limit_ns) {
+        record_error(err, MDLC_DEVERR_WAIT_TIMEOUT);
+        if (abort) *abort = 1;
+        return false;
+      }
+    }
+  }
+}
+
+MDLC_DEV void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// ------------------------------------------------------------ cp.async
+// 16-byte global->shared copy; src_bytes < 16 zero-fills the remainder
+// (src_bytes == 0 reads nothing and writes 16 zero bytes).
+MDLC_DEV void cp_async_16(uint32_t dst, const void* src, uint32_t src_bytes) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src),
+               "r"(src_bytes)
+               : "memory");
+}
+MDLC_DEV void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+MDLC_DEV void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
+}
+MDLC_DEV void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+// Arrive on the mbarrier once every cp.async this thread issued so far has
+// landed; .noinc: the arrival counts against the barrier's expected count.
+MDLC_DEV void cp_async_mbar_arrive_noinc(uint32_t bar) {
+  asm volatile("cp.async.mbarrier.arrive.noinc.shared::cta.b64 [%0];" ::"r"(bar) : "memory");
+}
+
+// ------------------------------------------------------------ TMA
+MDLC_DEV void tma_prefetch_desc(const void* tmap) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
+}
+// 2-D tiled load (no multicast) completing on an mbarrier transaction count.
+MDLC_DEV void tma_load_2d(uint32_t dst, const void* tmap, int32_t x, int32_t y, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+
+// ------------------------------------------------------------ tcgen05
+MDLC_DEV void tmem_alloc(uint32_t dst_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(dst_smem),
+               "r"(ncols)
+               : "memory");
+}
+MDLC_DEV void tmem_relinquish() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+}
+MDLC_DEV void tmem_dealloc(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols)
+               : "memory");
+}
+MDLC_DEV void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+MDLC_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+// Shared-memory matrix descriptor for a K-major operand stored in 128-byte
+// swizzled rows: 8-row groups 1024 bytes apart (SBO), LBO unused (1),
+// descriptor version 1 (sm_100), layout type 2 = SWIZZLE_128B.
+MDLC_DEV uint64_t umma_desc_sw128(uint32_t saddr) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) |
+         ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// Instruction descriptor, kind::f16 with bf16 operands and fp32 accumulator.
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
+  return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) |
+         ((uint32_t)(M >> 4) << 24);
+}
+// Instruction descriptor, kind::i8 with int32 accumulator; a_signed/b_signed
+// select s8 (1) or u8 (0) operands.
+__host__ __device__ constexpr uint32_t idesc_i8(int M, int N, int a_signed, int b_signed) {
+  return (2u << 4) | ((uint32_t)a_signed << 7) | ((uint32_t)b_signed << 10) |
+         ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+MDLC_DEV void umma_bf16(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+MDLC_DEV void umma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                      uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+// Arrive on an mbarrier once all previously issued tcgen05 async operations
+// of this thread have completed.
+MDLC_DEV void umma_commit(uint32_t bar) {
+  asm volatile(
+      "tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar)
+      : "memory");
+}
+
+// 32 lanes x 32-bit, 16 consecutive columns per thread.
+MDLC_DEV void tmem_ld16(uint32_t taddr, uint32_t (&v)[16]) {
+  asm volatile(
+      "tcgen05.ld.sync.aligned.32x32b.x16.b32 "
+      "{%0,%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15}, [%16];"
+      : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]),
+        "=r"(v[7]), "=r"(v[8]), "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]),
+        "=r"(v[14]), "=r"(v[15])
+      : "r"(taddr)
+      : "memory");
+}
+MDLC_DEV void tmem_ld_wait() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+
+// ------------------------------------------------------------ activations
+struct ActParams {
+  int act;
+  float alpha, beta, lo, hi;
+};
+
+MDLC_DEV float apply_act(float v, const ActParams& p) {
+  switch (p.act) {
+    case MDLC_ACT_RELU: return fmaxf(v, 0.0f);
+    case MDLC_ACT_CLIP: return fminf(fmaxf(v, p.lo), p.hi);
+    case MDLC_ACT_SIGMOID: return 1.0f / (1.0f + expf(-v));
+    case MDLC_ACT_TANH: return tanhf(v);
+    case MDLC_ACT_LEAKY_RELU: return v >= 0.0f ? v : p.alpha * v;
+    case MDLC_ACT_HARD_SIGMOID: return fminf(fmaxf(p.alpha * v + p.beta, 0.0f), 1.0f);
+    case MDLC_ACT_HARD_SWISH: return v * fminf(fmaxf(v / 6.0f + 0.5f, 0.0f), 1.0f);
+    case MDLC_ACT_GELU: return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+    default: return v;
+  }
+}
+
+// ------------------------------------------------------------ bf16 packing
+MDLC_DEV uint32_t pack_bf16x2(float lo, float hi) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+MDLC_DEV float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }
+MDLC_DEV float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
+
+// ------------------------------------------------------------ int8 requant
+// gemmlowp / TFLite fixed point: SaturatingRoundingDoublingHighMul followed
+// by RoundingDivideByPOT (round half away from zero).
+MDLC_DEV int32_t sat_rdh_mul(int32_t a, int32_t b) {
+  if (a == INT32_MIN && b == INT32_MIN) return INT32_MAX;
+  const long long ab = (long long)a * (long long)b;
+  const long long nudge = ab >= 0 ? (1ll << 30) : (1 - (1ll << 30));
+  return (int32_t)((ab + nudge) / (1ll << 31));
+}
+MDLC_DEV int32_t rounding_rshift(int32_t x, int shift) {
+  if (shift <= 0) return x;
+  const int32_t mask = (int32_t)((1ll << shift) - 1);
+  const int32_t rem = x & mask;
+  const int32_t threshold = (mask >> 1) + (x < 0 ? 1 : 0);
+  return (x >> shift) + (rem > threshold ? 1 : 0);
+}
+MDLC_DEV int32_t requant(int32_t acc, int32_t mult, int32_t shift) {
+  return rounding_rshift(sat_rdh_mul(acc, mult), shift);
+}
+
+}  // namespace mdlc

@@ -1,0 +1,396 @@
+// mdlc_conv2d dispatch, weight packing, the fp32 SIMT implicit GEMM and the
+// depthwise convolution kernel.
+//
+// Reference semantics: mdlc/runtime/ops.py:56-81 (conv = im2col + einsum,
+// grouped conv per group), ops.py:84-92 (gemm). The reference lowering runs
+// conv as explicit im2col + an fp32 FFMA GEMM for one image at a time
+// (mdlc/codegen/cuda/emit.py:159-209) and grouped/depthwise conv on the host
+// (emit.py:175-180); here every case is a device kernel over the whole batch.
+#include <cmath>
+#include <cstring>
+
+#include "common.cuh"
+#include "conv.h"
+
+namespace mdlc {
+namespace {
+
+// ------------------------------------------------------------ fp32 SIMT GEMM
+// 64x64 output tile per 256-thread CTA, 16-deep k slices staged in shared
+// memory, 4x4 register micro-tile per thread. Implicit im2col: A elements are
+// gathered from the NHWC input on the fly (padding reads as zero).
+struct F32Args {
+  const float* x;
+  const float* w;  // [kg_pad][ks]
+  const float* bias;
+  const float* res;
+  float* y;
+  int h, w_, cs, k, ks, res_s, r, s, sh, sw, pt, pl, dh, dw, oh, ow, M, kg;
+  ActParams act;
+};
+
+__global__ void __launch_bounds__(256) conv_f32_kernel(const F32Args a) {
+  __shared__ float As[16][64 + 4];
+  __shared__ float Bs[16][64];
+  const int tid = threadIdx.x;
+  const int m0 = blockIdx.x * 64, n0 = blockIdx.y * 64;
+  const int kq = tid & 15;
+  int img[4], ih0[4], iw0[4];
+  const int ohw = a.oh * a.ow;
+#pragma unroll
+  for (int q = 0; q < 4; ++q) {
+    const int m = m0 + (tid >> 4) + 16 * q;
+    if (m < a.M) {
+      img[q] = m / ohw;
+      const int rem = m - img[q] * ohw;
+      const int oy = rem / a.ow;
+      ih0[q] = oy * a.sh - a.pt;
+      iw0[q] = (rem - oy * a.ow) * a.sw - a.pl;
+    } else {
+      img[q] = -1; ih0[q] = 0; iw0[q] = 0;
+    }
+  }
+  const int ty = tid >> 4, tx = tid & 15;
+  float acc[4][4] = {};
+  const int RS = a.r * a.s;
+  for (int k0 = 0; k0 < a.kg; k0 += 16) {
+    const int kk = k0 + kq;
+    const int tap = kk / a.cs;
+    const int c = kk - tap * a.cs;
+    const int rr = tap / a.s;
+    const int dy = rr * a.dh, dx = (tap - rr * a.s) * a.dw;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      float v = 0.0f;
+      const int ih = ih0[q] + dy, iw = iw0[q] + dx;
+      if (img[q] >= 0 && tap < RS && (unsigned)ih < (unsigned)a.h && (unsigned)iw < (unsigned)a.w_)
+        v = __ldg(a.x + ((long long)(img[q] * a.h + ih) * a.w_ + iw) * a.cs + c);
+      As[kq][(tid >> 4) + 16 * q] = v;
+    }
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      const int e = tid + 256 * q;
+      const int kr = e >> 6, nn = e & 63;
+      const int kg_i = k0 + kr;
+      Bs[kr][nn] = (n0 + nn < a.ks && kg_i < a.kg) ? __ldg(a.w + (long long)kg_i * a.ks + n0 + nn) : 0.0f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int t = 0; t < 16; ++t) {
+      float av[4], bv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) av[i] = As[t][ty * 4 + i];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) bv[j] = Bs[t][tx * 4 + j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
+    }
+    __syncthreads();
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int m = m0 + ty * 4 + i;
+    if (m >= a.M) continue;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+      const int n = n0 + tx * 4 + j;
+      if (n >= a.ks) continue;
+      float v = 0.0f;
+      if (n < a.k) {
+        v = acc[i][j];
+        if (a.bias) v += a.bias[n];
+        if (a.res) v += a.res[(long long)m * a.res_s + n];
+        v = apply_act(v, a.act);
+      }
+      a.y[(long long)m * a.ks + n] = v;
+    }
+  }
+}
+
+// ------------------------------------------------------------ depthwise
+// One thread per (output pixel, 8-channel group): nine (or r*s) 16-byte
+// vector loads of the input, fp32 weights [r*s][cs] and fp32 accumulation.
+template <typename T>
+struct Vec8;
+template <>
+struct Vec8<__nv_bfloat16> {
+  static MDLC_DEV void load(const __nv_bfloat16* p, float (&f)[8]) {
+    const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+    f[0] = bf16_lo(u.x); f[1] = bf16_hi(u.x); f[2] = bf16_lo(u.y); f[3] = bf16_hi(u.y);
+    f[4] = bf16_lo(u.z); f[5] = bf16_hi(u.z); f[6] = bf16_lo(u.w); f[7] = bf16_hi(u.w);
+  }
+  static MDLC_DEV void store(__nv_bfloat16* p, const float (&f)[8]) {
+    *reinterpret_cast<uint4*>(p) = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
+                                              pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
+  }
+};
+template <>
+struct Vec8<float> {
+  static MDLC_DEV void load(const float* p, float (&f)[8]) {
+    const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+    const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  }
+  static MDLC_DEV void store(float* p, const float (&f)[8]) {
+    reinterpret_cast<float4*>(p)[0] = make_float4(f[0], f[1], f[2], f[3]);
+    reinterpret_cast<float4*>(p)[1] = make_float4(f[4], f[5], f[6], f[7]);
+  }
+};
+
+struct DwArgs {
+  const void* x;
+  const float* w;
+  const float* bias;
+  const void* res;
+  void* y;
+  int h, w_, cs, c, r, s, sh, sw, pt, pl, dh, dw, oh, ow, res_s;
+  long long total;  // M * cs/8
+  ActParams act;
+};
+
+template <typename T>
+__global__ void __launch_bounds__(256) conv_dw_kernel(const DwArgs a) {
+  const int G = a.cs >> 3;
+  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < a.total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int g = (int)(idx % G);
+    const long long m = idx / G;
+    const int ohw = a.oh * a.ow;
+    const int img = (int)(m / ohw);
+    const int rem = (int)(m - (long long)img * ohw);
+    const int oy = rem / a.ow, ox = rem - (rem / a.ow) * a.ow;
+    const int c0 = g * 8;
+    float acc[8];
+    if (a.bias) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = __ldg(a.bias + c0 + e);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
+    }
+    const T* xb = static_cast<const T*>(a.x) + (long long)img * a.h * a.w_ * a.cs + c0;
+    for (int rr = 0; rr < a.r; ++rr) {
+      const int ih = oy * a.sh - a.pt + rr * a.dh;
+      if ((unsigned)ih >= (unsigned)a.h) continue;
+      for (int ss = 0; ss < a.s; ++ss) {
+        const int iw = ox * a.sw - a.pl + ss * a.dw;
+        if ((unsigned)iw >= (unsigned)a.w_) continue;
+        float xv[8], wv[8];
+        Vec8<T>::load(xb + ((long long)ih * a.w_ + iw) * a.cs, xv);
+        Vec8<float>::load(a.w + (rr * a.s + ss) * a.cs + c0, wv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] = fmaf(xv[e], wv[e], acc[e]);
+      }
+    }
+    if (a.res) {
+      float rv[8];
+      Vec8<T>::load(static_cast<const T*>(a.res) + m * a.res_s + c0, rv);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] += rv[e];
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) acc[e] = (c0 + e < a.c) ? apply_act(acc[e], a.act) : 0.0f;
+    Vec8<T>::store(static_cast<T*>(a.y) + m * a.cs + c0, acc);
+  }
+}
+
+ActParams act_of(const mdlc_epilogue* epi) {
+  if (!epi) return ActParams{MDLC_ACT_NONE, 0.f, 0.f, -INFINITY, INFINITY};
+  return ActParams{epi->act, epi->alpha, epi->beta, epi->clip_lo, epi->clip_hi};
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+uint16_t f32_to_bf16_rne(float f) {
+  uint32_t u;
+  std::memcpy(&u, &f, 4);
+  if ((u & 0x7F800000u) == 0x7F800000u && (u & 0x7FFFFFu)) return (uint16_t)((u >> 16) | 0x40);
+  u += 0x7FFFu + ((u >> 16) & 1u);
+  return (uint16_t)(u >> 16);
+}
+
+int validate(mdlc_ctx* ctx, const mdlc_conv_desc* d) {
+  if (!d) return mdlc_set_error(ctx, MDLC_ERR_INVALID, "conv: null descriptor");
+  if (d->n <= 0 || d->h <= 0 || d->w <= 0 || d->c <= 0 || d->k <= 0 || d->r <= 0 || d->s <= 0 ||
+      d->oh <= 0 || d->ow <= 0 || d->stride_h <= 0 || d->stride_w <= 0 || d->dil_h <= 0 ||
+      d->dil_w <= 0 || d->pad_t < 0 || d->pad_l < 0 || d->groups <= 0)
+    return mdlc_set_error(ctx, MDLC_ERR_INVALID, "conv: non-positive dimension");
+  const bool i8 = d->in_type == MDLC_U8 || d->in_type == MDLC_S8;
+  const int align = i8 ? 16 : 8;
+  if (d->c_stride < d->c || d->c_stride % align)
+    return mdlc_set_error(ctx, MDLC_ERR_INVALID, "conv: c_stride %d must be >= c and a multiple of %d",
+                          d->c_stride, align);
+  const bool o8 = d->out_type == MDLC_U8 || d->out_type == MDLC_S8;
+  if (d->k_stride < d->k || d->k_stride % (o8 ? 16 : 8))
+    return mdlc_set_error(ctx, MDLC_ERR_INVALID, "conv: k_stride %d must be >= k and a multiple of %d",
+                          d->k_stride, o8 ? 16 : 8);
+  if (d->res_stride && (d->res_stride < d->k || d->res_stride % (o8 ? 16 : 8)))
+    return mdlc_set_error(ctx, MDLC_ERR_INVALID, "conv: bad res_stride %d", d->res_stride);
+  const long long pixels = (long long)d->n * d->h * d->w;
+  if (pixels * d->c_stride >= (1ll << 40) || (long long)d->n * d->oh * d->ow >= (1ll << 31) - 256)
+    return mdlc_set_error(ctx, MDLC_ERR_INVALID, "conv: tensor too large");
+  return MDLC_OK;
+}
+
+enum Path { kPathTC, kPathF32, kPathDW, kPathNone };
+
+Path path_of(const mdlc_conv_desc& d) {
+  if (d.groups == 1) {
+    if (d.in_type == MDLC_BF16 && (d.out_type == MDLC_BF16 || d.out_type == MDLC_F32)) return kPathTC;
+    if ((d.in_type == MDLC_U8 || d.in_type == MDLC_S8) &&
+        (d.out_type == MDLC_U8 || d.out_type == MDLC_S8 || d.out_type == MDLC_F32))
+      return kPathTC;
+    if (d.in_type == MDLC_F32 && d.out_type == MDLC_F32) return kPathF32;
+    return kPathNone;
+  }
+  if (d.groups == d.c && d.c == d.k && d.in_type == d.out_type &&
+      (d.in_type == MDLC_BF16 || d.in_type == MDLC_F32))
+    return kPathDW;
+  return kPathNone;
+}
+
+}  // namespace
+
+int conv_f32(mdlc_ctx* ctx, const mdlc_conv_desc& d, const float* x, const float* w, const float* bias,
+             const float* res, float* y, const mdlc_epilogue* epi) {
+  F32Args a{};
+  a.x = x; a.w = w; a.bias = bias; a.res = res; a.y = y;
+  a.h = d.h; a.w_ = d.w; a.cs = d.c_stride; a.k = d.k; a.ks = d.k_stride;
+  a.res_s = d.res_stride ? d.res_stride : d.k_stride;
+  a.r = d.r; a.s = d.s; a.sh = d.stride_h; a.sw = d.stride_w; a.pt = d.pad_t; a.pl = d.pad_l;
+  a.dh = d.dil_h; a.dw = d.dil_w; a.oh = d.oh; a.ow = d.ow;
+  a.M = d.n * d.oh * d.ow;
+  a.kg = d.r * d.s * d.c_stride;
+  a.act = act_of(epi);
+  dim3 grid((a.M + 63) / 64, (d.k_stride + 63) / 64);
+  conv_f32_kernel<<<grid, 256, 0, ctx->stream>>>(a);
+  mdlc_note_launch(ctx);
+  return mdlc_cuda_status(ctx, cudaGetLastError(), "conv_f32 launch");
+}
+
+int conv_dw(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const float* w, const float* bias,
+            const void* res, void* y, const mdlc_epilogue* epi) {
+  DwArgs a{};
+  a.x = x; a.w = w; a.bias = bias; a.res = res; a.y = y;
+  a.h = d.h; a.w_ = d.w; a.cs = d.c_stride; a.c = d.c; a.r = d.r; a.s = d.s;
+  a.sh = d.stride_h; a.sw = d.stride_w; a.pt = d.pad_t; a.pl = d.pad_l; a.dh = d.dil_h; a.dw = d.dil_w;
+  a.oh = d.oh; a.ow = d.ow; a.res_s = d.res_stride ? d.res_stride : d.c_stride;
+  a.total = (long long)d.n * d.oh * d.ow * (d.c_stride / 8);
+  a.act = act_of(epi);
+  long long blocks = (a.total + 255) / 256;
+  const long long cap = (long long)ctx->num_sms * 16;
+  if (blocks > cap) blocks = cap;
+  if (d.in_type == MDLC_BF16)
+    conv_dw_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, ctx->stream>>>(a);
+  else
+    conv_dw_kernel<float><<<(unsigned)blocks, 256, 0, ctx->stream>>>(a);
+  mdlc_note_launch(ctx);
+  return mdlc_cuda_status(ctx, cudaGetLastError(), "conv_dw launch");
+}
+
+}  // namespace mdlc
+
+using namespace mdlc;
+
+extern "C" int mdlc_conv_weight_bytes(const mdlc_conv_desc* d, size_t* bytes) {
+  if (!d || !bytes) return MDLC_ERR_INVALID;
+  const long long kg = (long long)d->r * d->s * d->c_stride;
+  switch (path_of(*d)) {
+    case kPathTC: {
+      const int esz = (d->in_type == MDLC_BF16) ? 2 : 1;
+      const long long kb = 128 / esz;
+      *bytes = (size_t)(((kg + kb - 1) / kb) * 128) * (size_t)d->k;
+      return MDLC_OK;
+    }
+    case kPathF32:
+      *bytes = (size_t)kg * d->k_stride * sizeof(float);
+      return MDLC_OK;
+    case kPathDW:
+      *bytes = (size_t)d->r * d->s * d->c_stride * sizeof(float);
+      return MDLC_OK;
+    default:
+      return MDLC_ERR_UNSUPPORTED;
+  }
+}
+
+extern "C" int mdlc_pack_conv_weights(const mdlc_conv_desc* d, const float* w, void* out) {
+  if (!d || !w || !out) return MDLC_ERR_INVALID;
+  size_t bytes = 0;
+  int st = mdlc_conv_weight_bytes(d, &bytes);
+  if (st) return st;
+  std::memset(out, 0, bytes);
+  const int C = d->c, K = d->k, R = d->r, S = d->s, cs = d->c_stride;
+  const int icg = C / d->groups;
+  auto W = [&](int o, int c, int r, int s) { return w[(((long long)o * icg + c) * R + r) * S + s]; };
+  switch (path_of(*d)) {
+    case kPathTC: {
+      const int esz = (d->in_type == MDLC_BF16) ? 2 : 1;
+      const long long kb = 128 / esz;
+      const long long kg_pad = ((1ll * R * S * cs + kb - 1) / kb) * kb;
+      for (int o = 0; o < K; ++o)
+        for (int r = 0; r < R; ++r)
+          for (int s = 0; s < S; ++s)
+            for (int c = 0; c < C; ++c) {
+              const long long idx = (long long)o * kg_pad + (long long)(r * S + s) * cs + c;
+              if (esz == 2)
+                static_cast<uint16_t*>(out)[idx] = f32_to_bf16_rne(W(o, c, r, s));
+              else
+                static_cast<int8_t*>(out)[idx] = (int8_t)lrintf(W(o, c, r, s));
+            }
+      return MDLC_OK;
+    }
+    case kPathF32: {
+      float* o_ = static_cast<float*>(out);
+      for (int o = 0; o < K; ++o)
+        for (int r = 0; r < R; ++r)
+          for (int s = 0; s < S; ++s)
+            for (int c = 0; c < C; ++c)
+              o_[((long long)(r * S + s) * cs + c) * d->k_stride + o] = W(o, c, r, s);
+      return MDLC_OK;
+    }
+    case kPathDW: {
+      float* o_ = static_cast<float*>(out);
+      for (int c = 0; c < C; ++c)
+        for (int r = 0; r < R; ++r)
+          for (int s = 0; s < S; ++s) o_[(r * S + s) * cs + c] = W(c, 0, r, s);
+      return MDLC_OK;
+    }
+    default:
+      return MDLC_ERR_UNSUPPORTED;
+  }
+}
+
+extern "C" int mdlc_conv2d(mdlc_ctx* ctx, const mdlc_conv_desc* d, const void* x, const void* w,
+                           const void* bias, const void* res, void* y, const mdlc_epilogue* epi,
+                           const mdlc_tile_cfg* cfg) {
+  if (!ctx) return MDLC_ERR_INVALID;
+  int st = validate(ctx, d);
+  if (st) return st;
+  if (!x || !w || !y) return mdlc_set_error(ctx, MDLC_ERR_INVALID, "conv: null tensor pointer");
+  if (!aligned16(x) || !aligned16(w) || !aligned16(y) || (bias && !aligned16(bias)) ||
+      (res && !aligned16(res)))
+    return mdlc_set_error(ctx, MDLC_ERR_INVALID, "conv: pointers must be 16-byte aligned");
+  cudaSetDevice(ctx->device);
+  switch (path_of(*d)) {
+    case kPathTC:
+      if ((d->in_type == MDLC_U8 || d->in_type == MDLC_S8) && d->out_type != MDLC_F32 &&
+          (!epi || !epi->rq_mult || !epi->rq_shift))
+        return mdlc_set_error(ctx, MDLC_ERR_INVALID, "conv int8: requantisation arrays required");
+      if ((d->in_type == MDLC_U8 || d->in_type == MDLC_S8) && d->out_type == MDLC_F32 &&
+          (!epi || !epi->deq_scale))
+        return mdlc_set_error(ctx, MDLC_ERR_INVALID, "conv int8: deq_scale required for float output");
+      return conv_tc(ctx, *d, x, w, bias, res, y, epi, cfg);
+    case kPathF32:
+      return conv_f32(ctx, *d, static_cast<const float*>(x), static_cast<const float*>(w),
+                      static_cast<const float*>(bias), static_cast<const float*>(res), static_cast<float*>(y),
+                      epi);
+    case kPathDW:
+      return conv_dw(ctx, *d, x, static_cast<const float*>(w), static_cast<const float*>(bias), res, y, epi);
+    default:
+      return mdlc_set_error(ctx, MDLC_ERR_UNSUPPORTED,
+                            "conv: groups=%d in_type=%d out_type=%d not supported", d->groups, d->in_type,
+                            d->out_type);
+  }
+}

@@ -1,0 +1,511 @@
+// Implicit-GEMM convolution / GEMM on the sm_100a tensor cores (tcgen05).
+//
+// GEMM view: D[M x N] = A[M x K] * B[N x K]^T with
+//   M = n*oh*ow output pixels (NHWC row order),
+//   N = output channels,
+//   K = r*s*c_stride (tap-major, channel-minor), padded to the k-block.
+// A is never materialised (no im2col buffer): four producer warps gather each
+// 128-pixel x 128-byte k-block straight from the NHWC input with 16-byte
+// cp.async (zero-fill, or a zero-point pattern for int8, at padded taps) and
+// write it in the 128-byte-swizzled K-major layout UMMA reads; completion is
+// signalled asynchronously (cp.async.mbarrier.arrive.noinc), so each producer
+// keeps up to STAGES k-blocks in flight. B (the packed
+// weights, [N][K_pad]) arrives by 2-D TMA with the same swizzle. One thread
+// issues tcgen05.mma (kind::f16 for bf16, kind::i8 for int8) into a TMEM
+// accumulator of 128 lanes x BN columns; four epilogue warps read it back
+// with tcgen05.ld and apply bias / residual / activation or the int8
+// requantisation before storing NHWC.
+//
+// The kernel is persistent: each CTA walks tiles (m-tile major, n-tile
+// minor) with a STAGES-deep shared-memory ring that runs across tiles and two
+// TMEM accumulators, so the epilogue of one tile overlaps the main loop of the
+// next. Warp roles (320 threads):
+//   warps 0-3  A producers (cp.async gather)
+//   warps 4-7  epilogue (warp w reads TMEM lanes 32*(w%4) .. +31)
+//   warp 8     B producer (TMA), lane 0
+//   warp 9     TMEM allocator + MMA issuer, lane 0
+// Every mbarrier wait is bounded; on expiry the CTA records
+// MDLC_DEVERR_WAIT_TIMEOUT, drains its in-flight copies and MMAs, frees TMEM
+// and exits.
+#include <cudaTypedefs.h>
+
+#include <mutex>
+
+#include "common.cuh"
+#include "conv.h"
+#include "runtime.h"
+
+namespace mdlc {
+namespace {
+
+constexpr int kThreads = 320;
+constexpr int kBM = 128;
+constexpr int kABytes = kBM * 128;  // one A stage: 128 rows x 128 bytes
+
+struct TcArgs {
+  const uint8_t* x;
+  void* y;
+  const void* bias;      // float[k] (bf16 path) or int32[k] (int8 path); may be null
+  const uint8_t* res;    // residual NHWC, may be null
+  const uint8_t* pad_src;  // 16-byte pad pattern (int8 zero point) or null for zero fill
+  int* err;
+  int n, h, w, cs;
+  int k, ks, res_s;
+  int r, s, sh, sw, pt, pl, dh, dw, oh, ow;
+  int M, num_kb, num_m_tiles, num_n_tiles;
+  int out_type, a_signed;
+  ActParams act;
+  const int32_t* rq_mult;
+  const int32_t* rq_shift;
+  int out_zp, qmin, qmax, res_zp, res_mult, res_shift;
+  const float* deq_scale;
+  const float* deq_bias;
+  unsigned long long wait_ns;
+};
+
+template <int BN, int STAGES>
+struct Smem {
+  static constexpr int kBBytes = BN * 128;
+  static constexpr int kA = 0;
+  static constexpr int kB = STAGES * kABytes;
+  static constexpr int kBar = kB + STAGES * kBBytes;
+  // barriers: fullA[S], fullB[S], empty[S], tfull[2], tempty[2], drain
+  static constexpr int kNumBars = 3 * STAGES + 5;
+  static constexpr int kMisc = kBar + kNumBars * 8;
+  static constexpr int kBytes = kMisc + 16;
+  static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
+};
+
+// ---------------------------------------------------------------- epilogue
+template <int ESZ>
+MDLC_DEV void store_chunk16(const TcArgs& a, int m, int nb0, const uint32_t (&v)[16]) {
+  const long long row = (long long)m * a.ks;
+  if constexpr (ESZ == 2) {
+    float f[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) f[e] = __uint_as_float(v[e]);
+    if (nb0 + 16 <= a.k) {
+      if (a.bias) {
+        const float4* b4 = reinterpret_cast<const float4*>(static_cast<const float*>(a.bias) + nb0);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 bb = __ldg(b4 + q);
+          f[4 * q] += bb.x; f[4 * q + 1] += bb.y; f[4 * q + 2] += bb.z; f[4 * q + 3] += bb.w;
+        }
+      }
+      if (a.res) {
+        const uint4* r4 = reinterpret_cast<const uint4*>(a.res + ((long long)m * a.res_s + nb0) * 2);
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          const uint4 rr = __ldg(r4 + q);
+          const uint32_t u[4] = {rr.x, rr.y, rr.z, rr.w};
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            f[8 * q + 2 * t] += bf16_lo(u[t]);
+            f[8 * q + 2 * t + 1] += bf16_hi(u[t]);
+          }
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 16; ++e) f[e] = apply_act(f[e], a.act);
+      if (a.out_type == MDLC_F32) {
+        float4* y4 = reinterpret_cast<float4*>(static_cast<float*>(a.y) + row + nb0);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) y4[q] = make_float4(f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]);
+      } else {
+        uint4* y4 = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.y) + row + nb0);
+#pragma unroll
+        for (int q = 0; q < 2; ++q)
+          y4[q] = make_uint4(pack_bf16x2(f[8 * q], f[8 * q + 1]), pack_bf16x2(f[8 * q + 2], f[8 * q + 3]),
+                             pack_bf16x2(f[8 * q + 4], f[8 * q + 5]), pack_bf16x2(f[8 * q + 6], f[8 * q + 7]));
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const int ch = nb0 + e;
+        if (ch >= a.ks) continue;
+        float val = 0.0f;
+        if (ch < a.k) {
+          val = f[e];
+          if (a.bias) val += static_cast<const float*>(a.bias)[ch];
+          if (a.res) {
+            const uint16_t rb = *reinterpret_cast<const uint16_t*>(a.res + ((long long)m * a.res_s + ch) * 2);
+            val += __uint_as_float((uint32_t)rb << 16);
+          }
+          val = apply_act(val, a.act);
+        }
+        if (a.out_type == MDLC_F32)
+          static_cast<float*>(a.y)[row + ch] = val;
+        else
+          static_cast<__nv_bfloat16*>(a.y)[row + ch] = __float2bfloat16_rn(val);
+      }
+    }
+  } else {
+    // int8 path: v holds int32 accumulators
+    const int32_t* bias32 = static_cast<const int32_t*>(a.bias);
+    if (a.out_type == MDLC_F32) {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const int ch = nb0 + e;
+        if (ch >= a.ks) continue;
+        float val = 0.0f;
+        if (ch < a.k) {
+          const int32_t acc = (int32_t)v[e] + (bias32 ? bias32[ch] : 0);
+          val = __fmul_rn((float)acc, a.deq_scale[ch]);
+          if (a.deq_bias) val = __fadd_rn(val, a.deq_bias[ch]);
+        }
+        static_cast<float*>(a.y)[row + ch] = val;
+      }
+      return;
+    }
+    uint32_t packed[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const int ch = nb0 + e;
+      int32_t q = 0;
+      if (ch < a.k) {
+        const int32_t acc = (int32_t)v[e] + (bias32 ? bias32[ch] : 0);
+        int32_t t = a.out_zp + requant(acc, a.rq_mult[ch], a.rq_shift[ch]);
+        if (a.res) {
+          const int32_t rq = (a.out_type == MDLC_S8)
+                                 ? (int32_t)(int8_t)a.res[(long long)m * a.res_s + ch]
+                                 : (int32_t)a.res[(long long)m * a.res_s + ch];
+          t += requant(rq - a.res_zp, a.res_mult, a.res_shift);
+        }
+        q = min(max(t, a.qmin), a.qmax);
+      }
+      packed[e >> 2] |= ((uint32_t)(q & 0xFF)) << (8 * (e & 3));
+    }
+    uint8_t* yb = static_cast<uint8_t*>(a.y) + row + nb0;
+    if (nb0 + 16 <= a.ks) {
+      *reinterpret_cast<uint4*>(yb) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 16; ++e)
+        if (nb0 + e < a.ks) yb[e] = (uint8_t)(packed[e >> 2] >> (8 * (e & 3)));
+    }
+  }
+}
+
+// ---------------------------------------------------------------- kernel
+template <int BN, int STAGES, int ESZ>
+__global__ void __launch_bounds__(kThreads, 1)
+    conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const TcArgs a) {
+  using L = Smem<BN, STAGES>;
+  constexpr int KB = 128 / ESZ;    // k-block elements (128 bytes)
+  constexpr int CHUNK = 16 / ESZ;  // elements per 16-byte chunk
+  constexpr uint32_t kTmemCols = 2 * BN;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t sA = sbase + L::kA, sB = sbase + L::kB, sbar = sbase + L::kBar;
+  auto fullA = [&](int i) { return sbar + 8u * i; };
+  auto fullB = [&](int i) { return sbar + 8u * (STAGES + i); };
+  auto empty = [&](int i) { return sbar + 8u * (2 * STAGES + i); };
+  auto tfull = [&](int i) { return sbar + 8u * (3 * STAGES + i); };
+  auto tempty = [&](int i) { return sbar + 8u * (3 * STAGES + 2 + i); };
+  const uint32_t drain = sbar + 8u * (3 * STAGES + 4);
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      mbar_init(fullA(i), 128);
+      mbar_init(fullB(i), 1);
+      mbar_init(empty(i), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(tfull(i), 1);
+      mbar_init(tempty(i), 128);
+    }
+    mbar_init(drain, 1);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 8 && lane == 0) tma_prefetch_desc(&tmap_w);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  const int num_tiles = a.num_m_tiles * a.num_n_tiles;
+  const int RS = a.r * a.s;
+
+  if (warp < 4) {
+    // ---------------- A producers: implicit im2col gather
+    const int j = tid & 7;     // 16-byte chunk within the 128-byte row
+    const int row0 = tid >> 3; // rows row0 + 16*i, i = 0..7
+    const uint32_t row_off = (uint32_t)row0 * 128u + (uint32_t)((j ^ (row0 & 7)) << 4);
+    const uint8_t* pad = a.pad_src ? a.pad_src : a.x;
+    const uint32_t pad_bytes = a.pad_src ? 16u : 0u;
+    const int ohw = a.oh * a.ow;
+    int it = 0;  // global k-block counter (stage ring position)
+    bool ok = true;
+    for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+      const int m0 = (tile / a.num_n_tiles) * kBM;
+      int ih0[8], iw0[8], nb[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int m = m0 + row0 + 16 * i;
+        if (m < a.M) {
+          const int img = m / ohw;
+          const int rem = m - img * ohw;
+          const int oy = rem / a.ow;
+          const int ox = rem - oy * a.ow;
+          ih0[i] = oy * a.sh - a.pt;
+          iw0[i] = ox * a.sw - a.pl;
+          nb[i] = img * a.h;
+        } else {
+          ih0[i] = -(1 << 29);
+          iw0[i] = 0;
+          nb[i] = 0;
+        }
+      }
+      for (int kb = 0; kb < a.num_kb; ++kb, ++it) {
+        const int st = it % STAGES;
+        if (!mbar_wait(empty(st), ((it / STAGES) & 1) ^ 1, abort_flag, a.err, a.wait_ns)) {
+          ok = false;
+          break;
+        }
+        const int kk = kb * KB + j * CHUNK;
+        const int tap = kk / a.cs;
+        const int c = kk - tap * a.cs;
+        const bool kvalid = tap < RS;
+        const int rr = tap / a.s;
+        const int dy = rr * a.dh, dx = (tap - rr * a.s) * a.dw;
+        const uint32_t dst0 = sA + st * kABytes + row_off;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int ih = ih0[i] + dy, iw = iw0[i] + dx;
+          const bool v = kvalid && (unsigned)ih < (unsigned)a.h && (unsigned)iw < (unsigned)a.w;
+          const uint8_t* src =
+              v ? a.x + ((long long)((nb[i] + ih) * a.w + iw) * a.cs + c) * ESZ : pad;
+          cp_async_16(dst0 + i * 2048u, src, v ? 16u : pad_bytes);
+        }
+        // the barrier phase completes when all 128 producers' copies have landed
+        cp_async_mbar_arrive_noinc(fullA(st));
+      }
+    }
+    cp_async_wait_all();
+  } else if (warp < 8) {
+    // ---------------- epilogue
+    const int ew = warp - 4;
+    const uint32_t lane_base = (uint32_t)(ew * 32) << 16;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
+      const int buf = local & 1;
+      bool ok = mbar_wait(tfull(buf), (local >> 1) & 1, abort_flag, a.err, a.wait_ns);
+      ok = __all_sync(0xffffffffu, ok);
+      if (!ok) break;
+      tc_fence_after();
+      const int m0 = (tile / a.num_n_tiles) * kBM;
+      const int n0 = (tile % a.num_n_tiles) * BN;
+      const int m = m0 + ew * 32 + lane;
+      const uint32_t taddr = tmem + lane_base + (uint32_t)(buf * BN);
+#pragma unroll 1
+      for (int c0 = 0; c0 < BN; c0 += 16) {
+        if (n0 + c0 >= a.ks) break;  // warp-uniform
+        uint32_t v[16];
+        tmem_ld16(taddr + c0, v);
+        tmem_ld_wait();
+        if (m < a.M) store_chunk16<ESZ>(a, m, n0 + c0, v);
+      }
+      tc_fence_before();
+      mbar_arrive(tempty(buf));
+    }
+  } else if (warp == 8) {
+    // ---------------- B producer (TMA)
+    if (lane == 0) {
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int n0 = (tile % a.num_n_tiles) * BN;
+        for (int kb = 0; kb < a.num_kb; ++kb, ++it) {
+          const int st = it % STAGES;
+          if (!mbar_wait(empty(st), ((it / STAGES) & 1) ^ 1, abort_flag, a.err, a.wait_ns)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(fullB(st), L::kBBytes);
+          tma_load_2d(sB + st * L::kBBytes, &tmap_w, kb * KB, n0, fullB(st));
+        }
+      }
+      if (!ok) {
+        // let the loads already issued land before the CTA's shared memory is released
+        for (int q = it - 1; q >= 0 && q >= it - STAGES; --q)
+          mbar_wait(fullB(q % STAGES), (q / STAGES) & 1, nullptr, a.err, 1000000ull);
+      }
+    }
+  } else {
+    // ---------------- MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = ESZ == 2 ? idesc_bf16(kBM, BN) : idesc_i8(kBM, BN, a.a_signed, 1);
+      int it = 0, local = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+        const int buf = local & 1;
+        if (!mbar_wait(tempty(buf), ((local >> 1) & 1) ^ 1, abort_flag, a.err, a.wait_ns)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(buf * BN);
+        for (int kb = 0; kb < a.num_kb; ++kb, ++it) {
+          const int st = it % STAGES;
+          const uint32_t par = (it / STAGES) & 1;
+          if (!mbar_wait(fullB(st), par, abort_flag, a.err, a.wait_ns) ||
+              !mbar_wait(fullA(st), par, abort_flag, a.err, a.wait_ns)) {
+            ok = false;
+            break;
+          }
+          // order the producers' generic-proxy cp.async writes before the
+          // async-proxy operand reads of tcgen05.mma
+          fence_proxy_async_smem();
+          tc_fence_after();
+          const uint32_t ab = sA + st * kABytes, bb = sB + st * L::kBBytes;
+#pragma unroll
+          for (int kq = 0; kq < 4; ++kq) {
+            const uint64_t ad = umma_desc_sw128(ab + kq * 32);
+            const uint64_t bd = umma_desc_sw128(bb + kq * 32);
+            if constexpr (ESZ == 2)
+              umma_bf16(d, ad, bd, idesc, (kb | kq) != 0);
+            else
+              umma_i8(d, ad, bd, idesc, (kb | kq) != 0);
+          }
+          umma_commit(empty(st));
+        }
+        if (ok) umma_commit(tfull(buf));
+      }
+      if (!ok) {
+        umma_commit(drain);
+        mbar_wait(drain, 0, nullptr, a.err, 1000000ull);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+// ---------------------------------------------------------------- host side
+PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+template <int BN, int STAGES, int ESZ>
+int launch_tc(mdlc_ctx* ctx, const CUtensorMap& tmap, const TcArgs& args) {
+  using L = Smem<BN, STAGES>;
+  static_assert(L::kAlloc <= 232448, "shared memory budget");
+  auto kern = conv_tc_kernel<BN, STAGES, ESZ>;
+  static bool attr_set[64] = {};
+  if (!attr_set[ctx->device & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+    if (e != cudaSuccess) return mdlc_cuda_status(ctx, e, "conv_tc smem attribute");
+    attr_set[ctx->device & 63] = true;
+  }
+  const int tiles = args.num_m_tiles * args.num_n_tiles;
+  const int grid = tiles < ctx->num_sms ? tiles : ctx->num_sms;
+  kern<<<grid, kThreads, L::kAlloc, ctx->stream>>>(tmap, args);
+  mdlc_note_launch(ctx);
+  return mdlc_cuda_status(ctx, cudaGetLastError(), "conv_tc launch");
+}
+
+}  // namespace
+
+int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w, const void* bias,
+            const void* res, void* y, const mdlc_epilogue* epi, const mdlc_tile_cfg* cfg) {
+  const bool int8 = d.in_type == MDLC_U8 || d.in_type == MDLC_S8;
+  const int esz = int8 ? 1 : 2;
+  const int kb_elems = 128 / esz;
+  const long long kg = (long long)d.r * d.s * d.c_stride;
+  const int num_kb = (int)((kg + kb_elems - 1) / kb_elems);
+  const long long M = (long long)d.n * d.oh * d.ow;
+  if (M <= 0 || M > (1ll << 31) - 256) return mdlc_set_error(ctx, MDLC_ERR_INVALID, "conv: bad M=%lld", M);
+
+  int bn = cfg && cfg->bn ? cfg->bn : 0;
+  int stages = cfg && cfg->stages ? cfg->stages : 0;
+  const int num_m = (int)((M + kBM - 1) / kBM);
+  if (!bn) {
+    bn = d.k_stride > 128 ? 256 : (d.k_stride > 64 ? 128 : 64);
+    // keep enough tiles in flight for the whole GPU
+    while (bn > 64 && (long long)num_m * ((d.k_stride + bn - 1) / bn) < ctx->num_sms) bn /= 2;
+  }
+  if (!stages) stages = bn == 256 ? 4 : (bn == 128 ? 6 : 8);
+  if (bn != 64 && bn != 128 && bn != 256)
+    return mdlc_set_error(ctx, MDLC_ERR_INVALID, "conv_tc: bn must be 64/128/256, got %d", bn);
+
+  auto encode = get_encode_fn();
+  if (!encode) return mdlc_set_error(ctx, MDLC_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
+  CUtensorMap tmap;
+  const cuuint64_t gdim[2] = {(cuuint64_t)num_kb * kb_elems, (cuuint64_t)d.k};
+  const cuuint64_t gstride[1] = {(cuuint64_t)num_kb * 128};
+  const cuuint32_t box[2] = {(cuuint32_t)kb_elems, (cuuint32_t)bn};
+  const cuuint32_t estride[2] = {1, 1};
+  CUresult cr = encode(&tmap, int8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                       const_cast<void*>(w), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                       CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                       CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (cr != CUDA_SUCCESS) return mdlc_set_error(ctx, MDLC_ERR_INVALID, "weight tensor map: CUresult %d", (int)cr);
+
+  TcArgs a{};
+  a.x = static_cast<const uint8_t*>(x);
+  a.y = y;
+  a.bias = bias;
+  a.res = static_cast<const uint8_t*>(res);
+  a.pad_src = nullptr;
+  a.err = ctx->d_err;
+  a.n = d.n; a.h = d.h; a.w = d.w; a.cs = d.c_stride;
+  a.k = d.k; a.ks = d.k_stride; a.res_s = d.res_stride ? d.res_stride : d.k_stride;
+  a.r = d.r; a.s = d.s; a.sh = d.stride_h; a.sw = d.stride_w; a.pt = d.pad_t; a.pl = d.pad_l;
+  a.dh = d.dil_h; a.dw = d.dil_w; a.oh = d.oh; a.ow = d.ow;
+  a.M = (int)M;
+  a.num_kb = num_kb;
+  a.num_m_tiles = num_m;
+  a.num_n_tiles = (d.k_stride + bn - 1) / bn;
+  a.out_type = d.out_type;
+  a.a_signed = d.in_type == MDLC_S8;
+  a.wait_ns = kWaitLimitNs;
+  if (epi) {
+    a.act = ActParams{epi->act, epi->alpha, epi->beta, epi->clip_lo, epi->clip_hi};
+    a.rq_mult = epi->rq_mult; a.rq_shift = epi->rq_shift;
+    a.out_zp = epi->out_zp; a.qmin = epi->qmin; a.qmax = epi->qmax;
+    a.res_zp = epi->res_zp; a.res_mult = epi->res_mult; a.res_shift = epi->res_shift;
+    a.deq_scale = epi->deq_scale; a.deq_bias = epi->deq_bias;
+  }
+  if (int8) a.pad_src = ctx->d_pad + 16 * (d.in_zp & 0xFF);
+
+#define MDLC_TC_CASE(BN_, ST_)                                                     \
+  if (bn == BN_ && stages == ST_)                                                  \
+    return int8 ? launch_tc<BN_, ST_, 1>(ctx, tmap, a) : launch_tc<BN_, ST_, 2>(ctx, tmap, a);
+  MDLC_TC_CASE(64, 4)
+  MDLC_TC_CASE(64, 8)
+  MDLC_TC_CASE(128, 4)
+  MDLC_TC_CASE(128, 6)
+  MDLC_TC_CASE(256, 3)
+  MDLC_TC_CASE(256, 4)
+#undef MDLC_TC_CASE
+  return mdlc_set_error(ctx, MDLC_ERR_UNSUPPORTED, "conv_tc: no kernel for bn=%d stages=%d", bn, stages);
+}
+
+}  // namespace mdlc

@@ -1,0 +1,38 @@
+// Host-side context shared by the translation units of libmdlc_b200.so.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdarg.h>
+
+#include <string>
+
+#include "mdlc_b200.h"
+
+static constexpr int kMaxEvents = 4096;
+// Device-side waits give up after this long (nanoseconds).
+static constexpr unsigned long long kWaitLimitNs = 2000000000ull;
+
+struct mdlc_ctx {
+  int device = 0;
+  int num_sms = 148;
+  cudaStream_t stream = nullptr;
+  int* d_err = nullptr;  // device error word (first failure wins)
+  uint8_t* d_pad = nullptr;  // 256 x 16-byte fill patterns (byte value v at v*16)
+  cudaGraph_t graph = nullptr;
+  cudaGraphExec_t graph_exec = nullptr;
+  bool capturing = false;
+  long long launches = 0;           // kernels launched by this context
+  long long captured_launches = 0;  // kernels inside the instantiated graph
+  cudaEvent_t events[kMaxEvents] = {};
+  std::string last_error;
+};
+
+int mdlc_set_error(mdlc_ctx* ctx, int status, const char* fmt, ...);
+int mdlc_cuda_status(mdlc_ctx* ctx, cudaError_t e, const char* what);
+
+inline void mdlc_note_launch(mdlc_ctx* ctx) {
+  if (ctx->capturing)
+    ctx->captured_launches++;
+  else
+    ctx->launches++;
+}

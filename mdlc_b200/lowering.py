@@ -1,0 +1,508 @@
+"""Lower a post-pass Graph IR to a list of backend steps.
+
+This replaces the reference's ``CudaCodegen.lower`` (``mdlc/codegen/cuda/emit.py:137-293``):
+instead of emitting CUDA C per node and bouncing unsupported ops to the host
+(``emit.py:32-35,148-157,175-180``), each IR node (or fused group of nodes)
+becomes one call of a prebuilt kernel in ``libmdlc_b200.so``:
+
+* ``Conv`` / ``FusedConvAct`` / ``FusedConvBNAct`` / ``Gemm`` / ``FusedGemmAct``
+  / ``MatMul`` -> ``conv`` step (implicit GEMM; depthwise when
+  ``group == C == K``), with bias and activation in the epilogue.
+* Backend-level epilogue fusion on top of the reference passes: a plain conv
+  whose single consumer is ``Add(conv, skip)`` (bare, or a ``FusedElementwise``
+  ``[Add, act]``) absorbs the add and activation as a residual epilogue; the
+  opset-17 GELU decomposition ``x * 0.5 * (1 + erf(x / sqrt 2))`` hanging off a
+  conv becomes a GELU epilogue.
+* ``MaxPool`` / ``AveragePool`` / ``GlobalAveragePool`` / ``ReduceMean`` over
+  H,W -> ``pool`` step.
+* Remaining elementwise nodes and ``FusedElementwise`` groups -> ``eltwise``
+  step (an interpreted register program, broadcasting per (n, c), per c, or
+  scalar operands).
+* ``Flatten`` / ``Reshape`` / ``Squeeze`` / ``Unsqueeze`` / ``Identity`` ->
+  zero-copy aliases when the NHWC storage order is unchanged.
+Nothing is executed on the host; an op the backend cannot lower raises at
+compile time (the executable's ``fallbacks()`` is always empty).
+"""
+
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass, field
+from typing import Optional
+
+import numpy as np
+
+from mdlc_b200 import _lib as L
+from mdlc_b200 import shapes as S
+
+
+class LoweringError(NotImplementedError):
+    pass
+
+
+ACT_CODES = {None: L.ACT_NONE, "Identity": L.ACT_NONE, "Relu": L.ACT_RELU, "Clip": L.ACT_CLIP,
+             "Relu6": L.ACT_CLIP, "Sigmoid": L.ACT_SIGMOID, "Tanh": L.ACT_TANH,
+             "LeakyRelu": L.ACT_LEAKY_RELU, "HardSigmoid": L.ACT_HARD_SIGMOID,
+             "HardSwish": L.ACT_HARD_SWISH, "Gelu": L.ACT_GELU}
+UNARY_EW = {"Relu": L.EW_RELU, "Clip": L.EW_CLIP, "Sigmoid": L.EW_SIGMOID, "Tanh": L.EW_TANH,
+            "LeakyRelu": L.EW_LEAKY_RELU, "HardSigmoid": L.EW_HARD_SIGMOID,
+            "HardSwish": L.EW_HARD_SWISH, "Erf": L.EW_ERF, "Gelu": L.EW_GELU}
+BINARY_EW = {"Add": L.EW_ADD, "Sub": L.EW_SUB, "Mul": L.EW_MUL, "Div": L.EW_DIV}
+ELEMENTWISE_OPS = set(UNARY_EW) | set(BINARY_EW)
+ALIAS_OPS = {"Flatten", "Reshape", "Squeeze", "Unsqueeze", "Identity"}
+
+
+def round_up(v: int, m: int) -> int:
+    return (v + m - 1) // m * m
+
+
+@dataclass
+class TensorSpec:
+    """An activation tensor stored NHWC with channel stride ``cs``."""
+
+    name: str
+    shape: tuple          # logical (reference) shape, NCHW or (N, C)
+    n: int
+    c: int
+    h: int
+    w: int
+    cs: int
+    dtype: int
+    alias_of: Optional[str] = None
+
+    @property
+    def nbytes(self) -> int:
+        return self.n * self.h * self.w * self.cs * L.ELEM_BYTES[self.dtype]
+
+
+@dataclass
+class Step:
+    kind: str                      # "conv" | "pool" | "eltwise"
+    inputs: list                   # activation tensors read
+    outputs: list                  # activation tensors written
+    nodes: list                    # IR node names covered
+    params: dict = field(default_factory=dict)
+
+    def label(self) -> str:
+        return f"{self.kind}[{'+'.join(self.nodes)}]"
+
+
+@dataclass
+class Lowered:
+    steps: list
+    tensors: dict                  # name -> TensorSpec
+    weights: dict                  # name -> (desc, oihw fp32 array, bias fp32 array)
+    consts: dict                   # name -> np.ndarray (eltwise operands uploaded once)
+    inputs: list
+    outputs: list
+    shapes: dict
+    dtype: int
+
+
+def _is_scalar(arr) -> bool:
+    return arr is not None and np.asarray(arr).size == 1
+
+
+class _Lowerer:
+    def __init__(self, graph, shapes: dict, dtype: int):
+        self.g = graph
+        self.shapes = shapes
+        self.dtype = dtype
+        self.consts = {}
+        self.weights = {}
+        self.tensors = {}
+        self.steps = []
+        self.order = graph.topo_sort()
+        self.pos = {id(n): k for k, n in enumerate(self.order)}
+        self.consumers = {}
+        for n in self.order:
+            for i in n.inputs:
+                if i:
+                    self.consumers.setdefault(i, []).append(n)
+        self.graph_outputs = set(graph.outputs)
+        self.absorbed = set()   # ids of nodes folded into another step
+        self.deferred = {}      # id(node) -> Step to emit at that node's position
+
+    # ---------------------------------------------------------- helpers
+    def const(self, name):
+        if not name:
+            return None
+        return self.g.initializers.get(name)
+
+    def uses(self, name) -> int:
+        return len(self.consumers.get(name, [])) + (1 if name in self.graph_outputs else 0)
+
+    def tensor(self, name) -> TensorSpec:
+        if name in self.tensors:
+            return self.tensors[name]
+        shp = tuple(self.shapes[name])
+        if len(shp) == 4:
+            n, c, h, w = shp
+        elif len(shp) == 2:
+            n, c, h, w = shp[0], shp[1], 1, 1
+        elif len(shp) == 3:
+            n, c, h, w = shp[0], shp[1], shp[2], 1
+        else:
+            raise LoweringError(f"tensor {name!r} of rank {len(shp)} is not supported")
+        t = TensorSpec(name, shp, n, c, h, w, round_up(c, 8), self.dtype)
+        self.tensors[name] = t
+        return t
+
+    # ---------------------------------------------------------- convs
+    def conv_step(self, node):
+        op, a = node.op_type, node.attrs
+        x = node.inputs[0]
+        xt = self.tensor(x)
+        if op in ("Conv", "FusedConvAct", "FusedConvBNAct"):
+            w = self.const(node.inputs[1])
+            if w is None:
+                raise LoweringError(f"{node.name}: conv weight must be constant")
+            b = self.const(node.inputs[2]) if len(node.inputs) > 2 and node.inputs[2] else None
+            if len(node.inputs) > 2 and node.inputs[2] and b is None:
+                raise LoweringError(f"{node.name}: conv bias must be constant")
+            oh, ow, (pt, pb), (pl, pr) = S.conv_geometry(a, (xt.n, xt.c, xt.h, xt.w), w.shape)
+            k, icg, r, s = w.shape
+            group = a.get("group", 1)
+            sh, sw = a.get("strides", [1, 1])
+            dh, dw = a.get("dilations", [1, 1])
+            if group != 1 and not (group == xt.c == k and icg == 1):
+                raise LoweringError(f"{node.name}: grouped conv with group={group} (not depthwise)")
+            wt = np.asarray(w, dtype=np.float32)
+            geom = dict(n=xt.n, h=xt.h, w=xt.w, c=xt.c, k=k, r=r, s=s, sh=sh, sw=sw, pt=pt, pl=pl,
+                        dh=dh, dw=dw, oh=oh, ow=ow, groups=group)
+        else:  # Gemm / FusedGemmAct / MatMul: y[M,N] = x[M,K] . W[N,K]^T
+            if op == "MatMul":
+                B = self.const(node.inputs[1])
+                if B is None or B.ndim != 2:
+                    raise LoweringError(f"{node.name}: MatMul needs a constant 2-D right operand")
+                wt, b = np.asarray(B, np.float32).T, None
+                alpha, beta = 1.0, 1.0
+            else:
+                if a.get("transA", 0):
+                    raise LoweringError(f"{node.name}: Gemm transA=1 is not supported")
+                B = self.const(node.inputs[1])
+                if B is None:
+                    raise LoweringError(f"{node.name}: Gemm weight must be constant")
+                wt = np.asarray(B, np.float32)
+                wt = wt if a.get("transB", 0) else wt.T
+                alpha, beta = float(a.get("alpha", 1.0)), float(a.get("beta", 1.0))
+                b = self.const(node.inputs[2]) if len(node.inputs) > 2 and node.inputs[2] else None
+                if len(node.inputs) > 2 and node.inputs[2] and b is None:
+                    raise LoweringError(f"{node.name}: Gemm C must be constant")
+                if b is not None:
+                    b = np.asarray(b, np.float32)
+                    if b.size not in (1, wt.shape[0]) or (b.ndim == 2 and b.shape[0] != 1):
+                        raise LoweringError(f"{node.name}: Gemm C of shape {b.shape} (full matrix) "
+                                            "is not supported")
+                    b = np.broadcast_to(b.reshape(-1), (wt.shape[0],)) * np.float32(beta)
+            if xt.h * xt.w != 1:
+                raise LoweringError(f"{node.name}: GEMM input must be 2-D")
+            if alpha != 1.0:
+                wt = wt * np.float32(alpha)
+            k, kin = wt.shape
+            if kin != xt.c:
+                raise LoweringError(f"{node.name}: GEMM inner dim {kin} != {xt.c}")
+            wt = wt.reshape(k, kin, 1, 1)
+            geom = dict(n=xt.n, h=1, w=1, c=xt.c, k=k, r=1, s=1, sh=1, sw=1, pt=0, pl=0, dh=1, dw=1,
+                        oh=1, ow=1, groups=1)
+        bias = np.zeros(round_up(geom["k"], 8), np.float32)
+        if b is not None:
+            bias[:geom["k"]] = np.asarray(b, np.float32).reshape(-1)
+        wname = f"{node.name or node.outputs[0]}.w"
+        self.weights[wname] = (geom, wt, bias)
+        act = a.get("activation") if op.startswith("Fused") else None
+        return Step("conv", [x], [node.outputs[0]], [node.name],
+                    dict(weight=wname, act=act, attrs=dict(a), residual=None))
+
+    def try_absorb_residual(self, node, step):
+        """Plain conv whose only consumer is Add(conv, skip) [+ activation]."""
+        t = node.outputs[0]
+        if self.uses(t) != 1 or t in self.graph_outputs:
+            return None
+        cons = self.consumers[t][0]
+        if id(cons) in self.absorbed:      # already fused into another conv's epilogue
+            return None
+        skip = act = None
+        act_attrs = {}
+        out = None
+        if cons.op_type == "Add" and len(cons.real_inputs()) == 2:
+            other = [i for i in cons.inputs if i != t]
+            if len(other) != 1 or self.const(other[0]) is not None:
+                return None
+            skip, out = other[0], cons.outputs[0]
+        elif cons.op_type == "FusedElementwise":
+            sub = cons.attrs["subgraph"]
+            if not (1 <= len(sub) <= 2 and sub[0].op_type == "Add") or len(cons.outputs) != 1:
+                return None
+            add = sub[0]
+            other = [i for i in add.inputs if i != t]
+            if t not in add.inputs or len(other) != 1 or self.const(other[0]) is not None:
+                return None
+            skip = other[0]
+            if len(sub) == 2:
+                a2 = sub[1]
+                if a2.op_type not in ACT_CODES or a2.inputs[0] != add.outputs[0]:
+                    return None
+                act = a2.op_type
+                if act == "Clip":
+                    lo = self._scalar_input(a2, 1, a2.attrs.get("min"))
+                    hi = self._scalar_input(a2, 2, a2.attrs.get("max"))
+                    if lo is False or hi is False:
+                        return None
+                    act_attrs = {"clip_min": lo, "clip_max": hi}
+                elif act in ("LeakyRelu", "HardSigmoid"):
+                    act_attrs = {k: v for k, v in a2.attrs.items() if k in ("alpha", "beta")}
+                out = a2.outputs[0]
+            else:
+                out = add.outputs[0]
+            if cons.outputs[0] != out:
+                return None
+        else:
+            return None
+        if tuple(self.shapes[skip]) != tuple(self.shapes[t]):
+            return None
+        step.inputs.append(skip)
+        step.outputs = [out]
+        step.nodes.append(cons.name)
+        step.params["residual"] = skip
+        step.params["act"] = act
+        step.params["attrs"].update(act_attrs)
+        return cons
+
+    def try_absorb_gelu(self, node, step):
+        """conv -> Div(t, sqrt2) -> Erf -> (Add 1, Mul t, Mul 0.5) as a GELU epilogue."""
+        t = node.outputs[0]
+        if t in self.graph_outputs:
+            return None
+        cons = self.consumers.get(t, [])
+        if len(cons) != 2:
+            return None
+        div = next((c for c in cons if c.op_type == "Div" and c.inputs[0] == t), None)
+        if div is None or not _is_scalar(self.const(div.inputs[1])):
+            return None
+        if not math.isclose(float(np.asarray(self.const(div.inputs[1])).item()), math.sqrt(2.0),
+                            rel_tol=1e-6):
+            return None
+        erf_nodes = self.consumers.get(div.outputs[0], [])
+        if len(erf_nodes) != 1 or erf_nodes[0].op_type != "Erf" or self.uses(div.outputs[0]) != 1:
+            return None
+        erf = erf_nodes[0]
+        tail = self.consumers.get(erf.outputs[0], [])
+        other = next(c for c in cons if c is not div)
+        if id(other) in self.absorbed:
+            return None
+        if len(tail) != 1 or tail[0] is not other or other.op_type != "FusedElementwise":
+            return None
+        sub = other.attrs["subgraph"]
+        if [s.op_type for s in sub] != ["Add", "Mul", "Mul"] or len(other.outputs) != 1:
+            return None
+        add, m1, m2 = sub
+        e = erf.outputs[0]
+
+        def const_is(name, val):
+            c = self.const(name)
+            return _is_scalar(c) and math.isclose(float(np.asarray(c).item()), val, rel_tol=1e-6)
+
+        ok = (e in add.inputs and any(const_is(i, 1.0) for i in add.inputs if i != e)
+              and set(m1.inputs) == {t, add.outputs[0]}
+              and m1.outputs[0] in m2.inputs and any(const_is(i, 0.5) for i in m2.inputs if i != m1.outputs[0])
+              and other.outputs[0] == m2.outputs[0])
+        if not ok:
+            return None
+        step.outputs = [other.outputs[0]]
+        step.nodes += [div.name, erf.name, other.name]
+        step.params["act"] = "Gelu"
+        self.absorbed.update({id(div), id(erf)})
+        return other
+
+    def _scalar_input(self, node, idx, fallback):
+        if len(node.inputs) > idx and node.inputs[idx]:
+            c = self.const(node.inputs[idx])
+            if not _is_scalar(c):
+                return False
+            return float(np.asarray(c).item())
+        return None if fallback is None else float(fallback)
+
+    # ---------------------------------------------------------- elementwise
+    def eltwise_step(self, node, sub, ext_inputs, outputs):
+        """Compile an elementwise (sub)graph into an interpreter program."""
+        out_shape = tuple(self.shapes[outputs[0]])
+        for o in outputs:
+            if tuple(self.shapes[o]) != out_shape:
+                raise LoweringError(f"{node.name}: elementwise outputs of different shapes")
+        o4 = self.tensor(outputs[0])
+        reg_of, tensor_inputs, bcast = {}, [], []
+        imm = {}
+        for e in ext_inputs:
+            c = self.const(e)
+            if _is_scalar(c):
+                imm[e] = float(np.asarray(c).item())
+                continue
+            if c is not None:
+                cshape = tuple(np.asarray(c).shape)
+                full = (1, o4.c, 1, 1)
+                cc = np.asarray(c, np.float32)
+                if cc.size == o4.c and cc.reshape(-1).shape[0] == o4.c and len(cshape) in (1, 3, 4):
+                    cname = f"{node.name}.{e}"
+                    padded = np.zeros(o4.cs, np.float32)
+                    padded[:o4.c] = cc.reshape(-1)
+                    self.consts[cname] = padded
+                    mode, src = L.BC_C, cname
+                else:
+                    raise LoweringError(f"{node.name}: constant operand {e!r} of shape {cshape} vs {full}")
+            else:
+                shp = tuple(self.shapes[e])
+                t = self.tensor(e)
+                if shp == out_shape:
+                    mode = L.BC_FULL
+                elif t.n == o4.n and t.c == o4.c and t.h * t.w == 1:
+                    mode = L.BC_NC
+                elif t.n == 1 and t.c == o4.c and t.h * t.w == 1:
+                    mode = L.BC_C
+                elif int(np.prod(shp)) == 1:
+                    mode = L.BC_SCALAR
+                else:
+                    raise LoweringError(f"{node.name}: operand {e!r} {shp} does not broadcast to {out_shape}")
+                src = e
+            if len(tensor_inputs) >= L.EW_MAX_INPUTS:
+                raise LoweringError(f"{node.name}: more than {L.EW_MAX_INPUTS} tensor operands")
+            reg_of[e] = len(tensor_inputs)
+            tensor_inputs.append(src)
+            bcast.append(mode)
+        code = []
+        free_regs = [r for r in range(8) if r >= len(tensor_inputs)]
+        remaining = {}
+        for sn in sub:
+            for i in sn.real_inputs():
+                remaining[i] = remaining.get(i, 0) + 1
+
+        def alloc():
+            if not free_regs:
+                raise LoweringError(f"{node.name}: elementwise program needs more than 8 registers")
+            return free_regs.pop(0)
+
+        for sn in sub:
+            op, ins = sn.op_type, [i for i in sn.inputs if i]
+            if op in BINARY_EW:
+                a_, b_ = ins[0], ins[1]
+                if a_ in imm and b_ in imm:
+                    raise LoweringError(f"{sn.name}: constant-only elementwise node")
+                if b_ in imm:
+                    opc = {"Add": L.EW_ADDI, "Sub": L.EW_SUBI, "Mul": L.EW_MULI, "Div": L.EW_DIVI}[op]
+                    ins_code = (opc, reg_of[a_], 0, imm[b_], 0.0)
+                elif a_ in imm:
+                    opc = {"Add": L.EW_ADDI, "Sub": L.EW_RSUBI, "Mul": L.EW_MULI, "Div": L.EW_RDIVI}[op]
+                    ins_code = (opc, reg_of[b_], 0, imm[a_], 0.0)
+                else:
+                    ins_code = (BINARY_EW[op], reg_of[a_], reg_of[b_], 0.0, 0.0)
+            elif op in UNARY_EW:
+                i0 = i1 = 0.0
+                if op == "Clip":
+                    lo = self._scalar_input(sn, 1, sn.attrs.get("min"))
+                    hi = self._scalar_input(sn, 2, sn.attrs.get("max"))
+                    if lo is False or hi is False:
+                        raise LoweringError(f"{sn.name}: Clip bounds must be constant scalars")
+                    i0 = -np.inf if lo is None else lo
+                    i1 = np.inf if hi is None else hi
+                elif op == "LeakyRelu":
+                    i0 = float(sn.attrs.get("alpha", 0.01))
+                elif op == "HardSigmoid":
+                    i0, i1 = float(sn.attrs.get("alpha", 0.2)), float(sn.attrs.get("beta", 0.5))
+                ins_code = (UNARY_EW[op], reg_of[ins[0]], 0, i0, i1)
+            else:
+                raise LoweringError(f"{sn.name}: {op} inside an elementwise group")
+            for i in sn.real_inputs():
+                remaining[i] -= 1
+                if remaining[i] == 0 and i in reg_of and i not in outputs and reg_of[i] >= len(tensor_inputs):
+                    free_regs.append(reg_of[i])
+                    free_regs.sort()
+            dst = alloc()
+            reg_of[sn.outputs[0]] = dst
+            opc, s0, s1, f0, f1 = ins_code
+            code.append((opc, dst, s0, s1, f0, f1))
+        if len(code) > L.EW_MAX_INSTR:
+            raise LoweringError(f"{node.name}: elementwise program longer than {L.EW_MAX_INSTR}")
+        if len(outputs) > L.EW_MAX_OUTPUTS:
+            raise LoweringError(f"{node.name}: more than {L.EW_MAX_OUTPUTS} outputs")
+        return Step("eltwise", [s for s in tensor_inputs if s not in self.consts], list(outputs), [node.name],
+                    dict(code=code, operands=tensor_inputs, bcast=bcast,
+                         out_regs=[reg_of[o] for o in outputs]))
+
+    # ---------------------------------------------------------- main walk
+    def run(self) -> Lowered:
+        for name in self.g.runtime_inputs:
+            self.tensor(name)
+        for node in self.order:
+            if id(node) in self.absorbed:
+                if id(node) in self.deferred:
+                    self.steps.append(self.deferred.pop(id(node)))
+                continue
+            op = node.op_type
+            if op in ("Conv", "FusedConvAct", "FusedConvBNAct", "Gemm", "FusedGemmAct", "MatMul"):
+                step = self.conv_step(node)
+                self.tensor(node.outputs[0])
+                absorbed = None
+                if not step.params["act"]:
+                    absorbed = self.try_absorb_residual(node, step) or self.try_absorb_gelu(node, step)
+                if absorbed is not None:
+                    self.absorbed.add(id(absorbed))
+                    self.deferred[id(absorbed)] = step
+                    for o in step.outputs:
+                        self.tensor(o)
+                else:
+                    self.steps.append(step)
+            elif op in ("MaxPool", "AveragePool"):
+                xt = self.tensor(node.inputs[0])
+                oh, ow, (pt, pb), (pl, pr) = S.pool_geometry(node.attrs, (xt.n, xt.c, xt.h, xt.w),
+                                                             op == "MaxPool")
+                if op == "MaxPool" and node.attrs.get("dilations", [1, 1]) != [1, 1]:
+                    raise LoweringError(f"{node.name}: dilated MaxPool")
+                kh, kw = node.attrs["kernel_shape"]
+                sh, sw = node.attrs.get("strides", [1, 1])
+                if op == "AveragePool" and node.attrs.get("count_include_pad", 0) and (pb > pt or pr > pl):
+                    raise LoweringError(f"{node.name}: asymmetric count_include_pad AveragePool")
+                self.tensor(node.outputs[0])
+                self.steps.append(Step("pool", [node.inputs[0]], [node.outputs[0]], [node.name],
+                                       dict(kind=0 if op == "MaxPool" else 1, kh=kh, kw=kw, sh=sh, sw=sw,
+                                            pt=pt, pl=pl, oh=oh, ow=ow,
+                                            cip=int(node.attrs.get("count_include_pad", 0)))))
+            elif op == "GlobalAveragePool" or (
+                    op == "ReduceMean" and self._reduce_axes(node) == [2, 3]
+                    and node.attrs.get("keepdims", 1)):
+                self.tensor(node.inputs[0])
+                self.tensor(node.outputs[0])
+                self.steps.append(Step("pool", [node.inputs[0]], [node.outputs[0]], [node.name], dict(kind=2)))
+            elif op in ALIAS_OPS:
+                src = self.tensor(node.inputs[0])
+                out_shape = tuple(self.shapes[node.outputs[0]])
+                dst = self.tensor(node.outputs[0])
+                same_order = (src.h * src.w == 1 and dst.h * dst.w == 1 and src.c == dst.c) or \
+                    (tuple(src.shape) == out_shape)
+                if not same_order or src.n != dst.n:
+                    raise LoweringError(f"{node.name}: {op} {src.shape}->{out_shape} changes NHWC order")
+                dst.alias_of = src.alias_of or src.name
+            elif op == "FusedElementwise":
+                sub = node.attrs["subgraph"]
+                for o in node.outputs:
+                    self.tensor(o)
+                self.steps.append(self.eltwise_step(node, sub, list(node.inputs), list(node.outputs)))
+            elif op in ELEMENTWISE_OPS:
+                self.tensor(node.outputs[0])
+                self.steps.append(self.eltwise_step(node, [node], node.real_inputs(), [node.outputs[0]]))
+            else:
+                raise LoweringError(f"no B200 lowering for op {op!r} (node {node.name!r})")
+        if self.deferred:
+            raise LoweringError("internal: unplaced fused step")
+        return Lowered(self.steps, self.tensors, self.weights, self.consts, list(self.g.runtime_inputs),
+                       list(self.g.outputs), self.shapes, self.dtype)
+
+    def _reduce_axes(self, node):
+        axes = node.attrs.get("axes")
+        if axes is None and len(node.inputs) > 1 and node.inputs[1]:
+            axes = [int(v) for v in np.asarray(self.const(node.inputs[1])).ravel()]
+        rank = len(self.shapes[node.inputs[0]])
+        return sorted(int(a) % rank for a in axes) if axes is not None else None
+
+
+def lower(graph, shapes: dict, dtype: int) -> Lowered:
+    return _Lowerer(graph, shapes, dtype).run()

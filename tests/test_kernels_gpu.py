@@ -1,0 +1,292 @@
+"""Kernel-level parity through the C ABI (``libmdlc_b200.so``) against the oracle.
+
+Each case builds NCHW fp32 inputs and OIHW weights, packs them through the
+library's own packer, runs one entry point on ``cuda:0`` and compares with
+:mod:`oracle.reference` evaluated on the *same* operands (bf16-rounded for the
+bf16 kernels, so the remaining difference is fp32 accumulation order plus the
+final bf16 rounding of the output).
+"""
+
+import numpy as np
+import pytest
+
+from oracle import reference as oref
+
+from mdlc_b200 import _lib as L
+
+pytestmark = pytest.mark.gpu
+
+
+def bf16_bits(x):
+    return (oref.round_bf16(x).view(np.uint32) >> 16).astype(np.uint16)
+
+
+def from_bf16_bits(b):
+    return (b.astype(np.uint32) << 16).view(np.float32)
+
+
+def nhwc(x, cs):
+    n, c, h, w = x.shape
+    out = np.zeros((n, h, w, cs), dtype=x.dtype)
+    out[..., :c] = x.transpose(0, 2, 3, 1)
+    return out
+
+
+@pytest.fixture(scope="module")
+def ctx():
+    c = L.Context(0)
+    yield c
+    c.close()
+
+
+def _rnd8(v):
+    return (v + 7) // 8 * 8
+
+
+def run_conv(ctx, x, w, b, *, stride=1, pad=0, dil=1, groups=1, dtype="bf16", act=L.ACT_NONE,
+             res=None, out_f32=False, cfg=None, clip=(0.0, 6.0)):
+    n, c, h, wd = x.shape
+    k, _, r, s = w.shape
+    oh = (h + 2 * pad - dil * (r - 1) - 1) // stride + 1
+    ow = (wd + 2 * pad - dil * (s - 1) - 1) // stride + 1
+    cs, ks = _rnd8(c), _rnd8(k)
+    et = L.BF16 if dtype == "bf16" else L.F32
+    ot = L.F32 if (out_f32 or dtype == "f32") else L.BF16
+    d = L.ConvDesc(n=n, h=h, w=wd, c=c, c_stride=cs, k=k, k_stride=ks, r=r, s=s, stride_h=stride,
+                   stride_w=stride, pad_t=pad, pad_l=pad, dil_h=dil, dil_w=dil, oh=oh, ow=ow,
+                   groups=groups, in_type=et, out_type=ot, res_stride=0, in_zp=0)
+    wp = L.pack_weights(d, w)
+    xh = nhwc(x, cs)
+    xd = ctx.to_device(bf16_bits(xh) if et == L.BF16 else xh.astype(np.float32))
+    wd_ = ctx.to_device(wp)
+    bias = np.zeros(ks, np.float32)
+    bias[:k] = b
+    bd = ctx.to_device(bias)
+    rd = 0
+    if res is not None:
+        rh = nhwc(res, ks)
+        rd = ctx.to_device(bf16_bits(rh) if et == L.BF16 else rh.astype(np.float32))
+    ebytes = 4 if ot == L.F32 else 2
+    yd = ctx.alloc(n * oh * ow * ks * ebytes)
+    ctx.memset(yd, 0xFF, n * oh * ow * ks * ebytes)   # poison: every element must be written
+    epi = L.Epilogue(act=act, alpha=0.01, beta=0.5, clip_lo=clip[0], clip_hi=clip[1])
+    tc = L.TileCfg(bn=cfg[0], stages=cfg[1], flags=0) if cfg else None
+    ctx.conv2d(d, xd, wd_, bd, rd, yd, epi, tc)
+    ctx.sync()
+    if ot == L.F32:
+        y = ctx.download(yd, (n, oh, ow, ks), np.float32)
+    else:
+        y = from_bf16_bits(ctx.download(yd, (n, oh, ow, ks), np.uint16))
+    for p in (xd, wd_, bd, yd) + ((rd,) if rd else ()):
+        ctx.free(p)
+    assert np.all(y[..., k:] == 0), "padding channels must be written as zero"
+    return y[..., :k].transpose(0, 3, 1, 2)
+
+
+def oracle_conv(x, w, b, *, stride=1, pad=0, dil=1, groups=1, act=None, res=None, bf16=True, clip=(0.0, 6.0)):
+    if bf16:
+        x, w = oref.round_bf16(x), oref.round_bf16(w)
+        res = None if res is None else oref.round_bf16(res)
+    y = oref.conv(x, w, b, strides=[stride, stride], pads=[pad] * 4, dilations=[dil, dil], group=groups)
+    if res is not None:
+        y = y + res
+    return oref.activation(act, y, {"clip_min": clip[0], "clip_max": clip[1], "alpha": 0.01, "beta": 0.5})
+
+
+def check(got, want, rel):
+    err = np.abs(got - want).max()
+    scale = max(np.abs(want).max(), 1e-6)
+    assert err <= rel * scale, f"max err {err:.3e} vs scale {scale:.3e} (rel {err / scale:.2e} > {rel})"
+
+
+CONV_CASES = [
+    # n, c, h, w, k, r, stride, pad, dil
+    (1, 64, 14, 14, 64, 3, 1, 1, 1),
+    (2, 64, 9, 11, 128, 3, 1, 1, 1),
+    (2, 128, 7, 7, 256, 3, 1, 1, 1),
+    (2, 256, 7, 7, 512, 3, 2, 1, 1),
+    (3, 3, 23, 23, 64, 7, 2, 3, 1),       # stem-like, c=3 padded to 8
+    (2, 64, 15, 15, 128, 1, 2, 0, 1),     # 1x1 stride-2 projection
+    (1, 24, 10, 10, 40, 3, 1, 2, 2),      # dilation, ragged channels
+    (5, 512, 1, 1, 1000, 1, 1, 0, 1),     # FC as 1x1 conv (k=1000 not a tile multiple)
+    (1, 16, 5, 5, 8, 3, 1, 1, 1),         # tiny
+]
+
+
+@pytest.mark.parametrize("case", CONV_CASES, ids=[str(c) for c in CONV_CASES])
+def test_conv_bf16_tcgen05(ctx, case):
+    n, c, h, w, k, r, st, pad, dil = case
+    rng = np.random.default_rng(sum(case))
+    x = rng.standard_normal((n, c, h, w)).astype(np.float32)
+    wt = (rng.standard_normal((k, c, r, r)) * np.sqrt(2.0 / (c * r * r))).astype(np.float32)
+    b = (rng.standard_normal(k) * 0.1).astype(np.float32)
+    got = run_conv(ctx, x, wt, b, stride=st, pad=pad, dil=dil, act=L.ACT_RELU)
+    want = oracle_conv(x, wt, b, stride=st, pad=pad, dil=dil, act="Relu")
+    check(got, want, 1e-2)
+
+
+@pytest.mark.parametrize("cfg", [(64, 4), (64, 8), (128, 4), (128, 6), (256, 3), (256, 4)])
+def test_conv_bf16_tile_configs(ctx, cfg):
+    """Every tile configuration the tuner may pick gives the same answer (odd M, k tail)."""
+    rng = np.random.default_rng(7)
+    x = rng.standard_normal((3, 96, 13, 13)).astype(np.float32)
+    wt = (rng.standard_normal((200, 96, 3, 3)) * 0.05).astype(np.float32)
+    b = (rng.standard_normal(200) * 0.1).astype(np.float32)
+    res = rng.standard_normal((3, 200, 13, 13)).astype(np.float32)
+    got = run_conv(ctx, x, wt, b, pad=1, act=L.ACT_RELU, res=res, cfg=cfg)
+    want = oracle_conv(x, wt, b, pad=1, act="Relu", res=res)
+    check(got, want, 1e-2)
+
+
+@pytest.mark.parametrize("act,name", [(L.ACT_NONE, None), (L.ACT_CLIP, "Clip"), (L.ACT_SIGMOID, "Sigmoid"),
+                                      (L.ACT_GELU, "Gelu"), (L.ACT_HARD_SWISH, "HardSwish"),
+                                      (L.ACT_LEAKY_RELU, "LeakyRelu"), (L.ACT_TANH, "Tanh")])
+def test_conv_bf16_epilogue_activations(ctx, act, name):
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((2, 32, 8, 8)).astype(np.float32)
+    wt = (rng.standard_normal((48, 32, 3, 3)) * 0.1).astype(np.float32)
+    b = (rng.standard_normal(48) * 0.1).astype(np.float32)
+    got = run_conv(ctx, x, wt, b, pad=1, act=act)
+    want = oracle_conv(x, wt, b, pad=1, act=name)
+    check(got, want, 1e-2)
+
+
+def test_conv_bf16_fp32_output(ctx):
+    rng = np.random.default_rng(11)
+    x = rng.standard_normal((4, 512, 1, 1)).astype(np.float32)
+    wt = (rng.standard_normal((1000, 512, 1, 1)) * 0.06).astype(np.float32)
+    b = (rng.standard_normal(1000) * 0.1).astype(np.float32)
+    got = run_conv(ctx, x, wt, b, out_f32=True)
+    want = oracle_conv(x, wt, b)
+    check(got, want, 2e-3)   # no output rounding: only accumulation order differs
+
+
+@pytest.mark.parametrize("case", [(2, 3, 11, 11, 16, 3, 1, 1), (1, 64, 9, 9, 64, 3, 2, 1), (3, 40, 6, 6, 24, 1, 1, 0)])
+def test_conv_fp32_simt(ctx, case):
+    n, c, h, w, k, r, st, pad = case
+    rng = np.random.default_rng(5)
+    x = rng.standard_normal((n, c, h, w)).astype(np.float32)
+    wt = (rng.standard_normal((k, c, r, r)) * 0.1).astype(np.float32)
+    b = (rng.standard_normal(k) * 0.1).astype(np.float32)
+    res = rng.standard_normal((n, k, (h + 2 * pad - r) // st + 1, (w + 2 * pad - r) // st + 1)).astype(np.float32)
+    got = run_conv(ctx, x, wt, b, stride=st, pad=pad, dtype="f32", act=L.ACT_RELU, res=res)
+    want = oracle_conv(x, wt, b, stride=st, pad=pad, act="Relu", res=res, bf16=False)
+    np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4)   # FP32_REDUCTION tier
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+@pytest.mark.parametrize("stride", [1, 2])
+def test_depthwise(ctx, dtype, stride):
+    rng = np.random.default_rng(9)
+    c = 96
+    x = rng.standard_normal((2, c, 13, 12)).astype(np.float32)
+    wt = (rng.standard_normal((c, 1, 3, 3)) * 0.3).astype(np.float32)
+    b = (rng.standard_normal(c) * 0.1).astype(np.float32)
+    got = run_conv(ctx, x, wt, b, stride=stride, pad=1, groups=c, dtype=dtype, act=L.ACT_CLIP)
+    # depthwise weights are kept in fp32; only activations are bf16
+    xr = oref.round_bf16(x) if dtype == "bf16" else x
+    want = oref.clip(oref.conv(xr, wt, b, strides=[stride] * 2, pads=[1] * 4, group=c), 0.0, 6.0)
+    if dtype == "bf16":
+        check(got, want, 1e-2)
+    else:
+        np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4)
+
+
+def _pool(ctx, x, kind, dtype, k=3, s=2, p=1):
+    n, c, h, w = x.shape
+    cs = _rnd8(c)
+    oh, ow = ((h + 2 * p - k) // s + 1, (w + 2 * p - k) // s + 1) if kind != 2 else (1, 1)
+    dt = L.BF16 if dtype == "bf16" else L.F32
+    d = L.PoolDesc(kind=kind, n=n, h=h, w=w, c=c, c_stride=cs, kh=k, kw=k, stride_h=s, stride_w=s,
+                   pad_t=p, pad_l=p, oh=oh, ow=ow, count_include_pad=0, dtype=dt)
+    xh = nhwc(x, cs)
+    xd = ctx.to_device(bf16_bits(xh) if dt == L.BF16 else xh)
+    eb = 2 if dt == L.BF16 else 4
+    yd = ctx.alloc(n * oh * ow * cs * eb)
+    ctx.pool2d(d, xd, yd)
+    ctx.sync()
+    y = ctx.download(yd, (n, oh, ow, cs), np.uint16 if dt == L.BF16 else np.float32)
+    y = from_bf16_bits(y) if dt == L.BF16 else y
+    ctx.free(xd)
+    ctx.free(yd)
+    return y[..., :c].transpose(0, 3, 1, 2)
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_pools(ctx, dtype):
+    rng = np.random.default_rng(13)
+    x = rng.standard_normal((2, 20, 15, 14)).astype(np.float32)
+    xr = oref.round_bf16(x) if dtype == "bf16" else x
+    got = _pool(ctx, x, 0, dtype)
+    np.testing.assert_array_equal(got, oref.maxpool(xr, kernel=[3, 3], strides=[2, 2], pads=[1] * 4))
+    got = _pool(ctx, x, 1, dtype)
+    want = oref.averagepool(xr, kernel=[3, 3], strides=[2, 2], pads=[1] * 4)
+    check(got, want, 1e-2 if dtype == "bf16" else 1e-6)
+    got = _pool(ctx, x, 2, dtype)
+    want = oref.global_average_pool(xr)
+    check(got, want, 1e-2 if dtype == "bf16" else 1e-6)
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_eltwise_program(ctx, dtype):
+    """relu(a + b) * c with c broadcast per (n, channel), plus a second output."""
+    rng = np.random.default_rng(17)
+    n, c, h, w = 2, 36, 5, 7
+    cs = _rnd8(c)
+    a = rng.standard_normal((n, c, h, w)).astype(np.float32)
+    b = rng.standard_normal((n, c, h, w)).astype(np.float32)
+    g = rng.standard_normal((n, c, 1, 1)).astype(np.float32)
+    dt = L.BF16 if dtype == "bf16" else L.F32
+    conv = (lambda t: bf16_bits(t)) if dt == L.BF16 else (lambda t: t)
+    ad, bd, gd = (ctx.to_device(conv(nhwc(t, cs))) for t in (a, b, g))
+    eb = 2 if dt == L.BF16 else 4
+    y0, y1 = ctx.alloc(n * h * w * cs * eb), ctx.alloc(n * h * w * cs * eb)
+    prog = L.EwProg(n=n, hw=h * w, c=c, c_stride=cs, dtype=dt, n_inputs=3, n_outputs=2, n_instr=3)
+    prog.bcast[0], prog.bcast[1], prog.bcast[2] = L.BC_FULL, L.BC_FULL, L.BC_NC
+    prog.code[0] = L.EwInstr(op=L.EW_ADD, dst=3, src0=0, src1=1)
+    prog.code[1] = L.EwInstr(op=L.EW_RELU, dst=4, src0=3, src1=0)
+    prog.code[2] = L.EwInstr(op=L.EW_MUL, dst=5, src0=4, src1=2)
+    prog.out_reg[0], prog.out_reg[1] = 5, 3
+    ctx.eltwise(prog, [ad, bd, gd], [y0, y1])
+    ctx.sync()
+    outs = []
+    for yd in (y0, y1):
+        y = ctx.download(yd, (n, h, w, cs), np.uint16 if dt == L.BF16 else np.float32)
+        y = from_bf16_bits(y) if dt == L.BF16 else y
+        assert np.all(y[..., c:] == 0)
+        outs.append(y[..., :c].transpose(0, 3, 1, 2))
+    if dt == L.BF16:
+        a, b, g = oref.round_bf16(a), oref.round_bf16(b), oref.round_bf16(g)
+    s = a + b
+    want0, want1 = np.maximum(s, 0) * g, s
+    check(outs[0], want0, 1e-2 if dt == L.BF16 else 1e-6)
+    check(outs[1], want1, 1e-2 if dt == L.BF16 else 1e-6)
+
+
+@pytest.mark.parametrize("dtype", [L.BF16, L.F32])
+def test_layout_roundtrip(ctx, dtype):
+    rng = np.random.default_rng(19)
+    x = rng.standard_normal((3, 5, 7, 9)).astype(np.float32)
+    xd = ctx.to_device(x)
+    cs = 8
+    eb = 2 if dtype == L.BF16 else 4
+    yd = ctx.alloc(3 * 7 * 9 * cs * eb)
+    zd = ctx.alloc(x.nbytes)
+    ctx.to_nhwc(xd, 3, 5, 7, 9, yd, cs, dtype)
+    ctx.to_nchw(yd, 3, 5, 7, 9, cs, dtype, zd)
+    ctx.sync()
+    z = ctx.download(zd, x.shape, np.float32)
+    want = oref.round_bf16(x) if dtype == L.BF16 else x
+    np.testing.assert_array_equal(z, want)
+    for p in (xd, yd, zd):
+        ctx.free(p)
+
+
+def test_bounded_wait_reports_timeout(ctx):
+    """A wait that can never complete gives up, sets the error word, and the
+    context stays usable (no fault, no hang)."""
+    ctx.timeout_probe(2000)   # 2 ms
+    ctx.check(ctx.lib.mdlc_sync(ctx.h, 10000), "sync")
+    assert ctx.check_flag() == L.DEVERR_WAIT_TIMEOUT
+    assert ctx.check_flag() == 0        # reading clears the word
+    test_layout_roundtrip(ctx, L.F32)   # still works afterwards
