@@ -108,8 +108,9 @@ typedef struct {
 /* Tile configuration for the tensor-core implicit GEMM (0 = library default). */
 typedef struct {
   int32_t bn;     /* output channels per CTA: 64, 128 or 256 */
-  int32_t stages; /* shared-memory pipeline depth: 2..8 */
-  int32_t flags;  /* reserved, 0 */
+  int32_t stages; /* shared-memory pipeline depth; built pairs: (64, 8), (128, 4), (256, 3) */
+  int32_t flags;  /* bit 0: gather the A operand with cp.async even when the layer
+                     qualifies for im2col-mode TMA loads */
 } mdlc_tile_cfg;
 
 /* Pooling over NHWC (reference: ops.py:109-150). kind: 0 max, 1 average,

@@ -50,27 +50,29 @@ MDLC_DEV bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(bar), "r"(parity)
+      : "r"(bar), "r"(parity), "r"(1000000u)
       : "memory");
   return ok != 0;
 }
 
 // Bounded wait for the phase with the given parity to complete. Gives up when
 // another role of the CTA has already given up (*abort != 0) or after
-// limit_ns; on time-out it records MDLC_DEVERR_WAIT_TIMEOUT and raises *abort.
-// Returns true when the phase completed.
+// limit_cycles SM clock cycles (clock64, cheap to read; the library passes 2x
+// the nanosecond limit, i.e. at least the limit at any clock up to 2 GHz); on
+// time-out it records MDLC_DEVERR_WAIT_TIMEOUT and raises *abort. Returns true
+// when the phase completed.
 MDLC_DEV bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort, int* err,
-                        uint64_t limit_ns) {
+                        uint64_t limit_cycles) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = globaltimer_ns();
+  const long long t0 = clock64();
   for (uint32_t i = 1;; ++i) {
     if (mbar_try_wait(bar, parity)) return true;
-    if ((i & 63u) == 0) {
+    if ((i & 3u) == 0) {
       if (abort && *abort) return false;
-      if (globaltimer_ns() - t0 > limit_ns) {
+      if ((unsigned long long)(clock64() - t0) > limit_cycles) {
         record_error(err, MDLC_DEVERR_WAIT_TIMEOUT);
         if (abort) *abort = 1;
         return false;
@@ -114,6 +116,37 @@ MDLC_DEV void tma_load_2d(uint32_t dst, const void* tmap, int32_t x, int32_t y, 
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar), "r"(x), "r"(y)
       : "memory");
+}
+
+// 4-D im2col-mode load (NHWC tensor map): 128 consecutive output pixels
+// starting at spatial coordinate (w, h) of image n, channels [c, c + box), with
+// the filter-tap offsets (off_w, off_h) added; padding reads as zero.
+MDLC_DEV void tma_load_im2col_4d(uint32_t dst, const void* tmap, int32_t c, int32_t w, int32_t h, int32_t n,
+                                 uint16_t off_w, uint16_t off_h, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.im2col.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2], {%7, %8};" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar), "r"(c), "r"(w), "r"(h), "r"(n), "h"(off_w), "h"(off_h)
+      : "memory");
+}
+
+// 2-D tiled store shared -> global (bulk-group completion); out-of-range rows
+// and columns of the box are not written.
+MDLC_DEV void tma_store_2d(const void* tmap, int32_t x, int32_t y, uint32_t src) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%2, %3}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(src), "r"(x), "r"(y)
+               : "memory");
+}
+MDLC_DEV void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// wait until at most N committed bulk groups still read their shared source
+template <int N>
+MDLC_DEV void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+template <int N>
+MDLC_DEV void bulk_wait() {
+  asm volatile("cp.async.bulk.wait_group %0;" ::"n"(N) : "memory");
 }
 
 // ------------------------------------------------------------ tcgen05
@@ -196,6 +229,22 @@ struct ActParams {
   int act;
   float alpha, beta, lo, hi;
 };
+
+MDLC_DEV float apply_act(float v, const ActParams& p);
+
+// Activation fixed at compile time (ACT >= 0) or chosen at run time (ACT == -1).
+// Fixing it keeps the unrolled epilogue small: every inlined copy of the
+// run-time switch carries the exp/tanh/erf paths.
+template <int ACT>
+MDLC_DEV float act_fn(float v, const ActParams& p) {
+  if constexpr (ACT == -1) return apply_act(v, p);
+  else if constexpr (ACT == MDLC_ACT_NONE) return v;
+  else if constexpr (ACT == MDLC_ACT_RELU) return fmaxf(v, 0.0f);
+  else if constexpr (ACT == MDLC_ACT_CLIP) return fminf(fmaxf(v, p.lo), p.hi);
+  else if constexpr (ACT == MDLC_ACT_GELU) return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+  else if constexpr (ACT == MDLC_ACT_SIGMOID) return 1.0f / (1.0f + expf(-v));
+  else return apply_act(v, p);
+}
 
 MDLC_DEV float apply_act(float v, const ActParams& p) {
   switch (p.act) {

@@ -60,7 +60,8 @@ struct TcArgs {
   int out_zp, qmin, qmax, res_zp, res_mult, res_shift;
   const float* deq_scale;
   const float* deq_bias;
-  unsigned long long wait_ns;
+  unsigned long long wait_cycles;
+  int tma_epi;  // bf16 output staged in shared memory and written by TMA stores
 };
 
 template <int BN, int STAGES>
@@ -68,9 +69,13 @@ struct Smem {
   static constexpr int kBBytes = BN * 128;
   static constexpr int kA = 0;
   static constexpr int kB = STAGES * kABytes;
-  static constexpr int kBar = kB + STAGES * kBBytes;
-  // barriers: fullA[S], fullB[S], empty[S], tfull[2], tempty[2], drain
-  static constexpr int kNumBars = 3 * STAGES + 5;
+  // epilogue staging: 4 warps x 2 buffers x (32 rows x 128 bytes)
+  static constexpr int kE = kB + STAGES * kBBytes;
+  // per-tile bias, double-buffered by tile parity (fp32, BN columns)
+  static constexpr int kBias = kE + 4 * 2 * 4096;
+  static constexpr int kBar = kBias + 2 * BN * 4;
+  // barriers: fullA[S], fullB[S], empty[S], tfull[2], tempty[2], drain, resid[4 warps][2 buffers]
+  static constexpr int kNumBars = 3 * STAGES + 13;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 16;
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
@@ -188,9 +193,11 @@ MDLC_DEV void store_chunk16(const TcArgs& a, int m, int nb0, const uint32_t (&v)
 }
 
 // ---------------------------------------------------------------- kernel
-template <int BN, int STAGES, int ESZ>
+template <int BN, int STAGES, int ESZ, int ACT, int AMODE>
 __global__ void __launch_bounds__(kThreads, 1)
-    conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const TcArgs a) {
+    conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_y,
+                   const __grid_constant__ CUtensorMap tmap_r, const __grid_constant__ CUtensorMap tmap_x,
+                   const TcArgs a) {
   using L = Smem<BN, STAGES>;
   constexpr int KB = 128 / ESZ;    // k-block elements (128 bytes)
   constexpr int CHUNK = 16 / ESZ;  // elements per 16-byte chunk
@@ -206,13 +213,14 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto tfull = [&](int i) { return sbar + 8u * (3 * STAGES + i); };
   auto tempty = [&](int i) { return sbar + 8u * (3 * STAGES + 2 + i); };
   const uint32_t drain = sbar + 8u * (3 * STAGES + 4);
+  auto resid = [&](int w, int b) { return sbar + 8u * (3 * STAGES + 5 + 2 * w + b); };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
     for (int i = 0; i < STAGES; ++i) {
-      mbar_init(fullA(i), 128);
+      mbar_init(fullA(i), AMODE ? 1 : 128);
       mbar_init(fullB(i), 1);
       mbar_init(empty(i), 1);
     }
@@ -221,6 +229,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       mbar_init(tempty(i), 128);
     }
     mbar_init(drain, 1);
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(resid(i, 0), 1);
+      mbar_init(resid(i, 1), 1);
+    }
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -228,7 +240,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     tmem_alloc(smem_u32(tmem_slot), kTmemCols);
     tmem_relinquish();
   }
-  if (warp == 8 && lane == 0) tma_prefetch_desc(&tmap_w);
+  if (warp == 8 && lane == 0) {
+    tma_prefetch_desc(&tmap_w);
+    if (AMODE) tma_prefetch_desc(&tmap_x);
+    if (a.tma_epi) {
+      tma_prefetch_desc(&tmap_y);
+      if (a.res) tma_prefetch_desc(&tmap_r);
+    }
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -237,7 +256,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int num_tiles = a.num_m_tiles * a.num_n_tiles;
   const int RS = a.r * a.s;
 
-  if (warp < 4) {
+  if (warp < 4 && AMODE == 0) {
     // ---------------- A producers: implicit im2col gather
     const int j = tid & 7;     // 16-byte chunk within the 128-byte row
     const int row0 = tid >> 3; // rows row0 + 16*i, i = 0..7
@@ -269,7 +288,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       for (int kb = 0; kb < a.num_kb; ++kb, ++it) {
         const int st = it % STAGES;
-        if (!mbar_wait(empty(st), ((it / STAGES) & 1) ^ 1, abort_flag, a.err, a.wait_ns)) {
+        if (!mbar_wait(empty(st), ((it / STAGES) & 1) ^ 1, abort_flag, a.err, a.wait_cycles)) {
           ok = false;
           break;
         }
@@ -293,44 +312,146 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     cp_async_wait_all();
-  } else if (warp < 8) {
+  } else if (warp >= 4 && warp < 8) {
     // ---------------- epilogue
     const int ew = warp - 4;
+    const int etid = tid - 128;
     const uint32_t lane_base = (uint32_t)(ew * 32) << 16;
-    int local = 0;
+    const uint32_t stage0 = sbase + L::kE + ew * 8192;
+    uint8_t* stage_ptr0 = smem + L::kE + ew * 8192;
+    const bool tma_epi = ESZ == 2 && a.tma_epi;
+    int local = 0, chunk_i = 0;
+    uint32_t res_use0 = 0, res_use1 = 0;  // completed loads per residual buffer (phase parity)
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int buf = local & 1;
-      bool ok = mbar_wait(tfull(buf), (local >> 1) & 1, abort_flag, a.err, a.wait_ns);
+      const int m0 = (tile / a.num_n_tiles) * kBM;
+      const int n0 = (tile % a.num_n_tiles) * BN;
+      float* sbias = reinterpret_cast<float*>(smem + L::kBias) + buf * BN;
+      if (tma_epi) {
+        // stage this tile's bias (and the first residual chunk) while the main loop runs
+        for (int i = etid; i < BN; i += 128)
+          sbias[i] = (a.bias && n0 + i < a.k) ? __ldg(static_cast<const float*>(a.bias) + n0 + i) : 0.0f;
+        if (a.res && lane == 0) {
+          bulk_wait_read<0>();
+          const int sbuf = chunk_i & 1;
+          mbar_arrive_expect_tx(resid(ew, sbuf), 4096);
+          tma_load_2d(stage0 + sbuf * 4096, &tmap_r, n0, m0 + ew * 32, resid(ew, sbuf));
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+      }
+      bool ok = mbar_wait(tfull(buf), (local >> 1) & 1, abort_flag, a.err, a.wait_cycles);
       ok = __all_sync(0xffffffffu, ok);
       if (!ok) break;
       tc_fence_after();
-      const int m0 = (tile / a.num_n_tiles) * kBM;
-      const int n0 = (tile % a.num_n_tiles) * BN;
       const int m = m0 + ew * 32 + lane;
       const uint32_t taddr = tmem + lane_base + (uint32_t)(buf * BN);
+      if (tma_epi) {
+        // 64-column chunks: TMEM -> registers -> (+bias, +residual tile, act) ->
+        // bf16 in a 128B-swizzled staging tile -> TMA store
+        const int sw = lane & 7;
 #pragma unroll 1
-      for (int c0 = 0; c0 < BN; c0 += 16) {
-        if (n0 + c0 >= a.ks) break;  // warp-uniform
-        uint32_t v[16];
-        tmem_ld16(taddr + c0, v);
-        tmem_ld_wait();
-        if (m < a.M) store_chunk16<ESZ>(a, m, n0 + c0, v);
+        for (int c0 = 0; c0 < BN; c0 += 64) {
+          if (n0 + c0 >= a.ks) break;  // warp-uniform
+          const int sbuf = chunk_i & 1;
+          const uint32_t sb = stage0 + sbuf * 4096;
+          uint8_t* sp = stage_ptr0 + sbuf * 4096 + lane * 128;
+          if (a.res) {
+            const uint32_t use = sbuf ? res_use1++ : res_use0++;
+            const bool rok = mbar_wait(resid(ew, sbuf), use & 1, abort_flag, a.err, a.wait_cycles);
+            if (!__all_sync(0xffffffffu, rok)) {
+              ok = false;
+              break;
+            }
+            if (c0 + 64 < BN && n0 + c0 + 64 < a.ks && lane == 0) {
+              // prefetch the next residual chunk into the other buffer once its store has read it
+              bulk_wait_read<0>();
+              mbar_arrive_expect_tx(resid(ew, sbuf ^ 1), 4096);
+              tma_load_2d(stage0 + (sbuf ^ 1) * 4096, &tmap_r, n0 + c0 + 64, m0 + ew * 32, resid(ew, sbuf ^ 1));
+            }
+          } else {
+            if (lane == 0) bulk_wait_read<1>();  // the store issued two chunks ago has read this buffer
+          }
+          __syncwarp();
+          uint32_t v[64];
+          tmem_ld16(taddr + c0, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
+          tmem_ld16(taddr + c0 + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
+          tmem_ld16(taddr + c0 + 32, *reinterpret_cast<uint32_t(*)[16]>(&v[32]));
+          tmem_ld16(taddr + c0 + 48, *reinterpret_cast<uint32_t(*)[16]>(&v[48]));
+          tmem_ld_wait();
+#pragma unroll
+          for (int q = 0; q < 8; ++q) {  // 8-column (16-byte) groups
+            uint4* qp = reinterpret_cast<uint4*>(sp + ((q ^ sw) << 4));
+            const float4 b0 = *reinterpret_cast<const float4*>(sbias + c0 + 8 * q);
+            const float4 b1 = *reinterpret_cast<const float4*>(sbias + c0 + 8 * q + 4);
+            float f[8] = {__uint_as_float(v[8 * q]) + b0.x, __uint_as_float(v[8 * q + 1]) + b0.y,
+                          __uint_as_float(v[8 * q + 2]) + b0.z, __uint_as_float(v[8 * q + 3]) + b0.w,
+                          __uint_as_float(v[8 * q + 4]) + b1.x, __uint_as_float(v[8 * q + 5]) + b1.y,
+                          __uint_as_float(v[8 * q + 6]) + b1.z, __uint_as_float(v[8 * q + 7]) + b1.w};
+            if (a.res) {
+              const uint4 r = *qp;
+              f[0] += bf16_lo(r.x); f[1] += bf16_hi(r.x); f[2] += bf16_lo(r.y); f[3] += bf16_hi(r.y);
+              f[4] += bf16_lo(r.z); f[5] += bf16_hi(r.z); f[6] += bf16_lo(r.w); f[7] += bf16_hi(r.w);
+            }
+            const int nb0 = n0 + c0 + 8 * q;
+#pragma unroll
+            for (int e = 0; e < 8; ++e) f[e] = (nb0 + e < a.k) ? act_fn<ACT>(f[e], a.act) : 0.0f;
+            *qp = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
+                             pack_bf16x2(f[6], f[7]));
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            tma_store_2d(&tmap_y, n0 + c0, m0 + ew * 32, sb);
+            bulk_commit();
+          }
+          ++chunk_i;
+        }
+        if (!ok) break;
+      } else {
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          if (n0 + c0 >= a.ks) break;  // warp-uniform
+          uint32_t v[16];
+          tmem_ld16(taddr + c0, v);
+          tmem_ld_wait();
+          if (m < a.M) store_chunk16<ESZ>(a, m, n0 + c0, v);
+        }
       }
       tc_fence_before();
       mbar_arrive(tempty(buf));
     }
+    if (lane == 0) bulk_wait<0>();
   } else if (warp == 8) {
-    // ---------------- B producer (TMA)
+    // ---------------- B producer (TMA); with AMODE 1 also the A operand by im2col TMA
     if (lane == 0) {
       int it = 0;
       bool ok = true;
+      const int cpb = a.cs / KB;  // k-blocks per filter tap (AMODE 1: cs % KB == 0)
+      const int ohw = a.oh * a.ow;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         const int n0 = (tile % a.num_n_tiles) * BN;
+        int xw = 0, xh = 0, xn = 0;
+        if (AMODE) {
+          const int m0 = (tile / a.num_n_tiles) * kBM;
+          xn = m0 / ohw;
+          const int rem = m0 - xn * ohw;
+          const int oy = rem / a.ow;
+          xh = oy * a.sh - a.pt;
+          xw = (rem - oy * a.ow) * a.sw - a.pl;
+        }
         for (int kb = 0; kb < a.num_kb; ++kb, ++it) {
           const int st = it % STAGES;
-          if (!mbar_wait(empty(st), ((it / STAGES) & 1) ^ 1, abort_flag, a.err, a.wait_ns)) {
+          if (!mbar_wait(empty(st), ((it / STAGES) & 1) ^ 1, abort_flag, a.err, a.wait_cycles)) {
             ok = false;
             break;
+          }
+          if (AMODE) {
+            const int tap = kb / cpb;
+            const int c0 = (kb - tap * cpb) * KB;
+            const int rr = tap / a.s;
+            mbar_arrive_expect_tx(fullA(st), kABytes);
+            tma_load_im2col_4d(sA + st * kABytes, &tmap_x, c0, xw, xh, xn, (uint16_t)((tap - rr * a.s) * a.dw),
+                               (uint16_t)(rr * a.dh), fullA(st));
           }
           mbar_arrive_expect_tx(fullB(st), L::kBBytes);
           tma_load_2d(sB + st * L::kBBytes, &tmap_w, kb * KB, n0, fullB(st));
@@ -338,19 +459,21 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) {
         // let the loads already issued land before the CTA's shared memory is released
-        for (int q = it - 1; q >= 0 && q >= it - STAGES; --q)
-          mbar_wait(fullB(q % STAGES), (q / STAGES) & 1, nullptr, a.err, 1000000ull);
+        for (int q = it - 1; q >= 0 && q >= it - STAGES; --q) {
+          mbar_wait(fullB(q % STAGES), (q / STAGES) & 1, nullptr, a.err, 2000000ull);
+          if (AMODE) mbar_wait(fullA(q % STAGES), (q / STAGES) & 1, nullptr, a.err, 2000000ull);
+        }
       }
     }
-  } else {
-    // ---------------- MMA issuer
+  } else if (warp == 9) {
+    // ---------------- MMA issuer (warps 0-3 idle here when A arrives by TMA)
     if (lane == 0) {
       const uint32_t idesc = ESZ == 2 ? idesc_bf16(kBM, BN) : idesc_i8(kBM, BN, a.a_signed, 1);
       int it = 0, local = 0;
       bool ok = true;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
         const int buf = local & 1;
-        if (!mbar_wait(tempty(buf), ((local >> 1) & 1) ^ 1, abort_flag, a.err, a.wait_ns)) {
+        if (!mbar_wait(tempty(buf), ((local >> 1) & 1) ^ 1, abort_flag, a.err, a.wait_cycles)) {
           ok = false;
           break;
         }
@@ -359,8 +482,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kb = 0; kb < a.num_kb; ++kb, ++it) {
           const int st = it % STAGES;
           const uint32_t par = (it / STAGES) & 1;
-          if (!mbar_wait(fullB(st), par, abort_flag, a.err, a.wait_ns) ||
-              !mbar_wait(fullA(st), par, abort_flag, a.err, a.wait_ns)) {
+          if (!mbar_wait(fullB(st), par, abort_flag, a.err, a.wait_cycles) ||
+              !mbar_wait(fullA(st), par, abort_flag, a.err, a.wait_cycles)) {
             ok = false;
             break;
           }
@@ -413,11 +536,60 @@ PFN_cuTensorMapEncodeTiled_v12000 get_encode_fn() {
   return fn;
 }
 
-template <int BN, int STAGES, int ESZ>
-int launch_tc(mdlc_ctx* ctx, const CUtensorMap& tmap, const TcArgs& args) {
+PFN_cuTensorMapEncodeIm2col_v12000 get_im2col_fn() {
+  static PFN_cuTensorMapEncodeIm2col_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    cudaDriverEntryPointQueryResult q;
+    void* p = nullptr;
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeIm2col", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeIm2col_v12000>(p);
+  });
+  return fn;
+}
+
+// im2col-mode tensor map over the NHWC input: 128 output pixels x one
+// 128-byte channel block per load. The pixel box corners follow from the
+// padding and the output extent: lower = -pad, upper = pad_end - (R-1)*dil
+// with pad_end chosen so the traversal yields exactly oh x ow positions.
+// Returns false when the layer does not fit the hardware's limits (channel
+// stride not a multiple of the block, corners outside [-128, 127], traversal
+// stride above 8, offsets of 128 or more) or is small (< 128 KiB), in which
+// case the kernel gathers A with cp.async instead.
+bool encode_im2col(CUtensorMap* m, const mdlc_conv_desc& d, const void* x, int esz) {
+  const int kb_elems = 128 / esz;
+  if (d.c_stride % kb_elems) return false;
+  if (d.stride_h > 8 || d.stride_w > 8) return false;
+  if ((d.r - 1) * d.dil_h >= 128 || (d.s - 1) * d.dil_w >= 128) return false;
+  const long long bytes = (long long)d.n * d.h * d.w * d.c_stride * esz;
+  if (bytes < 131072) return false;
+  const int lower_w = -d.pad_l, lower_h = -d.pad_t;
+  const int upper_w = (d.ow - 1) * d.stride_w + 1 - d.w - d.pad_l;
+  const int upper_h = (d.oh - 1) * d.stride_h + 1 - d.h - d.pad_t;
+  for (int v : {lower_w, lower_h, upper_w, upper_h})
+    if (v < -128 || v > 127) return false;
+  auto fn = get_im2col_fn();
+  if (!fn) return false;
+  const cuuint64_t gdim[4] = {(cuuint64_t)d.c_stride, (cuuint64_t)d.w, (cuuint64_t)d.h, (cuuint64_t)d.n};
+  const cuuint64_t gstride[3] = {(cuuint64_t)d.c_stride * esz, (cuuint64_t)d.w * d.c_stride * esz,
+                                 (cuuint64_t)d.h * d.w * d.c_stride * esz};
+  const int lower[2] = {lower_w, lower_h};
+  const int upper[2] = {upper_w, upper_h};
+  const cuuint32_t estride[4] = {1, (cuuint32_t)d.stride_w, (cuuint32_t)d.stride_h, 1};
+  return fn(m, esz == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(x),
+            gdim, gstride, lower, upper, (cuuint32_t)kb_elems, (cuuint32_t)kBM, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+template <int BN, int STAGES, int ESZ, int ACT, int AMODE>
+int launch_tc(mdlc_ctx* ctx, const CUtensorMap& tmap, const CUtensorMap& tmap_y, const CUtensorMap& tmap_r,
+              const CUtensorMap& tmap_x, const TcArgs& args) {
   using L = Smem<BN, STAGES>;
   static_assert(L::kAlloc <= 232448, "shared memory budget");
-  auto kern = conv_tc_kernel<BN, STAGES, ESZ>;
+  auto kern = conv_tc_kernel<BN, STAGES, ESZ, ACT, AMODE>;
   static bool attr_set[64] = {};
   if (!attr_set[ctx->device & 63]) {
     cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
@@ -426,7 +598,7 @@ int launch_tc(mdlc_ctx* ctx, const CUtensorMap& tmap, const TcArgs& args) {
   }
   const int tiles = args.num_m_tiles * args.num_n_tiles;
   const int grid = tiles < ctx->num_sms ? tiles : ctx->num_sms;
-  kern<<<grid, kThreads, L::kAlloc, ctx->stream>>>(tmap, args);
+  kern<<<grid, kThreads, L::kAlloc, ctx->stream>>>(tmap, tmap_y, tmap_r, tmap_x, args);
   mdlc_note_launch(ctx);
   return mdlc_cuda_status(ctx, cudaGetLastError(), "conv_tc launch");
 }
@@ -451,7 +623,7 @@ int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w
     // keep enough tiles in flight for the whole GPU
     while (bn > 64 && (long long)num_m * ((d.k_stride + bn - 1) / bn) < ctx->num_sms) bn /= 2;
   }
-  if (!stages) stages = bn == 256 ? 4 : (bn == 128 ? 6 : 8);
+  if (!stages) stages = bn == 256 ? 3 : (bn == 128 ? 4 : 8);
   if (bn != 64 && bn != 128 && bn != 256)
     return mdlc_set_error(ctx, MDLC_ERR_INVALID, "conv_tc: bn must be 64/128/256, got %d", bn);
 
@@ -485,7 +657,7 @@ int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w
   a.num_n_tiles = (d.k_stride + bn - 1) / bn;
   a.out_type = d.out_type;
   a.a_signed = d.in_type == MDLC_S8;
-  a.wait_ns = kWaitLimitNs;
+  a.wait_cycles = 2 * kWaitLimitNs;  // cycles: >= the nanosecond limit at clocks up to 2 GHz
   if (epi) {
     a.act = ActParams{epi->act, epi->alpha, epi->beta, epi->clip_lo, epi->clip_hi};
     a.rq_mult = epi->rq_mult; a.rq_shift = epi->rq_shift;
@@ -495,15 +667,59 @@ int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w
   }
   if (int8) a.pad_src = ctx->d_pad + 16 * (d.in_zp & 0xFF);
 
-#define MDLC_TC_CASE(BN_, ST_)                                                     \
-  if (bn == BN_ && stages == ST_)                                                  \
-    return int8 ? launch_tc<BN_, ST_, 1>(ctx, tmap, a) : launch_tc<BN_, ST_, 2>(ctx, tmap, a);
-  MDLC_TC_CASE(64, 4)
+  // A operand: im2col-mode TMA when the layer qualifies (zero padding only, so
+  // not for int8 inputs with a non-zero zero point), else the cp.async gather
+  CUtensorMap tmap_x = tmap;
+  const bool im2col = (!int8 || d.in_zp == 0) && !(cfg && (cfg->flags & 1)) &&
+                      encode_im2col(&tmap_x, d, x, esz);
+
+  // bf16 output: the epilogue stages 32x64 tiles in shared memory and writes
+  // them with 2-D TMA stores; a residual is brought in by TMA loads of the
+  // same tile shape. Boxes hanging over M or k_stride are clipped by TMA.
+  CUtensorMap tmap_y = tmap, tmap_r = tmap;
+  if (!int8 && d.out_type == MDLC_BF16) {
+    auto encode2d = [&](CUtensorMap* m, const void* base, int inner) {
+      const cuuint64_t gd[2] = {(cuuint64_t)inner, (cuuint64_t)M};
+      const cuuint64_t gs[1] = {(cuuint64_t)inner * 2};
+      const cuuint32_t bx[2] = {64, 32};
+      return encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), gd, gs, bx, estride,
+                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    };
+    if (encode2d(&tmap_y, y, d.k_stride) != CUDA_SUCCESS ||
+        (res && encode2d(&tmap_r, res, a.res_s) != CUDA_SUCCESS))
+      return mdlc_set_error(ctx, MDLC_ERR_INVALID, "output/residual tensor map encode failed");
+    a.tma_epi = 1;
+  }
+
+// Activation specialisations of the bf16 TMA epilogue: none, ReLU, Clip
+// (ReLU6), GELU, sigmoid; anything else (and the int8 / fp32-output paths)
+// uses the run-time switch.
+  const int act = a.act.act;
+  const int act_t = (!int8 && a.tma_epi &&
+                     (act == MDLC_ACT_NONE || act == MDLC_ACT_RELU || act == MDLC_ACT_CLIP ||
+                      act == MDLC_ACT_GELU || act == MDLC_ACT_SIGMOID)) ? act : -1;
+#define MDLC_TC_ACT(BN_, ST_, A_)                                                            \
+  if (act_t == A_)                                                                          \
+    return im2col ? launch_tc<BN_, ST_, 2, A_, 1>(ctx, tmap, tmap_y, tmap_r, tmap_x, a)     \
+                  : launch_tc<BN_, ST_, 2, A_, 0>(ctx, tmap, tmap_y, tmap_r, tmap_x, a);
+#define MDLC_TC_CASE(BN_, ST_)                                                               \
+  if (bn == BN_ && stages == ST_) {                                                         \
+    if (int8)                                                                               \
+      return im2col ? launch_tc<BN_, ST_, 1, -1, 1>(ctx, tmap, tmap_y, tmap_r, tmap_x, a)   \
+                    : launch_tc<BN_, ST_, 1, -1, 0>(ctx, tmap, tmap_y, tmap_r, tmap_x, a);  \
+    MDLC_TC_ACT(BN_, ST_, MDLC_ACT_NONE)                                                    \
+    MDLC_TC_ACT(BN_, ST_, MDLC_ACT_RELU)                                                    \
+    MDLC_TC_ACT(BN_, ST_, MDLC_ACT_CLIP)                                                    \
+    MDLC_TC_ACT(BN_, ST_, MDLC_ACT_GELU)                                                    \
+    MDLC_TC_ACT(BN_, ST_, MDLC_ACT_SIGMOID)                                                 \
+    return im2col ? launch_tc<BN_, ST_, 2, -1, 1>(ctx, tmap, tmap_y, tmap_r, tmap_x, a)     \
+                  : launch_tc<BN_, ST_, 2, -1, 0>(ctx, tmap, tmap_y, tmap_r, tmap_x, a);    \
+  }
   MDLC_TC_CASE(64, 8)
   MDLC_TC_CASE(128, 4)
-  MDLC_TC_CASE(128, 6)
   MDLC_TC_CASE(256, 3)
-  MDLC_TC_CASE(256, 4)
+#undef MDLC_TC_ACT
 #undef MDLC_TC_CASE
   return mdlc_set_error(ctx, MDLC_ERR_UNSUPPORTED, "conv_tc: no kernel for bn=%d stages=%d", bn, stages);
 }

@@ -235,22 +235,22 @@ int mdlc_launch_count(mdlc_ctx* ctx, long long* count) {
 // ---------------------------------------------------------------- probe
 // One thread initialises an mbarrier expecting one arrival that never comes
 // and waits on it with the library's bounded wait. The wait gives up after
-// limit_ns, records MDLC_DEVERR_WAIT_TIMEOUT and the kernel returns normally.
-__global__ void timeout_probe_kernel(int* err, uint64_t limit_ns) {
+// limit_cycles, records MDLC_DEVERR_WAIT_TIMEOUT and the kernel returns normally.
+__global__ void timeout_probe_kernel(int* err, uint64_t limit_cycles) {
   __shared__ __align__(8) uint64_t bar;
   __shared__ int abort_flag;
   if (threadIdx.x != 0) return;
   abort_flag = 0;
   mbar_init(smem_u32(&bar), 1);
   fence_mbar_init();
-  mbar_wait(smem_u32(&bar), 0, &abort_flag, err, limit_ns);
+  mbar_wait(smem_u32(&bar), 0, &abort_flag, err, limit_cycles);
   if (abort_flag) record_error(err, MDLC_DEVERR_WAIT_TIMEOUT);
 }
 
 extern "C" int mdlc_debug_timeout_probe(mdlc_ctx* ctx, int limit_us) {
   if (!ctx || limit_us <= 0 || limit_us > 2000000) return MDLC_ERR_INVALID;
   cudaSetDevice(ctx->device);
-  timeout_probe_kernel<<<1, 32, 0, ctx->stream>>>(ctx->d_err, (uint64_t)limit_us * 1000ull);
+  timeout_probe_kernel<<<1, 32, 0, ctx->stream>>>(ctx->d_err, (uint64_t)limit_us * 2000ull);
   mdlc_note_launch(ctx);
   return mdlc_cuda_status(ctx, cudaGetLastError(), "timeout probe launch");
 }
