@@ -204,6 +204,11 @@ int mdlc_nchw_to_nhwc(mdlc_ctx* ctx, const float* x, int n, int c, int h, int w,
                       int dtype, float inv_scale, int zp);
 int mdlc_nhwc_to_nchw(mdlc_ctx* ctx, const void* x, int n, int c, int h, int w, int cs, int dtype,
                       float* y, float scale, int zp);
+/* NCHW fp32 (h, w even) -> 2x2 space-to-depth NHWC: y[n][Y][X][(dy*2+dx)*c + ci]
+ * = x[n][ci][2Y+dy][2X+dx], channel stride cs >= 4c (pad channels zeroed).
+ * Feeds a stride-2 stem conv rewritten as a stride-1 conv (no reference
+ * counterpart: a layout choice of this backend). */
+int mdlc_nchw_to_s2d(mdlc_ctx* ctx, const float* x, int n, int c, int h, int w, void* y, int cs, int dtype);
 
 /* ---- CUDA graph capture of a whole run (b=1 latency) ------------------- */
 int mdlc_graph_begin(mdlc_ctx* ctx);

@@ -99,7 +99,7 @@ class _Device:
     def _desc(self, geom, lo):
         k = geom["k"]
         return L.ConvDesc(n=geom["n"], h=geom["h"], w=geom["w"], c=geom["c"],
-                          c_stride=lowering.round_up(geom["c"], 8), k=k, k_stride=lowering.round_up(k, 8),
+                          c_stride=geom.get("cs", lowering.round_up(geom["c"], 8)), k=k, k_stride=lowering.round_up(k, 8),
                           r=geom["r"], s=geom["s"], stride_h=geom["sh"], stride_w=geom["sw"],
                           pad_t=geom["pt"], pad_l=geom["pl"], dil_h=geom["dh"], dil_w=geom["dw"],
                           oh=geom["oh"], ow=geom["ow"], groups=geom["groups"], in_type=lo.dtype,
@@ -170,7 +170,11 @@ class _Device:
     def issue_inputs(self):
         for name in self.lo.inputs:
             t = self.lo.tensors[name]
-            self.ctx.to_nhwc(self.in_dev[name], t.n, t.c, t.h, t.w, self.ptr(name), t.cs, t.dtype)
+            if t.layout == "s2d2":
+                n, c, h, w = self.lo.shapes[name]
+                self.ctx.to_s2d(self.in_dev[name], n, c, h, w, self.ptr(name), t.cs, t.dtype)
+            else:
+                self.ctx.to_nhwc(self.in_dev[name], t.n, t.c, t.h, t.w, self.ptr(name), t.cs, t.dtype)
 
     def issue_outputs(self):
         for name in self.lo.outputs:

@@ -173,6 +173,13 @@ MDLC_DEV uint64_t umma_desc_sw128(uint32_t saddr) {
          ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
+// Same for the narrower K-major swizzles: layout 6 = SWIZZLE_32B (8 rows x
+// 32 bytes per atom, SBO 256), layout 4 = SWIZZLE_64B (8 x 64 bytes, SBO 512).
+MDLC_DEV uint64_t umma_desc_k(uint32_t saddr, uint32_t sbo_bytes, uint32_t layout) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) |
+         ((uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32) | ((uint64_t)1 << 46) | ((uint64_t)layout << 61);
+}
+
 // Instruction descriptor, kind::f16 with bf16 operands and fp32 accumulator.
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) |

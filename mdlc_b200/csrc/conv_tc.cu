@@ -445,13 +445,29 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          if (AMODE) {
+          if (AMODE == 1) {
             const int tap = kb / cpb;
             const int c0 = (kb - tap * cpb) * KB;
             const int rr = tap / a.s;
             mbar_arrive_expect_tx(fullA(st), kABytes);
             tma_load_im2col_4d(sA + st * kABytes, &tmap_x, c0, xw, xh, xn, (uint16_t)((tap - rr * a.s) * a.dw),
                                (uint16_t)(rr * a.dh), fullA(st));
+          } else if (AMODE >= 2) {
+            // AMODE 2: cs == 16 (4 taps per k-block, 32-byte rows); AMODE 3: cs == 32 (2 taps, 64-byte rows)
+            constexpr int TPB = AMODE == 2 ? 4 : 2;
+            constexpr uint32_t kTapBytes = kABytes / TPB;
+            mbar_arrive_expect_tx(fullA(st), kABytes);
+#pragma unroll
+            for (int j = 0; j < TPB; ++j) {
+              const int tap = kb * TPB + j;
+              const int rr = tap / a.s;
+              // taps past the end of the filter re-load tap 0: their weights are zero,
+              // so any finite data contributes nothing
+              const bool real = tap < RS;
+              tma_load_im2col_4d(sA + st * kABytes + j * kTapBytes, &tmap_x, 0, xw, xh, xn,
+                                 (uint16_t)(real ? (tap - rr * a.s) * a.dw : 0), (uint16_t)(real ? rr * a.dh : 0),
+                                 fullA(st));
+            }
           }
           mbar_arrive_expect_tx(fullB(st), L::kBBytes);
           tma_load_2d(sB + st * L::kBBytes, &tmap_w, kb * KB, n0, fullB(st));
@@ -494,7 +510,9 @@ __global__ void __launch_bounds__(kThreads, 1)
           const uint32_t ab = sA + st * kABytes, bb = sB + st * L::kBBytes;
 #pragma unroll
           for (int kq = 0; kq < 4; ++kq) {
-            const uint64_t ad = umma_desc_sw128(ab + kq * 32);
+            const uint64_t ad = AMODE == 2   ? umma_desc_k(ab + kq * (kABytes / 4), 256, 6)
+                                : AMODE == 3 ? umma_desc_k(ab + (kq >> 1) * (kABytes / 2) + (kq & 1) * 32, 512, 4)
+                                             : umma_desc_sw128(ab + kq * 32);
             const uint64_t bd = umma_desc_sw128(bb + kq * 32);
             if constexpr (ESZ == 2)
               umma_bf16(d, ad, bd, idesc, (kb | kq) != 0);
@@ -558,30 +576,42 @@ PFN_cuTensorMapEncodeIm2col_v12000 get_im2col_fn() {
 // stride not a multiple of the block, corners outside [-128, 127], traversal
 // stride above 8, offsets of 128 or more) or is small (< 128 KiB), in which
 // case the kernel gathers A with cp.async instead.
-bool encode_im2col(CUtensorMap* m, const mdlc_conv_desc& d, const void* x, int esz) {
+int encode_im2col(CUtensorMap* m, const mdlc_conv_desc& d, const void* x, int esz) {
   const int kb_elems = 128 / esz;
-  if (d.c_stride % kb_elems) return false;
-  if (d.stride_h > 8 || d.stride_w > 8) return false;
-  if ((d.r - 1) * d.dil_h >= 128 || (d.s - 1) * d.dil_w >= 128) return false;
+  // mode 1: 128-byte channel blocks; modes 2/3: the whole pixel (bf16 cs 16 / 32) per load
+  int mode = 0, cpp = kb_elems;
+  CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B;
+  if (d.c_stride % kb_elems == 0) {
+    mode = 1;
+  } else if (esz == 2 && d.c_stride == 16) {
+    mode = 2, cpp = 16, sw = CU_TENSOR_MAP_SWIZZLE_32B;
+  } else if (esz == 2 && d.c_stride == 32) {
+    mode = 3, cpp = 32, sw = CU_TENSOR_MAP_SWIZZLE_64B;
+  } else {
+    return 0;
+  }
+  if (d.stride_h > 8 || d.stride_w > 8) return 0;
+  if ((d.r - 1) * d.dil_h >= 128 || (d.s - 1) * d.dil_w >= 128) return 0;
   const long long bytes = (long long)d.n * d.h * d.w * d.c_stride * esz;
-  if (bytes < 131072) return false;
+  if (bytes < 131072) return 0;
   const int lower_w = -d.pad_l, lower_h = -d.pad_t;
   const int upper_w = (d.ow - 1) * d.stride_w + 1 - d.w - d.pad_l;
   const int upper_h = (d.oh - 1) * d.stride_h + 1 - d.h - d.pad_t;
   for (int v : {lower_w, lower_h, upper_w, upper_h})
-    if (v < -128 || v > 127) return false;
+    if (v < -128 || v > 127) return 0;
   auto fn = get_im2col_fn();
-  if (!fn) return false;
+  if (!fn) return 0;
   const cuuint64_t gdim[4] = {(cuuint64_t)d.c_stride, (cuuint64_t)d.w, (cuuint64_t)d.h, (cuuint64_t)d.n};
   const cuuint64_t gstride[3] = {(cuuint64_t)d.c_stride * esz, (cuuint64_t)d.w * d.c_stride * esz,
                                  (cuuint64_t)d.h * d.w * d.c_stride * esz};
   const int lower[2] = {lower_w, lower_h};
   const int upper[2] = {upper_w, upper_h};
   const cuuint32_t estride[4] = {1, (cuuint32_t)d.stride_w, (cuuint32_t)d.stride_h, 1};
-  return fn(m, esz == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 4, const_cast<void*>(x),
-            gdim, gstride, lower, upper, (cuuint32_t)kb_elems, (cuuint32_t)kBM, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
-            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  const bool ok = fn(m, esz == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 4,
+                     const_cast<void*>(x), gdim, gstride, lower, upper, (cuuint32_t)cpp, (cuuint32_t)kBM, estride,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  return ok ? mode : 0;
 }
 
 template <int BN, int STAGES, int ESZ, int ACT, int AMODE>
@@ -670,8 +700,7 @@ int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w
   // A operand: im2col-mode TMA when the layer qualifies (zero padding only, so
   // not for int8 inputs with a non-zero zero point), else the cp.async gather
   CUtensorMap tmap_x = tmap;
-  const bool im2col = (!int8 || d.in_zp == 0) && !(cfg && (cfg->flags & 1)) &&
-                      encode_im2col(&tmap_x, d, x, esz);
+  const int im2col = ((!int8 || d.in_zp == 0) && !(cfg && (cfg->flags & 1))) ? encode_im2col(&tmap_x, d, x, esz) : 0;
 
   // bf16 output: the epilogue stages 32x64 tiles in shared memory and writes
   // them with 2-D TMA stores; a residual is brought in by TMA loads of the
@@ -699,27 +728,34 @@ int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w
   const int act_t = (!int8 && a.tma_epi &&
                      (act == MDLC_ACT_NONE || act == MDLC_ACT_RELU || act == MDLC_ACT_CLIP ||
                       act == MDLC_ACT_GELU || act == MDLC_ACT_SIGMOID)) ? act : -1;
-#define MDLC_TC_ACT(BN_, ST_, A_)                                                            \
-  if (act_t == A_)                                                                          \
-    return im2col ? launch_tc<BN_, ST_, 2, A_, 1>(ctx, tmap, tmap_y, tmap_r, tmap_x, a)     \
-                  : launch_tc<BN_, ST_, 2, A_, 0>(ctx, tmap, tmap_y, tmap_r, tmap_x, a);
+#define MDLC_TC_LAUNCH(BN_, ST_, E_, A_)                                                      \
+  switch (im2col) {                                                                         \
+    case 1: return launch_tc<BN_, ST_, E_, A_, 1>(ctx, tmap, tmap_y, tmap_r, tmap_x, a);    \
+    case 2: if (BN_ <= 128) return launch_tc<BN_, ST_, E_, A_, 2>(ctx, tmap, tmap_y, tmap_r, tmap_x, a); break; \
+    case 3: if (BN_ <= 128) return launch_tc<BN_, ST_, E_, A_, 3>(ctx, tmap, tmap_y, tmap_r, tmap_x, a); break; \
+    default: break;                                                                         \
+  }                                                                                         \
+  return launch_tc<BN_, ST_, E_, A_, 0>(ctx, tmap, tmap_y, tmap_r, tmap_x, a);
+#define MDLC_TC_ACT(BN_, ST_, A_) \
+  if (act_t == A_) { MDLC_TC_LAUNCH(BN_, ST_, 2, A_) }
 #define MDLC_TC_CASE(BN_, ST_)                                                               \
   if (bn == BN_ && stages == ST_) {                                                         \
-    if (int8)                                                                               \
-      return im2col ? launch_tc<BN_, ST_, 1, -1, 1>(ctx, tmap, tmap_y, tmap_r, tmap_x, a)   \
-                    : launch_tc<BN_, ST_, 1, -1, 0>(ctx, tmap, tmap_y, tmap_r, tmap_x, a);  \
+    if (int8) {                                                                             \
+      if (im2col == 1) return launch_tc<BN_, ST_, 1, -1, 1>(ctx, tmap, tmap_y, tmap_r, tmap_x, a); \
+      return launch_tc<BN_, ST_, 1, -1, 0>(ctx, tmap, tmap_y, tmap_r, tmap_x, a);           \
+    }                                                                                       \
     MDLC_TC_ACT(BN_, ST_, MDLC_ACT_NONE)                                                    \
     MDLC_TC_ACT(BN_, ST_, MDLC_ACT_RELU)                                                    \
     MDLC_TC_ACT(BN_, ST_, MDLC_ACT_CLIP)                                                    \
     MDLC_TC_ACT(BN_, ST_, MDLC_ACT_GELU)                                                    \
     MDLC_TC_ACT(BN_, ST_, MDLC_ACT_SIGMOID)                                                 \
-    return im2col ? launch_tc<BN_, ST_, 2, -1, 1>(ctx, tmap, tmap_y, tmap_r, tmap_x, a)     \
-                  : launch_tc<BN_, ST_, 2, -1, 0>(ctx, tmap, tmap_y, tmap_r, tmap_x, a);    \
+    MDLC_TC_LAUNCH(BN_, ST_, 2, -1)                                                         \
   }
   MDLC_TC_CASE(64, 8)
   MDLC_TC_CASE(128, 4)
   MDLC_TC_CASE(256, 3)
 #undef MDLC_TC_ACT
+#undef MDLC_TC_LAUNCH
 #undef MDLC_TC_CASE
   return mdlc_set_error(ctx, MDLC_ERR_UNSUPPORTED, "conv_tc: no kernel for bn=%d stages=%d", bn, stages);
 }

@@ -417,6 +417,39 @@ __global__ void __launch_bounds__(256) to_nhwc_kernel(const float* x, int n, int
   }
 }
 
+// NCHW fp32 -> 2x2 space-to-depth NHWC; one thread per (image, output pixel,
+// 8-channel group), output pixel index fastest.
+template <int DT>
+__global__ void __launch_bounds__(256) to_s2d_kernel(const float* x, int c, int h, int w, void* y, int cs,
+                                                     long long total) {
+  const int G = cs >> 3;
+  const int h2 = h >> 1, w2 = w >> 1, hw2 = h2 * w2;
+  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int p = (int)(idx % hw2);
+    const long long t = idx / hw2;
+    const int g = (int)(t % G);
+    const int img = (int)(t / G);
+    const int Y = p / w2, X = p - (p / w2) * w2;
+    float v[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      const int cc = g * 8 + e;
+      v[e] = 0.0f;
+      if (cc < 4 * c) {
+        const int q = cc / c, ci = cc - q * c;
+        const int dy = q >> 1, dx = q & 1;
+        v[e] = __ldg(x + (((long long)img * c + ci) * h + 2 * Y + dy) * w + 2 * X + dx);
+      }
+    }
+    const long long o = ((long long)img * hw2 + p) * cs + g * 8;
+    if constexpr (DT == MDLC_F32)
+      V8<float>::store(static_cast<float*>(y) + o, v);
+    else
+      V8<__nv_bfloat16>::store(static_cast<__nv_bfloat16*>(y) + o, v);
+  }
+}
+
 template <int DT>
 __global__ void __launch_bounds__(256) to_nchw_kernel(const void* x, int n, int c, int hw, int cs, float* y,
                                                       float scale, int zp, long long total) {
@@ -458,6 +491,24 @@ extern "C" int mdlc_nchw_to_nhwc(mdlc_ctx* ctx, const float* x, int n, int c, in
   }
   mdlc_note_launch(ctx);
   return mdlc_cuda_status(ctx, cudaGetLastError(), "nchw_to_nhwc launch");
+}
+
+extern "C" int mdlc_nchw_to_s2d(mdlc_ctx* ctx, const float* x, int n, int c, int h, int w, void* y, int cs,
+                                int dtype) {
+  if (!ctx) return MDLC_ERR_INVALID;
+  if (!x || !y || n <= 0 || c <= 0 || h <= 0 || w <= 0 || (h & 1) || (w & 1) || cs < 4 * c || cs % 8)
+    return mdlc_set_error(ctx, MDLC_ERR_INVALID, "nchw_to_s2d: bad arguments");
+  cudaSetDevice(ctx->device);
+  const long long total = (long long)n * (h / 2) * (w / 2) * (cs / 8);
+  const unsigned grid = grid_for(ctx, total);
+  if (dtype == MDLC_BF16)
+    to_s2d_kernel<MDLC_BF16><<<grid, 256, 0, ctx->stream>>>(x, c, h, w, y, cs, total);
+  else if (dtype == MDLC_F32)
+    to_s2d_kernel<MDLC_F32><<<grid, 256, 0, ctx->stream>>>(x, c, h, w, y, cs, total);
+  else
+    return mdlc_set_error(ctx, MDLC_ERR_UNSUPPORTED, "nchw_to_s2d: dtype %d", dtype);
+  mdlc_note_launch(ctx);
+  return mdlc_cuda_status(ctx, cudaGetLastError(), "nchw_to_s2d launch");
 }
 
 extern "C" int mdlc_nhwc_to_nchw(mdlc_ctx* ctx, const void* x, int n, int c, int h, int w, int cs, int dtype,

@@ -69,6 +69,7 @@ class TensorSpec:
     cs: int
     dtype: int
     alias_of: Optional[str] = None
+    layout: str = "nhwc"   # "s2d2": 2x2 space-to-depth of a graph input (see space_to_depth_stem)
 
     @property
     def nbytes(self) -> int:
@@ -504,5 +505,62 @@ class _Lowerer:
         return sorted(int(a) % rank for a in axes) if axes is not None else None
 
 
-def lower(graph, shapes: dict, dtype: int) -> Lowered:
-    return _Lowerer(graph, shapes, dtype).run()
+def s2d_weights(wt: np.ndarray, pad_t: int, pad_l: int):
+    """Re-index a stride-2 conv's OIHW weights for a 2x2 space-to-depth input.
+
+    With X'[(dy, dx, c), Y, X] = x[c, 2Y + dy, 2X + dx], the tap r of the
+    original kernel reads row 2*oy + r - pad_t = 2*(oy + ty) + dy with
+    ty = floor((r - pad_t) / 2), dy = (r - pad_t) mod 2. The same conv is
+    therefore a stride-1 conv over X' with taps Ty = ty + ceil(pad_t / 2),
+    weight W'[o, (dy*2 + dx)*C + c, Ty, Tx] = w[o, c, r, s] (zero where r or s
+    falls outside the original kernel) and top/left padding ceil(pad / 2).
+    Returns (W', new_pad_t, new_pad_l).
+    """
+    k, c, R, S = wt.shape
+    pt2, pl2 = -(-pad_t // 2), -(-pad_l // 2)
+    R2 = (R - 1 - pad_t) // 2 + pt2 + 1
+    S2 = (S - 1 - pad_l) // 2 + pl2 + 1
+    out = np.zeros((k, 4 * c, R2, S2), np.float32)
+    for r in range(R):
+        ty, dy = divmod(r - pad_t, 2)
+        for s_ in range(S):
+            tx, dx = divmod(s_ - pad_l, 2)
+            out[:, (dy * 2 + dx) * c:(dy * 2 + dx + 1) * c, ty + pt2, tx + pl2] = wt[:, :, r, s_]
+    return out, pt2, pl2
+
+
+def space_to_depth_stem(lo: Lowered) -> None:
+    """Rewrite a stride-2 conv that reads a graph input with <= 4 channels
+    (the stem) as a stride-1 conv over the input's 2x2 space-to-depth form.
+
+    The graph-input conversion kernel writes the space-to-depth layout
+    directly, so the rewrite costs nothing at run time; it shrinks the
+    reduction from R*S*8 to about R*S*16/4 elements and makes every filter tap
+    a contiguous 32-byte run (16 channels) instead of a 16-byte one.
+    """
+    for name in lo.inputs:
+        t = lo.tensors.get(name)
+        if t is None or t.c > 4 or t.h % 2 or t.w % 2 or t.h * t.w == 1:
+            continue
+        readers = [st for st in lo.steps if name in st.inputs]
+        if len(readers) != 1 or readers[0].kind != "conv" or name in lo.outputs:
+            continue
+        st = readers[0]
+        if st.params.get("residual") or st.inputs[0] != name:
+            continue
+        geom, wt, bias = lo.weights[st.params["weight"]]
+        if geom["groups"] != 1 or geom["sh"] != 2 or geom["sw"] != 2 or geom["dh"] != 1 or geom["dw"] != 1:
+            continue
+        w2, pt2, pl2 = s2d_weights(wt, geom["pt"], geom["pl"])
+        g2 = dict(geom, h=geom["h"] // 2, w=geom["w"] // 2, c=4 * geom["c"], cs=16, r=w2.shape[2],
+                  s=w2.shape[3], sh=1, sw=1, pt=pt2, pl=pl2)
+        lo.weights[st.params["weight"]] = (g2, w2, bias)
+        t.layout, t.c, t.h, t.w, t.cs = "s2d2", 4 * t.c, t.h // 2, t.w // 2, 16
+        st.params["s2d"] = True
+
+
+def lower(graph, shapes: dict, dtype: int, s2d: bool = True) -> Lowered:
+    lo = _Lowerer(graph, shapes, dtype).run()
+    if s2d:
+        space_to_depth_stem(lo)
+    return lo

@@ -146,6 +146,9 @@ IM2COL_CASES = [
     (2, 256, 11, 9, 512, 3, 1, 1, 1),
     (2, 64, 23, 23, 64, 3, 1, 2, 2),
     (5, 192, 7, 7, 200, 3, 1, 1, 1),
+    (8, 16, 40, 40, 64, 4, 1, 2, 1),      # c = 16: one 32-byte pixel per load (SW32 A tiles)
+    (8, 16, 30, 30, 96, 1, 1, 0, 1),      # c = 16, 1x1: three padding taps per k-block
+    (6, 32, 33, 31, 128, 3, 2, 1, 1),     # c = 32: 64-byte pixels (SW64 A tiles), stride 2
 ]
 
 
