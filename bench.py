@@ -93,13 +93,20 @@ class ClockSampler:
 
 
 def conv_flops(exe):
-    """Algorithmic FLOPs of each conv step (2*N*OH*OW*K*C/g*R*S) for one shard."""
-    out = []
-    for c in exe.devices[0].calls:
-        if c[0] == "conv":
-            d = c[1]
-            out.append(2.0 * d.n * d.oh * d.ow * d.k * (d.c // d.groups) * d.r * d.s)
-    return out
+    """Algorithmic FLOPs of each conv step (2*N*OH*OW*K*C/g*R*S of the graph node,
+    before any backend rewrite such as the space-to-depth stem) for one shard."""
+    lo = exe.devices[0].lo
+    return [lo.weights[st.params["weight"]][0]["flops"] for st in lo.steps if st.kind == "conv"]
+
+
+def conv_traffic():
+    """DRAM bytes per conv_tc_kernel launch from the committed ncu launch list of
+    this workload (profiles/conv_tc_resnet18_b256_dram.json), or None."""
+    try:
+        with open(os.path.join(ROOT, "profiles", "conv_tc_resnet18_b256_dram.json")) as f:
+            return json.load(f)["dram_bytes_per_launch"]
+    except Exception:
+        return None
 
 
 def timed_steps(exe, steps, per_kernel=False):
@@ -322,7 +329,8 @@ def main() -> int:
             "roofline": {"kernel": "conv_tc_kernel (tcgen05 implicit GEMM)", "bound": "tensor",
                          "achieved": round(achieved_tf, 1),
                          "peak": peak_tf, "unit": "TFLOP/s", "frac": round(achieved_tf / peak_tf, 4),
-                         "peak_kind": f"{peak_kind} bf16 (burst)", "traffic": None,
+                         "peak_kind": f"{peak_kind} bf16 (burst)", "traffic": conv_traffic(),
+                         "traffic_unit": "bytes per launch (ncu dram read+write)",
                          "conv_share_of_step": round(conv_ms / inst_ms, 4) if inst_ms else None,
                          "flops_per_launch": round(conv_flops_step / len(flops)),
                          "avg_launch_ms": round(avg_launch_ms, 5)},

@@ -206,6 +206,8 @@ class _Lowerer:
             wt = wt.reshape(k, kin, 1, 1)
             geom = dict(n=xt.n, h=1, w=1, c=xt.c, k=k, r=1, s=1, sh=1, sw=1, pt=0, pl=0, dh=1, dw=1,
                         oh=1, ow=1, groups=1)
+        geom["flops"] = 2.0 * geom["n"] * geom["oh"] * geom["ow"] * geom["k"] * (geom["c"] // geom["groups"]) \
+            * geom["r"] * geom["s"]   # algorithmic work of the node as written in the graph
         bias = np.zeros(round_up(geom["k"], 8), np.float32)
         if b is not None:
             bias[:geom["k"]] = np.asarray(b, np.float32).reshape(-1)
