@@ -72,7 +72,8 @@ enum {
  *   int8 path : y = clamp(out_zp + requant(acc + bias32[k], rq_mult[k], rq_shift[k])
  *                         + requant(residual - res_zp, res_mult, res_shift), qmin, qmax)
  *               (gemmlowp fixed point; bias is int32 for the int8 path)
- *   int8 path with out_type F32: y = deq_scale[k] * (acc + bias32[k]) + deq_bias[k]  */
+ *   int8 path with out_type F32: y = act(deq_scale[k] * (acc + bias32[k]) + deq_bias[k]
+ *                                       (+ res_scale * (residual - res_zp)))  */
 typedef struct {
   int32_t act;
   float alpha;    /* LeakyRelu slope / HardSigmoid alpha */
@@ -80,11 +81,12 @@ typedef struct {
   float clip_lo;  /* Clip bounds (use +-INFINITY for one-sided) */
   float clip_hi;
   const int32_t* rq_mult;  /* [k] Q31 multipliers (int8 path) */
-  const int32_t* rq_shift; /* [k] right shifts >= 0 (int8 path) */
+  const int32_t* rq_shift; /* [k] shifts: > 0 right after the high multiply, < 0 left before it */
   int32_t out_zp, qmin, qmax;
   int32_t res_zp, res_mult, res_shift;
   const float* deq_scale; /* [k] (int8 path, float output) */
   const float* deq_bias;  /* [k] (int8 path, float output) */
+  float res_scale;        /* residual dequantisation scale (int8 path, float output) */
 } mdlc_epilogue;
 
 /* 2-D convolution over NHWC tensors (groups == 1: implicit GEMM; groups == c
@@ -205,10 +207,12 @@ int mdlc_nchw_to_nhwc(mdlc_ctx* ctx, const float* x, int n, int c, int h, int w,
 int mdlc_nhwc_to_nchw(mdlc_ctx* ctx, const void* x, int n, int c, int h, int w, int cs, int dtype,
                       float* y, float scale, int zp);
 /* NCHW fp32 (h, w even) -> 2x2 space-to-depth NHWC: y[n][Y][X][(dy*2+dx)*c + ci]
- * = x[n][ci][2Y+dy][2X+dx], channel stride cs >= 4c (pad channels zeroed).
+ * = x[n][ci][2Y+dy][2X+dx], channel stride cs >= 4c (pad channels zeroed); 8-bit
+ * dtypes quantise like mdlc_nchw_to_nhwc.
  * Feeds a stride-2 stem conv rewritten as a stride-1 conv (no reference
  * counterpart: a layout choice of this backend). */
-int mdlc_nchw_to_s2d(mdlc_ctx* ctx, const float* x, int n, int c, int h, int w, void* y, int cs, int dtype);
+int mdlc_nchw_to_s2d(mdlc_ctx* ctx, const float* x, int n, int c, int h, int w, void* y, int cs, int dtype,
+                     float inv_scale, int zp);
 
 /* ---- CUDA graph capture of a whole run (b=1 latency) ------------------- */
 int mdlc_graph_begin(mdlc_ctx* ctx);

@@ -42,7 +42,7 @@ class Epilogue(C.Structure):
                 ("rq_mult", C.c_void_p), ("rq_shift", C.c_void_p),
                 ("out_zp", C.c_int32), ("qmin", C.c_int32), ("qmax", C.c_int32),
                 ("res_zp", C.c_int32), ("res_mult", C.c_int32), ("res_shift", C.c_int32),
-                ("deq_scale", C.c_void_p), ("deq_bias", C.c_void_p)]
+                ("deq_scale", C.c_void_p), ("deq_bias", C.c_void_p), ("res_scale", C.c_float)]
 
 
 class ConvDesc(C.Structure):
@@ -102,7 +102,7 @@ SIGNATURES = {
     "mdlc_eltwise": ([_P, C.POINTER(EwProg), C.POINTER(C.c_void_p), C.POINTER(C.c_void_p)], C.c_int),
     "mdlc_nchw_to_nhwc": ([_P, _P, _I, _I, _I, _I, _P, _I, _I, C.c_float, _I], C.c_int),
     "mdlc_nhwc_to_nchw": ([_P, _P, _I, _I, _I, _I, _I, _I, _P, C.c_float, _I], C.c_int),
-    "mdlc_nchw_to_s2d": ([_P, _P, _I, _I, _I, _I, _P, _I, _I], C.c_int),
+    "mdlc_nchw_to_s2d": ([_P, _P, _I, _I, _I, _I, _P, _I, _I, C.c_float, _I], C.c_int),
     "mdlc_graph_begin": ([_P], C.c_int),
     "mdlc_graph_end": ([_P], C.c_int),
     "mdlc_graph_launch": ([_P], C.c_int),
@@ -243,9 +243,9 @@ class Context:
         self.check(self.lib.mdlc_nchw_to_nhwc(self.h, C.c_void_p(x), n, c, h, w, C.c_void_p(y), cs, dtype,
                                               C.c_float(inv_scale), zp), "nchw_to_nhwc")
 
-    def to_s2d(self, x, n, c, h, w, y, cs, dtype) -> None:
-        self.check(self.lib.mdlc_nchw_to_s2d(self.h, C.c_void_p(x), n, c, h, w, C.c_void_p(y), cs, dtype),
-                   "nchw_to_s2d")
+    def to_s2d(self, x, n, c, h, w, y, cs, dtype, inv_scale=1.0, zp=0) -> None:
+        self.check(self.lib.mdlc_nchw_to_s2d(self.h, C.c_void_p(x), n, c, h, w, C.c_void_p(y), cs, dtype,
+                                             C.c_float(inv_scale), zp), "nchw_to_s2d")
 
     def to_nchw(self, x, n, c, h, w, cs, dtype, y, scale=1.0, zp=0) -> None:
         self.check(self.lib.mdlc_nhwc_to_nchw(self.h, C.c_void_p(x), n, c, h, w, cs, dtype, C.c_void_p(y),

@@ -34,7 +34,7 @@ from mdlc_b200 import _lib as L
 from mdlc_b200 import lowering, memory
 from mdlc_b200 import shapes as S
 
-DTYPES = {"bf16": L.BF16, "fp32": L.F32, "f32": L.F32}
+DTYPES = {"bf16": L.BF16, "fp32": L.F32, "f32": L.F32, "int8": L.U8}
 
 
 def _has_static_shapes(graph) -> bool:
@@ -67,16 +67,30 @@ class _Device:
         self.batch = batch
         lo = exe._lowered_for(batch)
         self.lo = lo
-        self.plan = memory.plan_arena(lo.steps, lo.tensors, lo.inputs, lo.outputs)
+        self.plan = memory.plan_arena(lo.steps, lo.tensors, lo.inputs, lo.outputs, reuse=not exe.keep_all)
+        self.q = exe.qplan
         self.arena = self.ctx.alloc(max(self.plan.total_bytes, 256))
         self.addr = {name: self.arena + off for name, off in self.plan.offsets.items()}
         # weights (packed on the host by the library's packer, uploaded once)
         self.wbuf, self.bbuf = {}, {}
+        self.qbuf = {}
         for wname, (geom, wt, bias) in lo.weights.items():
             desc = self._desc(geom, lo)
-            packed = L.pack_weights(desc, wt)
-            self.wbuf[wname] = self.ctx.to_device(packed)
-            self.bbuf[wname] = self.ctx.to_device(bias)
+            if self.q is not None:
+                cq = self.q.convs[wname]
+                ks = desc.k_stride
+                pad = lambda a, dt: np.concatenate([np.asarray(a, dt), np.zeros(ks - len(a), dt)])
+                self.wbuf[wname] = self.ctx.to_device(L.pack_weights(desc, cq.w_q))
+                self.bbuf[wname] = self.ctx.to_device(pad(cq.bias32, np.int32))
+                self.qbuf[wname] = {
+                    "mult": self.ctx.to_device(pad(cq.mult, np.int32)),
+                    "shift": self.ctx.to_device(pad(cq.shift, np.int32)),
+                    "deq_scale": self.ctx.to_device(pad(cq.deq_scale, np.float32)) if cq.deq_scale is not None else 0,
+                    "deq_bias": self.ctx.to_device(pad(cq.deq_bias, np.float32)) if cq.deq_bias is not None else 0}
+            else:
+                packed = L.pack_weights(desc, wt)
+                self.wbuf[wname] = self.ctx.to_device(packed)
+                self.bbuf[wname] = self.ctx.to_device(bias)
         self.cbuf = {name: self.ctx.to_device(arr) for name, arr in lo.consts.items()}
         # staging: fp32 NCHW feeds / outputs on device and pinned on the host
         self.in_dev, self.in_host, self.out_dev, self.out_host = {}, {}, {}, {}
@@ -98,8 +112,10 @@ class _Device:
 
     def _desc(self, geom, lo):
         k = geom["k"]
+        a8 = 16 if lo.dtype in (L.U8, L.S8) else 8
         return L.ConvDesc(n=geom["n"], h=geom["h"], w=geom["w"], c=geom["c"],
-                          c_stride=geom.get("cs", lowering.round_up(geom["c"], 8)), k=k, k_stride=lowering.round_up(k, 8),
+                          c_stride=geom.get("cs", lowering.round_up(geom["c"], a8)), k=k,
+                          k_stride=lowering.round_up(k, a8),
                           r=geom["r"], s=geom["s"], stride_h=geom["sh"], stride_w=geom["sw"],
                           pad_t=geom["pt"], pad_l=geom["pl"], dil_h=geom["dh"], dil_w=geom["dw"],
                           oh=geom["oh"], ow=geom["ow"], groups=geom["groups"], in_type=lo.dtype,
@@ -121,6 +137,22 @@ class _Device:
                                  clip_hi=np.inf if a.get("clip_max") is None else float(a["clip_max"]))
                 if act == "HardSigmoid":
                     epi.alpha = float(a.get("alpha", 0.2))
+                if self.q is not None:
+                    cq = self.q.convs[st.params["weight"]]
+                    qb = self.qbuf[st.params["weight"]]
+                    s_x, zp_x = self.q.tensors[self._store(st.inputs[0])]
+                    d.in_zp = zp_x
+                    if yt.dtype != L.F32:
+                        epi.act = L.ACT_NONE     # the activation is the integer clamp
+                    epi.rq_mult, epi.rq_shift = qb["mult"], qb["shift"]
+                    epi.deq_scale, epi.deq_bias = qb["deq_scale"] or None, qb["deq_bias"] or None
+                    if cq.residual:
+                        epi.res_zp = self.q.tensors[self._store(cq.residual)][1]
+                        epi.res_mult, epi.res_shift = cq.res_mult, cq.res_shift
+                        epi.res_scale = cq.res_scale
+                    if yt.dtype != L.F32:
+                        epi.out_zp = self.q.tensors[st.outputs[0]][1]
+                        epi.qmin, epi.qmax = cq.qmin, cq.qmax
                 cfg = None
                 if self.exe.tuner is not None:
                     choice = self.exe.tuner("conv", dict(geom, dtype=lo.dtype))
@@ -138,6 +170,8 @@ class _Device:
                                stride_w=p.get("sw", 1), pad_t=p.get("pt", 0), pad_l=p.get("pl", 0),
                                oh=p.get("oh", 1), ow=p.get("ow", 1), count_include_pad=p.get("cip", 0),
                                dtype=xt.dtype)
+                if self.q is not None and p["kind"] == 2:
+                    d.rq_mult, d.rq_shift, d.in_zp, d.out_zp = self.q.gap[st.outputs[0]]
                 calls.append(("pool", d, self.ptr(st.inputs[0]), self.ptr(st.outputs[0])))
             else:
                 yt = lo.tensors[st.outputs[0]]
@@ -167,20 +201,45 @@ class _Device:
             else:
                 ctx.eltwise(c[1], c[2], c[3])
 
+    def _store(self, name):
+        return memory.storage_of(self.lo.tensors, name)
+
     def issue_inputs(self):
         for name in self.lo.inputs:
             t = self.lo.tensors[name]
+            inv, zp = 1.0, 0
+            if self.q is not None:
+                s_x, zp = self.q.tensors[name]
+                inv = float(np.float32(1.0) / np.float32(s_x))
             if t.layout == "s2d2":
                 n, c, h, w = self.lo.shapes[name]
-                self.ctx.to_s2d(self.in_dev[name], n, c, h, w, self.ptr(name), t.cs, t.dtype)
+                self.ctx.to_s2d(self.in_dev[name], n, c, h, w, self.ptr(name), t.cs, t.dtype, inv, zp)
             else:
-                self.ctx.to_nhwc(self.in_dev[name], t.n, t.c, t.h, t.w, self.ptr(name), t.cs, t.dtype)
+                self.ctx.to_nhwc(self.in_dev[name], t.n, t.c, t.h, t.w, self.ptr(name), t.cs, t.dtype, inv, zp)
 
     def issue_outputs(self):
         for name in self.lo.outputs:
             t = self.lo.tensors[name]
             if self.out_dev[name] is not None:
-                self.ctx.to_nchw(self.ptr(name), t.n, t.c, t.h, t.w, t.cs, t.dtype, self.out_dev[name])
+                scale, zp = (1.0, 0) if self.q is None or t.dtype == L.F32 else self.q.tensors[self._store(name)]
+                self.ctx.to_nchw(self.ptr(name), t.n, t.c, t.h, t.w, t.cs, t.dtype, self.out_dev[name],
+                                 float(scale), zp)
+
+    def read_tensors(self):
+        """Every stored activation as an NCHW array (a keep_all executable keeps
+        each one in its own buffer): float32 values of fp32 executables, the
+        uint8 codes (or fp32 logits) of int8 ones."""
+        if self.lo.dtype not in (L.F32, L.U8):
+            raise ValueError("read_tensors: fp32 and int8 executables only")
+        self.ctx.sync()
+        out = {}
+        for name, t in self.lo.tensors.items():
+            if t.alias_of or name not in self.addr or t.layout != "nhwc":
+                continue
+            npdt = np.float32 if t.dtype == L.F32 else np.uint8
+            a = self.ctx.download(self.addr[name], (t.n, t.h, t.w, t.cs), npdt)[..., :t.c]
+            out[name] = a.transpose(0, 3, 1, 2).reshape(self.lo.shapes[name])
+        return out
 
     def out_src(self, name):
         return self.out_dev[name] if self.out_dev[name] is not None else self.ptr(name)
@@ -251,10 +310,14 @@ class _Device:
 class Executable:
     """A compiled graph bound to one or more B200s."""
 
-    def __init__(self, graph, *, dtype="bf16", batch=None, devices=1, tuner=None, mem_plan=None):
+    def __init__(self, graph, *, dtype="bf16", batch=None, devices=1, tuner=None, mem_plan=None,
+                 keep_all=False, calib=None):
         if dtype not in DTYPES:
             raise ValueError(f"dtype must be one of {sorted(DTYPES)}")
         self.graph = graph
+        self.keep_all = keep_all
+        self.qplan = None
+        self.calib = calib
         self.dtype_name = dtype
         self.dtype = DTYPES[dtype]
         self.tuner = tuner
@@ -277,6 +340,15 @@ class Executable:
         self.shard = self.batch // ndev
         self._lowered = {}
         self.lowered = self._lowered_for(self.shard)   # validates the graph (raises on gaps)
+        if self.dtype == L.U8:
+            from mdlc_b200 import quant
+            ranges = calib
+            if ranges is None or isinstance(ranges, list):
+                batches = ranges if ranges is not None else quant.calibration_batches(graph)
+                ranges = quant.calibrate(graph, batches, device=devs[0])
+            self.ranges = ranges
+            lo_orig = lowering.lower(graph, S.infer(graph, self.shard), L.U8, s2d=False)
+            self.qplan = quant.build_plan(lo_orig, self.lowered, ranges, graph)
         self.devices = [_Device(self, d, self.shard) for d in devs]
 
     def _lowered_for(self, batch):
@@ -347,6 +419,12 @@ class Executable:
         for d in self.devices:
             d.ctx.sync()
 
+    def read_tensors(self, device: int = 0) -> dict:
+        """Every stored activation of one device's last forward (``keep_all`` executables)."""
+        if not self.keep_all:
+            raise ValueError("read_tensors needs an executable compiled with keep_all=True")
+        return self.devices[device].read_tensors()
+
     def time_ms(self, iters: int = 50, warmup: int = 10, use_graph: bool = False) -> float:
         """Device time per forward (CUDA events on each device's stream; max over devices)."""
         for _ in range(warmup):
@@ -394,7 +472,12 @@ class Executable:
 
 
 def compile(graph, *, mem_plan=None, dtype: str = "bf16", batch=None, devices=1, tuner=None,
-            schedule_fn=None) -> Executable:
-    """Compile a post-pass Graph IR for B200 execution (see module docstring)."""
+            schedule_fn=None, calib=None) -> Executable:
+    """Compile a post-pass Graph IR for B200 execution (see module docstring).
+
+    ``dtype="int8"`` quantises the graph (:mod:`mdlc_b200.quant`): ``calib`` is
+    either a dict of per-tensor (min, max) ranges, a list of feed dicts to
+    calibrate on, or None for 32 seeded N(0, 1) batches of 4 images.
+    """
     return Executable(graph, dtype=dtype, batch=batch, devices=devices, tuner=tuner or schedule_fn,
-                      mem_plan=mem_plan)
+                      mem_plan=mem_plan, calib=calib)

@@ -291,7 +291,14 @@ MDLC_DEV int32_t rounding_rshift(int32_t x, int shift) {
   const int32_t threshold = (mask >> 1) + (x < 0 ? 1 : 0);
   return (x >> shift) + (rem > threshold ? 1 : 0);
 }
+// MultiplyByQuantizedMultiplier: shift > 0 right-shifts after the high
+// multiply; shift < 0 left-shifts the input first (saturated to int32).
 MDLC_DEV int32_t requant(int32_t acc, int32_t mult, int32_t shift) {
+  if (shift < 0) {
+    long long v = (long long)acc << (-shift);
+    v = v > INT32_MAX ? INT32_MAX : (v < INT32_MIN ? INT32_MIN : v);
+    return sat_rdh_mul((int32_t)v, mult);
+  }
   return rounding_rshift(sat_rdh_mul(acc, mult), shift);
 }
 

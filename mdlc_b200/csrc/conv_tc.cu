@@ -60,6 +60,7 @@ struct TcArgs {
   int out_zp, qmin, qmax, res_zp, res_mult, res_shift;
   const float* deq_scale;
   const float* deq_bias;
+  float res_scale;
   unsigned long long wait_cycles;
   int tma_epi;  // bf16 output staged in shared memory and written by TMA stores
 };
@@ -158,6 +159,12 @@ MDLC_DEV void store_chunk16(const TcArgs& a, int m, int nb0, const uint32_t (&v)
           const int32_t acc = (int32_t)v[e] + (bias32 ? bias32[ch] : 0);
           val = __fmul_rn((float)acc, a.deq_scale[ch]);
           if (a.deq_bias) val = __fadd_rn(val, a.deq_bias[ch]);
+          if (a.res) {
+            const int32_t rq = a.a_signed ? (int32_t)(int8_t)a.res[(long long)m * a.res_s + ch]
+                                          : (int32_t)a.res[(long long)m * a.res_s + ch];
+            val = __fadd_rn(val, __fmul_rn((float)(rq - a.res_zp), a.res_scale));
+          }
+          val = apply_act(val, a.act);
         }
         static_cast<float*>(a.y)[row + ch] = val;
       }
@@ -453,7 +460,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             tma_load_im2col_4d(sA + st * kABytes, &tmap_x, c0, xw, xh, xn, (uint16_t)((tap - rr * a.s) * a.dw),
                                (uint16_t)(rr * a.dh), fullA(st));
           } else if (AMODE >= 2) {
-            // AMODE 2: cs == 16 (4 taps per k-block, 32-byte rows); AMODE 3: cs == 32 (2 taps, 64-byte rows)
+            // AMODE 2: 32-byte pixels (bf16 cs 16 / int8 cs 32), 4 taps per k-block;
+            // AMODE 3: 64-byte pixels (bf16 cs 32 / int8 cs 64), 2 taps per k-block
             constexpr int TPB = AMODE == 2 ? 4 : 2;
             constexpr uint32_t kTapBytes = kABytes / TPB;
             mbar_arrive_expect_tx(fullA(st), kABytes);
@@ -581,12 +589,13 @@ int encode_im2col(CUtensorMap* m, const mdlc_conv_desc& d, const void* x, int es
   // mode 1: 128-byte channel blocks; modes 2/3: the whole pixel (bf16 cs 16 / 32) per load
   int mode = 0, cpp = kb_elems;
   CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_128B;
+  const int pixel_bytes = d.c_stride * esz;
   if (d.c_stride % kb_elems == 0) {
     mode = 1;
-  } else if (esz == 2 && d.c_stride == 16) {
-    mode = 2, cpp = 16, sw = CU_TENSOR_MAP_SWIZZLE_32B;
-  } else if (esz == 2 && d.c_stride == 32) {
-    mode = 3, cpp = 32, sw = CU_TENSOR_MAP_SWIZZLE_64B;
+  } else if (pixel_bytes == 32) {
+    mode = 2, cpp = d.c_stride, sw = CU_TENSOR_MAP_SWIZZLE_32B;
+  } else if (pixel_bytes == 64) {
+    mode = 3, cpp = d.c_stride, sw = CU_TENSOR_MAP_SWIZZLE_64B;
   } else {
     return 0;
   }
@@ -693,7 +702,7 @@ int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w
     a.rq_mult = epi->rq_mult; a.rq_shift = epi->rq_shift;
     a.out_zp = epi->out_zp; a.qmin = epi->qmin; a.qmax = epi->qmax;
     a.res_zp = epi->res_zp; a.res_mult = epi->res_mult; a.res_shift = epi->res_shift;
-    a.deq_scale = epi->deq_scale; a.deq_bias = epi->deq_bias;
+    a.deq_scale = epi->deq_scale; a.deq_bias = epi->deq_bias; a.res_scale = epi->res_scale;
   }
   if (int8) a.pad_src = ctx->d_pad + 16 * (d.in_zp & 0xFF);
 
@@ -740,10 +749,7 @@ int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w
   if (act_t == A_) { MDLC_TC_LAUNCH(BN_, ST_, 2, A_) }
 #define MDLC_TC_CASE(BN_, ST_)                                                               \
   if (bn == BN_ && stages == ST_) {                                                         \
-    if (int8) {                                                                             \
-      if (im2col == 1) return launch_tc<BN_, ST_, 1, -1, 1>(ctx, tmap, tmap_y, tmap_r, tmap_x, a); \
-      return launch_tc<BN_, ST_, 1, -1, 0>(ctx, tmap, tmap_y, tmap_r, tmap_x, a);           \
-    }                                                                                       \
+    if (int8) { MDLC_TC_LAUNCH(BN_, ST_, 1, -1) }                                           \
     MDLC_TC_ACT(BN_, ST_, MDLC_ACT_NONE)                                                    \
     MDLC_TC_ACT(BN_, ST_, MDLC_ACT_RELU)                                                    \
     MDLC_TC_ACT(BN_, ST_, MDLC_ACT_CLIP)                                                    \

@@ -421,7 +421,7 @@ __global__ void __launch_bounds__(256) to_nhwc_kernel(const float* x, int n, int
 // 8-channel group), output pixel index fastest.
 template <int DT>
 __global__ void __launch_bounds__(256) to_s2d_kernel(const float* x, int c, int h, int w, void* y, int cs,
-                                                     long long total) {
+                                                     float inv_scale, int zp, long long total) {
   const int G = cs >> 3;
   const int h2 = h >> 1, w2 = w >> 1, hw2 = h2 * w2;
   for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
@@ -443,10 +443,24 @@ __global__ void __launch_bounds__(256) to_s2d_kernel(const float* x, int c, int 
       }
     }
     const long long o = ((long long)img * hw2 + p) * cs + g * 8;
-    if constexpr (DT == MDLC_F32)
+    if constexpr (DT == MDLC_F32) {
       V8<float>::store(static_cast<float*>(y) + o, v);
-    else
+    } else if constexpr (DT == MDLC_BF16) {
       V8<__nv_bfloat16>::store(static_cast<__nv_bfloat16*>(y) + o, v);
+    } else {
+      uint32_t lo = 0, hi = 0;
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        int q = 0;
+        if (g * 8 + e < 4 * c) {
+          q = __float2int_rn(__fmul_rn(v[e], inv_scale)) + zp;
+          q = DT == MDLC_S8 ? min(max(q, -128), 127) : min(max(q, 0), 255);
+        }
+        const uint32_t b = (uint32_t)(q & 0xFF) << (8 * (e & 3));
+        if (e < 4) lo |= b; else hi |= b;
+      }
+      *reinterpret_cast<uint2*>(static_cast<uint8_t*>(y) + o) = make_uint2(lo, hi);
+    }
   }
 }
 
@@ -494,19 +508,21 @@ extern "C" int mdlc_nchw_to_nhwc(mdlc_ctx* ctx, const float* x, int n, int c, in
 }
 
 extern "C" int mdlc_nchw_to_s2d(mdlc_ctx* ctx, const float* x, int n, int c, int h, int w, void* y, int cs,
-                                int dtype) {
+                                int dtype, float inv_scale, int zp) {
   if (!ctx) return MDLC_ERR_INVALID;
-  if (!x || !y || n <= 0 || c <= 0 || h <= 0 || w <= 0 || (h & 1) || (w & 1) || cs < 4 * c || cs % 8)
+  const int align = (dtype == MDLC_U8 || dtype == MDLC_S8) ? 16 : 8;
+  if (!x || !y || n <= 0 || c <= 0 || h <= 0 || w <= 0 || (h & 1) || (w & 1) || cs < 4 * c || cs % align)
     return mdlc_set_error(ctx, MDLC_ERR_INVALID, "nchw_to_s2d: bad arguments");
   cudaSetDevice(ctx->device);
   const long long total = (long long)n * (h / 2) * (w / 2) * (cs / 8);
   const unsigned grid = grid_for(ctx, total);
-  if (dtype == MDLC_BF16)
-    to_s2d_kernel<MDLC_BF16><<<grid, 256, 0, ctx->stream>>>(x, c, h, w, y, cs, total);
-  else if (dtype == MDLC_F32)
-    to_s2d_kernel<MDLC_F32><<<grid, 256, 0, ctx->stream>>>(x, c, h, w, y, cs, total);
-  else
-    return mdlc_set_error(ctx, MDLC_ERR_UNSUPPORTED, "nchw_to_s2d: dtype %d", dtype);
+  switch (dtype) {
+    case MDLC_BF16: to_s2d_kernel<MDLC_BF16><<<grid, 256, 0, ctx->stream>>>(x, c, h, w, y, cs, inv_scale, zp, total); break;
+    case MDLC_F32: to_s2d_kernel<MDLC_F32><<<grid, 256, 0, ctx->stream>>>(x, c, h, w, y, cs, inv_scale, zp, total); break;
+    case MDLC_U8: to_s2d_kernel<MDLC_U8><<<grid, 256, 0, ctx->stream>>>(x, c, h, w, y, cs, inv_scale, zp, total); break;
+    case MDLC_S8: to_s2d_kernel<MDLC_S8><<<grid, 256, 0, ctx->stream>>>(x, c, h, w, y, cs, inv_scale, zp, total); break;
+    default: return mdlc_set_error(ctx, MDLC_ERR_UNSUPPORTED, "nchw_to_s2d: dtype %d", dtype);
+  }
   mdlc_note_launch(ctx);
   return mdlc_cuda_status(ctx, cudaGetLastError(), "nchw_to_s2d launch");
 }

@@ -145,7 +145,7 @@ class _Lowerer:
             n, c, h, w = shp[0], shp[1], shp[2], 1
         else:
             raise LoweringError(f"tensor {name!r} of rank {len(shp)} is not supported")
-        t = TensorSpec(name, shp, n, c, h, w, round_up(c, 8), self.dtype)
+        t = TensorSpec(name, shp, n, c, h, w, round_up(c, 16 if self.dtype in (L.U8, L.S8) else 8), self.dtype)
         self.tensors[name] = t
         return t
 
@@ -208,7 +208,7 @@ class _Lowerer:
                         oh=1, ow=1, groups=1)
         geom["flops"] = 2.0 * geom["n"] * geom["oh"] * geom["ow"] * geom["k"] * (geom["c"] // geom["groups"]) \
             * geom["r"] * geom["s"]   # algorithmic work of the node as written in the graph
-        bias = np.zeros(round_up(geom["k"], 8), np.float32)
+        bias = np.zeros(round_up(geom["k"], 16), np.float32)
         if b is not None:
             bias[:geom["k"]] = np.asarray(b, np.float32).reshape(-1)
         wname = f"{node.name or node.outputs[0]}.w"
@@ -555,7 +555,7 @@ def space_to_depth_stem(lo: Lowered) -> None:
             continue
         w2, pt2, pl2 = s2d_weights(wt, geom["pt"], geom["pl"])
         g2 = dict(geom, h=geom["h"] // 2, w=geom["w"] // 2, c=4 * geom["c"], cs=16, r=w2.shape[2],
-                  s=w2.shape[3], sh=1, sw=1, pt=pt2, pl=pl2)
+                  s=w2.shape[3], sh=1, sw=1, pt=pt2, pl=pl2, pt_orig=geom["pt"], pl_orig=geom["pl"])
         lo.weights[st.params["weight"]] = (g2, w2, bias)
         t.layout, t.c, t.h, t.w, t.cs = "s2d2", 4 * t.c, t.h // 2, t.w // 2, 16
         st.params["s2d"] = True

@@ -52,7 +52,9 @@ def storage_of(tensors: dict, name: str) -> str:
     return t.alias_of or name
 
 
-def plan_arena(steps, tensors, inputs, outputs) -> ArenaPlan:
+def plan_arena(steps, tensors, inputs, outputs, reuse: bool = True) -> ArenaPlan:
+    """Best-fit liveness plan; ``reuse=False`` gives every tensor its own buffer
+    (calibration executables read every activation after the run)."""
     out_store = {storage_of(tensors, o) for o in outputs}
     last_use = {}
     for k, st in enumerate(steps):
@@ -85,6 +87,8 @@ def plan_arena(steps, tensors, inputs, outputs) -> ArenaPlan:
         return best
 
     def release(names, k):
+        if not reuse:
+            return
         for e in names:
             if e in out_store or e not in assign:
                 continue
