@@ -43,7 +43,14 @@ sys.path.insert(0, ROOT)
 
 METRIC = "ResNet-18 images/s (b=256, 1/2/4/8 B200)"
 WORKLOAD = "resnet18_bf16_b256"
-GFLOP_PER_IMAGE = 3.628  # conv + FC, 1.8141 GMAC per 224x224 image
+# other configurations measured with the same harness (``--workload``); the
+# default line is the headline metric above
+WORKLOADS = {
+    "resnet18_bf16_b256": ("resnet18", "bf16", 256),
+    "resnet18_int8_b1024": ("resnet18", "int8", 1024),
+    "resnet18_fp32_b256": ("resnet18", "fp32", 256),
+    "mobilenetv2_bf16_b256": ("mobilenetv2", "bf16", 256),
+}
 
 
 def _peaks():
@@ -150,6 +157,46 @@ def timed_steps(exe, steps, per_kernel=False):
     return total, inst, conv_ms, len(conv_slots)
 
 
+def g1_graph(model):
+    from mdlc_b200 import builders, passes
+    return passes.default_pipeline(builders.BUILDERS[model](batch=1, seed=0))
+
+
+def b1_latency(g, dtype, device, iters, calib=None):
+    """b=1 forward latency (CUDA graph): p50/p99 of per-forward CUDA-event times
+    with the input resident, and p50 of the host wall time of the public
+    ``run_pinned`` call (pinned H2D of the image, forward, D2H of the logits)."""
+    from mdlc_b200.compiler import compile as mdlc_compile
+    exe = mdlc_compile(g, dtype=dtype, batch=1, devices=[device], calib=calib)
+    try:
+        dev = exe.devices[0]
+        ctx = dev.ctx
+        exe.pinned_inputs()["input"][...] = np.random.default_rng(7).standard_normal(
+            (1, 3, 224, 224), dtype=np.float32)
+        for _ in range(20):
+            exe.run_pinned(use_graph=True)
+        dev_ms, wall_ms = [], []
+        for i in range(iters):
+            ctx.event_record(3000)
+            dev.forward(True)
+            ctx.event_record(3001)
+            ctx.sync()
+            dev_ms.append(ctx.event_elapsed(3000, 3001))
+        for i in range(iters):
+            t0 = time.perf_counter()
+            exe.run_pinned(use_graph=True)
+            wall_ms.append(1e3 * (time.perf_counter() - t0))
+        dev_ms.sort()
+        return {"p50_ms": round(statistics.median(dev_ms), 4),
+                "p99_ms": round(dev_ms[min(len(dev_ms) - 1, int(0.99 * len(dev_ms)))], 4),
+                "p50_e2e_ms": round(statistics.median(wall_ms), 4), "iters": iters,
+                "how": "CUDA graph of the whole forward; device p50/p99 from CUDA events around each "
+                       "replay (input resident); e2e = host wall time of run_pinned (H2D 602112 B, "
+                       "forward, D2H of the logits, sync)"}
+    finally:
+        exe.close()
+
+
 def cpu_baseline_sample(images=8, seed=0):
     """Oracle (reference algorithm) b=1 forwards on the host; returns (img/s, seconds)."""
     from mdlc_b200 import builders, passes
@@ -222,6 +269,8 @@ def main() -> int:
     ap.add_argument("--batch", type=int, default=256, help="images per GPU")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-sample", type=int, default=12, help="b=1 oracle forwards for cpu_baseline")
+    ap.add_argument("--workload", default=WORKLOAD, choices=sorted(WORKLOADS))
+    ap.add_argument("--latency-iters", type=int, default=200, help="b=1 forwards for the p50 latency")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
@@ -246,8 +295,11 @@ def main() -> int:
     from mdlc_b200 import builders, passes
     from mdlc_b200.compiler import compile as mdlc_compile
 
-    g = passes.default_pipeline(builders.resnet18(batch=args.batch, seed=0))
-    exe = mdlc_compile(g, dtype="bf16", devices=[local])
+    model, dtype, default_batch = WORKLOADS[args.workload]
+    if args.workload != WORKLOAD and args.batch == 256:
+        args.batch = default_batch
+    g = passes.default_pipeline(builders.BUILDERS[model](batch=args.batch, seed=0))
+    exe = mdlc_compile(g, dtype=dtype, devices=[local])
     dev = exe.devices[0]
     ins, outs = exe.pinned_inputs(), exe.pinned_outputs()
     rng = np.random.default_rng(1234 + rank)
@@ -303,39 +355,49 @@ def main() -> int:
     logits = outs["logits"]
     assert np.isfinite(logits).all()
 
+    latency = None
+    if rank == 0 and args.latency_iters > 0:
+        latency = b1_latency(g1_graph(model), dtype, local, args.latency_iters,
+                             calib=getattr(exe, "ranges", None))
+
     if rank == 0:
         peak_tf, _, peak_kind = _peaks()
+        if dtype == "int8":
+            peak_tf, peak_kind = 2 * peak_tf, f"2x {peak_kind}"     # int8 dense rate = 2x bf16
         conv_flops_step = sum(flops)
         avg_launch_ms = conv_ms / nconv
         achieved_tf = (conv_flops_step / len(flops)) / (avg_launch_ms / 1e3) / 1e12
         cpu = None
-        if world == 1 and args.cpu_sample > 0:
+        if world == 1 and args.cpu_sample > 0 and model == "resnet18":
             ips, dt = cpu_baseline_sample(args.cpu_sample)
             cpu = {"value": round(ips, 4), "unit": "images/s", "cores": 1, "kind": "port",
                    "sample": f"{args.cpu_sample} ResNet-18 b=1 forwards ({dt:.1f} s), NumPy oracle "
                              "(reference algorithm: im2col + single-threaded einsum)"}
         in_bytes = int(np.prod(g.value_info["input"].shape)) * 4
         line = {
-            "metric": METRIC, "value": round(value, 1), "unit": "images/s", "n_gpus": world,
+            "metric": METRIC if args.workload == WORKLOAD else f"{model} {dtype} images/s",
+            "value": round(value, 1), "unit": "images/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": {"bf16": "bf16", "fp32": "f32", "int8": "u8 x s8 -> s32"}[dtype],
             "data": "synthetic (N(0,1) 3x224x224 images, random Kaiming weights)",
-            "config": {"workload": WORKLOAD, "model": "resnet18", "per_gpu_batch": args.batch,
+            "config": {"workload": args.workload, "model": model, "per_gpu_batch": args.batch,
                        "global_batch": args.batch * world, "image": 224, "parallelism": f"dp{world}",
                        "l2": "working set > 126 MB L2 (input 154 MB fp32 + activations), no flush needed"},
             "e2e": {"value": round(e2e_value, 1), "unit": "images/s", "h2d_bytes_per_step": in_bytes,
                     "d2h_bytes_per_step": int(np.prod(logits.shape)) * 4,
                     "wall_s": round(e2e_wall, 4)},
+            "latency_b1": latency,
             "roofline": {"kernel": "conv_tc_kernel (tcgen05 implicit GEMM)", "bound": "tensor",
                          "achieved": round(achieved_tf, 1),
                          "peak": peak_tf, "unit": "TFLOP/s", "frac": round(achieved_tf / peak_tf, 4),
-                         "peak_kind": f"{peak_kind} bf16 (burst)", "traffic": conv_traffic(),
+                         "peak_kind": f"{peak_kind} bf16 (burst)", "traffic": conv_traffic() if args.workload == WORKLOAD else None,
                          "traffic_unit": "bytes per launch (ncu dram read+write)",
                          "conv_share_of_step": round(conv_ms / inst_ms, 4) if inst_ms else None,
                          "flops_per_launch": round(conv_flops_step / len(flops)),
                          "avg_launch_ms": round(avg_launch_ms, 5)},
             "gpu_launches": launches,
-            "network_tflops": round(world * args.batch * GFLOP_PER_IMAGE / (ms_per_step / 1e3) / 1e3, 1),
+            "network_tflops": round(world * conv_flops_step / (ms_per_step / 1e3) / 1e12, 1),
         }
         if clocks:
             line["clocks"] = clocks

@@ -69,9 +69,10 @@ enum {
 
 /* Fused epilogue applied to every conv / GEMM output element:
  *   float path: y = act(acc + bias[k] (+ residual))
- *   int8 path : y = clamp(out_zp + requant(acc + bias32[k], rq_mult[k], rq_shift[k])
- *                         + requant(residual - res_zp, res_mult, res_shift), qmin, qmax)
- *               (gemmlowp fixed point; bias is int32 for the int8 path)
+ *   int8 path : y = out_zp + clamp(rint(f), qmin - out_zp, qmax - out_zp) with
+ *               f = fp32(acc + bias32[k]) * rq_scale[k] (+ fp32(residual - res_zp) * res_scale),
+ *               every product and sum one IEEE fp32 rounding (no fused multiply-add),
+ *               rint = round half to even; bias is int32 for the int8 path
  *   int8 path with out_type F32: y = act(deq_scale[k] * (acc + bias32[k]) + deq_bias[k]
  *                                       (+ res_scale * (residual - res_zp)))  */
 typedef struct {
@@ -80,13 +81,13 @@ typedef struct {
   float beta;     /* HardSigmoid beta */
   float clip_lo;  /* Clip bounds (use +-INFINITY for one-sided) */
   float clip_hi;
-  const int32_t* rq_mult;  /* [k] Q31 multipliers (int8 path) */
-  const int32_t* rq_shift; /* [k] shifts: > 0 right after the high multiply, < 0 left before it */
+  const float* rq_scale;  /* [k] requantisation scales s_x * s_w[k] / s_y (int8 path, 8-bit output) */
   int32_t out_zp, qmin, qmax;
-  int32_t res_zp, res_mult, res_shift;
+  int32_t res_zp;
+  float res_scale;        /* residual scale: s_res / s_y (8-bit output) or s_res (float output) */
+  int32_t res_signed;     /* int8 path: residual codes are signed int8 (else uint8) */
   const float* deq_scale; /* [k] (int8 path, float output) */
   const float* deq_bias;  /* [k] (int8 path, float output) */
-  float res_scale;        /* residual dequantisation scale (int8 path, float output) */
 } mdlc_epilogue;
 
 /* 2-D convolution over NHWC tensors (groups == 1: implicit GEMM; groups == c

@@ -39,10 +39,10 @@ class MdlcError(RuntimeError):
 class Epilogue(C.Structure):
     _fields_ = [("act", C.c_int32), ("alpha", C.c_float), ("beta", C.c_float),
                 ("clip_lo", C.c_float), ("clip_hi", C.c_float),
-                ("rq_mult", C.c_void_p), ("rq_shift", C.c_void_p),
+                ("rq_scale", C.c_void_p),
                 ("out_zp", C.c_int32), ("qmin", C.c_int32), ("qmax", C.c_int32),
-                ("res_zp", C.c_int32), ("res_mult", C.c_int32), ("res_shift", C.c_int32),
-                ("deq_scale", C.c_void_p), ("deq_bias", C.c_void_p), ("res_scale", C.c_float)]
+                ("res_zp", C.c_int32), ("res_scale", C.c_float), ("res_signed", C.c_int32),
+                ("deq_scale", C.c_void_p), ("deq_bias", C.c_void_p)]
 
 
 class ConvDesc(C.Structure):

@@ -83,8 +83,7 @@ class _Device:
                 self.wbuf[wname] = self.ctx.to_device(L.pack_weights(desc, cq.w_q))
                 self.bbuf[wname] = self.ctx.to_device(pad(cq.bias32, np.int32))
                 self.qbuf[wname] = {
-                    "mult": self.ctx.to_device(pad(cq.mult, np.int32)),
-                    "shift": self.ctx.to_device(pad(cq.shift, np.int32)),
+                    "scale": self.ctx.to_device(pad(cq.rq_scale, np.float32)),
                     "deq_scale": self.ctx.to_device(pad(cq.deq_scale, np.float32)) if cq.deq_scale is not None else 0,
                     "deq_bias": self.ctx.to_device(pad(cq.deq_bias, np.float32)) if cq.deq_bias is not None else 0}
             else:
@@ -128,6 +127,7 @@ class _Device:
                 geom, _, _ = lo.weights[st.params["weight"]]
                 d = self._desc(geom, lo)
                 yt = lo.tensors[st.outputs[0]]
+                d.in_type = lo.tensors[st.inputs[0]].dtype   # int8 graphs: signed network input
                 d.out_type = yt.dtype
                 a = st.params["attrs"]
                 act = st.params["act"]
@@ -144,12 +144,12 @@ class _Device:
                     d.in_zp = zp_x
                     if yt.dtype != L.F32:
                         epi.act = L.ACT_NONE     # the activation is the integer clamp
-                    epi.rq_mult, epi.rq_shift = qb["mult"], qb["shift"]
+                    epi.rq_scale = qb["scale"]
                     epi.deq_scale, epi.deq_bias = qb["deq_scale"] or None, qb["deq_bias"] or None
                     if cq.residual:
                         epi.res_zp = self.q.tensors[self._store(cq.residual)][1]
-                        epi.res_mult, epi.res_shift = cq.res_mult, cq.res_shift
                         epi.res_scale = cq.res_scale
+                        epi.res_signed = int(lo.tensors[cq.residual].dtype == L.S8)
                     if yt.dtype != L.F32:
                         epi.out_zp = self.q.tensors[st.outputs[0]][1]
                         epi.qmin, epi.qmax = cq.qmin, cq.qmax
@@ -228,7 +228,7 @@ class _Device:
     def read_tensors(self):
         """Every stored activation as an NCHW array (a keep_all executable keeps
         each one in its own buffer): float32 values of fp32 executables, the
-        uint8 codes (or fp32 logits) of int8 ones."""
+        8-bit codes (or fp32 logits) of int8 ones."""
         if self.lo.dtype not in (L.F32, L.U8):
             raise ValueError("read_tensors: fp32 and int8 executables only")
         self.ctx.sync()
@@ -236,7 +236,7 @@ class _Device:
         for name, t in self.lo.tensors.items():
             if t.alias_of or name not in self.addr or t.layout != "nhwc":
                 continue
-            npdt = np.float32 if t.dtype == L.F32 else np.uint8
+            npdt = {L.F32: np.float32, L.S8: np.int8}.get(t.dtype, np.uint8)
             a = self.ctx.download(self.addr[name], (t.n, t.h, t.w, t.cs), npdt)[..., :t.c]
             out[name] = a.transpose(0, 3, 1, 2).reshape(self.lo.shapes[name])
         return out

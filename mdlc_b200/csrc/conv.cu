@@ -376,8 +376,8 @@ extern "C" int mdlc_conv2d(mdlc_ctx* ctx, const mdlc_conv_desc* d, const void* x
   switch (path_of(*d)) {
     case kPathTC:
       if ((d->in_type == MDLC_U8 || d->in_type == MDLC_S8) && d->out_type != MDLC_F32 &&
-          (!epi || !epi->rq_mult || !epi->rq_shift))
-        return mdlc_set_error(ctx, MDLC_ERR_INVALID, "conv int8: requantisation arrays required");
+          (!epi || !epi->rq_scale))
+        return mdlc_set_error(ctx, MDLC_ERR_INVALID, "conv int8: requantisation scales required");
       if ((d->in_type == MDLC_U8 || d->in_type == MDLC_S8) && d->out_type == MDLC_F32 &&
           (!epi || !epi->deq_scale))
         return mdlc_set_error(ctx, MDLC_ERR_INVALID, "conv int8: deq_scale required for float output");

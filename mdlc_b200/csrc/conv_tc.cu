@@ -55,26 +55,30 @@ struct TcArgs {
   int M, num_kb, num_m_tiles, num_n_tiles;
   int out_type, a_signed;
   ActParams act;
-  const int32_t* rq_mult;
-  const int32_t* rq_shift;
-  int out_zp, qmin, qmax, res_zp, res_mult, res_shift;
+  const float* rq_scale;
+  int out_zp, qlo, qhi, res_zp;  // qlo / qhi: clamp bounds relative to out_zp
+  float res_scale;
+  int res_signed;
   const float* deq_scale;
   const float* deq_bias;
-  float res_scale;
   unsigned long long wait_cycles;
-  int tma_epi;  // bf16 output staged in shared memory and written by TMA stores
+  int tma_epi;  // bf16 / 8-bit output staged in shared memory and written by TMA stores
 };
 
-template <int BN, int STAGES>
+template <int BN, int STAGES, int ESZ>
 struct Smem {
   static constexpr int kBBytes = BN * 128;
   static constexpr int kA = 0;
   static constexpr int kB = STAGES * kABytes;
-  // epilogue staging: 4 warps x 2 buffers x (32 rows x 128 bytes)
+  // epilogue staging: 4 warps x 2 buffers x (32 rows x 64 columns), rows of
+  // 128 bytes (bf16, 128-byte swizzle) or 64 bytes (8-bit, 64-byte swizzle)
+  static constexpr int kEBuf = 32 * 64 * ESZ;
   static constexpr int kE = kB + STAGES * kBBytes;
-  // per-tile bias, double-buffered by tile parity (fp32, BN columns)
-  static constexpr int kBias = kE + 4 * 2 * 4096;
-  static constexpr int kBar = kBias + 2 * BN * 4;
+  // per-tile epilogue parameters, double-buffered by tile parity: the fp32
+  // bias (bf16), or the int32 bias and fp32 requantisation scale (8-bit)
+  static constexpr int kParamWords = ESZ == 2 ? 1 : 2;
+  static constexpr int kBias = kE + 4 * 2 * kEBuf;
+  static constexpr int kBar = kBias + 2 * kParamWords * BN * 4;
   // barriers: fullA[S], fullB[S], empty[S], tfull[2], tempty[2], drain, resid[4 warps][2 buffers]
   static constexpr int kNumBars = 3 * STAGES + 13;
   static constexpr int kMisc = kBar + kNumBars * 8;
@@ -160,8 +164,8 @@ MDLC_DEV void store_chunk16(const TcArgs& a, int m, int nb0, const uint32_t (&v)
           val = __fmul_rn((float)acc, a.deq_scale[ch]);
           if (a.deq_bias) val = __fadd_rn(val, a.deq_bias[ch]);
           if (a.res) {
-            const int32_t rq = a.a_signed ? (int32_t)(int8_t)a.res[(long long)m * a.res_s + ch]
-                                          : (int32_t)a.res[(long long)m * a.res_s + ch];
+            const int32_t rq = a.res_signed ? (int32_t)(int8_t)a.res[(long long)m * a.res_s + ch]
+                                            : (int32_t)a.res[(long long)m * a.res_s + ch];
             val = __fadd_rn(val, __fmul_rn((float)(rq - a.res_zp), a.res_scale));
           }
           val = apply_act(val, a.act);
@@ -177,14 +181,13 @@ MDLC_DEV void store_chunk16(const TcArgs& a, int m, int nb0, const uint32_t (&v)
       int32_t q = 0;
       if (ch < a.k) {
         const int32_t acc = (int32_t)v[e] + (bias32 ? bias32[ch] : 0);
-        int32_t t = a.out_zp + requant(acc, a.rq_mult[ch], a.rq_shift[ch]);
+        float f = __fmul_rn((float)acc, a.rq_scale[ch]);
         if (a.res) {
-          const int32_t rq = (a.out_type == MDLC_S8)
-                                 ? (int32_t)(int8_t)a.res[(long long)m * a.res_s + ch]
-                                 : (int32_t)a.res[(long long)m * a.res_s + ch];
-          t += requant(rq - a.res_zp, a.res_mult, a.res_shift);
+          const int32_t rq = a.res_signed ? (int32_t)(int8_t)a.res[(long long)m * a.res_s + ch]
+                                          : (int32_t)a.res[(long long)m * a.res_s + ch];
+          f = __fadd_rn(f, __fmul_rn((float)(rq - a.res_zp), a.res_scale));
         }
-        q = min(max(t, a.qmin), a.qmax);
+        q = min(max(__float2int_rn(f), a.qlo), a.qhi) + a.out_zp;
       }
       packed[e >> 2] |= ((uint32_t)(q & 0xFF)) << (8 * (e & 3));
     }
@@ -205,7 +208,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_y,
                    const __grid_constant__ CUtensorMap tmap_r, const __grid_constant__ CUtensorMap tmap_x,
                    const TcArgs a) {
-  using L = Smem<BN, STAGES>;
+  using L = Smem<BN, STAGES, ESZ>;
   constexpr int KB = 128 / ESZ;    // k-block elements (128 bytes)
   constexpr int CHUNK = 16 / ESZ;  // elements per 16-byte chunk
   constexpr uint32_t kTmemCols = 2 * BN;
@@ -324,9 +327,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int ew = warp - 4;
     const int etid = tid - 128;
     const uint32_t lane_base = (uint32_t)(ew * 32) << 16;
-    const uint32_t stage0 = sbase + L::kE + ew * 8192;
-    uint8_t* stage_ptr0 = smem + L::kE + ew * 8192;
-    const bool tma_epi = ESZ == 2 && a.tma_epi;
+    constexpr int kEBuf = L::kEBuf;
+    const uint32_t stage0 = sbase + L::kE + ew * 2 * kEBuf;
+    uint8_t* stage_ptr0 = smem + L::kE + ew * 2 * kEBuf;
+    const bool tma_epi = a.tma_epi;
     int local = 0, chunk_i = 0;
     uint32_t res_use0 = 0, res_use1 = 0;  // completed loads per residual buffer (phase parity)
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
@@ -334,15 +338,24 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int m0 = (tile / a.num_n_tiles) * kBM;
       const int n0 = (tile % a.num_n_tiles) * BN;
       float* sbias = reinterpret_cast<float*>(smem + L::kBias) + buf * BN;
+      int32_t* sq = reinterpret_cast<int32_t*>(smem + L::kBias) + buf * 2 * BN;  // 8-bit: bias32 | scale
       if (tma_epi) {
-        // stage this tile's bias (and the first residual chunk) while the main loop runs
-        for (int i = etid; i < BN; i += 128)
-          sbias[i] = (a.bias && n0 + i < a.k) ? __ldg(static_cast<const float*>(a.bias) + n0 + i) : 0.0f;
+        // stage this tile's epilogue parameters (and the first residual chunk) while the main loop runs
+        if constexpr (ESZ == 2) {
+          for (int i = etid; i < BN; i += 128)
+            sbias[i] = (a.bias && n0 + i < a.k) ? __ldg(static_cast<const float*>(a.bias) + n0 + i) : 0.0f;
+        } else {
+          for (int i = etid; i < BN; i += 128) {
+            const bool v = n0 + i < a.k;
+            sq[i] = (v && a.bias) ? __ldg(static_cast<const int32_t*>(a.bias) + n0 + i) : 0;
+            sq[BN + i] = v ? __float_as_int(__ldg(a.rq_scale + n0 + i)) : 0;
+          }
+        }
         if (a.res && lane == 0) {
           bulk_wait_read<0>();
           const int sbuf = chunk_i & 1;
-          mbar_arrive_expect_tx(resid(ew, sbuf), 4096);
-          tma_load_2d(stage0 + sbuf * 4096, &tmap_r, n0, m0 + ew * 32, resid(ew, sbuf));
+          mbar_arrive_expect_tx(resid(ew, sbuf), kEBuf);
+          tma_load_2d(stage0 + sbuf * kEBuf, &tmap_r, n0, m0 + ew * 32, resid(ew, sbuf));
         }
         asm volatile("bar.sync 1, 128;" ::: "memory");
       }
@@ -354,14 +367,15 @@ __global__ void __launch_bounds__(kThreads, 1)
       const uint32_t taddr = tmem + lane_base + (uint32_t)(buf * BN);
       if (tma_epi) {
         // 64-column chunks: TMEM -> registers -> (+bias, +residual tile, act) ->
-        // bf16 in a 128B-swizzled staging tile -> TMA store
-        const int sw = lane & 7;
+        // bf16 in a 128B-swizzled staging tile (8-bit: requantised codes in a
+        // 64B-swizzled tile) -> TMA store
+        const int sw = ESZ == 2 ? (lane & 7) : ((lane >> 1) & 3);
 #pragma unroll 1
         for (int c0 = 0; c0 < BN; c0 += 64) {
           if (n0 + c0 >= a.ks) break;  // warp-uniform
           const int sbuf = chunk_i & 1;
-          const uint32_t sb = stage0 + sbuf * 4096;
-          uint8_t* sp = stage_ptr0 + sbuf * 4096 + lane * 128;
+          const uint32_t sb = stage0 + sbuf * kEBuf;
+          uint8_t* sp = stage_ptr0 + sbuf * kEBuf + lane * (64 * ESZ);
           if (a.res) {
             const uint32_t use = sbuf ? res_use1++ : res_use0++;
             const bool rok = mbar_wait(resid(ew, sbuf), use & 1, abort_flag, a.err, a.wait_cycles);
@@ -372,8 +386,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (c0 + 64 < BN && n0 + c0 + 64 < a.ks && lane == 0) {
               // prefetch the next residual chunk into the other buffer once its store has read it
               bulk_wait_read<0>();
-              mbar_arrive_expect_tx(resid(ew, sbuf ^ 1), 4096);
-              tma_load_2d(stage0 + (sbuf ^ 1) * 4096, &tmap_r, n0 + c0 + 64, m0 + ew * 32, resid(ew, sbuf ^ 1));
+              mbar_arrive_expect_tx(resid(ew, sbuf ^ 1), kEBuf);
+              tma_load_2d(stage0 + (sbuf ^ 1) * kEBuf, &tmap_r, n0 + c0 + 64, m0 + ew * 32, resid(ew, sbuf ^ 1));
             }
           } else {
             if (lane == 0) bulk_wait_read<1>();  // the store issued two chunks ago has read this buffer
@@ -385,6 +399,31 @@ __global__ void __launch_bounds__(kThreads, 1)
           tmem_ld16(taddr + c0 + 32, *reinterpret_cast<uint32_t(*)[16]>(&v[32]));
           tmem_ld16(taddr + c0 + 48, *reinterpret_cast<uint32_t(*)[16]>(&v[48]));
           tmem_ld_wait();
+          if constexpr (ESZ == 1) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {  // 16-column (16-byte) groups
+              uint4* qp = reinterpret_cast<uint4*>(sp + ((q ^ sw) << 4));
+              uint4 rr = make_uint4(0, 0, 0, 0);
+              if (a.res) rr = *qp;
+              const uint32_t rw[4] = {rr.x, rr.y, rr.z, rr.w};
+              uint32_t packed[4] = {0, 0, 0, 0};
+#pragma unroll
+              for (int e = 0; e < 16; ++e) {
+                const int col = c0 + 16 * q + e;
+                const int32_t acc = (int32_t)v[16 * q + e] + sq[col];
+                float f = __fmul_rn((float)acc, __int_as_float(sq[BN + col]));
+                if (a.res) {
+                  const uint32_t byte = (rw[e >> 2] >> (8 * (e & 3))) & 0xFFu;
+                  const int32_t rq = a.res_signed ? (int32_t)(int8_t)byte : (int32_t)byte;
+                  f = __fadd_rn(f, __fmul_rn((float)(rq - a.res_zp), a.res_scale));
+                }
+                int32_t t = min(max(__float2int_rn(f), a.qlo), a.qhi) + a.out_zp;
+                if (n0 + col >= a.k) t = 0;
+                packed[e >> 2] |= ((uint32_t)t & 0xFFu) << (8 * (e & 3));
+              }
+              *qp = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+            }
+          } else {
 #pragma unroll
           for (int q = 0; q < 8; ++q) {  // 8-column (16-byte) groups
             uint4* qp = reinterpret_cast<uint4*>(sp + ((q ^ sw) << 4));
@@ -404,6 +443,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             for (int e = 0; e < 8; ++e) f[e] = (nb0 + e < a.k) ? act_fn<ACT>(f[e], a.act) : 0.0f;
             *qp = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
                              pack_bf16x2(f[6], f[7]));
+          }
           }
           fence_proxy_async_smem();
           __syncwarp();
@@ -626,7 +666,7 @@ int encode_im2col(CUtensorMap* m, const mdlc_conv_desc& d, const void* x, int es
 template <int BN, int STAGES, int ESZ, int ACT, int AMODE>
 int launch_tc(mdlc_ctx* ctx, const CUtensorMap& tmap, const CUtensorMap& tmap_y, const CUtensorMap& tmap_r,
               const CUtensorMap& tmap_x, const TcArgs& args) {
-  using L = Smem<BN, STAGES>;
+  using L = Smem<BN, STAGES, ESZ>;
   static_assert(L::kAlloc <= 232448, "shared memory budget");
   auto kern = conv_tc_kernel<BN, STAGES, ESZ, ACT, AMODE>;
   static bool attr_set[64] = {};
@@ -699,10 +739,10 @@ int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w
   a.wait_cycles = 2 * kWaitLimitNs;  // cycles: >= the nanosecond limit at clocks up to 2 GHz
   if (epi) {
     a.act = ActParams{epi->act, epi->alpha, epi->beta, epi->clip_lo, epi->clip_hi};
-    a.rq_mult = epi->rq_mult; a.rq_shift = epi->rq_shift;
-    a.out_zp = epi->out_zp; a.qmin = epi->qmin; a.qmax = epi->qmax;
-    a.res_zp = epi->res_zp; a.res_mult = epi->res_mult; a.res_shift = epi->res_shift;
-    a.deq_scale = epi->deq_scale; a.deq_bias = epi->deq_bias; a.res_scale = epi->res_scale;
+    a.rq_scale = epi->rq_scale;
+    a.out_zp = epi->out_zp; a.qlo = epi->qmin - epi->out_zp; a.qhi = epi->qmax - epi->out_zp;
+    a.res_zp = epi->res_zp; a.res_scale = epi->res_scale; a.res_signed = epi->res_signed;
+    a.deq_scale = epi->deq_scale; a.deq_bias = epi->deq_bias;
   }
   if (int8) a.pad_src = ctx->d_pad + 16 * (d.in_zp & 0xFF);
 
@@ -715,14 +755,18 @@ int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w
   // them with 2-D TMA stores; a residual is brought in by TMA loads of the
   // same tile shape. Boxes hanging over M or k_stride are clipped by TMA.
   CUtensorMap tmap_y = tmap, tmap_r = tmap;
-  if (!int8 && d.out_type == MDLC_BF16) {
+  const bool out8 = d.out_type == MDLC_U8 || d.out_type == MDLC_S8;
+  if ((!int8 && d.out_type == MDLC_BF16) || (int8 && out8)) {
+    // 32 rows x 64 columns: 128-byte rows with 128-byte swizzle (bf16), 64-byte
+    // rows with 64-byte swizzle (8-bit)
     auto encode2d = [&](CUtensorMap* m, const void* base, int inner) {
       const cuuint64_t gd[2] = {(cuuint64_t)inner, (cuuint64_t)M};
-      const cuuint64_t gs[1] = {(cuuint64_t)inner * 2};
+      const cuuint64_t gs[1] = {(cuuint64_t)inner * esz};
       const cuuint32_t bx[2] = {64, 32};
-      return encode(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), gd, gs, bx, estride,
-                    CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                    CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      return encode(m, int8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
+                    const_cast<void*>(base), gd, gs, bx, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                    int8 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     };
     if (encode2d(&tmap_y, y, d.k_stride) != CUDA_SUCCESS ||
         (res && encode2d(&tmap_r, res, a.res_s) != CUDA_SUCCESS))

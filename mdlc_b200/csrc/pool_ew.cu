@@ -92,6 +92,126 @@ __global__ void __launch_bounds__(256) pool_kernel(const mdlc_pool_desc d, const
   }
 }
 
+// Packed 8-channel max: bf16 pairs through __hmax2, fp32 through fmaxf.
+template <typename T>
+struct MaxV8;
+template <>
+struct MaxV8<__nv_bfloat16> {
+  using V = uint4;
+  static MDLC_DEV V lowest() {
+    const uint32_t ni = 0xFF80FF80u;  // two bf16 -inf
+    return make_uint4(ni, ni, ni, ni);
+  }
+  static MDLC_DEV V load(const char* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+  static MDLC_DEV uint32_t m2(uint32_t a, uint32_t b) {
+    __nv_bfloat162 r = __hmax2(*reinterpret_cast<__nv_bfloat162*>(&a), *reinterpret_cast<__nv_bfloat162*>(&b));
+    return *reinterpret_cast<uint32_t*>(&r);
+  }
+  static MDLC_DEV V max(V a, V b) { return make_uint4(m2(a.x, b.x), m2(a.y, b.y), m2(a.z, b.z), m2(a.w, b.w)); }
+  static MDLC_DEV void store(char* p, V v) { *reinterpret_cast<uint4*>(p) = v; }
+  static constexpr int kBytes = 2;
+  static constexpr int kVec = 8;  // channels per vector
+};
+// 8-bit codes: 16 channels per vector, byte-wise max (exact on codes).
+template <>
+struct MaxV8<uint8_t> {
+  using V = uint4;
+  static MDLC_DEV V lowest() { return make_uint4(0, 0, 0, 0); }
+  static MDLC_DEV V load(const char* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+  static MDLC_DEV V max(V a, V b) {
+    return make_uint4(__vmaxu4(a.x, b.x), __vmaxu4(a.y, b.y), __vmaxu4(a.z, b.z), __vmaxu4(a.w, b.w));
+  }
+  static MDLC_DEV void store(char* p, V v) { *reinterpret_cast<uint4*>(p) = v; }
+  static constexpr int kBytes = 1;
+  static constexpr int kVec = 16;
+};
+template <>
+struct MaxV8<int8_t> {
+  using V = uint4;
+  static MDLC_DEV V lowest() {
+    const uint32_t m = 0x80808080u;
+    return make_uint4(m, m, m, m);
+  }
+  static MDLC_DEV V load(const char* p) { return __ldg(reinterpret_cast<const uint4*>(p)); }
+  static MDLC_DEV V max(V a, V b) {
+    return make_uint4(__vmaxs4(a.x, b.x), __vmaxs4(a.y, b.y), __vmaxs4(a.z, b.z), __vmaxs4(a.w, b.w));
+  }
+  static MDLC_DEV void store(char* p, V v) { *reinterpret_cast<uint4*>(p) = v; }
+  static constexpr int kBytes = 1;
+  static constexpr int kVec = 16;
+};
+template <>
+struct MaxV8<float> {
+  struct V { float4 a, b; };
+  static MDLC_DEV V lowest() {
+    return V{make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY),
+             make_float4(-INFINITY, -INFINITY, -INFINITY, -INFINITY)};
+  }
+  static MDLC_DEV V load(const char* p) {
+    return V{__ldg(reinterpret_cast<const float4*>(p)), __ldg(reinterpret_cast<const float4*>(p) + 1)};
+  }
+  static MDLC_DEV float4 m4(float4 a, float4 b) {
+    return make_float4(fmaxf(a.x, b.x), fmaxf(a.y, b.y), fmaxf(a.z, b.z), fmaxf(a.w, b.w));
+  }
+  static MDLC_DEV V max(V a, V b) { return V{m4(a.a, b.a), m4(a.b, b.b)}; }
+  static MDLC_DEV void store(char* p, V v) {
+    reinterpret_cast<float4*>(p)[0] = v.a;
+    reinterpret_cast<float4*>(p)[1] = v.b;
+  }
+  static constexpr int kBytes = 4;
+  static constexpr int kVec = 8;
+};
+
+// 3x3 / stride-2 max pool (the ResNet stem pool). Each thread owns one
+// (image, output column, 16-byte channel group) and walks kStrip output rows: the
+// horizontal max of every input row is taken once and the row shared by
+// vertically adjacent windows is carried over, so an output row costs two
+// input rows of three 16-byte loads. Channel group fastest: a warp reads whole
+// pixels. Padded channels are zero in the input, so they stay zero.
+template <typename T, int kStrip>
+__global__ void __launch_bounds__(256) maxpool3s2_kernel(const mdlc_pool_desc d, const void* x, void* y,
+                                                         int strips, int total) {
+  using M = MaxV8<T>;
+  const int G = d.c_stride / M::kVec;
+  const long long row_bytes = (long long)d.w * d.c_stride * M::kBytes;
+  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += gridDim.x * blockDim.x) {
+    const int g = idx % G;
+    int t = idx / G;
+    const int ox = t % d.ow;
+    t /= d.ow;
+    const int strip = t % strips;
+    const int img = t / strips;
+    const int iw0 = ox * 2 - d.pad_l;
+    const char* xi = static_cast<const char*>(x) + (long long)img * d.h * row_bytes + (long long)g * M::kVec * M::kBytes;
+    const long long px = (long long)d.c_stride * M::kBytes;
+    auto hrow = [&](int ih) {
+      typename M::V r = M::lowest();
+      if ((unsigned)ih < (unsigned)d.h) {
+        const char* rp = xi + ih * row_bytes;
+#pragma unroll
+        for (int kx = 0; kx < 3; ++kx) {
+          const int iw = iw0 + kx;
+          if ((unsigned)iw < (unsigned)d.w) r = M::max(r, M::load(rp + iw * px));
+        }
+      }
+      return r;
+    };
+    const int oy0 = strip * kStrip;
+    typename M::V carry = hrow(oy0 * 2 - d.pad_t);
+    char* yo = static_cast<char*>(y) + (((long long)img * d.oh + oy0) * d.ow + ox) * px + (long long)g * M::kVec * M::kBytes;
+    const long long orow = (long long)d.ow * px;
+#pragma unroll
+    for (int j = 0; j < kStrip; ++j) {
+      const int oy = oy0 + j;
+      if (oy >= d.oh) break;
+      const typename M::V a = hrow(oy * 2 - d.pad_t + 1);
+      const typename M::V b = hrow(oy * 2 - d.pad_t + 2);
+      M::store(yo + j * orow, M::max(carry, M::max(a, b)));
+      carry = b;
+    }
+  }
+}
+
 template <typename T>
 __global__ void __launch_bounds__(256) pool_max_u8_kernel(const mdlc_pool_desc d, const uint8_t* x,
                                                           uint8_t* y, long long total) {
@@ -306,10 +426,22 @@ extern "C" int mdlc_pool2d(mdlc_ctx* ctx, const mdlc_pool_desc* d, const void* x
   } else {
     if (d->oh <= 0 || d->ow <= 0 || d->kh <= 0 || d->kw <= 0 || d->stride_h <= 0 || d->stride_w <= 0)
       return mdlc_set_error(ctx, MDLC_ERR_INVALID, "pool: bad window");
+    constexpr int kStrip = 8;
+    const int strips = (d->oh + kStrip - 1) / kStrip;
+    const long long strip_total = (long long)d->n * strips * d->ow * (d->c_stride / (q ? 16 : 8));
+    const bool s32 = d->kind == 0 && d->kh == 3 && d->kw == 3 && d->stride_h == 2 && d->stride_w == 2 &&
+                     d->pad_t <= 1 && d->pad_l <= 1 && strip_total < (1LL << 31) &&
+                     (d->oh - 1) * 2 - d->pad_t < d->h && (d->ow - 1) * 2 - d->pad_l < d->w;
     if (q) {
       if (d->kind != 0) return mdlc_set_error(ctx, MDLC_ERR_UNSUPPORTED, "pool: int8 average pool");
       const long long total = (long long)d->n * d->oh * d->ow * (d->c_stride / 16);
-      if (d->dtype == MDLC_U8)
+      if (s32 && d->dtype == MDLC_U8)
+        maxpool3s2_kernel<uint8_t, kStrip><<<grid_for(ctx, strip_total), 256, 0, ctx->stream>>>(
+            *d, x, y, strips, (int)strip_total);
+      else if (s32)
+        maxpool3s2_kernel<int8_t, kStrip><<<grid_for(ctx, strip_total), 256, 0, ctx->stream>>>(
+            *d, x, y, strips, (int)strip_total);
+      else if (d->dtype == MDLC_U8)
         pool_max_u8_kernel<uint8_t><<<grid_for(ctx, total), 256, 0, ctx->stream>>>(
             *d, static_cast<const uint8_t*>(x), static_cast<uint8_t*>(y), total);
       else
@@ -317,7 +449,13 @@ extern "C" int mdlc_pool2d(mdlc_ctx* ctx, const mdlc_pool_desc* d, const void* x
             *d, static_cast<const uint8_t*>(x), static_cast<uint8_t*>(y), total);
     } else {
       const long long total = (long long)d->n * d->oh * d->ow * (d->c_stride / 8);
-      if (d->dtype == MDLC_BF16)
+      if (s32 && d->dtype == MDLC_BF16)
+        maxpool3s2_kernel<__nv_bfloat16, kStrip><<<grid_for(ctx, strip_total), 256, 0, ctx->stream>>>(
+            *d, x, y, strips, (int)strip_total);
+      else if (s32 && d->dtype == MDLC_F32)
+        maxpool3s2_kernel<float, kStrip><<<grid_for(ctx, strip_total), 256, 0, ctx->stream>>>(
+            *d, x, y, strips, (int)strip_total);
+      else if (d->dtype == MDLC_BF16)
         pool_kernel<__nv_bfloat16><<<grid_for(ctx, total), 256, 0, ctx->stream>>>(*d, x, y, total);
       else if (d->dtype == MDLC_F32)
         pool_kernel<float><<<grid_for(ctx, total), 256, 0, ctx->stream>>>(*d, x, y, total);
@@ -464,6 +602,83 @@ __global__ void __launch_bounds__(256) to_s2d_kernel(const float* x, int c, int 
   }
 }
 
+// The image-stem case of the above: at most 4 input channels into CS = 16 or
+// 32 output channels. One thread per output pixel reads one float2 (two
+// horizontally adjacent inputs) per (channel, row) -- coalesced across the
+// warp -- and writes the pixel's CS channels with full-width vector stores, so
+// the input is read once and every byte written is a whole 32-byte sector.
+template <int DT, int C, int CS>
+__global__ void __launch_bounds__(256) to_s2d16_kernel(const float* x, int h, int w, void* y, float inv_scale,
+                                                       int zp, int total) {
+  const int w2 = w >> 1, hw2 = (h >> 1) * w2;
+  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += gridDim.x * blockDim.x) {
+    const int img = idx / hw2;
+    const int p = idx - img * hw2;
+    const int Y = p / w2, X = p - Y * w2;
+    float v[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) v[e] = 0.0f;
+#pragma unroll
+    for (int ci = 0; ci < C; ++ci)
+#pragma unroll
+      for (int dy = 0; dy < 2; ++dy) {
+        const float2 f = __ldg(reinterpret_cast<const float2*>(
+            x + (((long long)img * C + ci) * h + 2 * Y + dy) * w + 2 * X));
+        v[(2 * dy) * C + ci] = f.x;
+        v[(2 * dy + 1) * C + ci] = f.y;
+      }
+    const long long o = (long long)idx * CS;
+    if constexpr (DT == MDLC_F32) {
+      float4* yo = reinterpret_cast<float4*>(static_cast<float*>(y) + o);
+#pragma unroll
+      for (int j = 0; j < CS / 4; ++j)
+        yo[j] = j < 4 ? make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]) : make_float4(0, 0, 0, 0);
+    } else if constexpr (DT == MDLC_BF16) {
+      uint32_t u[8];
+#pragma unroll
+      for (int j = 0; j < 8; ++j) u[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
+      uint4* yo = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(y) + o);
+      yo[0] = make_uint4(u[0], u[1], u[2], u[3]);
+      yo[1] = make_uint4(u[4], u[5], u[6], u[7]);
+#pragma unroll
+      for (int j = 2; j < CS / 8; ++j) yo[j] = make_uint4(0, 0, 0, 0);
+    } else {
+      uint32_t u[4] = {0, 0, 0, 0};
+#pragma unroll
+      for (int e = 0; e < 4 * C; ++e) {
+        int q = __float2int_rn(__fmul_rn(v[e], inv_scale)) + zp;
+        q = DT == MDLC_S8 ? min(max(q, -128), 127) : min(max(q, 0), 255);
+        u[e >> 2] |= (uint32_t)(q & 0xFF) << (8 * (e & 3));
+      }
+      uint4* yo = reinterpret_cast<uint4*>(static_cast<uint8_t*>(y) + o);
+      yo[0] = make_uint4(u[0], u[1], u[2], u[3]);
+#pragma unroll
+      for (int j = 1; j < CS / 16; ++j) yo[j] = make_uint4(0, 0, 0, 0);
+    }
+  }
+}
+
+template <int DT, int CS>
+void launch_s2d16(mdlc_ctx* ctx, const float* x, int c, int h, int w, void* y, float inv_scale, int zp,
+                  int total) {
+  const unsigned grid = grid_for(ctx, total);
+  switch (c) {
+    case 1: to_s2d16_kernel<DT, 1, CS><<<grid, 256, 0, ctx->stream>>>(x, h, w, y, inv_scale, zp, total); break;
+    case 2: to_s2d16_kernel<DT, 2, CS><<<grid, 256, 0, ctx->stream>>>(x, h, w, y, inv_scale, zp, total); break;
+    case 3: to_s2d16_kernel<DT, 3, CS><<<grid, 256, 0, ctx->stream>>>(x, h, w, y, inv_scale, zp, total); break;
+    default: to_s2d16_kernel<DT, 4, CS><<<grid, 256, 0, ctx->stream>>>(x, h, w, y, inv_scale, zp, total); break;
+  }
+}
+
+template <int DT>
+void launch_s2d_stem(mdlc_ctx* ctx, const float* x, int c, int h, int w, void* y, int cs, float inv_scale,
+                     int zp, int total) {
+  if (cs == 16)
+    launch_s2d16<DT, 16>(ctx, x, c, h, w, y, inv_scale, zp, total);
+  else
+    launch_s2d16<DT, 32>(ctx, x, c, h, w, y, inv_scale, zp, total);
+}
+
 template <int DT>
 __global__ void __launch_bounds__(256) to_nchw_kernel(const void* x, int n, int c, int hw, int cs, float* y,
                                                       float scale, int zp, long long total) {
@@ -514,7 +729,20 @@ extern "C" int mdlc_nchw_to_s2d(mdlc_ctx* ctx, const float* x, int n, int c, int
   if (!x || !y || n <= 0 || c <= 0 || h <= 0 || w <= 0 || (h & 1) || (w & 1) || cs < 4 * c || cs % align)
     return mdlc_set_error(ctx, MDLC_ERR_INVALID, "nchw_to_s2d: bad arguments");
   cudaSetDevice(ctx->device);
-  const long long total = (long long)n * (h / 2) * (w / 2) * (cs / 8);
+  const long long pixels = (long long)n * (h / 2) * (w / 2);
+  if ((cs == 16 || cs == 32) && c <= 4 && pixels < (1LL << 31) && !(reinterpret_cast<uintptr_t>(x) & 7) &&
+      !(reinterpret_cast<uintptr_t>(y) & 15)) {
+    switch (dtype) {
+      case MDLC_BF16: launch_s2d_stem<MDLC_BF16>(ctx, x, c, h, w, y, cs, inv_scale, zp, (int)pixels); break;
+      case MDLC_F32: launch_s2d_stem<MDLC_F32>(ctx, x, c, h, w, y, cs, inv_scale, zp, (int)pixels); break;
+      case MDLC_U8: launch_s2d_stem<MDLC_U8>(ctx, x, c, h, w, y, cs, inv_scale, zp, (int)pixels); break;
+      case MDLC_S8: launch_s2d_stem<MDLC_S8>(ctx, x, c, h, w, y, cs, inv_scale, zp, (int)pixels); break;
+      default: return mdlc_set_error(ctx, MDLC_ERR_UNSUPPORTED, "nchw_to_s2d: dtype %d", dtype);
+    }
+    mdlc_note_launch(ctx);
+    return mdlc_cuda_status(ctx, cudaGetLastError(), "nchw_to_s2d launch");
+  }
+  const long long total = pixels * (cs / 8);
   const unsigned grid = grid_for(ctx, total);
   switch (dtype) {
     case MDLC_BF16: to_s2d_kernel<MDLC_BF16><<<grid, 256, 0, ctx->stream>>>(x, c, h, w, y, cs, inv_scale, zp, total); break;

@@ -538,7 +538,8 @@ def space_to_depth_stem(lo: Lowered) -> None:
     The graph-input conversion kernel writes the space-to-depth layout
     directly, so the rewrite costs nothing at run time; it shrinks the
     reduction from R*S*8 to about R*S*16/4 elements and makes every filter tap
-    a contiguous 32-byte run (16 channels) instead of a 16-byte one.
+    a contiguous 32-byte run (16 bf16 channels, or 32 8-bit channels) that the
+    im2col tensor-memory-accelerator path loads whole.
     """
     for name in lo.inputs:
         t = lo.tensors.get(name)
@@ -554,15 +555,22 @@ def space_to_depth_stem(lo: Lowered) -> None:
         if geom["groups"] != 1 or geom["sh"] != 2 or geom["sw"] != 2 or geom["dh"] != 1 or geom["dw"] != 1:
             continue
         w2, pt2, pl2 = s2d_weights(wt, geom["pt"], geom["pl"])
-        g2 = dict(geom, h=geom["h"] // 2, w=geom["w"] // 2, c=4 * geom["c"], cs=16, r=w2.shape[2],
+        cs = 32 if t.dtype in (L.U8, L.S8) else 16      # 32-byte pixels either way
+        g2 = dict(geom, h=geom["h"] // 2, w=geom["w"] // 2, c=4 * geom["c"], cs=cs, r=w2.shape[2],
                   s=w2.shape[3], sh=1, sw=1, pt=pt2, pl=pl2, pt_orig=geom["pt"], pl_orig=geom["pl"])
         lo.weights[st.params["weight"]] = (g2, w2, bias)
-        t.layout, t.c, t.h, t.w, t.cs = "s2d2", 4 * t.c, t.h // 2, t.w // 2, 16
+        t.layout, t.c, t.h, t.w, t.cs = "s2d2", 4 * t.c, t.h // 2, t.w // 2, cs
         st.params["s2d"] = True
 
 
 def lower(graph, shapes: dict, dtype: int, s2d: bool = True) -> Lowered:
+    """Lower a post-pass graph to backend steps. For 8-bit lowering the graph
+    inputs are signed (symmetric int8, zero point 0: padded taps read real
+    zeros) and every other activation is unsigned."""
     lo = _Lowerer(graph, shapes, dtype).run()
+    if dtype == L.U8:
+        for name in lo.inputs:
+            lo.tensors[name].dtype = L.S8
     if s2d:
         space_to_depth_stem(lo)
     return lo

@@ -2,26 +2,30 @@
 
 The reference has no quantised operators (``DType.INT8`` exists only as a type,
 ``mdlc/ir/tensor.py:29``; "INT8/DP4A path not started", ``docs/GAPS.md:128``), so
-this module defines the scheme, following the gemmlowp / TFLite fixed-point
-convention (the published method):
+this module defines the scheme: gemmlowp / TFLite-style asymmetric uint8
+activations and symmetric per-channel int8 weights, with fbgemm-style fp32
+requantisation (published methods):
 
 * activations: per-tensor asymmetric uint8, ``q = clamp(rint(x / s) + zp, 0, 255)``
   with ``s = (max(hi, 0) - min(lo, 0)) / 255`` and ``zp = rint(-min(lo, 0) / s)``,
   ranges calibrated on seeded N(0, 1) batches run through the backend's own fp32
-  executable;
+  executable; the network input is symmetric int8 instead
+  (``s = max(|lo|, |hi|) / 127``, zero point 0, ``q = clamp(rint(x / s), -128, 127)``)
+  so that the first conv's padded taps are real zeros;
 * weights: per-output-channel symmetric int8, ``s_w[k] = max|w[k]| / 127``,
   ``w_q = clamp(rint(w / s_w), -127, 127)``;
 * conv / GEMM: int32 accumulation ``acc = sum(x_q * w_q)`` with padded taps reading
   the input zero point, ``bias32 = rint(b / (s_x s_w)) - zp_x * sum(w_q)``, then
-  ``y_q = clamp(zp_y + requant(acc + bias32, M[k], sh[k])
-  [+ requant(res_q - zp_r, M_r, sh_r)], qmin, qmax)`` with
-  ``requant(v, M, sh) = RoundingDivideByPOT(SaturatingRoundingDoublingHighMul(v', M), max(sh, 0))``
-  where ``v' = sat_int32(v * 2^max(-sh, 0))`` and ``M * 2^-(31+sh)`` is the real
-  multiplier; the activation (ReLU / ReLU6) is the clamp. A layer with fp32 output
-  (the logits) computes ``y = act(float32(acc + bias32) * float32(s_x s_w[k]) + float32(b[k])
-  [+ float32(res_q - zp_r) * s_r])`` in float32 arithmetic;
+  ``f = float32(acc + bias32) * r[k] [+ float32(res_q - zp_r) * r_res]`` with
+  ``r[k] = float32(s_x s_w[k] / s_y)``, ``r_res = float32(s_r / s_y)``, each product
+  and sum rounded once in IEEE float32 (no fused multiply-add), and
+  ``y_q = zp_y + clamp(rint(f), qmin - zp_y, qmax - zp_y)`` (round half to even);
+  the activation (ReLU / ReLU6) is the clamp. A layer with fp32 output (the
+  logits) computes ``y = act(float32(acc + bias32) * float32(s_x s_w[k]) + float32(b[k])
+  [+ float32(res_q - zp_r) * s_r])`` in the same float32 arithmetic;
 * max pooling works on the codes (output keeps the input's scale and zero point);
-  global average pooling requantises ``sum(q - zp_in)`` by ``s_in / (H W s_out)``.
+  global average pooling requantises ``sum(q - zp_in)`` by ``s_in / (H W s_out)`` in
+  gemmlowp fixed point (SaturatingRoundingDoublingHighMul + RoundingDivideByPOT).
 
 Bit-exactness is defined against the integer NumPy restatement in the test
 oracle, which consumes the same :class:`QuantPlan`.
@@ -44,6 +48,12 @@ def act_qparams(lo: float, hi: float):
     scale = np.float32((hi - lo) / 255.0) if hi > lo else np.float32(1.0)
     zp = int(np.clip(np.rint(-lo / float(scale)), 0, 255))
     return scale, zp
+
+
+def sym_qparams(lo: float, hi: float):
+    """(scale, 0) of a per-tensor symmetric int8 quantiser for [lo, hi]."""
+    amax = max(abs(float(lo)), abs(float(hi)))
+    return (np.float32(amax / 127.0) if amax > 0 else np.float32(1.0)), 0
 
 
 def quantize_multiplier(real: float):
@@ -76,13 +86,10 @@ class ConvQ:
     w_q_orig: np.ndarray     # int8 codes, OIHW of the graph node (for the oracle)
     s_w: np.ndarray          # float32 [k]
     bias32: np.ndarray       # int32 [k]
-    mult: np.ndarray         # int32 [k]
-    shift: np.ndarray        # int32 [k]
+    rq_scale: np.ndarray     # float32 [k] s_x s_w[k] / s_y (8-bit output)
     qmin: int = 0
     qmax: int = 255
-    res_mult: int = 0
-    res_shift: int = 0
-    res_scale: float = 0.0                # float32 residual scale (fp32 output)
+    res_scale: float = 0.0   # float32 residual scale: s_r / s_y (8-bit output), s_r (fp32 output)
     deq_scale: np.ndarray | None = None   # float32 [k] (fp32 output)
     deq_bias: np.ndarray | None = None    # float32 [k] (fp32 output)
     act: str | None = None
@@ -95,6 +102,7 @@ class QuantPlan:
     convs: dict              # weight name -> ConvQ
     gap: dict                # output name -> (mult, shift, in_zp, out_zp)
     steps: list              # lowered steps (names, grouping), shared with the oracle
+    signed: set = field(default_factory=set)   # tensors holding signed int8 codes
 
 
 def _act_range(act, attrs, s_y, zp_y):
@@ -117,9 +125,13 @@ def build_plan(lo_f32, lo_i8, ranges: dict, graph) -> QuantPlan:
     ``ranges`` maps activation tensor names to (min, max) observed in fp32;
     ``lo_f32`` supplies the unrewritten fp32 weights of each step.
     """
-    tensors = {}
+    tensors, signed = {}, set()
     for name in lo_i8.inputs:
-        tensors[name] = act_qparams(*ranges[name])
+        if lo_i8.tensors[name].dtype == L.S8:
+            tensors[name] = sym_qparams(*ranges[name])
+            signed.add(name)
+        else:
+            tensors[name] = act_qparams(*ranges[name])
     convs, gap = {}, {}
     for st in lo_i8.steps:
         y = st.outputs[0]
@@ -160,28 +172,25 @@ def build_plan(lo_f32, lo_i8, ranges: dict, graph) -> QuantPlan:
         wsum = w_q_orig.reshape(k, -1).sum(axis=1).astype(np.int64)
         out_t = lo_i8.tensors[y]
         q = ConvQ(x=x, y=y, residual=st.params.get("residual"), w_q=w_q, w_q_orig=w_q_orig, s_w=s_w,
-                  bias32=None, mult=None, shift=None, act=st.params.get("act"), nodes=list(st.nodes))
+                  bias32=None, rq_scale=np.zeros(k, np.float32), act=st.params.get("act"),
+                  nodes=list(st.nodes))
         if out_t.dtype == L.F32:
             q.bias32 = (-zp_x * wsum).astype(np.int32)
             q.deq_scale = (np.float32(s_x) * s_w).astype(np.float32)
             q.deq_bias = b.astype(np.float32)
-            q.mult = np.zeros(k, np.int32)
-            q.shift = np.zeros(k, np.int32)
             if q.residual:
-                q.res_scale = float(tensors[q.residual][0])
+                q.res_scale = float(np.float32(tensors[q.residual][0]))
         else:
             s_y, zp_y = act_qparams(*ranges[y])
             tensors[y] = (s_y, zp_y)
             q.bias32 = (np.rint(b / acc_scale).astype(np.int64) - zp_x * wsum).astype(np.int32)
-            ms = [quantize_multiplier(float(acc_scale[i]) / float(s_y)) for i in range(k)]
-            q.mult = np.array([m for m, _ in ms], np.int32)
-            q.shift = np.array([s for _, s in ms], np.int32)
+            q.rq_scale = (acc_scale / np.float64(s_y)).astype(np.float32)
             q.qmin, q.qmax = _act_range(q.act, st.params["attrs"], s_y, zp_y)
             if q.residual:
-                s_r, zp_r = tensors[q.residual]
-                q.res_mult, q.res_shift = quantize_multiplier(float(s_r) / float(s_y))
+                s_r, _ = tensors[q.residual]
+                q.res_scale = float(np.float32(np.float64(s_r) / np.float64(s_y)))
         convs[st.params["weight"]] = q
-    return QuantPlan(tensors, convs, gap, lo_i8.steps)
+    return QuantPlan(tensors, convs, gap, lo_i8.steps, signed)
 
 
 def calibrate(graph, batches, *, device: int = 0) -> dict:

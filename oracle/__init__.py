@@ -10,7 +10,7 @@ backend (``mdlc_b200``) never imports it and has no CPU fallback.
   fixtures produced by importing the reference itself
   (``tests/golden/make_golden.py``).
 * :mod:`oracle.quant` is the INT8 restatement (calibration, per-channel weight
-  quantisation, int32 accumulation, gemmlowp-style fixed-point requantise). The
+  quantisation, int32 accumulation, fp32 / fixed-point requantisation). The
   reference has no quantised ops, so its parity is defined by this restatement
   ("parity unpinned by the reference" for INT8).
 """

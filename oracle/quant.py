@@ -3,14 +3,17 @@
 The reference has no quantised operators (``mdlc/ir/tensor.py:29``,
 ``docs/GAPS.md:128``), so this module *defines* INT8 parity: given the same
 quantisation plan as the device (scales, zero points, int8 weight codes, int32
-biases, fixed-point multipliers), it evaluates the network in exact integer
-arithmetic:
+biases, requantisation scales), it evaluates the network with exact integer
+accumulation and IEEE float32 requantisation:
 
 * conv / GEMM: im2col of the uint8 codes padded with the input zero point, then
   an int64 ``einsum("ok,nkp->nop")`` — the reference's conv algorithm
   (``mdlc/runtime/ops.py:35-81``) on integers — plus the int32 bias;
-* requantisation: gemmlowp's SaturatingRoundingDoublingHighMul (truncating
-  division by 2^31) followed by RoundingDivideByPOT (round half away from zero);
+* conv requantisation in IEEE float32, one rounding per product and sum:
+  ``zp + clip(rint(f32(acc + bias32) * r[k] [+ f32(res - zp_r) * r_res]), qmin - zp, qmax - zp)``;
+* global-average-pool requantisation in gemmlowp fixed point:
+  SaturatingRoundingDoublingHighMul (truncating division by 2^31) followed by
+  RoundingDivideByPOT (round half away from zero);
 * max pool on codes over in-bounds taps; global average pool as an int32 sum of
   ``q - zp`` requantised;
 * fp32 logits ``act(float32(acc + bias32) * float32(scale) + float32(bias)
@@ -60,13 +63,14 @@ def requant(v, mult, shift):
     return rdbpot(srdhm(v, mult), np.maximum(shift, 0))
 
 
-def quantize_input(x, scale, zp):
+def quantize_input(x, scale, zp, signed=False):
     inv = np.float32(1.0) / np.float32(scale)
-    return np.clip(np.rint(np.asarray(x, np.float32) * inv).astype(np.int64) + zp, 0, 255)
+    q = np.rint(np.asarray(x, np.float32) * inv).astype(np.int64) + zp
+    return np.clip(q, -128, 127) if signed else np.clip(q, 0, 255)
 
 
 def conv_int(xq, wq, zp, attrs):
-    """int64 conv of uint8 codes (N,C,H,W) with zero-point padding (ops.py:56-81)."""
+    """int64 conv of 8-bit codes (N,C,H,W) with zero-point padding (ops.py:56-81)."""
     n, c, ih, iw = xq.shape
     k, _, kh, kw = wq.shape
     sh, sw = attrs.get("strides", [1, 1])
@@ -101,7 +105,7 @@ def run_int8(graph, plan, feeds):
     env = {}
     for name in graph.runtime_inputs:
         s, zp = plan.tensors[name]
-        env[name] = quantize_input(feeds[name], s, zp)
+        env[name] = quantize_input(feeds[name], s, zp, name in plan.signed)
     for st in plan.steps:
         if st.kind == "pool":
             x = env[src(st.inputs[0])]
@@ -145,12 +149,13 @@ def run_int8(graph, plan, feeds):
             env[st.outputs[0]] = y.reshape(y.shape[0], k) if node.op_type in ("Gemm", "FusedGemmAct", "MatMul") else y
         else:
             zp_y = plan.tensors[st.outputs[0]][1]
-            t = zp_y + requant(acc, cq.mult.reshape(1, k, 1, 1), cq.shift.reshape(1, k, 1, 1))
+            f = acc.astype(np.float32) * cq.rq_scale.astype(np.float32).reshape(1, k, 1, 1)
             if cq.residual:
                 r = env[src(cq.residual)]
                 zp_r = plan.tensors[src(cq.residual)][1]
-                t = t + requant(r - zp_r, cq.res_mult, cq.res_shift)
-            t = np.clip(t, cq.qmin, cq.qmax)
+                f = f + (r - zp_r).astype(np.float32) * np.float32(cq.res_scale)
+            assert f.dtype == np.float32
+            t = np.clip(np.rint(f), cq.qmin - zp_y, cq.qmax - zp_y).astype(np.int64) + zp_y
             env[st.outputs[0]] = t.reshape(t.shape[0], k) if node.op_type in ("Gemm", "FusedGemmAct", "MatMul") else t
     outs = {o: env[src(o)] for o in graph.outputs}
     outs["__codes__"] = env

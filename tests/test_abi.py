@@ -37,7 +37,7 @@ def test_struct_layouts_match_header():
     assert C.sizeof(L.TileCfg) == 12
     assert C.sizeof(L.EwInstr) == 12
     assert C.sizeof(L.EwProg) == 8 * 4 + 4 * 4 + 2 * 4 + 24 * 12
-    assert C.sizeof(L.Epilogue) == 5 * 4 + 4 + 2 * 8 + 6 * 4 + 2 * 8 + 8  # padding before pointers / at the end
+    assert C.sizeof(L.Epilogue) == 5 * 4 + 4 + 8 + 4 * 4 + 4 + 4 + 2 * 8  # padding before the first pointer
 
 
 def test_version_and_no_device_here():

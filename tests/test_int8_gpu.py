@@ -1,8 +1,8 @@
 """INT8 executables on the B200 against the integer restatement (bit-exact).
 
 The device quantises the fp32 feeds, runs the tcgen05 ``kind::i8`` convs with
-the fixed-point requantisation epilogue, max-pools codes, requantises the
-global average pool and dequantises the logits. Every stored code and the fp32
+the fp32 requantisation epilogue, max-pools codes, requantises the global
+average pool in fixed point and dequantises the logits. Every stored code and the fp32
 logits must equal ``oracle.quant.run_int8`` evaluated under the executable's
 own quantisation plan (calibrated on the GPU).
 """
@@ -44,7 +44,7 @@ def _compare(exe, g, feeds):
             continue
         got = codes[name]
         ref = np.asarray(ref)
-        if got.dtype == np.uint8:
+        if got.dtype in (np.uint8, np.int8):
             ref = ref.astype(np.int64)
             bad = np.argwhere(got.astype(np.int64) != ref)
             assert bad.size == 0, (f"{name}: {len(bad)} of {got.size} codes differ; first at {bad[0].tolist()}: "

@@ -269,6 +269,86 @@ def test_pools(ctx, dtype):
 
 
 @pytest.mark.parametrize("dtype", ["bf16", "f32"])
+@pytest.mark.parametrize("shape,k,s,p", [((3, 64, 37, 30), 3, 2, 1), ((2, 24, 40, 41), 3, 2, 0),
+                                         ((1, 16, 112, 112), 3, 2, 1), ((2, 8, 9, 10), 3, 1, 1),
+                                         ((2, 40, 12, 12), 2, 2, 0)])
+def test_maxpool_shapes(ctx, dtype, shape, k, s, p):
+    """3x3/2 row-strip kernel (several strips, with and without padding) and the
+    generic window kernel, bit-exact (max is exact in either precision)."""
+    x = np.random.default_rng(29).standard_normal(shape).astype(np.float32)
+    xr = oref.round_bf16(x) if dtype == "bf16" else x
+    got = _pool(ctx, x, 0, dtype, k=k, s=s, p=p)
+    np.testing.assert_array_equal(got, oref.maxpool(xr, kernel=[k, k], strides=[s, s], pads=[p] * 4))
+
+
+@pytest.mark.parametrize("dtype", [L.U8, L.S8])
+@pytest.mark.parametrize("shape,k,s,p", [((2, 64, 37, 30), 3, 2, 1), ((1, 16, 20, 20), 3, 2, 0),
+                                         ((2, 32, 9, 10), 3, 1, 1)])
+def test_maxpool_codes(ctx, dtype, shape, k, s, p):
+    """8-bit max pooling on codes (strip kernel for 3x3/2, generic otherwise)."""
+    n, c, h, w = shape
+    rng = np.random.default_rng(37)
+    npdt = np.uint8 if dtype == L.U8 else np.int8
+    info = np.iinfo(npdt)
+    x = rng.integers(info.min, info.max + 1, shape).astype(npdt)
+    cs = (c + 15) // 16 * 16
+    oh, ow = (h + 2 * p - k) // s + 1, (w + 2 * p - k) // s + 1
+    d = L.PoolDesc(kind=0, n=n, h=h, w=w, c=c, c_stride=cs, kh=k, kw=k, stride_h=s, stride_w=s,
+                   pad_t=p, pad_l=p, oh=oh, ow=ow, count_include_pad=0, dtype=dtype)
+    xd = ctx.to_device(nhwc(x, cs))
+    yd = ctx.alloc(n * oh * ow * cs)
+    ctx.pool2d(d, xd, yd)
+    ctx.sync()
+    y = ctx.download(yd, (n, oh, ow, cs), npdt)[..., :c].transpose(0, 3, 1, 2)
+    want = oref.maxpool(x.astype(np.float32), kernel=[k, k], strides=[s, s], pads=[p] * 4)
+    np.testing.assert_array_equal(y.astype(np.float32), want)
+    ctx.free(xd)
+    ctx.free(yd)
+
+
+def _s2d_ref(x):
+    n, c, h, w = x.shape
+    t = x.reshape(n, c, h // 2, 2, w // 2, 2).transpose(0, 2, 4, 3, 5, 1)   # n, Y, X, dy, dx, c
+    return t.reshape(n, h // 2, w // 2, 4 * c)
+
+
+@pytest.mark.parametrize("dtype", [L.BF16, L.F32, L.U8, L.S8])
+@pytest.mark.parametrize("shape,cs", [((2, 3, 20, 18), 16), ((1, 4, 8, 6), 16), ((2, 1, 6, 4), 16),
+                                      ((2, 3, 20, 18), 32), ((2, 5, 10, 12), 24)])
+def test_space_to_depth_input(ctx, dtype, shape, cs):
+    """fp32 NCHW -> 2x2 space-to-depth NHWC (16-channel stem kernel and the
+    generic one), quantising for 8-bit types."""
+    x = np.random.default_rng(31).standard_normal(shape).astype(np.float32)
+    n, c, h, w = shape
+    q8 = dtype in (L.U8, L.S8)
+    if q8:
+        cs = max(cs, 16) if cs % 16 == 0 else 32
+    zp = 0 if dtype == L.S8 else 77
+    xd = ctx.to_device(x)
+    eb = {L.BF16: 2, L.F32: 4, L.U8: 1, L.S8: 1}[dtype]
+    yd = ctx.alloc(n * (h // 2) * (w // 2) * cs * eb)
+    inv = 1.0 / np.float32(0.05)
+    ctx.to_s2d(xd, n, c, h, w, yd, cs, dtype, float(np.float32(inv)), zp)
+    ctx.sync()
+    npdt = {L.BF16: np.uint16, L.F32: np.float32, L.U8: np.uint8, L.S8: np.int8}[dtype]
+    y = ctx.download(yd, (n, h // 2, w // 2, cs), npdt)
+    ref = _s2d_ref(x)
+    if dtype == L.BF16:
+        np.testing.assert_array_equal(y[..., :4 * c], bf16_bits(ref))
+        assert np.all(y[..., 4 * c:] == 0)
+    elif dtype == L.F32:
+        np.testing.assert_array_equal(y[..., :4 * c], ref)
+        assert np.all(y[..., 4 * c:] == 0)
+    else:
+        lo, hi = (-128, 127) if dtype == L.S8 else (0, 255)
+        q = np.clip(np.rint(ref * np.float32(inv)).astype(np.int64) + zp, lo, hi)
+        np.testing.assert_array_equal(y[..., :4 * c].astype(np.int64), q)
+        assert np.all(y[..., 4 * c:] == 0)
+    ctx.free(xd)
+    ctx.free(yd)
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
 def test_eltwise_program(ctx, dtype):
     """relu(a + b) * c with c broadcast per (n, channel), plus a second output."""
     rng = np.random.default_rng(17)

@@ -96,9 +96,9 @@ def test_plan_structure_resnet18():
     assert len(plan.convs) == 21 and len(plan.gap) == 1
     for cq in plan.convs.values():
         assert np.all(np.abs(cq.w_q_orig) <= 127) and np.all(cq.w_q_orig == np.rint(cq.w_q_orig))
-        assert cq.bias32.dtype == np.int32
+        assert cq.bias32.dtype == np.int32 and cq.rq_scale.dtype == np.float32
         if cq.deq_scale is None:
-            assert np.all((cq.mult == 0) | ((cq.mult >= 1 << 30) & (cq.shift >= 0)))
+            assert np.all(cq.rq_scale > 0) and np.all(np.isfinite(cq.rq_scale))
     # the stem's space-to-depth weights hold the same codes
     stem = next(c for w, c in plan.convs.items() if w.startswith("conv1"))
     assert stem.w_q.shape[1] == 12 and np.abs(stem.w_q).sum() == np.abs(stem.w_q_orig).sum()
