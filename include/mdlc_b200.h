@@ -175,8 +175,22 @@ int mdlc_host_free(mdlc_ctx* ctx, void* host);
 int mdlc_upload(mdlc_ctx* ctx, void* dev, const void* host, size_t bytes);      /* async on the stream */
 int mdlc_download(mdlc_ctx* ctx, void* host, const void* dev, size_t bytes);    /* async on the stream */
 int mdlc_memset(mdlc_ctx* ctx, void* dev, int value, size_t bytes);
-int mdlc_sync(mdlc_ctx* ctx, int timeout_ms);
+int mdlc_sync(mdlc_ctx* ctx, int timeout_ms);   /* waits for both streams of the context */
 int mdlc_check_flag(mdlc_ctx* ctx, int* flag); /* reads and clears the device error word */
+
+/* ---- copy stream: overlap host<->device transfers with compute ---------
+ * Every context owns a compute stream (all kernels) and a copy stream.
+ * Transfers may go on either; ordering between the two goes through fences:
+ * mdlc_fence_record(ctx, id, s) marks the current end of stream s as fence id
+ * (in [0, 64)), mdlc_fence_wait(ctx, id, s) makes later work on stream s wait
+ * for the last recorded fence id (a fence never recorded is already passed),
+ * and mdlc_fence_sync blocks the host on it. */
+enum { MDLC_STREAM_COMPUTE = 0, MDLC_STREAM_COPY = 1 };
+int mdlc_upload_on(mdlc_ctx* ctx, int stream, void* dev, const void* host, size_t bytes);
+int mdlc_download_on(mdlc_ctx* ctx, int stream, void* host, const void* dev, size_t bytes);
+int mdlc_fence_record(mdlc_ctx* ctx, int id, int stream);
+int mdlc_fence_wait(mdlc_ctx* ctx, int id, int stream);
+int mdlc_fence_sync(mdlc_ctx* ctx, int id, int timeout_ms);
 
 /* ---- kernels (all asynchronous on the context stream) ------------------ */
 /* Replaces conv lowering (mdlc/codegen/cuda/emit.py:159-209: im2col + gemm),
@@ -222,7 +236,8 @@ int mdlc_graph_launch(mdlc_ctx* ctx);
 int mdlc_graph_reset(mdlc_ctx* ctx);
 
 /* ---- timing on the context stream (replaces nvrtc_runtime.py:211-225) -- */
-int mdlc_event_record(mdlc_ctx* ctx, int slot); /* slot in [0, 4096) */
+int mdlc_event_record(mdlc_ctx* ctx, int slot); /* slot in [0, 4096), on the compute stream */
+int mdlc_event_record_on(mdlc_ctx* ctx, int slot, int stream);
 int mdlc_event_elapsed(mdlc_ctx* ctx, int start_slot, int stop_slot, float* ms);
 /* number of kernels this context has launched (including graph replays) */
 int mdlc_launch_count(mdlc_ctx* ctx, long long* count);

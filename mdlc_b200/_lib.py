@@ -17,6 +17,7 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 LIB_PATH = os.path.join(HERE, "libmdlc_b200.so")
 
 OK, ERR_INVALID, ERR_CUDA, ERR_UNSUPPORTED, ERR_TIMEOUT, ERR_DEVICE, ERR_NOMEM = 0, -1, -2, -3, -4, -5, -6
+STREAM_COMPUTE, STREAM_COPY = 0, 1
 DEVERR_NONE, DEVERR_WAIT_TIMEOUT, DEVERR_BOUNDS, DEVERR_INJECTED = 0, 1, 2, 3
 F32, BF16, S8, U8, S32 = 0, 1, 2, 3, 4
 (ACT_NONE, ACT_RELU, ACT_CLIP, ACT_SIGMOID, ACT_TANH, ACT_LEAKY_RELU, ACT_HARD_SIGMOID,
@@ -94,6 +95,11 @@ SIGNATURES = {
     "mdlc_memset": ([_P, _P, C.c_int, _S], C.c_int),
     "mdlc_sync": ([_P, C.c_int], C.c_int),
     "mdlc_check_flag": ([_P, C.POINTER(C.c_int)], C.c_int),
+    "mdlc_upload_on": ([_P, C.c_int, _P, _P, _S], C.c_int),
+    "mdlc_download_on": ([_P, C.c_int, _P, _P, _S], C.c_int),
+    "mdlc_fence_record": ([_P, C.c_int, C.c_int], C.c_int),
+    "mdlc_fence_wait": ([_P, C.c_int, C.c_int], C.c_int),
+    "mdlc_fence_sync": ([_P, C.c_int, C.c_int], C.c_int),
     "mdlc_conv2d": ([_P, C.POINTER(ConvDesc), _P, _P, _P, _P, _P, C.POINTER(Epilogue),
                      C.POINTER(TileCfg)], C.c_int),
     "mdlc_conv_weight_bytes": ([C.POINTER(ConvDesc), C.POINTER(C.c_size_t)], C.c_int),
@@ -108,6 +114,7 @@ SIGNATURES = {
     "mdlc_graph_launch": ([_P], C.c_int),
     "mdlc_graph_reset": ([_P], C.c_int),
     "mdlc_event_record": ([_P, C.c_int], C.c_int),
+    "mdlc_event_record_on": ([_P, C.c_int, C.c_int], C.c_int),
     "mdlc_event_elapsed": ([_P, C.c_int, C.c_int, C.POINTER(C.c_float)], C.c_int),
     "mdlc_launch_count": ([_P, C.POINTER(C.c_longlong)], C.c_int),
     "mdlc_debug_timeout_probe": ([_P, C.c_int], C.c_int),
@@ -212,6 +219,24 @@ class Context:
         self.check(self.lib.mdlc_download(self.h, C.c_void_p(host_ptr), C.c_void_p(dev),
                                           C.c_size_t(nbytes)), "download")
 
+    # -- copy stream and fences (transfers overlapped with compute) ------
+    def upload_on(self, stream: int, dev: int, host_ptr: int, nbytes: int) -> None:
+        self.check(self.lib.mdlc_upload_on(self.h, int(stream), C.c_void_p(dev), C.c_void_p(host_ptr),
+                                           C.c_size_t(nbytes)), "upload_on")
+
+    def download_on(self, stream: int, host_ptr: int, dev: int, nbytes: int) -> None:
+        self.check(self.lib.mdlc_download_on(self.h, int(stream), C.c_void_p(host_ptr), C.c_void_p(dev),
+                                             C.c_size_t(nbytes)), "download_on")
+
+    def fence_record(self, fence: int, stream: int) -> None:
+        self.check(self.lib.mdlc_fence_record(self.h, int(fence), int(stream)), "fence_record")
+
+    def fence_wait(self, fence: int, stream: int) -> None:
+        self.check(self.lib.mdlc_fence_wait(self.h, int(fence), int(stream)), "fence_wait")
+
+    def fence_sync(self, fence: int, timeout_ms: int = 60000) -> None:
+        self.check(self.lib.mdlc_fence_sync(self.h, int(fence), int(timeout_ms)), "fence_sync")
+
     def memset(self, dev: int, value: int, nbytes: int) -> None:
         self.check(self.lib.mdlc_memset(self.h, C.c_void_p(dev), int(value), C.c_size_t(nbytes)), "memset")
 
@@ -264,8 +289,11 @@ class Context:
     def graph_reset(self):
         self.check(self.lib.mdlc_graph_reset(self.h), "graph_reset")
 
-    def event_record(self, slot: int):
-        self.check(self.lib.mdlc_event_record(self.h, int(slot)), "event_record")
+    def event_record(self, slot: int, stream: int = 0):
+        if stream:
+            self.check(self.lib.mdlc_event_record_on(self.h, int(slot), int(stream)), "event_record_on")
+        else:
+            self.check(self.lib.mdlc_event_record(self.h, int(slot)), "event_record")
 
     def event_elapsed(self, a: int, b: int) -> float:
         ms = C.c_float(0)

@@ -91,18 +91,20 @@ class _Device:
                 self.wbuf[wname] = self.ctx.to_device(packed)
                 self.bbuf[wname] = self.ctx.to_device(bias)
         self.cbuf = {name: self.ctx.to_device(arr) for name, arr in lo.consts.items()}
-        # staging: fp32 NCHW feeds / outputs on device and pinned on the host
+        # staging: fp32 NCHW feeds / outputs on device and pinned on the host, in
+        # two slots (slot 1 allocated on first use) so that one slot's upload can
+        # overlap the other slot's forward
         self.in_dev, self.in_host, self.out_dev, self.out_host = {}, {}, {}, {}
         for name in lo.inputs:
             nbytes = int(np.prod(lo.shapes[name])) * 4
-            self.in_dev[name] = self.ctx.alloc(nbytes)
-            self.in_host[name] = self.ctx.host_alloc(nbytes)
+            self.in_dev[name] = [self.ctx.alloc(nbytes), None]
+            self.in_host[name] = [self.ctx.host_alloc(nbytes), None]
         for name in lo.outputs:
             nbytes = int(np.prod(lo.shapes[name])) * 4
             t = lo.tensors[name]
             direct = t.dtype == L.F32 and t.cs == t.c and t.h * t.w == 1
             self.out_dev[name] = None if direct else self.ctx.alloc(nbytes)
-            self.out_host[name] = self.ctx.host_alloc(nbytes)
+            self.out_host[name] = [self.ctx.host_alloc(nbytes), None]
         self.calls = self._prepare()
         self.graph_ready = False
 
@@ -204,7 +206,19 @@ class _Device:
     def _store(self, name):
         return memory.storage_of(self.lo.tensors, name)
 
-    def issue_inputs(self):
+    def _slot(self, slot):
+        if slot not in (0, 1):
+            raise ValueError("slot must be 0 or 1")
+        if slot == 1 and self.lo.inputs and self.in_dev[self.lo.inputs[0]][1] is None:
+            for name in self.lo.inputs:
+                nbytes = int(np.prod(self.lo.shapes[name])) * 4
+                self.in_dev[name][1] = self.ctx.alloc(nbytes)
+                self.in_host[name][1] = self.ctx.host_alloc(nbytes)
+            for name in self.lo.outputs:
+                self.out_host[name][1] = self.ctx.host_alloc(int(np.prod(self.lo.shapes[name])) * 4)
+        return slot
+
+    def issue_inputs(self, slot=0):
         for name in self.lo.inputs:
             t = self.lo.tensors[name]
             inv, zp = 1.0, 0
@@ -213,9 +227,10 @@ class _Device:
                 inv = float(np.float32(1.0) / np.float32(s_x))
             if t.layout == "s2d2":
                 n, c, h, w = self.lo.shapes[name]
-                self.ctx.to_s2d(self.in_dev[name], n, c, h, w, self.ptr(name), t.cs, t.dtype, inv, zp)
+                self.ctx.to_s2d(self.in_dev[name][slot], n, c, h, w, self.ptr(name), t.cs, t.dtype, inv, zp)
             else:
-                self.ctx.to_nhwc(self.in_dev[name], t.n, t.c, t.h, t.w, self.ptr(name), t.cs, t.dtype, inv, zp)
+                self.ctx.to_nhwc(self.in_dev[name][slot], t.n, t.c, t.h, t.w, self.ptr(name), t.cs, t.dtype,
+                                 inv, zp)
 
     def issue_outputs(self):
         for name in self.lo.outputs:
@@ -271,37 +286,64 @@ class _Device:
         lo = self.lo
         for name in lo.inputs:
             arr = np.ascontiguousarray(feeds_slice[name], dtype=np.float32)
-            host = np.ctypeslib.as_array((C.c_float * arr.size).from_address(self.in_host[name]))
+            host = np.ctypeslib.as_array((C.c_float * arr.size).from_address(self.in_host[name][0]))
             host[:] = arr.reshape(-1)
-            self.ctx.upload_async(self.in_dev[name], self.in_host[name], arr.nbytes)
+            self.ctx.upload_async(self.in_dev[name][0], self.in_host[name][0], arr.nbytes)
         self.forward(use_graph)
         outs = {}
         for name in lo.outputs:
             n = int(np.prod(lo.shapes[name]))
-            self.ctx.download_async(self.out_host[name], self.out_src(name), n * 4)
+            self.ctx.download_async(self.out_host[name][0], self.out_src(name), n * 4)
         self.ctx.sync()
         for name in lo.outputs:
             n = int(np.prod(lo.shapes[name]))
-            host = np.ctypeslib.as_array((C.c_float * n).from_address(self.out_host[name]))
+            host = np.ctypeslib.as_array((C.c_float * n).from_address(self.out_host[name][0]))
             outs[name] = host.copy().reshape(lo.shapes[name])
         return outs
 
-    def pinned_views(self):
+    def pinned_views(self, slot=0):
         lo = self.lo
+        slot = self._slot(slot)
         ins = {n: np.ctypeslib.as_array((C.c_float * int(np.prod(lo.shapes[n]))).from_address(
-            self.in_host[n])).reshape(lo.shapes[n]) for n in lo.inputs}
+            self.in_host[n][slot])).reshape(lo.shapes[n]) for n in lo.inputs}
         outs = {n: np.ctypeslib.as_array((C.c_float * int(np.prod(lo.shapes[n]))).from_address(
-            self.out_host[n])).reshape(lo.shapes[n]) for n in lo.outputs}
+            self.out_host[n][slot])).reshape(lo.shapes[n]) for n in lo.outputs}
         return ins, outs
 
     def issue_pinned(self, use_graph=False):
         """H2D from the pinned feed buffers, forward, D2H into the pinned output buffers."""
         lo = self.lo
         for name in lo.inputs:
-            self.ctx.upload_async(self.in_dev[name], self.in_host[name], int(np.prod(lo.shapes[name])) * 4)
+            self.ctx.upload_async(self.in_dev[name][0], self.in_host[name][0], int(np.prod(lo.shapes[name])) * 4)
         self.forward(use_graph)
         for name in lo.outputs:
-            self.ctx.download_async(self.out_host[name], self.out_src(name), int(np.prod(lo.shapes[name])) * 4)
+            self.ctx.download_async(self.out_host[name][0], self.out_src(name), int(np.prod(lo.shapes[name])) * 4)
+
+    # fences: 0 + slot upload landed, 2 + slot upload consumed, 4 + slot outputs read back
+    def submit(self, slot):
+        """Pipelined forward of one slot: the upload of the slot's pinned feeds
+        runs on the copy stream (after the slot's previous feeds were consumed),
+        the forward and the read-back of its outputs on the compute stream after
+        the upload, so an upload overlaps the other slot's forward."""
+        ctx, lo = self.ctx, self.lo
+        slot = self._slot(slot)
+        ctx.fence_wait(2 + slot, L.STREAM_COPY)
+        for name in lo.inputs:
+            ctx.upload_on(L.STREAM_COPY, self.in_dev[name][slot], self.in_host[name][slot],
+                          int(np.prod(lo.shapes[name])) * 4)
+        ctx.fence_record(0 + slot, L.STREAM_COPY)
+        ctx.fence_wait(0 + slot, L.STREAM_COMPUTE)
+        self.issue_inputs(slot)
+        ctx.fence_record(2 + slot, L.STREAM_COMPUTE)
+        self.issue_steps()
+        self.issue_outputs()
+        for name in lo.outputs:
+            ctx.download_on(L.STREAM_COMPUTE, self.out_host[name][slot], self.out_src(name),
+                            int(np.prod(lo.shapes[name])) * 4)
+        ctx.fence_record(4 + slot, L.STREAM_COMPUTE)
+
+    def wait(self, slot, timeout_ms=60000):
+        self.ctx.fence_sync(4 + slot, timeout_ms)
 
     def close(self):
         self.ctx.close()
@@ -395,13 +437,31 @@ class Executable:
         return {o: np.concatenate([r[o] for r in results], axis=0) if len(results) > 1 else results[0][o]
                 for o in self.lowered.outputs}
 
-    def pinned_inputs(self, device: int = 0) -> dict:
-        """Numpy views of a device's pinned feed buffers (fill them, then ``run_pinned``)."""
-        return self.devices[device].pinned_views()[0]
+    def pinned_inputs(self, device: int = 0, slot: int = 0) -> dict:
+        """Numpy views of a device's pinned feed buffers (fill them, then
+        ``run_pinned`` for slot 0, or ``submit(slot)``)."""
+        return self.devices[device].pinned_views(slot)[0]
 
-    def pinned_outputs(self, device: int = 0) -> dict:
-        """Numpy views of a device's pinned output buffers (valid after ``run_pinned`` + ``sync``)."""
-        return self.devices[device].pinned_views()[1]
+    def pinned_outputs(self, device: int = 0, slot: int = 0) -> dict:
+        """Numpy views of a device's pinned output buffers (valid after
+        ``run_pinned`` + ``sync``, or ``wait(slot)``)."""
+        return self.devices[device].pinned_views(slot)[1]
+
+    def submit(self, slot: int = 0) -> None:
+        """Asynchronous, double-buffered serving call: upload the pinned feeds of
+        ``slot`` (0 or 1) on each device's copy stream, run the forward and read
+        the outputs back into the slot's pinned outputs. Alternating slots lets
+        the upload of one batch overlap the forward of the other. Fill a slot's
+        inputs / read its outputs only after ``wait(slot)``."""
+        for d in self.devices:
+            d.submit(slot)
+
+    def wait(self, slot: int = 0) -> dict:
+        """Block until the last ``submit(slot)`` has finished; returns device
+        0's pinned output views for the slot. Device errors surface at ``sync``."""
+        for d in self.devices:
+            d.wait(slot)
+        return self.pinned_outputs(0, slot)
 
     def run_pinned(self, use_graph: bool = False, sync: bool = True) -> None:
         """Zero-copy host API: pinned H2D of the feeds, forward, D2H of the outputs."""

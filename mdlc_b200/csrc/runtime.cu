@@ -54,6 +54,7 @@ int mdlc_ctx_create(int device, mdlc_ctx** out) {
   ctx->device = device;
   ctx->num_sms = prop.multiProcessorCount;
   if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
+      cudaStreamCreateWithFlags(&ctx->copy_stream, cudaStreamNonBlocking) != cudaSuccess ||
       cudaMalloc(&ctx->d_err, 256) != cudaSuccess ||
       cudaMemset(ctx->d_err, 0, 256) != cudaSuccess || cudaMalloc(&ctx->d_pad, 4096) != cudaSuccess) {
     delete ctx;
@@ -68,6 +69,7 @@ int mdlc_ctx_create(int device, mdlc_ctx** out) {
     }
   }
   for (int i = 0; i < kMaxEvents; ++i) cudaEventCreate(&ctx->events[i]);
+  for (int i = 0; i < kMaxFences; ++i) cudaEventCreateWithFlags(&ctx->fences[i], cudaEventDisableTiming);
   *out = ctx;
   return MDLC_OK;
 }
@@ -76,12 +78,16 @@ int mdlc_ctx_destroy(mdlc_ctx* ctx) {
   if (!ctx) return MDLC_OK;
   cudaSetDevice(ctx->device);
   cudaStreamSynchronize(ctx->stream);
+  if (ctx->copy_stream) cudaStreamSynchronize(ctx->copy_stream);
   if (ctx->graph_exec) cudaGraphExecDestroy(ctx->graph_exec);
   if (ctx->graph) cudaGraphDestroy(ctx->graph);
   for (int i = 0; i < kMaxEvents; ++i) cudaEventDestroy(ctx->events[i]);
+  for (int i = 0; i < kMaxFences; ++i)
+    if (ctx->fences[i]) cudaEventDestroy(ctx->fences[i]);
   cudaFree(ctx->d_err);
   cudaFree(ctx->d_pad);
   cudaStreamDestroy(ctx->stream);
+  if (ctx->copy_stream) cudaStreamDestroy(ctx->copy_stream);
   delete ctx;
   return MDLC_OK;
 }
@@ -141,13 +147,63 @@ int mdlc_memset(mdlc_ctx* ctx, void* dev, int value, size_t bytes) {
   return mdlc_cuda_status(ctx, cudaMemsetAsync(dev, value, bytes, ctx->stream), "memset");
 }
 
+static cudaStream_t stream_of(mdlc_ctx* ctx, int s) {
+  return s == MDLC_STREAM_COPY ? ctx->copy_stream : (s == MDLC_STREAM_COMPUTE ? ctx->stream : nullptr);
+}
+
+int mdlc_upload_on(mdlc_ctx* ctx, int stream, void* dev, const void* host, size_t bytes) {
+  if (!ctx || !stream_of(ctx, stream) || (!dev && bytes) || (!host && bytes)) return MDLC_ERR_INVALID;
+  cudaSetDevice(ctx->device);
+  return mdlc_cuda_status(
+      ctx, cudaMemcpyAsync(dev, host, bytes, cudaMemcpyHostToDevice, stream_of(ctx, stream)), "upload");
+}
+
+int mdlc_download_on(mdlc_ctx* ctx, int stream, void* host, const void* dev, size_t bytes) {
+  if (!ctx || !stream_of(ctx, stream) || (!dev && bytes) || (!host && bytes)) return MDLC_ERR_INVALID;
+  cudaSetDevice(ctx->device);
+  return mdlc_cuda_status(
+      ctx, cudaMemcpyAsync(host, dev, bytes, cudaMemcpyDeviceToHost, stream_of(ctx, stream)), "download");
+}
+
+int mdlc_fence_record(mdlc_ctx* ctx, int id, int stream) {
+  if (!ctx || id < 0 || id >= kMaxFences || !stream_of(ctx, stream)) return MDLC_ERR_INVALID;
+  cudaSetDevice(ctx->device);
+  return mdlc_cuda_status(ctx, cudaEventRecord(ctx->fences[id], stream_of(ctx, stream)), "fence record");
+}
+
+int mdlc_fence_wait(mdlc_ctx* ctx, int id, int stream) {
+  if (!ctx || id < 0 || id >= kMaxFences || !stream_of(ctx, stream)) return MDLC_ERR_INVALID;
+  cudaSetDevice(ctx->device);
+  return mdlc_cuda_status(ctx, cudaStreamWaitEvent(stream_of(ctx, stream), ctx->fences[id], 0), "fence wait");
+}
+
+int mdlc_fence_sync(mdlc_ctx* ctx, int id, int timeout_ms) {
+  if (!ctx || id < 0 || id >= kMaxFences) return MDLC_ERR_INVALID;
+  cudaSetDevice(ctx->device);
+  const auto t0 = std::chrono::steady_clock::now();
+  for (;;) {
+    cudaError_t e = cudaEventQuery(ctx->fences[id]);
+    if (e == cudaSuccess) return MDLC_OK;
+    if (e != cudaErrorNotReady) return mdlc_cuda_status(ctx, e, "fence sync");
+    if (timeout_ms > 0 && std::chrono::duration_cast<std::chrono::milliseconds>(
+                              std::chrono::steady_clock::now() - t0).count() > timeout_ms)
+      return mdlc_set_error(ctx, MDLC_ERR_TIMEOUT, "fence %d not reached after %d ms", id, timeout_ms);
+    std::this_thread::sleep_for(std::chrono::microseconds(20));
+  }
+}
+
 int mdlc_sync(mdlc_ctx* ctx, int timeout_ms) {
   if (!ctx) return MDLC_ERR_INVALID;
   cudaSetDevice(ctx->device);
-  if (timeout_ms <= 0) return mdlc_cuda_status(ctx, cudaStreamSynchronize(ctx->stream), "sync");
+  if (timeout_ms <= 0) {
+    cudaError_t e = cudaStreamSynchronize(ctx->copy_stream);
+    if (e == cudaSuccess) e = cudaStreamSynchronize(ctx->stream);
+    return mdlc_cuda_status(ctx, e, "sync");
+  }
   const auto t0 = std::chrono::steady_clock::now();
   for (;;) {
-    cudaError_t e = cudaStreamQuery(ctx->stream);
+    cudaError_t e = cudaStreamQuery(ctx->copy_stream);
+    if (e == cudaSuccess) e = cudaStreamQuery(ctx->stream);
     if (e == cudaSuccess) return MDLC_OK;
     if (e != cudaErrorNotReady) return mdlc_cuda_status(ctx, e, "sync");
     auto ms = std::chrono::duration_cast<std::chrono::milliseconds>(
@@ -214,6 +270,12 @@ int mdlc_event_record(mdlc_ctx* ctx, int slot) {
   if (!ctx || slot < 0 || slot >= kMaxEvents) return MDLC_ERR_INVALID;
   cudaSetDevice(ctx->device);
   return mdlc_cuda_status(ctx, cudaEventRecord(ctx->events[slot], ctx->stream), "event record");
+}
+
+int mdlc_event_record_on(mdlc_ctx* ctx, int slot, int stream) {
+  if (!ctx || slot < 0 || slot >= kMaxEvents || !stream_of(ctx, stream)) return MDLC_ERR_INVALID;
+  cudaSetDevice(ctx->device);
+  return mdlc_cuda_status(ctx, cudaEventRecord(ctx->events[slot], stream_of(ctx, stream)), "event record");
 }
 
 int mdlc_event_elapsed(mdlc_ctx* ctx, int a, int b, float* ms) {

@@ -9,13 +9,15 @@
 #include "mdlc_b200.h"
 
 static constexpr int kMaxEvents = 4096;
+static constexpr int kMaxFences = 64;
 // Device-side waits give up after this long (nanoseconds).
 static constexpr unsigned long long kWaitLimitNs = 2000000000ull;
 
 struct mdlc_ctx {
   int device = 0;
   int num_sms = 148;
-  cudaStream_t stream = nullptr;
+  cudaStream_t stream = nullptr;       // compute stream (every kernel)
+  cudaStream_t copy_stream = nullptr;  // host<->device transfers overlapped with compute
   int* d_err = nullptr;  // device error word (first failure wins)
   uint8_t* d_pad = nullptr;  // 256 x 16-byte fill patterns (byte value v at v*16)
   cudaGraph_t graph = nullptr;
@@ -24,6 +26,7 @@ struct mdlc_ctx {
   long long launches = 0;           // kernels launched by this context
   long long captured_launches = 0;  // kernels inside the instantiated graph
   cudaEvent_t events[kMaxEvents] = {};
+  cudaEvent_t fences[kMaxFences] = {};  // cross-stream ordering (no timing)
   std::string last_error;
 };
 

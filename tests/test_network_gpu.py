@@ -141,3 +141,27 @@ def test_cuda_graph_replay_matches_eager():
     replay = exe.run(feeds, use_graph=True)["logits"]
     np.testing.assert_array_equal(eager, replay)
     exe.close()
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "int8"])
+def test_double_buffered_submit_matches_run(dtype):
+    """submit(slot)/wait(slot) (upload on the copy stream overlapping the other
+    slot's forward) returns exactly what run() returns, batch after batch."""
+    g = passes.default_pipeline(builders.resnet18(batch=2, image=64))
+    exe = compile(g, dtype=dtype, batch=2)
+    try:
+        rng = np.random.default_rng(3)
+        xs = [rng.standard_normal((2, 3, 64, 64)).astype(np.float32) for _ in range(5)]
+        want = [exe.run({"input": x})["logits"].copy() for x in xs]
+        seq = xs + xs[:3]
+        for i, x in enumerate(seq):
+            s = i % 2
+            if i >= 2:
+                np.testing.assert_array_equal(exe.wait(s)["logits"], want[(i - 2) % len(xs)])
+            exe.pinned_inputs(slot=s)["input"][...] = x
+            exe.submit(s)
+        for i in (len(seq) - 2, len(seq) - 1):
+            np.testing.assert_array_equal(exe.wait(i % 2)["logits"], want[i % len(xs)])
+        exe.sync()
+    finally:
+        exe.close()
