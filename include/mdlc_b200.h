@@ -113,7 +113,9 @@ typedef struct {
   int32_t bn;     /* output channels per CTA: 64, 128 or 256 */
   int32_t stages; /* shared-memory pipeline depth; built pairs: (64, 8), (128, 4), (256, 3) */
   int32_t flags;  /* bit 0: gather the A operand with cp.async even when the layer
-                     qualifies for im2col-mode TMA loads */
+                     qualifies for TMA loads; bit 1: per-tap TMA loads (im2col mode)
+                     instead of the halo band of stride-1 layers; bit 2: load one halo band
+                     per tile for stride-1 layers instead of one load per tap */
 } mdlc_tile_cfg;
 
 /* Pooling over NHWC (reference: ops.py:109-150). kind: 0 max, 1 average,

@@ -130,6 +130,26 @@ MDLC_DEV void tma_load_im2col_4d(uint32_t dst, const void* tmap, int32_t c, int3
       : "memory");
 }
 
+// 4-D tiled load (no multicast); coordinates may be negative or past the end
+// (those elements read as zero).
+MDLC_DEV void tma_load_4d(uint32_t dst, const void* tmap, int32_t c0, int32_t c1, int32_t c2, int32_t c3,
+                          uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5, %6}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+      : "memory");
+}
+
+// 4-D tiled store shared -> global; box elements past the end of the tensor
+// are not written (coordinates must be non-negative).
+MDLC_DEV void tma_store_4d(const void* tmap, int32_t c0, int32_t c1, int32_t c2, int32_t c3, uint32_t src) {
+  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.bulk_group [%0, {%2, %3, %4, %5}], [%1];" ::"l"(
+                   reinterpret_cast<uint64_t>(tmap)),
+               "r"(src), "r"(c0), "r"(c1), "r"(c2), "r"(c3)
+               : "memory");
+}
+
 // 2-D tiled store shared -> global (bulk-group completion); out-of-range rows
 // and columns of the box are not written.
 MDLC_DEV void tma_store_2d(const void* tmap, int32_t x, int32_t y, uint32_t src) {
@@ -171,6 +191,16 @@ MDLC_DEV void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;
 MDLC_DEV uint64_t umma_desc_sw128(uint32_t saddr) {
   return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) |
          ((uint64_t)(1024 >> 4) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
+}
+
+// 128-byte swizzled K-major operand whose 8-row groups are sbo_bytes apart
+// (a multiple of 1024, so every group starts at the same swizzle phase). The
+// start may sit at any 128-byte row inside the swizzle atom: the swizzle is a
+// function of the shared-memory address bits, which the tensor memory
+// accelerator used when it wrote the rows.
+MDLC_DEV uint64_t umma_desc_sw128_sbo(uint32_t saddr, uint32_t sbo_bytes) {
+  return (uint64_t)((saddr >> 4) & 0x3FFFu) | ((uint64_t)1 << 16) |
+         ((uint64_t)((sbo_bytes >> 4) & 0x3FFFu) << 32) | ((uint64_t)1 << 46) | ((uint64_t)2 << 61);
 }
 
 // Same for the narrower K-major swizzles: layout 6 = SWIZZLE_32B (8 rows x

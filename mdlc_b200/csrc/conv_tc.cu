@@ -42,6 +42,23 @@ constexpr int kThreads = 320;
 constexpr int kBM = 128;
 constexpr int kABytes = kBM * 128;  // one A stage: 128 rows x 128 bytes
 
+// Halo mode (AMODE 4, stride-1 convs): a tile is kHaloTH output rows x
+// kHaloTW output columns of one image (M = 128). For each channel block the
+// padded input band of the tile -- (kHaloTH + r - 1) rows of kHaloSlots
+// pixel slots of P bytes (P = 32 or 64: the whole pixel, 32/64-byte swizzle;
+// P = 128: one 128-byte channel block, 128-byte swizzle) -- is loaded by ONE
+// tiled TMA and every filter tap (ty, tx) reads it in place: A row (oy, ox) of
+// tap (ty, tx) is band pixel (oy + ty, ox + tx), i.e. the operand starts at
+// band row ty, column tx, with 8-row groups (one output row each)
+// kHaloSlots * P bytes apart (a multiple of the swizzle repeat, 8 * P). Each
+// input byte crosses into shared memory once per tile instead of once per tap.
+constexpr int kHaloTW = 8, kHaloTH = 16, kHaloSlots = 16, kHaloMaxR = 5;
+constexpr int kHaloRowBytes = kHaloSlots * 128;  // band row stride at P = 128
+constexpr int kHaloBytes = (kHaloTH + kHaloMaxR - 1) * kHaloRowBytes;
+constexpr int kHaloStages = 2;
+static_assert(kHaloTW * kHaloTH == kBM, "a halo tile is one M tile");
+static_assert(kHaloSlots % 8 == 0, "band rows must keep the swizzle phase");
+
 struct TcArgs {
   const uint8_t* x;
   void* y;
@@ -63,13 +80,15 @@ struct TcArgs {
   const float* deq_bias;
   unsigned long long wait_cycles;
   int tma_epi;  // bf16 / 8-bit output staged in shared memory and written by TMA stores
+  int tiles_x, tiles_y, halo_rows, cpb;  // halo mode: tile grid per image, band rows, channel blocks
+  int band_px;                           // halo mode: bytes per band pixel slot (32, 64 or 128)
 };
 
-template <int BN, int STAGES, int ESZ>
+template <int BN, int STAGES, int ESZ, int AMODE>
 struct Smem {
   static constexpr int kBBytes = BN * 128;
   static constexpr int kA = 0;
-  static constexpr int kB = STAGES * kABytes;
+  static constexpr int kB = AMODE == 4 ? kHaloStages * kHaloBytes : STAGES * kABytes;
   // epilogue staging: 4 warps x 2 buffers x (32 rows x 64 columns), rows of
   // 128 bytes (bf16, 128-byte swizzle) or 64 bytes (8-bit, 64-byte swizzle)
   static constexpr int kEBuf = 32 * 64 * ESZ;
@@ -79,8 +98,9 @@ struct Smem {
   static constexpr int kParamWords = ESZ == 2 ? 1 : 2;
   static constexpr int kBias = kE + 4 * 2 * kEBuf;
   static constexpr int kBar = kBias + 2 * kParamWords * BN * 4;
-  // barriers: fullA[S], fullB[S], empty[S], tfull[2], tempty[2], drain, resid[4 warps][2 buffers]
-  static constexpr int kNumBars = 3 * STAGES + 13;
+  // barriers: fullA[S], fullB[S], empty[S], tfull[2], tempty[2], drain, resid[4 warps][2 buffers],
+  // band full[2], band empty[2]
+  static constexpr int kNumBars = 3 * STAGES + 13 + 2 * kHaloStages;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 16;
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
@@ -208,7 +228,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_y,
                    const __grid_constant__ CUtensorMap tmap_r, const __grid_constant__ CUtensorMap tmap_x,
                    const TcArgs a) {
-  using L = Smem<BN, STAGES, ESZ>;
+  using L = Smem<BN, STAGES, ESZ, AMODE>;
   constexpr int KB = 128 / ESZ;    // k-block elements (128 bytes)
   constexpr int CHUNK = 16 / ESZ;  // elements per 16-byte chunk
   constexpr uint32_t kTmemCols = 2 * BN;
@@ -224,13 +244,24 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto tempty = [&](int i) { return sbar + 8u * (3 * STAGES + 2 + i); };
   const uint32_t drain = sbar + 8u * (3 * STAGES + 4);
   auto resid = [&](int w, int b) { return sbar + 8u * (3 * STAGES + 5 + 2 * w + b); };
+  auto hfull = [&](int i) { return sbar + 8u * (3 * STAGES + 13 + i); };
+  auto hempty = [&](int i) { return sbar + 8u * (3 * STAGES + 13 + kHaloStages + i); };
+  // halo mode: tile -> (image, tile row, tile column)
+  auto halo_tile = [&](int mt, int& img, int& ty, int& tx) {
+    tx = mt % a.tiles_x;
+    const int t = mt / a.tiles_x;
+    ty = t % a.tiles_y;
+    img = t / a.tiles_y;
+  };
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
     for (int i = 0; i < STAGES; ++i) {
-      mbar_init(fullA(i), AMODE ? 1 : 128);
+      // A arrives from 128 gathering threads (AMODE 0), from one TMA issuer per
+      // k-block (AMODE 1) or from one issuer per tap of the k-block (AMODE 2 / 3)
+      mbar_init(fullA(i), AMODE == 0 ? 128 : (AMODE == 2 ? 4 : (AMODE == 3 ? 2 : 1)));
       mbar_init(fullB(i), 1);
       mbar_init(empty(i), 1);
     }
@@ -242,6 +273,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int i = 0; i < 4; ++i) {
       mbar_init(resid(i, 0), 1);
       mbar_init(resid(i, 1), 1);
+    }
+    for (int i = 0; i < kHaloStages; ++i) {
+      mbar_init(hfull(i), 1);
+      mbar_init(hempty(i), 1);
     }
     *abort_flag = 0;
     fence_mbar_init();
@@ -322,6 +357,64 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     cp_async_wait_all();
+  } else if (warp < 4 && AMODE >= 1 && AMODE <= 3) {
+    // ---------------- A producers (TMA), lane 0 of warps 0-3. Each issuing
+    // thread sustains about one TMA load per few hundred cycles, so the loads
+    // are spread: AMODE 1 deals stages to warps (stage st belongs to warp
+    // st % min(4, STAGES), so every use of a stage is issued -- and its empty
+    // barrier awaited -- by one thread in order, which the parity waits need);
+    // AMODE 2 / 3 (4 / 2 taps per k-block) give warp j tap j of every k-block.
+    constexpr int TPB = AMODE == 2 ? 4 : (AMODE == 3 ? 2 : 1);
+    constexpr int kAIssuers = AMODE == 1 ? (STAGES < 4 ? STAGES : 4) : TPB;
+    if (lane == 0 && warp < kAIssuers) {
+      constexpr uint32_t kTapBytes = kABytes / TPB;
+      int it = 0, last = -1;
+      bool ok = true;
+      const int cpb = a.cs / KB;  // k-blocks per filter tap (AMODE 1: cs % KB == 0)
+      const int ohw = a.oh * a.ow;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int m0 = (tile / a.num_n_tiles) * kBM;
+        const int xn = m0 / ohw;
+        const int rem = m0 - xn * ohw;
+        const int oy = rem / a.ow;
+        const int xh = oy * a.sh - a.pt;
+        const int xw = (rem - oy * a.ow) * a.sw - a.pl;
+        for (int kb = 0; kb < a.num_kb; ++kb, ++it) {
+          if (AMODE == 1 && (it % STAGES) % kAIssuers != warp) continue;
+          const int st = it % STAGES;
+          if (!mbar_wait(empty(st), ((it / STAGES) & 1) ^ 1, abort_flag, a.err, a.wait_cycles)) {
+            ok = false;
+            break;
+          }
+          if (AMODE == 1) {
+            const int tap = kb / cpb;
+            const int c0 = (kb - tap * cpb) * KB;
+            const int rr = tap / a.s;
+            mbar_arrive_expect_tx(fullA(st), kABytes);
+            tma_load_im2col_4d(sA + st * kABytes, &tmap_x, c0, xw, xh, xn, (uint16_t)((tap - rr * a.s) * a.dw),
+                               (uint16_t)(rr * a.dh), fullA(st));
+          } else {
+            // AMODE 2: 32-byte pixels (bf16 cs 16 / int8 cs 32); AMODE 3: 64-byte
+            // pixels (bf16 cs 32 / int8 cs 64). Taps past the end of the filter
+            // re-load tap 0: their weights are zero, so finite data adds nothing.
+            const int tap = kb * TPB + warp;
+            const int rr = tap / a.s;
+            const bool real = tap < RS;
+            mbar_arrive_expect_tx(fullA(st), kTapBytes);
+            tma_load_im2col_4d(sA + st * kABytes + warp * kTapBytes, &tmap_x, 0, xw, xh, xn,
+                               (uint16_t)(real ? (tap - rr * a.s) * a.dw : 0), (uint16_t)(real ? rr * a.dh : 0),
+                               fullA(st));
+          }
+          last = it;
+        }
+      }
+      if (!ok) {
+        // let this thread's loads land before the CTA's shared memory is released
+        for (int q = last; q >= 0 && q > last - STAGES; --q)
+          if (AMODE != 1 || (q % STAGES) % kAIssuers == warp)
+            mbar_wait(fullA(q % STAGES), (q / STAGES) & 1, nullptr, a.err, 2000000ull);
+      }
+    }
   } else if (warp >= 4 && warp < 8) {
     // ---------------- epilogue
     const int ew = warp - 4;
@@ -333,10 +426,26 @@ __global__ void __launch_bounds__(kThreads, 1)
     const bool tma_epi = a.tma_epi;
     int local = 0, chunk_i = 0;
     uint32_t res_use0 = 0, res_use1 = 0;  // completed loads per residual buffer (phase parity)
+    int res_pending = -1;                 // residual buffer with a load in flight not yet awaited
+    uint32_t res_pending_par = 0;
     for (int tile = blockIdx.x; tile < num_tiles; tile += gridDim.x, ++local) {
       const int buf = local & 1;
       const int m0 = (tile / a.num_n_tiles) * kBM;
       const int n0 = (tile % a.num_n_tiles) * BN;
+      // this warp's 32 rows of the output tile, as 2-D (pixel row) or halo-mode
+      // 4-D (channel, column, row, image) TMA coordinates
+      int hx = 0, hy = 0, himg = 0;
+      if constexpr (AMODE == 4) {
+        halo_tile(tile / a.num_n_tiles, himg, hy, hx);
+        hx *= kHaloTW;
+        hy = hy * kHaloTH + ew * (32 / kHaloTW);
+      }
+      auto load_res = [&](uint32_t dst, int c, uint32_t bar) {
+        if constexpr (AMODE == 4)
+          tma_load_4d(dst, &tmap_r, c, hx, hy, himg, bar);
+        else
+          tma_load_2d(dst, &tmap_r, c, m0 + ew * 32, bar);
+      };
       float* sbias = reinterpret_cast<float*>(smem + L::kBias) + buf * BN;
       int32_t* sq = reinterpret_cast<int32_t*>(smem + L::kBias) + buf * 2 * BN;  // 8-bit: bias32 | scale
       if (tma_epi) {
@@ -351,11 +460,15 @@ __global__ void __launch_bounds__(kThreads, 1)
             sq[BN + i] = v ? __float_as_int(__ldg(a.rq_scale + n0 + i)) : 0;
           }
         }
-        if (a.res && lane == 0) {
-          bulk_wait_read<0>();
+        if (a.res) {
           const int sbuf = chunk_i & 1;
-          mbar_arrive_expect_tx(resid(ew, sbuf), kEBuf);
-          tma_load_2d(stage0 + sbuf * kEBuf, &tmap_r, n0, m0 + ew * 32, resid(ew, sbuf));
+          if (lane == 0) {
+            bulk_wait_read<0>();
+            mbar_arrive_expect_tx(resid(ew, sbuf), kEBuf);
+            load_res(stage0 + sbuf * kEBuf, n0, resid(ew, sbuf));
+          }
+          res_pending = sbuf;
+          res_pending_par = (sbuf ? res_use1 : res_use0) & 1;
         }
         asm volatile("bar.sync 1, 128;" ::: "memory");
       }
@@ -383,11 +496,16 @@ __global__ void __launch_bounds__(kThreads, 1)
               ok = false;
               break;
             }
-            if (c0 + 64 < BN && n0 + c0 + 64 < a.ks && lane == 0) {
+            res_pending = -1;
+            if (c0 + 64 < BN && n0 + c0 + 64 < a.ks) {
               // prefetch the next residual chunk into the other buffer once its store has read it
-              bulk_wait_read<0>();
-              mbar_arrive_expect_tx(resid(ew, sbuf ^ 1), kEBuf);
-              tma_load_2d(stage0 + (sbuf ^ 1) * kEBuf, &tmap_r, n0 + c0 + 64, m0 + ew * 32, resid(ew, sbuf ^ 1));
+              if (lane == 0) {
+                bulk_wait_read<0>();
+                mbar_arrive_expect_tx(resid(ew, sbuf ^ 1), kEBuf);
+                load_res(stage0 + (sbuf ^ 1) * kEBuf, n0 + c0 + 64, resid(ew, sbuf ^ 1));
+              }
+              res_pending = sbuf ^ 1;
+              res_pending_par = (sbuf ^ 1 ? res_use1 : res_use0) & 1;
             }
           } else {
             if (lane == 0) bulk_wait_read<1>();  // the store issued two chunks ago has read this buffer
@@ -448,7 +566,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           fence_proxy_async_smem();
           __syncwarp();
           if (lane == 0) {
-            tma_store_2d(&tmap_y, n0 + c0, m0 + ew * 32, sb);
+            if constexpr (AMODE == 4)
+              tma_store_4d(&tmap_y, n0 + c0, hx, hy, himg, sb);
+            else
+              tma_store_2d(&tmap_y, n0 + c0, m0 + ew * 32, sb);
             bulk_commit();
           }
           ++chunk_i;
@@ -467,55 +588,63 @@ __global__ void __launch_bounds__(kThreads, 1)
       tc_fence_before();
       mbar_arrive(tempty(buf));
     }
+    // a residual load still in flight (the loop was left on an abort) must land
+    // before the CTA's shared memory is released
+    if (res_pending >= 0 && lane == 0)
+      mbar_wait(resid(ew, res_pending), res_pending_par, nullptr, a.err, 2000000ull);
     if (lane == 0) bulk_wait<0>();
   } else if (warp == 8) {
-    // ---------------- B producer (TMA); with AMODE 1 also the A operand by im2col TMA
-    if (lane == 0) {
-      int it = 0;
+    // ---------------- B producer (TMA); with AMODE >= 1 also the A operand by TMA
+    if (lane == 0 && AMODE == 4) {
+      // halo mode: one band per (tile, channel block), then the weights of every tap
+      int it = 0, hit = 0;
       bool ok = true;
-      const int cpb = a.cs / KB;  // k-blocks per filter tap (AMODE 1: cs % KB == 0)
-      const int ohw = a.oh * a.ow;
+      const uint32_t band_bytes = (uint32_t)a.halo_rows * kHaloSlots * a.band_px;
+      // k-blocks per band: one per tap (128-byte channel blocks, weight k-block
+      // tap * cpb + cb), or every k-block of the filter (whole-pixel bands)
+      const int kpb = a.band_px == 128 ? RS : a.num_kb;
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         const int n0 = (tile % a.num_n_tiles) * BN;
-        int xw = 0, xh = 0, xn = 0;
-        if (AMODE) {
-          const int m0 = (tile / a.num_n_tiles) * kBM;
-          xn = m0 / ohw;
-          const int rem = m0 - xn * ohw;
-          const int oy = rem / a.ow;
-          xh = oy * a.sh - a.pt;
-          xw = (rem - oy * a.ow) * a.sw - a.pl;
+        int img, ty, tx;
+        halo_tile(tile / a.num_n_tiles, img, ty, tx);
+        for (int cb = 0; cb < a.cpb && ok; ++cb, ++hit) {
+          const int hs = hit % kHaloStages;
+          if (!mbar_wait(hempty(hs), ((hit / kHaloStages) & 1) ^ 1, abort_flag, a.err, a.wait_cycles)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(hfull(hs), band_bytes);
+          tma_load_4d(sA + hs * kHaloBytes, &tmap_x, cb * KB, tx * kHaloTW - a.pl, ty * kHaloTH - a.pt, img,
+                      hfull(hs));
+          for (int j = 0; j < kpb; ++j, ++it) {
+            const int st = it % STAGES;
+            if (!mbar_wait(empty(st), ((it / STAGES) & 1) ^ 1, abort_flag, a.err, a.wait_cycles)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(fullB(st), L::kBBytes);
+            tma_load_2d(sB + st * L::kBBytes, &tmap_w, (a.band_px == 128 ? j * a.cpb + cb : j) * KB, n0, fullB(st));
+          }
         }
+      }
+      if (!ok) {
+        // let the loads already issued land before the CTA's shared memory is released
+        for (int q = it - 1; q >= 0 && q >= it - STAGES; --q)
+          mbar_wait(fullB(q % STAGES), (q / STAGES) & 1, nullptr, a.err, 2000000ull);
+        for (int q = hit - 1; q >= 0 && q >= hit - kHaloStages; --q)
+          mbar_wait(hfull(q % kHaloStages), (q / kHaloStages) & 1, nullptr, a.err, 2000000ull);
+      }
+    } else if (lane == 0) {
+      // weights only: the A operand comes from warps 0-3 (gather or TMA)
+      int it = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int n0 = (tile % a.num_n_tiles) * BN;
         for (int kb = 0; kb < a.num_kb; ++kb, ++it) {
           const int st = it % STAGES;
           if (!mbar_wait(empty(st), ((it / STAGES) & 1) ^ 1, abort_flag, a.err, a.wait_cycles)) {
             ok = false;
             break;
-          }
-          if (AMODE == 1) {
-            const int tap = kb / cpb;
-            const int c0 = (kb - tap * cpb) * KB;
-            const int rr = tap / a.s;
-            mbar_arrive_expect_tx(fullA(st), kABytes);
-            tma_load_im2col_4d(sA + st * kABytes, &tmap_x, c0, xw, xh, xn, (uint16_t)((tap - rr * a.s) * a.dw),
-                               (uint16_t)(rr * a.dh), fullA(st));
-          } else if (AMODE >= 2) {
-            // AMODE 2: 32-byte pixels (bf16 cs 16 / int8 cs 32), 4 taps per k-block;
-            // AMODE 3: 64-byte pixels (bf16 cs 32 / int8 cs 64), 2 taps per k-block
-            constexpr int TPB = AMODE == 2 ? 4 : 2;
-            constexpr uint32_t kTapBytes = kABytes / TPB;
-            mbar_arrive_expect_tx(fullA(st), kABytes);
-#pragma unroll
-            for (int j = 0; j < TPB; ++j) {
-              const int tap = kb * TPB + j;
-              const int rr = tap / a.s;
-              // taps past the end of the filter re-load tap 0: their weights are zero,
-              // so any finite data contributes nothing
-              const bool real = tap < RS;
-              tma_load_im2col_4d(sA + st * kABytes + j * kTapBytes, &tmap_x, 0, xw, xh, xn,
-                                 (uint16_t)(real ? (tap - rr * a.s) * a.dw : 0), (uint16_t)(real ? rr * a.dh : 0),
-                                 fullA(st));
-            }
           }
           mbar_arrive_expect_tx(fullB(st), L::kBBytes);
           tma_load_2d(sB + st * L::kBBytes, &tmap_w, kb * KB, n0, fullB(st));
@@ -523,15 +652,70 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       if (!ok) {
         // let the loads already issued land before the CTA's shared memory is released
-        for (int q = it - 1; q >= 0 && q >= it - STAGES; --q) {
+        for (int q = it - 1; q >= 0 && q >= it - STAGES; --q)
           mbar_wait(fullB(q % STAGES), (q / STAGES) & 1, nullptr, a.err, 2000000ull);
-          if (AMODE) mbar_wait(fullA(q % STAGES), (q / STAGES) & 1, nullptr, a.err, 2000000ull);
-        }
       }
     }
   } else if (warp == 9) {
     // ---------------- MMA issuer (warps 0-3 idle here when A arrives by TMA)
-    if (lane == 0) {
+    if (lane == 0 && AMODE == 4) {
+      const uint32_t idesc = ESZ == 2 ? idesc_bf16(kBM, BN) : idesc_i8(kBM, BN, a.a_signed, 1);
+      int it = 0, hit = 0, local = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+        const int buf = local & 1;
+        if (!mbar_wait(tempty(buf), ((local >> 1) & 1) ^ 1, abort_flag, a.err, a.wait_cycles)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(buf * BN);
+        for (int cb = 0; cb < a.cpb && ok; ++cb, ++hit) {
+          const int hs = hit % kHaloStages;
+          if (!mbar_wait(hfull(hs), (hit / kHaloStages) & 1, abort_flag, a.err, a.wait_cycles)) {
+            ok = false;
+            break;
+          }
+          const uint32_t band = sA + hs * kHaloBytes;
+          const int P = a.band_px;
+          const int kpb = P == 128 ? RS : a.num_kb;
+          const uint32_t sbo = (uint32_t)(kHaloSlots * P);
+          const uint32_t layout = P == 32 ? 6u : (P == 64 ? 4u : 2u);
+          for (int j = 0; j < kpb; ++j, ++it) {
+            const int st = it % STAGES;
+            if (!mbar_wait(fullB(st), (it / STAGES) & 1, abort_flag, a.err, a.wait_cycles)) {
+              ok = false;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t bb = sB + st * L::kBBytes;
+#pragma unroll
+            for (int kq = 0; kq < 4; ++kq) {
+              // the 32 K bytes of this MMA: tap and byte offset inside the band pixel;
+              // taps past the end of the filter have zero weights and re-read tap 0
+              const int kbyte = P == 128 ? j * P + kq * 32 : (j * 4 + kq) * 32;
+              int tap = kbyte / P;
+              if (tap >= RS) tap = 0;
+              const int ty = tap / a.s, tx = tap - ty * a.s;
+              const uint32_t a0 = band + (uint32_t)(ty * kHaloSlots + tx) * (uint32_t)P + (uint32_t)(kbyte % P);
+              const uint64_t ad = umma_desc_k(a0, sbo, layout);
+              const uint64_t bd = umma_desc_sw128(bb + kq * 32);
+              if constexpr (ESZ == 2)
+                umma_bf16(d, ad, bd, idesc, (cb | j | kq) != 0);
+              else
+                umma_i8(d, ad, bd, idesc, (cb | j | kq) != 0);
+            }
+            umma_commit(empty(st));
+          }
+          if (ok) umma_commit(hempty(hs));  // the band is free once its MMAs have read it
+        }
+        if (ok) umma_commit(tfull(buf));
+      }
+      if (!ok) {
+        umma_commit(drain);
+        mbar_wait(drain, 0, nullptr, a.err, 1000000ull);
+      }
+    } else if (lane == 0) {
       const uint32_t idesc = ESZ == 2 ? idesc_bf16(kBM, BN) : idesc_i8(kBM, BN, a.a_signed, 1);
       int it = 0, local = 0;
       bool ok = true;
@@ -666,7 +850,7 @@ int encode_im2col(CUtensorMap* m, const mdlc_conv_desc& d, const void* x, int es
 template <int BN, int STAGES, int ESZ, int ACT, int AMODE>
 int launch_tc(mdlc_ctx* ctx, const CUtensorMap& tmap, const CUtensorMap& tmap_y, const CUtensorMap& tmap_r,
               const CUtensorMap& tmap_x, const TcArgs& args) {
-  using L = Smem<BN, STAGES, ESZ>;
+  using L = Smem<BN, STAGES, ESZ, AMODE>;
   static_assert(L::kAlloc <= 232448, "shared memory budget");
   auto kern = conv_tc_kernel<BN, STAGES, ESZ, ACT, AMODE>;
   static bool attr_set[64] = {};
@@ -694,9 +878,26 @@ int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w
   const long long M = (long long)d.n * d.oh * d.ow;
   if (M <= 0 || M > (1ll << 31) - 256) return mdlc_set_error(ctx, MDLC_ERR_INVALID, "conv: bad M=%lld", M);
 
+  // halo mode (AMODE 4): stride-1 convs with a TMA-stored output on images
+  // large enough that 16x8 tiles waste little, on request (flags bit 2): it
+  // moves fewer bytes, but the per-tap loads are not what bounds these layers
+  // on this part (single-CTA MMA rate and TMA issue rate are), so the per-tap
+  // modes are the default.
+  const bool out8 = d.out_type == MDLC_U8 || d.out_type == MDLC_S8;
+  const bool out_tma = (!int8 && d.out_type == MDLC_BF16) || (int8 && out8);
+  const int pixel_bytes = d.c_stride * esz;
+  const int band_px = pixel_bytes % 128 == 0 ? 128 : (pixel_bytes == 32 || pixel_bytes == 64 ? pixel_bytes : 0);
+  const bool halo = out_tma && band_px && d.stride_h == 1 && d.stride_w == 1 && d.dil_h == 1 && d.dil_w == 1 &&
+                    d.r * d.s > 1 && d.r <= kHaloMaxR && d.s <= kHaloSlots - kHaloTW + 1 && d.oh >= 14 &&
+                    d.ow >= 14 && (!int8 || d.in_zp == 0) && !(cfg && (cfg->flags & 3)) && cfg &&
+                    (cfg->flags & 4);
+  const int tiles_x = (d.ow + kHaloTW - 1) / kHaloTW, tiles_y = (d.oh + kHaloTH - 1) / kHaloTH;
+
   int bn = cfg && cfg->bn ? cfg->bn : 0;
   int stages = cfg && cfg->stages ? cfg->stages : 0;
-  const int num_m = (int)((M + kBM - 1) / kBM);
+  const long long num_m_ll = halo ? (long long)d.n * tiles_x * tiles_y : (M + kBM - 1) / kBM;
+  if (num_m_ll > (1ll << 30)) return mdlc_set_error(ctx, MDLC_ERR_INVALID, "conv: too many tiles");
+  const int num_m = (int)num_m_ll;
   if (!bn) {
     bn = d.k_stride > 128 ? 256 : (d.k_stride > 64 ? 128 : 64);
     // keep enough tiles in flight for the whole GPU
@@ -733,6 +934,10 @@ int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w
   a.M = (int)M;
   a.num_kb = num_kb;
   a.num_m_tiles = num_m;
+  a.tiles_x = tiles_x; a.tiles_y = tiles_y;
+  a.halo_rows = kHaloTH + d.r - 1;
+  a.band_px = band_px;
+  a.cpb = band_px == 128 ? pixel_bytes / 128 : 1;
   a.num_n_tiles = (d.k_stride + bn - 1) / bn;
   a.out_type = d.out_type;
   a.a_signed = d.in_type == MDLC_S8;
@@ -749,27 +954,54 @@ int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w
   // A operand: im2col-mode TMA when the layer qualifies (zero padding only, so
   // not for int8 inputs with a non-zero zero point), else the cp.async gather
   CUtensorMap tmap_x = tmap;
-  const int im2col = ((!int8 || d.in_zp == 0) && !(cfg && (cfg->flags & 1))) ? encode_im2col(&tmap_x, d, x, esz) : 0;
+  const auto dt = int8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  int amode = 0;
+  if (halo) {
+    // the input band of a tile: one channel block (band_px bytes) x kHaloSlots
+    // pixels x halo_rows rows of one image, swizzled at band_px bytes;
+    // out-of-image pixels read 0
+    const cuuint64_t gd[4] = {(cuuint64_t)d.c_stride, (cuuint64_t)d.w, (cuuint64_t)d.h, (cuuint64_t)d.n};
+    const cuuint64_t gs[3] = {(cuuint64_t)d.c_stride * esz, (cuuint64_t)d.w * d.c_stride * esz,
+                              (cuuint64_t)d.h * d.w * d.c_stride * esz};
+    const cuuint32_t bx[4] = {(cuuint32_t)(band_px / esz), (cuuint32_t)kHaloSlots, (cuuint32_t)a.halo_rows, 1};
+    const cuuint32_t es4[4] = {1, 1, 1, 1};
+    const auto bsw = band_px == 32 ? CU_TENSOR_MAP_SWIZZLE_32B
+                                   : (band_px == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B);
+    if (encode(&tmap_x, dt, 4, const_cast<void*>(x), gd, gs, bx, es4, CU_TENSOR_MAP_INTERLEAVE_NONE, bsw,
+               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return mdlc_set_error(ctx, MDLC_ERR_INVALID, "halo input tensor map encode failed");
+    amode = 4;
+  } else if ((!int8 || d.in_zp == 0) && !(cfg && (cfg->flags & 1))) {
+    amode = encode_im2col(&tmap_x, d, x, esz);
+  }
 
-  // bf16 output: the epilogue stages 32x64 tiles in shared memory and writes
-  // them with 2-D TMA stores; a residual is brought in by TMA loads of the
-  // same tile shape. Boxes hanging over M or k_stride are clipped by TMA.
+  // bf16 / 8-bit output: the epilogue stages 32x64 tiles in shared memory and
+  // writes them with TMA stores; a residual is brought in by TMA loads of the
+  // same tile shape. Boxes hanging over the tensor are clipped by TMA.
   CUtensorMap tmap_y = tmap, tmap_r = tmap;
-  const bool out8 = d.out_type == MDLC_U8 || d.out_type == MDLC_S8;
-  if ((!int8 && d.out_type == MDLC_BF16) || (int8 && out8)) {
+  if (out_tma) {
     // 32 rows x 64 columns: 128-byte rows with 128-byte swizzle (bf16), 64-byte
-    // rows with 64-byte swizzle (8-bit)
-    auto encode2d = [&](CUtensorMap* m, const void* base, int inner) {
+    // rows with 64-byte swizzle (8-bit). Halo mode addresses the same 32 rows
+    // as 4 output rows x 8 columns of one image (4-D box).
+    const auto swz = int8 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B;
+    auto encode_out = [&](CUtensorMap* m, const void* base, int inner) {
+      if (amode == 4) {
+        const cuuint64_t gd[4] = {(cuuint64_t)inner, (cuuint64_t)d.ow, (cuuint64_t)d.oh, (cuuint64_t)d.n};
+        const cuuint64_t gs[3] = {(cuuint64_t)inner * esz, (cuuint64_t)d.ow * inner * esz,
+                                  (cuuint64_t)d.oh * d.ow * inner * esz};
+        const cuuint32_t bx[4] = {64, (cuuint32_t)kHaloTW, (cuuint32_t)(32 / kHaloTW), 1};
+        const cuuint32_t es4[4] = {1, 1, 1, 1};
+        return encode(m, dt, 4, const_cast<void*>(base), gd, gs, bx, es4, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                      CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+      }
       const cuuint64_t gd[2] = {(cuuint64_t)inner, (cuuint64_t)M};
       const cuuint64_t gs[1] = {(cuuint64_t)inner * esz};
       const cuuint32_t bx[2] = {64, 32};
-      return encode(m, int8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
-                    const_cast<void*>(base), gd, gs, bx, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                    int8 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B,
+      return encode(m, dt, 2, const_cast<void*>(base), gd, gs, bx, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
                     CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     };
-    if (encode2d(&tmap_y, y, d.k_stride) != CUDA_SUCCESS ||
-        (res && encode2d(&tmap_r, res, a.res_s) != CUDA_SUCCESS))
+    if (encode_out(&tmap_y, y, d.k_stride) != CUDA_SUCCESS ||
+        (res && encode_out(&tmap_r, res, a.res_s) != CUDA_SUCCESS))
       return mdlc_set_error(ctx, MDLC_ERR_INVALID, "output/residual tensor map encode failed");
     a.tma_epi = 1;
   }
@@ -782,8 +1014,9 @@ int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w
                      (act == MDLC_ACT_NONE || act == MDLC_ACT_RELU || act == MDLC_ACT_CLIP ||
                       act == MDLC_ACT_GELU || act == MDLC_ACT_SIGMOID)) ? act : -1;
 #define MDLC_TC_LAUNCH(BN_, ST_, E_, A_)                                                      \
-  switch (im2col) {                                                                         \
+  switch (amode) {                                                                          \
     case 1: return launch_tc<BN_, ST_, E_, A_, 1>(ctx, tmap, tmap_y, tmap_r, tmap_x, a);    \
+    case 4: return launch_tc<BN_, ST_, E_, A_, 4>(ctx, tmap, tmap_y, tmap_r, tmap_x, a);    \
     case 2: if (BN_ <= 128) return launch_tc<BN_, ST_, E_, A_, 2>(ctx, tmap, tmap_y, tmap_r, tmap_x, a); break; \
     case 3: if (BN_ <= 128) return launch_tc<BN_, ST_, E_, A_, 3>(ctx, tmap, tmap_y, tmap_r, tmap_x, a); break; \
     default: break;                                                                         \

@@ -179,6 +179,44 @@ def test_conv_im2col_tma_matches_gather(ctx, case):
     np.testing.assert_array_equal(tma, gather)
 
 
+HALO_CASES = [
+    # n, c, h, w, k, r, pad   (stride 1, output >= 14x14: the halo-band main loop)
+    (4, 16, 40, 40, 64, 4, 2),       # 32-byte pixels (the space-to-depth stem shape)
+    (2, 32, 30, 26, 96, 3, 1),       # 64-byte pixels, ragged tiles
+    (2, 16, 20, 20, 32, 5, 2),       # 32-byte pixels, 25 taps: the last k-block half padding
+    (2, 64, 56, 56, 64, 3, 1),       # ResNet-18 layer1 (128-byte blocks on request)
+    (2, 64, 20, 30, 128, 3, 1),      # ragged tile grid (12 of 16 rows, 6 of 8 columns in the last tiles)
+    (1, 128, 28, 28, 128, 3, 1),     # two channel blocks per band
+    (1, 256, 14, 14, 256, 3, 1),     # four channel blocks, 256-wide tiles
+    (2, 64, 17, 15, 64, 5, 2),       # 5x5: the tallest band
+    (1, 64, 16, 18, 64, 3, 0),       # no padding
+]
+
+
+@pytest.mark.parametrize("case", HALO_CASES, ids=[str(c) for c in HALO_CASES])
+def test_conv_halo_band_matches_per_tap_paths(ctx, case):
+    """Stride-1 convs read each input band once and every tap from shared memory
+    (halo mode); the result matches the per-tap im2col-TMA and cp.async paths
+    (bit for bit with one channel block, where the accumulation order is the
+    same) and the oracle."""
+    n, c, h, w, k, r, pad = case
+    rng = np.random.default_rng(200 + sum(case))
+    x = rng.standard_normal((n, c, h, w)).astype(np.float32)
+    wt = (rng.standard_normal((k, c, r, r)) * np.sqrt(2.0 / (c * r * r))).astype(np.float32)
+    b = (rng.standard_normal(k) * 0.1).astype(np.float32)
+    oh, ow = h + 2 * pad - r + 1, w + 2 * pad - r + 1
+    res = rng.standard_normal((n, k, oh, ow)).astype(np.float32)
+    halo = run_conv(ctx, x, wt, b, pad=pad, act=L.ACT_RELU, res=res, flags=4)
+    per_tap = run_conv(ctx, x, wt, b, pad=pad, act=L.ACT_RELU, res=res, flags=2)
+    gather = run_conv(ctx, x, wt, b, pad=pad, act=L.ACT_RELU, res=res, flags=1)
+    want = oracle_conv(x, wt, b, pad=pad, act="Relu", res=res)
+    check(halo, want, 1e-2)
+    check(per_tap, want, 1e-2)
+    np.testing.assert_array_equal(per_tap, gather)
+    if c <= 64:   # one band per tile: same accumulation order as the per-tap loads
+        np.testing.assert_array_equal(halo, per_tap)
+
+
 @pytest.mark.parametrize("act,name", [(L.ACT_NONE, None), (L.ACT_CLIP, "Clip"), (L.ACT_SIGMOID, "Sigmoid"),
                                       (L.ACT_GELU, "Gelu"), (L.ACT_HARD_SWISH, "HardSwish"),
                                       (L.ACT_LEAKY_RELU, "LeakyRelu"), (L.ACT_TANH, "Tanh")])
