@@ -259,9 +259,11 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   if (tid == 0) {
     for (int i = 0; i < STAGES; ++i) {
-      // A arrives from 128 gathering threads (AMODE 0), from one TMA issuer per
-      // k-block (AMODE 1) or from one issuer per tap of the k-block (AMODE 2 / 3)
-      mbar_init(fullA(i), AMODE == 0 ? 128 : (AMODE == 2 ? 4 : (AMODE == 3 ? 2 : 1)));
+      // fullA completes a stage (A and B landed): A arrives from 128 gathering
+      // threads (AMODE 0), from one TMA issuer per k-block (AMODE 1) or from one
+      // issuer per tap of the k-block (AMODE 2 / 3); B adds one arrival. Halo
+      // mode signals B on fullB and the band on hfull instead.
+      mbar_init(fullA(i), AMODE == 4 ? 1 : 1 + (AMODE == 0 ? 128 : (AMODE == 2 ? 4 : (AMODE == 3 ? 2 : 1))));
       mbar_init(fullB(i), 1);
       mbar_init(empty(i), 1);
     }
@@ -646,14 +648,14 @@ __global__ void __launch_bounds__(kThreads, 1)
             ok = false;
             break;
           }
-          mbar_arrive_expect_tx(fullB(st), L::kBBytes);
-          tma_load_2d(sB + st * L::kBBytes, &tmap_w, kb * KB, n0, fullB(st));
+          mbar_arrive_expect_tx(fullA(st), L::kBBytes);
+          tma_load_2d(sB + st * L::kBBytes, &tmap_w, kb * KB, n0, fullA(st));
         }
       }
       if (!ok) {
         // let the loads already issued land before the CTA's shared memory is released
         for (int q = it - 1; q >= 0 && q >= it - STAGES; --q)
-          mbar_wait(fullB(q % STAGES), (q / STAGES) & 1, nullptr, a.err, 2000000ull);
+          mbar_wait(fullA(q % STAGES), (q / STAGES) & 1, nullptr, a.err, 2000000ull);
       }
     }
   } else if (warp == 9) {
@@ -687,7 +689,6 @@ __global__ void __launch_bounds__(kThreads, 1)
               ok = false;
               break;
             }
-            tc_fence_after();
             const uint32_t bb = sB + st * L::kBBytes;
 #pragma unroll
             for (int kq = 0; kq < 4; ++kq) {
@@ -730,15 +731,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         for (int kb = 0; kb < a.num_kb; ++kb, ++it) {
           const int st = it % STAGES;
           const uint32_t par = (it / STAGES) & 1;
-          if (!mbar_wait(fullB(st), par, abort_flag, a.err, a.wait_cycles) ||
-              !mbar_wait(fullA(st), par, abort_flag, a.err, a.wait_cycles)) {
+          if (!mbar_wait(fullA(st), par, abort_flag, a.err, a.wait_cycles)) {
             ok = false;
             break;
           }
-          // order the producers' generic-proxy cp.async writes before the
-          // async-proxy operand reads of tcgen05.mma
-          fence_proxy_async_smem();
-          tc_fence_after();
+          // cp.async writes A through the generic proxy: order them before the
+          // async-proxy operand reads of tcgen05.mma. TMA-written operands are
+          // ordered by the mbarrier completion itself.
+          if constexpr (AMODE == 0) {
+            fence_proxy_async_smem();
+            tc_fence_after();
+          }
           const uint32_t ab = sA + st * kABytes, bb = sB + st * L::kBBytes;
 #pragma unroll
           for (int kq = 0; kq < 4; ++kq) {
