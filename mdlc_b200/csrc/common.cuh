@@ -109,7 +109,7 @@ MDLC_DEV void cp_async_mbar_arrive_noinc(uint32_t bar) {
 MDLC_DEV void tma_prefetch_desc(const void* tmap) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(tmap)) : "memory");
 }
-// 2-D tiled load (no multicast) completing on an mbarrier transaction count.
+// 2-D tiled load into this CTA's shared memory, completing on an mbarrier transaction count.
 MDLC_DEV void tma_load_2d(uint32_t dst, const void* tmap, int32_t x, int32_t y, uint32_t bar) {
   asm volatile(
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
@@ -130,7 +130,7 @@ MDLC_DEV void tma_load_im2col_4d(uint32_t dst, const void* tmap, int32_t c, int3
       : "memory");
 }
 
-// 4-D tiled load (no multicast); coordinates may be negative or past the end
+// 4-D tiled load into this CTA's shared memory; coordinates may be negative or past the end
 // (those elements read as zero).
 MDLC_DEV void tma_load_4d(uint32_t dst, const void* tmap, int32_t c0, int32_t c1, int32_t c2, int32_t c3,
                           uint32_t bar) {
