@@ -196,6 +196,129 @@ __global__ void __launch_bounds__(256) conv_dw_kernel(const DwArgs a) {
   }
 }
 
+// Depthwise 3x3 (stride 1 or 2, dilation 1) over NHWC, 8 channels per
+// thread. Each thread owns one (image, output column, 8-channel group) and
+// walks a strip of kDwStrip output rows: the three input pixels of every input
+// row it needs sit in a register ring (consecutive output rows share two
+// (stride 1) or one (stride 2) of their three input rows), and the group's 72
+// weights stay in registers. An input pixel is read from the cache hierarchy
+// about three times instead of nine, a weight once per strip; at stride 1 the
+// next output row's new input row is loaded before the current row is
+// computed. Taps are summed in the same (row, column) order as conv_dw_kernel.
+constexpr int kDwStrip = 8;
+template <typename T>
+struct DwPix;
+template <>
+struct DwPix<__nv_bfloat16> {
+  uint4 v;
+  MDLC_DEV void load(const __nv_bfloat16* p) { v = __ldg(reinterpret_cast<const uint4*>(p)); }
+  MDLC_DEV void zero() { v = make_uint4(0, 0, 0, 0); }
+  MDLC_DEV void get(float (&f)[8]) const {
+    f[0] = bf16_lo(v.x); f[1] = bf16_hi(v.x); f[2] = bf16_lo(v.y); f[3] = bf16_hi(v.y);
+    f[4] = bf16_lo(v.z); f[5] = bf16_hi(v.z); f[6] = bf16_lo(v.w); f[7] = bf16_hi(v.w);
+  }
+};
+template <>
+struct DwPix<float> {
+  float4 a, b;
+  MDLC_DEV void load(const float* p) {
+    a = __ldg(reinterpret_cast<const float4*>(p));
+    b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+  }
+  MDLC_DEV void zero() { a = b = make_float4(0.f, 0.f, 0.f, 0.f); }
+  MDLC_DEV void get(float (&f)[8]) const {
+    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+  }
+};
+
+template <typename T, int SH>
+__global__ void __launch_bounds__(128) conv_dw3_kernel(const DwArgs a, int strips, int total) {
+  const int G = a.cs >> 3;
+  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += gridDim.x * blockDim.x) {
+    const int g = idx % G;
+    int t = idx / G;
+    const int ox = t % a.ow;
+    t /= a.ow;
+    const int strip = t % strips;
+    const int img = t / strips;
+    const int c0 = g * 8;
+    float w[9][8];
+#pragma unroll
+    for (int tap = 0; tap < 9; ++tap) Vec8<float>::load(a.w + tap * a.cs + c0, w[tap]);
+    float bias[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) bias[e] = a.bias ? __ldg(a.bias + c0 + e) : 0.0f;
+    const int iw0 = ox * a.sw - a.pl;
+    const bool cv0 = (unsigned)iw0 < (unsigned)a.w_, cv1 = (unsigned)(iw0 + 1) < (unsigned)a.w_,
+               cv2 = (unsigned)(iw0 + 2) < (unsigned)a.w_;
+    const T* xi = static_cast<const T*>(a.x) + (long long)img * a.h * a.w_ * a.cs + c0;
+    auto load_row = [&](int ih, DwPix<T> (&r)[3]) {
+      if ((unsigned)ih < (unsigned)a.h) {
+        const T* p = xi + ((long long)ih * a.w_ + iw0) * a.cs;
+        if (cv0) r[0].load(p); else r[0].zero();
+        if (cv1) r[1].load(p + a.cs); else r[1].zero();
+        if (cv2) r[2].load(p + 2 * a.cs); else r[2].zero();
+      } else {
+        r[0].zero(); r[1].zero(); r[2].zero();
+      }
+    };
+    auto accumulate = [&](const DwPix<T> (&r)[3], int row, float (&acc)[8]) {
+#pragma unroll
+      for (int s = 0; s < 3; ++s) {
+        float xv[8];
+        r[s].get(xv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] = fmaf(xv[e], w[row * 3 + s][e], acc[e]);
+      }
+    };
+    const int oy0 = strip * kDwStrip;
+    const int oy1 = min(oy0 + kDwStrip, a.oh);
+    int ih = oy0 * SH - a.pt;
+    // r0..r2: the current output row's input rows; n0 (stride 1): the next
+    // output row's new input row, loaded before the current row is computed so
+    // the load overlaps the arithmetic
+    DwPix<T> r0[3], r1[3], r2[3], n0[3];
+    load_row(ih, r0);
+    load_row(ih + 1, r1);
+    load_row(ih + 2, r2);
+    for (int oy = oy0; oy < oy1; ++oy) {
+      const bool more = oy + 1 < oy1;
+      if (SH == 1 && more) load_row(ih + 3, n0);
+      float acc[8];
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = bias[e];
+      accumulate(r0, 0, acc);
+      accumulate(r1, 1, acc);
+      accumulate(r2, 2, acc);
+      const long long m = ((long long)img * a.oh + oy) * a.ow + ox;
+      if (a.res) {
+        float rv[8];
+        Vec8<T>::load(static_cast<const T*>(a.res) + m * a.res_s + c0, rv);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) acc[e] += rv[e];
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) acc[e] = (c0 + e < a.c) ? apply_act(acc[e], a.act) : 0.0f;
+      Vec8<T>::store(static_cast<T*>(a.y) + m * a.cs + c0, acc);
+      if (more) {
+        if (SH == 1) {
+#pragma unroll
+          for (int s = 0; s < 3; ++s) { r0[s] = r1[s]; r1[s] = r2[s]; r2[s] = n0[s]; }
+          ih += 1;
+        } else {
+          // stride 2: the two new rows are loaded here (prefetching them costs more
+          // registers than it saves)
+#pragma unroll
+          for (int s = 0; s < 3; ++s) r0[s] = r2[s];
+          load_row(ih + 3, r1);
+          load_row(ih + 4, r2);
+          ih += 2;
+        }
+      }
+    }
+  }
+}
+
 ActParams act_of(const mdlc_epilogue* epi) {
   if (!epi) return ActParams{MDLC_ACT_NONE, 0.f, 0.f, -INFINITY, INFINITY};
   return ActParams{epi->act, epi->alpha, epi->beta, epi->clip_lo, epi->clip_hi};
@@ -279,6 +402,24 @@ int conv_dw(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const float* 
   a.oh = d.oh; a.ow = d.ow; a.res_s = d.res_stride ? d.res_stride : d.c_stride;
   a.total = (long long)d.n * d.oh * d.ow * (d.c_stride / 8);
   a.act = act_of(epi);
+  const int strips = (d.oh + kDwStrip - 1) / kDwStrip;
+  const long long strip_total = (long long)d.n * strips * d.ow * (d.c_stride / 8);
+  if (d.r == 3 && d.s == 3 && d.dil_h == 1 && d.dil_w == 1 && d.stride_h == d.stride_w &&
+      (d.stride_h == 1 || d.stride_h == 2) && strip_total < (1LL << 31)) {
+    long long blocks = (strip_total + 127) / 128;
+    const long long cap = (long long)ctx->num_sms * 32;
+    if (blocks > cap) blocks = cap;
+    const bool bf = d.in_type == MDLC_BF16;
+    if (d.stride_h == 1) {
+      if (bf) conv_dw3_kernel<__nv_bfloat16, 1><<<(unsigned)blocks, 128, 0, ctx->stream>>>(a, strips, (int)strip_total);
+      else conv_dw3_kernel<float, 1><<<(unsigned)blocks, 128, 0, ctx->stream>>>(a, strips, (int)strip_total);
+    } else {
+      if (bf) conv_dw3_kernel<__nv_bfloat16, 2><<<(unsigned)blocks, 128, 0, ctx->stream>>>(a, strips, (int)strip_total);
+      else conv_dw3_kernel<float, 2><<<(unsigned)blocks, 128, 0, ctx->stream>>>(a, strips, (int)strip_total);
+    }
+    mdlc_note_launch(ctx);
+    return mdlc_cuda_status(ctx, cudaGetLastError(), "conv_dw3 launch");
+  }
   long long blocks = (a.total + 255) / 256;
   const long long cap = (long long)ctx->num_sms * 16;
   if (blocks > cap) blocks = cap;

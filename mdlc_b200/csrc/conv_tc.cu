@@ -526,19 +526,30 @@ __global__ void __launch_bounds__(kThreads, 1)
               uint4 rr = make_uint4(0, 0, 0, 0);
               if (a.res) rr = *qp;
               const uint32_t rw[4] = {rr.x, rr.y, rr.z, rr.w};
+              // this group's 16 int32 biases and fp32 scales as 128-bit loads
+              const int col0 = c0 + 16 * q;
+              int32_t bq[16];
+              float sc[16];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const int4 bb = *reinterpret_cast<const int4*>(sq + col0 + 4 * j);
+                const float4 ss = *reinterpret_cast<const float4*>(sq + BN + col0 + 4 * j);
+                bq[4 * j] = bb.x; bq[4 * j + 1] = bb.y; bq[4 * j + 2] = bb.z; bq[4 * j + 3] = bb.w;
+                sc[4 * j] = ss.x; sc[4 * j + 1] = ss.y; sc[4 * j + 2] = ss.z; sc[4 * j + 3] = ss.w;
+              }
+              const bool full = n0 + col0 + 16 <= a.k;  // group-uniform: no pad columns
               uint32_t packed[4] = {0, 0, 0, 0};
 #pragma unroll
               for (int e = 0; e < 16; ++e) {
-                const int col = c0 + 16 * q + e;
-                const int32_t acc = (int32_t)v[16 * q + e] + sq[col];
-                float f = __fmul_rn((float)acc, __int_as_float(sq[BN + col]));
+                const int32_t acc = (int32_t)v[16 * q + e] + bq[e];
+                float f = __fmul_rn((float)acc, sc[e]);
                 if (a.res) {
                   const uint32_t byte = (rw[e >> 2] >> (8 * (e & 3))) & 0xFFu;
                   const int32_t rq = a.res_signed ? (int32_t)(int8_t)byte : (int32_t)byte;
                   f = __fadd_rn(f, __fmul_rn((float)(rq - a.res_zp), a.res_scale));
                 }
                 int32_t t = min(max(__float2int_rn(f), a.qlo), a.qhi) + a.out_zp;
-                if (n0 + col >= a.k) t = 0;
+                if (!full && n0 + col0 + e >= a.k) t = 0;
                 packed[e >> 2] |= ((uint32_t)t & 0xFFu) << (8 * (e & 3));
               }
               *qp = make_uint4(packed[0], packed[1], packed[2], packed[3]);

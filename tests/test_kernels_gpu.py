@@ -253,18 +253,33 @@ def test_conv_fp32_simt(ctx, case):
     np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4)   # FP32_REDUCTION tier
 
 
+DW_CASES = [
+    # n, c, h, w, r, stride, pad, residual   (3x3 dilation 1: the row-strip kernel; others generic)
+    (2, 96, 13, 12, 3, 1, 1, False),
+    (2, 96, 13, 12, 3, 2, 1, False),
+    (1, 40, 35, 9, 3, 2, 1, False),      # 3 strips, ragged channel groups
+    (2, 24, 20, 17, 3, 1, 0, True),      # no padding, residual
+    (2, 32, 11, 10, 5, 1, 2, False),     # 5x5: generic kernel
+]
+
+
 @pytest.mark.parametrize("dtype", ["bf16", "f32"])
-@pytest.mark.parametrize("stride", [1, 2])
-def test_depthwise(ctx, dtype, stride):
-    rng = np.random.default_rng(9)
-    c = 96
-    x = rng.standard_normal((2, c, 13, 12)).astype(np.float32)
-    wt = (rng.standard_normal((c, 1, 3, 3)) * 0.3).astype(np.float32)
+@pytest.mark.parametrize("case", DW_CASES, ids=[str(c) for c in DW_CASES])
+def test_depthwise(ctx, dtype, case):
+    n, c, h, w, r, stride, pad, with_res = case
+    rng = np.random.default_rng(9 + sum(case))
+    x = rng.standard_normal((n, c, h, w)).astype(np.float32)
+    wt = (rng.standard_normal((c, 1, r, r)) * 0.3).astype(np.float32)
     b = (rng.standard_normal(c) * 0.1).astype(np.float32)
-    got = run_conv(ctx, x, wt, b, stride=stride, pad=1, groups=c, dtype=dtype, act=L.ACT_CLIP)
+    oh, ow = (h + 2 * pad - r) // stride + 1, (w + 2 * pad - r) // stride + 1
+    res = rng.standard_normal((n, c, oh, ow)).astype(np.float32) if with_res else None
+    got = run_conv(ctx, x, wt, b, stride=stride, pad=pad, groups=c, dtype=dtype, act=L.ACT_CLIP, res=res)
     # depthwise weights are kept in fp32; only activations are bf16
     xr = oref.round_bf16(x) if dtype == "bf16" else x
-    want = oref.clip(oref.conv(xr, wt, b, strides=[stride] * 2, pads=[1] * 4, group=c), 0.0, 6.0)
+    y = oref.conv(xr, wt, b, strides=[stride] * 2, pads=[pad] * 4, group=c)
+    if res is not None:
+        y = y + (oref.round_bf16(res) if dtype == "bf16" else res)
+    want = oref.clip(y, 0.0, 6.0)
     if dtype == "bf16":
         check(got, want, 1e-2)
     else:
