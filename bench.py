@@ -19,8 +19,9 @@ Reported line (rank 0):
   (upload, forward, read-back in sequence);
 * ``roofline`` of the dominant kernel (the tcgen05 implicit-GEMM conv):
   algorithmic conv FLOPs per launch / average launch time, from CUDA events
-  recorded around every conv launch inside the timed region, against the
-  measured bf16 tensor peak in MEASURED_PEAKS.json;
+  recorded around every conv launch in a second timed pass of the same
+  forwards (the pass ``value`` is timed on carries no per-kernel events),
+  against the measured bf16 tensor peak in MEASURED_PEAKS.json;
 * ``cpu_baseline`` the NumPy oracle (same algorithm as the reference executor,
   single-threaded einsum) on a bounded sample of b=1 forwards.
 
@@ -52,6 +53,7 @@ WORKLOADS = {
     "resnet18_int8_b1024": ("resnet18", "int8", 1024),
     "resnet18_fp32_b256": ("resnet18", "fp32", 256),
     "mobilenetv2_bf16_b256": ("mobilenetv2", "bf16", 256),
+    "repvit_bf16_b256": ("repvit", "bf16", 256),
 }
 
 
@@ -118,23 +120,33 @@ def conv_traffic():
         return None
 
 
-def timed_steps(exe, steps, per_kernel=False):
-    """Issue `steps` forwards between CUDA events on the device stream. With
-    per_kernel, the first min(steps, 90) steps also record events around every
-    conv launch (event slots are finite); returns (total_ms, instrumented_ms,
-    conv_ms, conv_launches)."""
+def timed_steps(exe, steps):
+    """`steps` forwards issued back to back between two CUDA events on the
+    device stream (inputs resident); returns the elapsed ms."""
     dev = exe.devices[0]
     ctx = dev.ctx
+    ctx.event_record(0)
+    for _ in range(steps):
+        dev.issue_forward()
+    ctx.event_record(1)
+    ctx.sync()
+    return ctx.event_elapsed(0, 1)
+
+
+def conv_launch_times(exe, steps):
+    """A second timed pass of the same forwards with CUDA events recorded
+    around every conv launch (kept out of the region `value` is measured on,
+    since the extra event records cost the stream a little). Event slots are
+    finite, so at most ~2000 conv launches are instrumented. Returns
+    (pass_ms, conv_ms, conv_launches, forwards)."""
+    dev = exe.devices[0]
+    ctx = dev.ctx
+    per_fwd = sum(1 for c in dev.calls if c[0] == "conv")
+    steps = max(1, min(steps, (4000 // 2) // max(per_fwd, 1)))
     slot = 3
     conv_slots = []
-    inst_steps = min(steps, 90) if per_kernel else 0
     ctx.event_record(0)
-    for i in range(steps):
-        if i >= inst_steps:
-            if i == inst_steps and per_kernel:
-                ctx.event_record(2)
-            dev.issue_forward()
-            continue
+    for _ in range(steps):
         dev.issue_inputs()
         for c in dev.calls:
             if c[0] == "conv":
@@ -150,13 +162,9 @@ def timed_steps(exe, steps, per_kernel=False):
                 ctx.eltwise(c[1], c[2], c[3])
         dev.issue_outputs()
     ctx.event_record(1)
-    if per_kernel and inst_steps == steps:
-        ctx.event_record(2)
     ctx.sync()
-    total = ctx.event_elapsed(0, 1)
-    inst = ctx.event_elapsed(0, 2) if per_kernel else 0.0
     conv_ms = sum(ctx.event_elapsed(a, b) for a, b in conv_slots)
-    return total, inst, conv_ms, len(conv_slots)
+    return ctx.event_elapsed(0, 1), conv_ms, len(conv_slots), steps
 
 
 def g1_graph(model):
@@ -235,7 +243,7 @@ def run_reference_arm(args, rank, world):
     if rank != 0:
         return 0
     import multiprocessing as mp
-    cores = os.cpu_count() or 1
+    cores = args.ref_procs or os.cpu_count() or 1
     per_proc = 2
     total_imgs, wall = 0, []
     ctx = mp.get_context("spawn")
@@ -273,25 +281,17 @@ def main() -> int:
     ap.add_argument("--cpu-sample", type=int, default=12, help="b=1 oracle forwards for cpu_baseline")
     ap.add_argument("--workload", default=WORKLOAD, choices=sorted(WORKLOADS))
     ap.add_argument("--latency-iters", type=int, default=200, help="b=1 forwards for the p50 latency")
+    ap.add_argument("--ref-procs", type=int, default=0, help="reference arm: host processes (0 = every core)")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
 
-    rank = int(os.environ.get("RANK", "0"))
-    world = int(os.environ.get("WORLD_SIZE", "1"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    dist = None
-    if world > 1:
-        import datetime
-        import torch
-        import torch.distributed as dist
-        torch.cuda.set_device(local)
-        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
-                                device_id=torch.device("cuda", local))
+    from mdlc_b200 import dist as mdist
+    dist = mdist.from_env()
+    rank, world, local = dist.rank, dist.world, dist.local_rank
 
     if args.impl == "reference":
         rc = run_reference_arm(args, rank, world)
-        if dist is not None:
-            dist.destroy_process_group()
+        dist.close()
         return rc
 
     from mdlc_b200 import builders, passes
@@ -309,19 +309,7 @@ def main() -> int:
     exe.run_pinned()                       # stage the input once (resident for `value`)
     flops = conv_flops(exe)
 
-    def barrier():
-        if dist is not None:
-            import torch
-            torch.cuda.synchronize()
-            dist.barrier()
-
-    def max_over_ranks(v):
-        if dist is None:
-            return v
-        import torch
-        t = torch.tensor([v], dtype=torch.float64, device="cuda")
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        return float(t.item())
+    barrier, max_over_ranks = dist.barrier, dist.max
 
     # ---- warm-up
     for _ in range(args.warmup):
@@ -332,13 +320,18 @@ def main() -> int:
     barrier()
     sampler = ClockSampler(local) if rank == 0 else None
     launches0 = dev.ctx.launch_count()
-    total_ms, inst_ms, conv_ms, nconv = timed_steps(exe, args.steps, per_kernel=True)
+    total_ms = timed_steps(exe, args.steps)
     launches = dev.ctx.launch_count() - launches0
     clocks = sampler.stop() if sampler else None
     barrier()
     total_ms = max_over_ranks(total_ms)
     ms_per_step = total_ms / args.steps
     value = world * args.batch / (ms_per_step / 1e3)
+
+    # ---- per-kernel CUDA events for the roofline (a second timed pass)
+    barrier()
+    inst_ms, conv_ms, nconv, inst_steps = conv_launch_times(exe, args.steps)
+    barrier()
 
     # ---- e2e through the public host API: every step uploads its fp32 input
     # from pinned host memory and reads its logits back. Serial form: one
@@ -417,7 +410,9 @@ def main() -> int:
                          "traffic_unit": "bytes per launch (ncu dram read+write)",
                          "conv_share_of_step": round(conv_ms / inst_ms, 4) if inst_ms else None,
                          "flops_per_launch": round(conv_flops_step / len(flops)),
-                         "avg_launch_ms": round(avg_launch_ms, 5)},
+                         "avg_launch_ms": round(avg_launch_ms, 5),
+                         "how": f"CUDA events around each of the {nconv} conv launches of {inst_steps} "
+                                "forwards, in a timed pass after the one `value` is measured on"},
             "gpu_launches": launches,
             "network_tflops": round(world * conv_flops_step / (ms_per_step / 1e3) / 1e12, 1),
         }
@@ -427,9 +422,8 @@ def main() -> int:
             line["cpu_baseline"] = cpu
         print(json.dumps(line), flush=True)
     exe.close()
-    if dist is not None:
-        dist.barrier()
-        dist.destroy_process_group()
+    dist.barrier()
+    dist.close()
     return 0
 
 

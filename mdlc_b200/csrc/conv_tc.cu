@@ -538,17 +538,26 @@ __global__ void __launch_bounds__(kThreads, 1)
                 sc[4 * j] = ss.x; sc[4 * j + 1] = ss.y; sc[4 * j + 2] = ss.z; sc[4 * j + 3] = ss.w;
               }
               const bool full = n0 + col0 + 16 <= a.k;  // group-uniform: no pad columns
+              // exact small-integer <-> float conversions without the conversion
+              // unit: 1.5 * 2^23 in the exponent, value in the low mantissa bits
+              // (|x| < 2^22; round-to-nearest-even like __float2int_rn)
+              constexpr float kMagic = 12582912.0f;
+              constexpr int32_t kMagicBits = 0x4B400000;
+              const float qlo_f = (float)a.qlo, qhi_f = (float)a.qhi;
               uint32_t packed[4] = {0, 0, 0, 0};
 #pragma unroll
               for (int e = 0; e < 16; ++e) {
                 const int32_t acc = (int32_t)v[16 * q + e] + bq[e];
-                float f = __fmul_rn((float)acc, sc[e]);
+                float f = __fmul_rn(__int2float_rn(acc), sc[e]);
                 if (a.res) {
                   const uint32_t byte = (rw[e >> 2] >> (8 * (e & 3))) & 0xFFu;
                   const int32_t rq = a.res_signed ? (int32_t)(int8_t)byte : (int32_t)byte;
-                  f = __fadd_rn(f, __fmul_rn((float)(rq - a.res_zp), a.res_scale));
+                  const float rf = __fsub_rn(__int_as_float(rq - a.res_zp + kMagicBits), kMagic);
+                  f = __fadd_rn(f, __fmul_rn(rf, a.res_scale));
                 }
-                int32_t t = min(max(__float2int_rn(f), a.qlo), a.qhi) + a.out_zp;
+                // clamp then round == round then clamp (integer bounds)
+                f = fminf(fmaxf(f, qlo_f), qhi_f);
+                int32_t t = __float_as_int(__fadd_rn(f, kMagic)) - kMagicBits + a.out_zp;
                 if (!full && n0 + col0 + e >= a.k) t = 0;
                 packed[e >> 2] |= ((uint32_t)t & 0xFFu) << (8 * (e & 3));
               }

@@ -165,3 +165,26 @@ def test_double_buffered_submit_matches_run(dtype):
         exe.sync()
     finally:
         exe.close()
+
+
+@pytest.mark.parametrize("batch,image", [(2, 64), (1, 224)])
+def test_repvit_matches_oracle(batch, image):
+    """RepViT-style graph: GELU epilogues (the Erf
+    decomposition fused into the conv), squeeze-excite (global pool, two FCs,
+    broadcast multiply), folded depthwise mixers, ReduceMean head. The
+    reference executor has no Erf / ReduceMean, so the oracle's extension of it
+    is the parity target; bf16 is also held to the bf16-emulating oracle."""
+    g, feeds = _case("repvit", dict(batch=batch, image=image))
+    want = oref.run(g, feeds)["logits"]
+    emu = oref.run(g, feeds, bf16_emulation=True)["logits"]
+    scale = np.abs(want).max()
+    for dtype, rel in (("fp32", 1e-3), ("bf16", 3e-2)):
+        exe = compile(g, dtype=dtype)
+        assert exe.fallbacks() == []
+        got = exe.run(feeds)["logits"]
+        err = np.abs(got - want).max()
+        assert err <= rel * scale, f"{dtype}: max abs err {err:.4g} vs logit scale {scale:.4g}"
+        if dtype == "bf16":
+            err_e = np.abs(got - emu).max()
+            assert err_e <= 1e-2 * scale, f"bf16 vs bf16-emulating oracle: {err_e:.4g} (scale {scale:.4g})"
+        exe.close()
