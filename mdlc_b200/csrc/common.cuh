@@ -269,6 +269,68 @@ struct ActParams {
 
 MDLC_DEV float apply_act(float v, const ActParams& p);
 
+// GELU(x) = x * Phi(x) = 0.5 x (1 + erf(x / sqrt 2)), branch-free so the
+// independent elements of an epilogue chunk interleave (erff branches on |x|,
+// which left the epilogue one latency chain at a time). erfc(z), z >= 0, is the
+// Chebyshev-fitted erfcc of Numerical Recipes (Press et al., 2nd ed., sec. 6.2:
+// erfc(z) ~ t exp(-z^2 + P(t)), t = 1 / (1 + z / 2), fractional error < 1.2e-7);
+// then 1 + erf(z) = 2 - erfc(z) for x >= 0 and erfc(|z|) for x < 0.
+MDLC_DEV float gelu_f(float x) {
+  const float z = fabsf(x) * 0.70710678118654752f;
+  const float t = __fdividef(1.0f, fmaf(0.5f, z, 1.0f));
+  float p = fmaf(t, 0.17087277f, -0.82215223f);
+  p = fmaf(t, p, 1.48851587f);
+  p = fmaf(t, p, -1.13520398f);
+  p = fmaf(t, p, 0.27886807f);
+  p = fmaf(t, p, -0.18628806f);
+  p = fmaf(t, p, 0.09678418f);
+  p = fmaf(t, p, 0.37409196f);
+  p = fmaf(t, p, 1.00002368f);
+  p = fmaf(t, p, -1.26551223f);
+  const float e = t * __expf(fmaf(-z, z, p));
+  return 0.5f * x * (x >= 0.0f ? 2.0f - e : e);
+}
+
+// Eight elements at once, each stage of the formula applied to all eight
+// before the next, so the eight dependency chains interleave (one epilogue
+// warp per scheduler has no other warps to hide their latency).
+MDLC_DEV void gelu8(float (&x)[8]) {
+  float z[8], t[8], p[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) z[i] = fabsf(x[i]) * 0.70710678118654752f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) t[i] = __fdividef(1.0f, fmaf(0.5f, z[i], 1.0f));
+#pragma unroll
+  for (int i = 0; i < 8; ++i) p[i] = fmaf(t[i], 0.17087277f, -0.82215223f);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) p[i] = fmaf(t[i], p[i], 1.48851587f);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) p[i] = fmaf(t[i], p[i], -1.13520398f);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) p[i] = fmaf(t[i], p[i], 0.27886807f);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) p[i] = fmaf(t[i], p[i], -0.18628806f);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) p[i] = fmaf(t[i], p[i], 0.09678418f);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) p[i] = fmaf(t[i], p[i], 0.37409196f);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) p[i] = fmaf(t[i], p[i], 1.00002368f);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) p[i] = fmaf(t[i], p[i], -1.26551223f);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) p[i] = t[i] * __expf(fmaf(-z[i], z[i], p[i]));
+#pragma unroll
+  for (int i = 0; i < 8; ++i) x[i] = 0.5f * x[i] * (x[i] >= 0.0f ? 2.0f - p[i] : p[i]);
+}
+MDLC_DEV void sigmoid8(float (&x)[8]) {
+  float e[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) e[i] = expf(-x[i]);
+#pragma unroll
+  for (int i = 0; i < 8; ++i) x[i] = 1.0f / (1.0f + e[i]);
+}
+
 // Activation fixed at compile time (ACT >= 0) or chosen at run time (ACT == -1).
 // Fixing it keeps the unrolled epilogue small: every inlined copy of the
 // run-time switch carries the exp/tanh/erf paths.
@@ -278,7 +340,7 @@ MDLC_DEV float act_fn(float v, const ActParams& p) {
   else if constexpr (ACT == MDLC_ACT_NONE) return v;
   else if constexpr (ACT == MDLC_ACT_RELU) return fmaxf(v, 0.0f);
   else if constexpr (ACT == MDLC_ACT_CLIP) return fminf(fmaxf(v, p.lo), p.hi);
-  else if constexpr (ACT == MDLC_ACT_GELU) return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+  else if constexpr (ACT == MDLC_ACT_GELU) return gelu_f(v);
   else if constexpr (ACT == MDLC_ACT_SIGMOID) return 1.0f / (1.0f + expf(-v));
   else return apply_act(v, p);
 }
@@ -292,7 +354,7 @@ MDLC_DEV float apply_act(float v, const ActParams& p) {
     case MDLC_ACT_LEAKY_RELU: return v >= 0.0f ? v : p.alpha * v;
     case MDLC_ACT_HARD_SIGMOID: return fminf(fmaxf(p.alpha * v + p.beta, 0.0f), 1.0f);
     case MDLC_ACT_HARD_SWISH: return v * fminf(fmaxf(v / 6.0f + 0.5f, 0.0f), 1.0f);
-    case MDLC_ACT_GELU: return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+    case MDLC_ACT_GELU: return gelu_f(v);
     default: return v;
   }
 }

@@ -359,7 +359,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
     }
     cp_async_wait_all();
-  } else if (warp < 4 && AMODE >= 1 && AMODE <= 3) {
+  } else if (warp < 4 && ((AMODE >= 1 && AMODE <= 3) || AMODE == 5)) {
     // ---------------- A producers (TMA), lane 0 of warps 0-3. Each issuing
     // thread sustains about one TMA load per few hundred cycles, so the loads
     // are spread: AMODE 1 deals stages to warps (stage st belongs to warp
@@ -367,7 +367,8 @@ __global__ void __launch_bounds__(kThreads, 1)
     // barrier awaited -- by one thread in order, which the parity waits need);
     // AMODE 2 / 3 (4 / 2 taps per k-block) give warp j tap j of every k-block.
     constexpr int TPB = AMODE == 2 ? 4 : (AMODE == 3 ? 2 : 1);
-    constexpr int kAIssuers = AMODE == 1 ? (STAGES < 4 ? STAGES : 4) : TPB;
+    constexpr bool kWhole = AMODE == 1 || AMODE == 5;  // one load per k-block
+    constexpr int kAIssuers = kWhole ? (STAGES < 4 ? STAGES : 4) : TPB;
     if (lane == 0 && warp < kAIssuers) {
       constexpr uint32_t kTapBytes = kABytes / TPB;
       int it = 0, last = -1;
@@ -382,13 +383,17 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int xh = oy * a.sh - a.pt;
         const int xw = (rem - oy * a.ow) * a.sw - a.pl;
         for (int kb = 0; kb < a.num_kb; ++kb, ++it) {
-          if (AMODE == 1 && (it % STAGES) % kAIssuers != warp) continue;
+          if (kWhole && (it % STAGES) % kAIssuers != warp) continue;
           const int st = it % STAGES;
           if (!mbar_wait(empty(st), ((it / STAGES) & 1) ^ 1, abort_flag, a.err, a.wait_cycles)) {
             ok = false;
             break;
           }
-          if (AMODE == 1) {
+          if (AMODE == 5) {
+            // 1x1 / stride 1 / no padding: A is the [M, cs] activation matrix itself
+            mbar_arrive_expect_tx(fullA(st), kABytes);
+            tma_load_2d(sA + st * kABytes, &tmap_x, kb * KB, m0, fullA(st));
+          } else if (AMODE == 1) {
             const int tap = kb / cpb;
             const int c0 = (kb - tap * cpb) * KB;
             const int rr = tap / a.s;
@@ -413,7 +418,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!ok) {
         // let this thread's loads land before the CTA's shared memory is released
         for (int q = last; q >= 0 && q > last - STAGES; --q)
-          if (AMODE != 1 || (q % STAGES) % kAIssuers == warp)
+          if (!kWhole || (q % STAGES) % kAIssuers == warp)
             mbar_wait(fullA(q % STAGES), (q / STAGES) & 1, nullptr, a.err, 2000000ull);
       }
     }
@@ -513,12 +518,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) bulk_wait_read<1>();  // the store issued two chunks ago has read this buffer
           }
           __syncwarp();
+          // Cheap activations: the whole 64-column chunk is loaded and its eight
+          // 8-column groups unrolled. Expensive ones (GELU, sigmoid, the run-time
+          // switch) keep the loop rolled over 16-column loads, so the inlined
+          // activation is not copied 64 times into the instruction stream.
+          constexpr bool kHeavy =
+              ESZ == 2 && (ACT == MDLC_ACT_GELU || ACT == MDLC_ACT_SIGMOID || ACT == -1);
           uint32_t v[64];
-          tmem_ld16(taddr + c0, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
-          tmem_ld16(taddr + c0 + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
-          tmem_ld16(taddr + c0 + 32, *reinterpret_cast<uint32_t(*)[16]>(&v[32]));
-          tmem_ld16(taddr + c0 + 48, *reinterpret_cast<uint32_t(*)[16]>(&v[48]));
-          tmem_ld_wait();
+          if constexpr (!kHeavy) {
+            tmem_ld16(taddr + c0, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
+            tmem_ld16(taddr + c0 + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
+            tmem_ld16(taddr + c0 + 32, *reinterpret_cast<uint32_t(*)[16]>(&v[32]));
+            tmem_ld16(taddr + c0 + 48, *reinterpret_cast<uint32_t(*)[16]>(&v[48]));
+            tmem_ld_wait();
+          }
           if constexpr (ESZ == 1) {
 #pragma unroll
             for (int q = 0; q < 4; ++q) {  // 16-column (16-byte) groups
@@ -544,45 +557,84 @@ __global__ void __launch_bounds__(kThreads, 1)
               constexpr float kMagic = 12582912.0f;
               constexpr int32_t kMagicBits = 0x4B400000;
               const float qlo_f = (float)a.qlo, qhi_f = (float)a.qhi;
-              uint32_t packed[4] = {0, 0, 0, 0};
+              // each stage over all 16 elements before the next, so their
+              // dependency chains interleave
+              float f[16];
 #pragma unroll
-              for (int e = 0; e < 16; ++e) {
-                const int32_t acc = (int32_t)v[16 * q + e] + bq[e];
-                float f = __fmul_rn(__int2float_rn(acc), sc[e]);
-                if (a.res) {
+              for (int e = 0; e < 16; ++e) f[e] = __fmul_rn(__int2float_rn((int32_t)v[16 * q + e] + bq[e]), sc[e]);
+              if (a.res) {
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
                   const uint32_t byte = (rw[e >> 2] >> (8 * (e & 3))) & 0xFFu;
                   const int32_t rq = a.res_signed ? (int32_t)(int8_t)byte : (int32_t)byte;
                   const float rf = __fsub_rn(__int_as_float(rq - a.res_zp + kMagicBits), kMagic);
-                  f = __fadd_rn(f, __fmul_rn(rf, a.res_scale));
+                  f[e] = __fadd_rn(f[e], __fmul_rn(rf, a.res_scale));
                 }
-                // clamp then round == round then clamp (integer bounds)
-                f = fminf(fmaxf(f, qlo_f), qhi_f);
-                int32_t t = __float_as_int(__fadd_rn(f, kMagic)) - kMagicBits + a.out_zp;
-                if (!full && n0 + col0 + e >= a.k) t = 0;
-                packed[e >> 2] |= ((uint32_t)t & 0xFFu) << (8 * (e & 3));
               }
+              // clamp then round == round then clamp (integer bounds)
+              int32_t t[16];
+#pragma unroll
+              for (int e = 0; e < 16; ++e)
+                t[e] = __float_as_int(__fadd_rn(fminf(fmaxf(f[e], qlo_f), qhi_f), kMagic)) - kMagicBits + a.out_zp;
+              if (!full) {
+#pragma unroll
+                for (int e = 0; e < 16; ++e)
+                  if (n0 + col0 + e >= a.k) t[e] = 0;
+              }
+              uint32_t packed[4] = {0, 0, 0, 0};
+#pragma unroll
+              for (int e = 0; e < 16; ++e) packed[e >> 2] |= ((uint32_t)t[e] & 0xFFu) << (8 * (e & 3));
               *qp = make_uint4(packed[0], packed[1], packed[2], packed[3]);
             }
           } else {
-#pragma unroll
-          for (int q = 0; q < 8; ++q) {  // 8-column (16-byte) groups
+          // one 8-column (16-byte) group: + bias (+ residual), activation, bf16
+          auto group = [&](int q, const uint32_t* vv) {
             uint4* qp = reinterpret_cast<uint4*>(sp + ((q ^ sw) << 4));
             const float4 b0 = *reinterpret_cast<const float4*>(sbias + c0 + 8 * q);
             const float4 b1 = *reinterpret_cast<const float4*>(sbias + c0 + 8 * q + 4);
-            float f[8] = {__uint_as_float(v[8 * q]) + b0.x, __uint_as_float(v[8 * q + 1]) + b0.y,
-                          __uint_as_float(v[8 * q + 2]) + b0.z, __uint_as_float(v[8 * q + 3]) + b0.w,
-                          __uint_as_float(v[8 * q + 4]) + b1.x, __uint_as_float(v[8 * q + 5]) + b1.y,
-                          __uint_as_float(v[8 * q + 6]) + b1.z, __uint_as_float(v[8 * q + 7]) + b1.w};
+            float f[8] = {__uint_as_float(vv[0]) + b0.x, __uint_as_float(vv[1]) + b0.y,
+                          __uint_as_float(vv[2]) + b0.z, __uint_as_float(vv[3]) + b0.w,
+                          __uint_as_float(vv[4]) + b1.x, __uint_as_float(vv[5]) + b1.y,
+                          __uint_as_float(vv[6]) + b1.z, __uint_as_float(vv[7]) + b1.w};
             if (a.res) {
               const uint4 r = *qp;
               f[0] += bf16_lo(r.x); f[1] += bf16_hi(r.x); f[2] += bf16_lo(r.y); f[3] += bf16_hi(r.y);
               f[4] += bf16_lo(r.z); f[5] += bf16_hi(r.z); f[6] += bf16_lo(r.w); f[7] += bf16_hi(r.w);
             }
             const int nb0 = n0 + c0 + 8 * q;
+            if constexpr (ACT == MDLC_ACT_GELU) {
+              gelu8(f);
+            } else if constexpr (ACT == MDLC_ACT_SIGMOID) {
+              sigmoid8(f);
+            } else {
 #pragma unroll
-            for (int e = 0; e < 8; ++e) f[e] = (nb0 + e < a.k) ? act_fn<ACT>(f[e], a.act) : 0.0f;
+              for (int e = 0; e < 8; ++e) f[e] = act_fn<ACT>(f[e], a.act);
+            }
+#pragma unroll
+            for (int e = 0; e < 8; ++e) f[e] = (nb0 + e < a.k) ? f[e] : 0.0f;
             *qp = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
                              pack_bf16x2(f[6], f[7]));
+          };
+          if constexpr (kHeavy) {
+            // two 16-column register buffers: the next load is in flight while
+            // the current columns are computed
+            uint32_t va[16], vb[16];
+            tmem_ld16(taddr + c0, va);
+            tmem_ld_wait();
+#pragma unroll 1
+            for (int j = 0; j < 4; j += 2) {
+              tmem_ld16(taddr + c0 + 16 * (j + 1), vb);
+              group(2 * j, va);
+              group(2 * j + 1, va + 8);
+              tmem_ld_wait();
+              if (j + 2 < 4) tmem_ld16(taddr + c0 + 16 * (j + 2), va);
+              group(2 * j + 2, vb);
+              group(2 * j + 3, vb + 8);
+              tmem_ld_wait();
+            }
+          } else {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) group(q, v + 8 * q);
           }
           }
           fence_proxy_async_smem();
@@ -994,6 +1046,19 @@ int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w
                CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
       return mdlc_set_error(ctx, MDLC_ERR_INVALID, "halo input tensor map encode failed");
     amode = 4;
+  } else if (d.r == 1 && d.s == 1 && d.stride_h == 1 && d.stride_w == 1 && d.pad_t == 0 && d.pad_l == 0 &&
+             d.oh == d.h && d.ow == d.w && !(cfg && (cfg->flags & 1))) {
+    // pointwise conv / GEMM: A is the [M, cs] activation matrix; a 2-D tiled
+    // load fetches each 128-row x 128-byte k-block (channels past cs read 0,
+    // and no padding exists, so any input zero point is exact)
+    const cuuint64_t gd[2] = {(cuuint64_t)d.c_stride, (cuuint64_t)M};
+    const cuuint64_t gs[1] = {(cuuint64_t)d.c_stride * esz};
+    const cuuint32_t bx[2] = {(cuuint32_t)kb_elems, (cuuint32_t)kBM};
+    if (encode(&tmap_x, dt, 2, const_cast<void*>(x), gd, gs, bx, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+      return mdlc_set_error(ctx, MDLC_ERR_INVALID, "pointwise input tensor map encode failed");
+    amode = 5;
   } else if ((!int8 || d.in_zp == 0) && !(cfg && (cfg->flags & 1))) {
     amode = encode_im2col(&tmap_x, d, x, esz);
   }
@@ -1040,6 +1105,7 @@ int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w
   switch (amode) {                                                                          \
     case 1: return launch_tc<BN_, ST_, E_, A_, 1>(ctx, tmap, tmap_y, tmap_r, tmap_x, a);    \
     case 4: return launch_tc<BN_, ST_, E_, A_, 4>(ctx, tmap, tmap_y, tmap_r, tmap_x, a);    \
+    case 5: return launch_tc<BN_, ST_, E_, A_, 5>(ctx, tmap, tmap_y, tmap_r, tmap_x, a);    \
     case 2: if (BN_ <= 128) return launch_tc<BN_, ST_, E_, A_, 2>(ctx, tmap, tmap_y, tmap_r, tmap_x, a); break; \
     case 3: if (BN_ <= 128) return launch_tc<BN_, ST_, E_, A_, 3>(ctx, tmap, tmap_y, tmap_r, tmap_x, a); break; \
     default: break;                                                                         \

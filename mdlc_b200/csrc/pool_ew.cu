@@ -250,16 +250,23 @@ __global__ void __launch_bounds__(256) pool_max_u8_kernel(const mdlc_pool_desc d
 // One CTA per (image, 256-channel block): 32 channel groups x 8 pixel slices,
 // fp32 sums, shared-memory reduction over the slices.
 template <typename T>
+// One block per (image, up to 32 channel groups): the 256 threads split the
+// pixels over however many groups the block holds (a 56-channel tensor keeps
+// every thread busy, not 7 of 32 lanes), then reduce the slices in shared memory.
 __global__ void __launch_bounds__(256) gap_kernel(const mdlc_pool_desc d, const void* x, void* y) {
-  __shared__ float part[8][32][8];
+  __shared__ float part[256][8];
   const int img = blockIdx.x;
-  const int gl = threadIdx.x & 31, slice = threadIdx.x >> 5;
-  const int g = blockIdx.y * 32 + gl;
+  const int g0 = blockIdx.y * 32;
+  const int gb = min(32, (d.c_stride >> 3) - g0);  // channel groups in this block
+  const int slices = 256 / gb;
+  const int t = threadIdx.x;
+  const int gl = t % gb, slice = t / gb;
   const int hw = d.h * d.w;
   float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  if (g * 8 < d.c_stride) {
-    const char* xb = static_cast<const char*>(x) + ((long long)img * hw * d.c_stride + g * 8) * V8<T>::kBytes;
-    for (int p = slice; p < hw; p += 8) {
+  if (slice < slices) {
+    const char* xb =
+        static_cast<const char*>(x) + ((long long)img * hw * d.c_stride + (g0 + gl) * 8) * V8<T>::kBytes;
+    for (int p = slice; p < hw; p += slices) {
       float v[8];
       V8<T>::load(xb + (long long)p * d.c_stride * V8<T>::kBytes, v);
 #pragma unroll
@@ -267,14 +274,14 @@ __global__ void __launch_bounds__(256) gap_kernel(const mdlc_pool_desc d, const 
     }
   }
 #pragma unroll
-  for (int e = 0; e < 8; ++e) part[slice][gl][e] = acc[e];
+  for (int e = 0; e < 8; ++e) part[t][e] = acc[e];
   __syncthreads();
-  if (slice == 0 && g * 8 < d.c_stride) {
+  if (t < gb) {
+    const int g = g0 + t;
 #pragma unroll
     for (int e = 0; e < 8; ++e) {
       float s = 0.0f;
-#pragma unroll
-      for (int q = 0; q < 8; ++q) s += part[q][gl][e];
+      for (int q = 0; q < slices; ++q) s += part[q * gb + t][e];
       acc[e] = (g * 8 + e < d.c) ? s / (float)hw : 0.0f;
     }
     V8<T>::store(static_cast<char*>(y) + ((long long)img * d.c_stride + g * 8) * V8<T>::kBytes, acc);
@@ -311,7 +318,7 @@ MDLC_DEV float ew_unary(int op, float v, float i0, float i1) {
     case MDLC_EW_HARD_SIGMOID: return fminf(fmaxf(i0 * v + i1, 0.0f), 1.0f);
     case MDLC_EW_HARD_SWISH: return v * fminf(fmaxf(v / 6.0f + 0.5f, 0.0f), 1.0f);
     case MDLC_EW_ERF: return erff(v);
-    case MDLC_EW_GELU: return 0.5f * v * (1.0f + erff(v * 0.70710678118654752f));
+    case MDLC_EW_GELU: return gelu_f(v);
     case MDLC_EW_ADDI: return v + i0;
     case MDLC_EW_SUBI: return v - i0;
     case MDLC_EW_RSUBI: return i0 - v;

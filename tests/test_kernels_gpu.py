@@ -179,6 +179,33 @@ def test_conv_im2col_tma_matches_gather(ctx, case):
     np.testing.assert_array_equal(tma, gather)
 
 
+POINTWISE_CASES = [
+    # n, c, h, w, k   (1x1, stride 1, no padding: A by 2-D tiled TMA of the [M, cs] matrix)
+    (4, 24, 28, 28, 144),     # MobileNetV2 expand: 24 channels (48-byte rows), one partial k-block
+    (2, 56, 30, 30, 112),     # RepViT widths: 56 of 64 channels, ragged last M tile
+    (2, 112, 14, 15, 56),     # two k-blocks, the second partial
+    (3, 512, 1, 1, 1000),     # FC as a 1x1 conv over 1x1 images
+]
+
+
+@pytest.mark.parametrize("case", POINTWISE_CASES, ids=[str(c) for c in POINTWISE_CASES])
+def test_conv_pointwise_tma_matches_gather(ctx, case):
+    """Pointwise convs load A as a plain 2-D tile of the activation matrix
+    (channels past cs read as zero); the result equals the cp.async gather's
+    bit for bit and the oracle within tolerance."""
+    n, c, h, w, k = case
+    rng = np.random.default_rng(300 + sum(case))
+    x = rng.standard_normal((n, c, h, w)).astype(np.float32)
+    wt = (rng.standard_normal((k, c, 1, 1)) * np.sqrt(2.0 / c)).astype(np.float32)
+    b = (rng.standard_normal(k) * 0.1).astype(np.float32)
+    res = rng.standard_normal((n, k, h, w)).astype(np.float32)
+    tma = run_conv(ctx, x, wt, b, act=L.ACT_RELU, res=res)
+    gather = run_conv(ctx, x, wt, b, act=L.ACT_RELU, res=res, flags=1)
+    want = oracle_conv(x, wt, b, act="Relu", res=res)
+    check(tma, want, 1e-2)
+    np.testing.assert_array_equal(tma, gather)
+
+
 HALO_CASES = [
     # n, c, h, w, k, r, pad   (stride 1, output >= 14x14: the halo-band main loop)
     (4, 16, 40, 40, 64, 4, 2),       # 32-byte pixels (the space-to-depth stem shape)
