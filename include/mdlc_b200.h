@@ -207,6 +207,34 @@ int mdlc_conv_weight_bytes(const mdlc_conv_desc* desc, size_t* bytes);
  * layout the kernel for desc reads; int8 paths take already-quantised int8
  * values stored as float. Host-only. */
 int mdlc_pack_conv_weights(const mdlc_conv_desc* desc, const float* host_w_oihw, void* host_out);
+/* Depthwise convolution (groups == c == k): the entry point of
+ * mdlc_conv2d's depthwise path with the shape checked. Replaces the grouped
+ * conv host fallback (emit.py:175-180, ops.py:68-78). Weights packed by
+ * mdlc_pack_conv_weights. */
+int mdlc_dwconv2d(mdlc_ctx* ctx, const mdlc_conv_desc* desc, const void* x, const void* w_packed,
+                  const void* bias, const void* residual, void* y, const mdlc_epilogue* epi);
+
+/* GEMM y[m, n] = act(a[m, k] . op(b) + bias) on the convolution kernels (a
+ * 1x1 convolution over m one-pixel images). Replaces the Gemm / MatMul
+ * lowering (emit.py:211-244, ops.py:84-92). a is row-major with row stride lda
+ * elements (>= k; a multiple of 8, or 16 for 8-bit types); y is row-major with
+ * row stride round_up(n, 8) (16 for 8-bit outputs), pad columns written as 0.
+ * op(b) = b^T when trans_b (b stored [n, k], ONNX transB = 1, the FC layout),
+ * else b ([k, n]); alpha is folded into the packed weights by
+ * mdlc_pack_gemm_weights and beta into bias by the caller (bias: n floats, or
+ * int32 for 8-bit types). trans_a = 1 is rejected (MDLC_ERR_UNSUPPORTED). */
+typedef struct {
+  int32_t m, n, k;
+  int32_t lda;
+  int32_t trans_a, trans_b;
+  float alpha;
+  int32_t in_type, out_type;
+} mdlc_gemm_desc;
+int mdlc_gemm_weight_bytes(const mdlc_gemm_desc* desc, size_t* bytes);
+int mdlc_pack_gemm_weights(const mdlc_gemm_desc* desc, const float* host_b, void* host_out); /* host-only */
+int mdlc_gemm(mdlc_ctx* ctx, const mdlc_gemm_desc* desc, const void* a, const void* b_packed, const void* bias,
+              void* y, const mdlc_epilogue* epi, const mdlc_tile_cfg* cfg);
+
 /* Replaces the MaxPool / AveragePool / GlobalAveragePool host fallbacks
  * (emit.py:32-35, ops.py:109-150). */
 int mdlc_pool2d(mdlc_ctx* ctx, const mdlc_pool_desc* desc, const void* x, void* y);

@@ -53,6 +53,12 @@ class ConvDesc(C.Structure):
         "res_stride", "in_zp")]
 
 
+class GemmDesc(C.Structure):
+    _fields_ = [("m", C.c_int32), ("n", C.c_int32), ("k", C.c_int32), ("lda", C.c_int32),
+                ("trans_a", C.c_int32), ("trans_b", C.c_int32), ("alpha", C.c_float),
+                ("in_type", C.c_int32), ("out_type", C.c_int32)]
+
+
 class TileCfg(C.Structure):
     _fields_ = [("bn", C.c_int32), ("stages", C.c_int32), ("flags", C.c_int32)]
 
@@ -105,6 +111,10 @@ SIGNATURES = {
     "mdlc_conv_weight_bytes": ([C.POINTER(ConvDesc), C.POINTER(C.c_size_t)], C.c_int),
     "mdlc_pack_conv_weights": ([C.POINTER(ConvDesc), _P, _P], C.c_int),
     "mdlc_pool2d": ([_P, C.POINTER(PoolDesc), _P, _P], C.c_int),
+    "mdlc_dwconv2d": ([_P, C.POINTER(ConvDesc), _P, _P, _P, _P, _P, C.POINTER(Epilogue)], C.c_int),
+    "mdlc_gemm_weight_bytes": ([C.POINTER(GemmDesc), C.POINTER(C.c_size_t)], C.c_int),
+    "mdlc_pack_gemm_weights": ([C.POINTER(GemmDesc), _P, _P], C.c_int),
+    "mdlc_gemm": ([_P, C.POINTER(GemmDesc), _P, _P, _P, _P, C.POINTER(Epilogue), C.POINTER(TileCfg)], C.c_int),
     "mdlc_eltwise": ([_P, C.POINTER(EwProg), C.POINTER(C.c_void_p), C.POINTER(C.c_void_p)], C.c_int),
     "mdlc_nchw_to_nhwc": ([_P, _P, _I, _I, _I, _I, _P, _I, _I, C.c_float, _I], C.c_int),
     "mdlc_nhwc_to_nchw": ([_P, _P, _I, _I, _I, _I, _I, _I, _P, C.c_float, _I], C.c_int),
@@ -254,6 +264,18 @@ class Context:
                                         C.byref(epi) if epi is not None else None,
                                         C.byref(cfg) if cfg is not None else None), "conv2d")
 
+    def dwconv2d(self, desc: ConvDesc, x, w, bias, res, y, epi: Epilogue | None = None) -> None:
+        self.check(self.lib.mdlc_dwconv2d(self.h, C.byref(desc), C.c_void_p(x), C.c_void_p(w),
+                                          C.c_void_p(bias or 0), C.c_void_p(res or 0), C.c_void_p(y),
+                                          C.byref(epi) if epi is not None else None), "dwconv2d")
+
+    def gemm(self, desc: GemmDesc, a, b_packed, bias, y, epi: Epilogue | None = None,
+             cfg: TileCfg | None = None) -> None:
+        self.check(self.lib.mdlc_gemm(self.h, C.byref(desc), C.c_void_p(a), C.c_void_p(b_packed),
+                                      C.c_void_p(bias or 0), C.c_void_p(y),
+                                      C.byref(epi) if epi is not None else None,
+                                      C.byref(cfg) if cfg is not None else None), "gemm")
+
     def pool2d(self, desc: PoolDesc, x, y) -> None:
         self.check(self.lib.mdlc_pool2d(self.h, C.byref(desc), C.c_void_p(x), C.c_void_p(y)), "pool2d")
 
@@ -337,6 +359,28 @@ def weight_bytes(desc: ConvDesc) -> int:
     if st != OK:
         raise MdlcError(st, "conv_weight_bytes: unsupported conv configuration")
     return n.value
+
+
+def gemm_weight_bytes(desc: GemmDesc) -> int:
+    n = C.c_size_t(0)
+    st = load().mdlc_gemm_weight_bytes(C.byref(desc), C.byref(n))
+    if st != OK:
+        raise MdlcError(st, "gemm_weight_bytes: unsupported GEMM configuration")
+    return n.value
+
+
+def pack_gemm_weights(desc: GemmDesc, b: np.ndarray) -> np.ndarray:
+    """Pack B ([n, k] when ``desc.trans_b``, else [k, n]) scaled by ``desc.alpha`` (host)."""
+    shape = (desc.n, desc.k) if desc.trans_b else (desc.k, desc.n)
+    b = np.ascontiguousarray(b, dtype=np.float32)
+    if b.shape != shape:
+        raise ValueError(f"B has shape {b.shape}, descriptor wants {shape}")
+    out = np.empty(gemm_weight_bytes(desc), dtype=np.uint8)
+    st = load().mdlc_pack_gemm_weights(C.byref(desc), b.ctypes.data_as(C.c_void_p),
+                                       out.ctypes.data_as(C.c_void_p))
+    if st != OK:
+        raise MdlcError(st, "pack_gemm_weights failed")
+    return out
 
 
 def pack_weights(desc: ConvDesc, w_oihw: np.ndarray) -> np.ndarray:

@@ -491,3 +491,87 @@ def test_bounded_wait_reports_timeout(ctx):
     assert ctx.check_flag() == L.DEVERR_WAIT_TIMEOUT
     assert ctx.check_flag() == 0        # reading clears the word
     test_layout_roundtrip(ctx, L.F32)   # still works afterwards
+
+
+GEMM_CASES = [
+    # m, n, k, lda, trans_b, alpha, dtype
+    (37, 1000, 512, 512, 1, 1.0, "bf16"),     # FC layout (ONNX transB = 1), ragged m and n
+    (64, 96, 200, 208, 0, 0.5, "bf16"),       # [k, n] operand, row padding in a, alpha folded
+    (5, 24, 40, 40, 1, 2.0, "f32"),           # fp32: SIMT kernel
+]
+
+
+@pytest.mark.parametrize("case", GEMM_CASES, ids=[str(c) for c in GEMM_CASES])
+def test_gemm_entry_point(ctx, case):
+    """mdlc_gemm: y = act(alpha * a . op(b) + bias) against the oracle's Gemm."""
+    m, n, k, lda, tb, alpha, dtype = case
+    rng = np.random.default_rng(m + n + k)
+    a = rng.standard_normal((m, k)).astype(np.float32)
+    b = (rng.standard_normal((n, k) if tb else (k, n)) * 0.05).astype(np.float32)
+    bias = (rng.standard_normal(n) * 0.1).astype(np.float32)
+    et = L.BF16 if dtype == "bf16" else L.F32
+    d = L.GemmDesc(m=m, n=n, k=k, lda=lda, trans_a=0, trans_b=tb, alpha=alpha, in_type=et, out_type=et)
+    bp = ctx.to_device(L.pack_gemm_weights(d, b))
+    ah = np.zeros((m, lda), np.float32)
+    ah[:, :k] = a
+    ad = ctx.to_device(bf16_bits(ah) if et == L.BF16 else ah)
+    bd = ctx.to_device(bias)
+    ns = _rnd8(n)
+    eb = 2 if et == L.BF16 else 4
+    yd = ctx.alloc(m * ns * eb)
+    ctx.memset(yd, 0xFF, m * ns * eb)
+    ctx.gemm(d, ad, bp, bd, yd, L.Epilogue(act=L.ACT_RELU))
+    ctx.sync()
+    y = ctx.download(yd, (m, ns), np.uint16 if et == L.BF16 else np.float32)
+    y = from_bf16_bits(y) if et == L.BF16 else y
+    for p in (bp, ad, bd, yd):
+        ctx.free(p)
+    assert np.all(y[:, n:] == 0), "padding columns must be written as zero"
+    ar = oref.round_bf16(a) if et == L.BF16 else a
+    bw = np.float32(alpha) * (b if tb else b.T)
+    br = oref.round_bf16(bw) if et == L.BF16 else bw
+    want = np.maximum(ar @ br.T + bias, 0)
+    if et == L.BF16:
+        check(y[:, :n], want, 1e-2)
+    else:
+        np.testing.assert_allclose(y[:, :n], want, rtol=1e-4, atol=1e-4)
+
+
+def test_gemm_rejects_trans_a(ctx):
+    d = L.GemmDesc(m=4, n=8, k=8, lda=8, trans_a=1, trans_b=1, alpha=1.0, in_type=L.BF16, out_type=L.BF16)
+    with pytest.raises(L.MdlcError, match="trans_a"):
+        ctx.gemm(d, 0, 0, 0, 0)
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+def test_dwconv2d_entry_point(ctx, dtype):
+    """mdlc_dwconv2d gives the bytes mdlc_conv2d gives for the same depthwise
+    conv, and refuses a grouped conv that is not depthwise."""
+    n, c, h, w = 2, 48, 15, 13
+    rng = np.random.default_rng(48)
+    x = rng.standard_normal((n, c, h, w)).astype(np.float32)
+    wt = (rng.standard_normal((c, 1, 3, 3)) * 0.3).astype(np.float32)
+    b = (rng.standard_normal(c) * 0.1).astype(np.float32)
+    et = L.BF16 if dtype == "bf16" else L.F32
+    cs = _rnd8(c)
+    d = L.ConvDesc(n=n, h=h, w=w, c=c, c_stride=cs, k=c, k_stride=cs, r=3, s=3, stride_h=2, stride_w=2,
+                   pad_t=1, pad_l=1, dil_h=1, dil_w=1, oh=8, ow=7, groups=c, in_type=et, out_type=et)
+    wp = ctx.to_device(L.pack_weights(d, wt))
+    xh = nhwc(x, cs)
+    xd = ctx.to_device(bf16_bits(xh) if et == L.BF16 else xh)
+    bd = ctx.to_device(np.pad(b, (0, cs - c)))
+    nb = n * 8 * 7 * cs * (2 if et == L.BF16 else 4)
+    y1, y2 = ctx.alloc(nb), ctx.alloc(nb)
+    epi = L.Epilogue(act=L.ACT_CLIP, clip_lo=0.0, clip_hi=6.0)
+    ctx.conv2d(d, xd, wp, bd, 0, y1, epi)
+    ctx.dwconv2d(d, xd, wp, bd, 0, y2, epi)
+    ctx.sync()
+    r1 = ctx.download(y1, (nb,), np.uint8)
+    r2 = ctx.download(y2, (nb,), np.uint8)
+    bad = L.ConvDesc(**{f: getattr(d, f) for f, _ in L.ConvDesc._fields_})
+    bad.groups = c // 2
+    with pytest.raises(L.MdlcError, match="groups"):
+        ctx.dwconv2d(bad, xd, wp, bd, 0, y2, epi)
+    for p in (wp, xd, bd, y1, y2):
+        ctx.free(p)
+    np.testing.assert_array_equal(r1, r2)
