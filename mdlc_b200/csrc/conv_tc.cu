@@ -106,6 +106,20 @@ struct Smem {
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
 };
 
+// Resident CTAs per SM. A single thread issues every tcgen05.mma of a CTA,
+// and between k-blocks it also waits on the stage's full barrier (~100 cycles
+// even when the phase is already complete) and commits the stage's empty
+// barrier (~40 cycles); the issue queue is too shallow to cover that with
+// N <= 128 instructions (measured: one issuer sustains one 128x128x16 MMA per
+// ~96 cycles with a wait and commit per k-block, two issuers the full rate of
+// one per 64). So configurations whose shared memory allows it run two CTAs
+// per SM, whose issuers fill each other's gaps; the kernel is then compiled
+// for at most 96 registers per thread (2 x 320 threads).
+template <int BN, int STAGES, int ESZ, int AMODE>
+struct Occ {
+  static constexpr int value = Smem<BN, STAGES, ESZ, AMODE>::kAlloc <= 113 * 1024 ? 2 : 1;
+};
+
 // ---------------------------------------------------------------- epilogue
 template <int ESZ>
 MDLC_DEV void store_chunk16(const TcArgs& a, int m, int nb0, const uint32_t (&v)[16]) {
@@ -224,7 +238,7 @@ MDLC_DEV void store_chunk16(const TcArgs& a, int m, int nb0, const uint32_t (&v)
 
 // ---------------------------------------------------------------- kernel
 template <int BN, int STAGES, int ESZ, int ACT, int AMODE>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, (Occ<BN, STAGES, ESZ, AMODE>::value))
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_y,
                    const __grid_constant__ CUtensorMap tmap_r, const __grid_constant__ CUtensorMap tmap_x,
                    const TcArgs a) {
@@ -935,7 +949,8 @@ int launch_tc(mdlc_ctx* ctx, const CUtensorMap& tmap, const CUtensorMap& tmap_y,
     attr_set[ctx->device & 63] = true;
   }
   const int tiles = args.num_m_tiles * args.num_n_tiles;
-  const int grid = tiles < ctx->num_sms ? tiles : ctx->num_sms;
+  const int slots = ctx->num_sms * Occ<BN, STAGES, ESZ, AMODE>::value;
+  const int grid = tiles < slots ? tiles : slots;
   kern<<<grid, kThreads, L::kAlloc, ctx->stream>>>(tmap, tmap_y, tmap_r, tmap_x, args);
   mdlc_note_launch(ctx);
   return mdlc_cuda_status(ctx, cudaGetLastError(), "conv_tc launch");
@@ -978,7 +993,14 @@ int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w
     // keep enough tiles in flight for the whole GPU
     while (bn > 64 && (long long)num_m * ((d.k_stride + bn - 1) / bn) < ctx->num_sms) bn /= 2;
   }
-  if (!stages) stages = bn == 256 ? 3 : (bn == 128 ? 4 : 8);
+  // 64- and 128-wide tiles: the two-CTAs-per-SM configurations (see Occ)
+  // when every SM gets more than one tile; otherwise each CTA runs alone on
+  // its SM and the deep single-CTA pipelines are faster
+  if (!stages) {
+    const long long tiles = (long long)num_m * ((d.k_stride + bn - 1) / bn);
+    const bool pair = tiles > ctx->num_sms;
+    stages = bn == 256 ? 3 : (bn == 128 ? (pair ? 2 : 4) : (pair ? 3 : 8));
+  }
   if (bn != 64 && bn != 128 && bn != 256)
     return mdlc_set_error(ctx, MDLC_ERR_INVALID, "conv_tc: bn must be 64/128/256, got %d", bn);
 
@@ -1123,9 +1145,11 @@ int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w
     MDLC_TC_ACT(BN_, ST_, MDLC_ACT_SIGMOID)                                                 \
     MDLC_TC_LAUNCH(BN_, ST_, 2, -1)                                                         \
   }
+  MDLC_TC_CASE(64, 3)
+  MDLC_TC_CASE(128, 2)
+  MDLC_TC_CASE(256, 3)
   MDLC_TC_CASE(64, 8)
   MDLC_TC_CASE(128, 4)
-  MDLC_TC_CASE(256, 3)
 #undef MDLC_TC_ACT
 #undef MDLC_TC_LAUNCH
 #undef MDLC_TC_CASE

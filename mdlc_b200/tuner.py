@@ -5,7 +5,8 @@ a schedule search per GEMM shape with a JSON cache, measured on a GPU when
 one is available, an analytical cost model otherwise) for the B200 kernels:
 the search space is the conv kernel's tile width ``bn`` (64/128/256 output
 channels per CTA) and shared-memory pipeline depth ``stages`` — the only
-knobs of the prebuilt kernel — and the cache key is
+knobs of the prebuilt kernel; the shallow (64, 3) and (128, 2) pipelines fit
+two CTAs on one SM — and the cache key is
 ``(kind, n, h, w, c, k, r, s, stride, pad, dtype, arch)``.
 
 ``Tuner`` is passed to :func:`mdlc_b200.compile` as ``tuner=`` (the
@@ -27,8 +28,22 @@ import numpy as np
 
 from mdlc_b200 import _lib as L
 
-CONFIGS = ((64, 8), (128, 4), (256, 3))
-KERNEL_TAG = "conv_tc_v1"
+CONFIGS = ((64, 3), (128, 2), (256, 3), (64, 8), (128, 4))
+KERNEL_TAG = "conv_tc_v2"
+# resident CTAs per SM of each configuration (shared memory <= 113 KB: two)
+CTAS_PER_SM = {(64, 3): 2, (128, 2): 2, (256, 3): 1, (64, 8): 1, (128, 4): 1}
+# Cost-model constants, fitted to B200 measurements of this kernel (b=256
+# ResNet-18 layers, CUDA events): tensor-pipe cycles of one 128 x bn x 16 bf16
+# MMA with operands fresh from the stage ring; the cycles one CTA's issuing
+# thread adds per k-block for narrow tiles (barrier waits, commits, operand
+# hand-offs: 64-wide 819 and 128-wide 867 cycles per k-block against 252 / 256
+# of MMAs), which a second resident CTA overlaps; and the operand load latency
+# that bounds an SM's L2 -> shared-memory bandwidth to the bytes its stage
+# rings hold in flight (Little's law), up to a sustained maximum.
+MMA_CYCLES = {64: 63.0, 128: 64.0, 256: 128.0}
+ISSUE_GAP = 560.0
+LOAD_LATENCY = 2700.0
+L2_MAX_BYTES_PER_CYCLE = 64.0
 
 
 def round_up(v, m):
@@ -80,17 +95,27 @@ class ConvShape:
 
 
 def analytical_cost(shape: ConvShape, bn: int, stages: int, num_sms: int = 148) -> float:
-    """Relative time estimate without a device: L2->SM bytes per tile (A gathered
-    per k-block, B per k-block) x tiles, inflated by wave quantisation, with a
-    latency penalty for shallow pipelines."""
+    """Estimated SM cycles without a device. Per k-block an SM is bound by its
+    MMA issue (4 MMAs plus the issuer's gap for narrow tiles, overlapped by as
+    many issuers as CTAs share the SM), by the tensor pipe, or by the L2 -> SM
+    operand bytes (A and B tiles) at the bandwidth its in-flight stages
+    sustain; the busiest SM gets ``ceil(tiles /
+    num_sms)`` tiles, and with one tile per SM the pipeline's fill latency
+    shows."""
     d = shape.desc()
     m = shape.n * shape.oh * shape.ow
     tiles = -(-m // 128) * -(-d.k_stride // bn)
     kb = -(-shape.r * shape.s * d.c_stride // (128 // L.ELEM_BYTES[shape.dtype]))
-    per_tile = kb * (128 * 128 + bn * 128)
-    waves = -(-tiles // num_sms)
-    quant = waves * num_sms / tiles
-    return per_tile * tiles * quant * (1.0 + 0.5 / stages)
+    occ = CTAS_PER_SM.get((bn, stages), 1)
+    per_sm = -(-tiles // num_sms)
+    conc = min(occ, per_sm)               # CTAs of this configuration busy on one SM
+    issue = 4 * MMA_CYCLES[bn] + (ISSUE_GAP if bn < 256 else 0.0)
+    pipe = max(issue / conc, 4 * MMA_CYCLES[bn])
+    stage_bytes = 128 * 128 + bn * 128
+    bw = min(L2_MAX_BYTES_PER_CYCLE, conc * stages * stage_bytes / LOAD_LATENCY)
+    per_kb = max(pipe, stage_bytes / bw)
+    latency = 1.0 + 1.0 / stages if per_sm == 1 else 1.0   # one tile per SM: nothing overlaps its fill
+    return per_sm * kb * per_kb * latency
 
 
 class _Bench:
