@@ -245,7 +245,8 @@ __global__ void __launch_bounds__(kThreads, (Occ<BN, STAGES, ESZ, AMODE>::value)
   using L = Smem<BN, STAGES, ESZ, AMODE>;
   constexpr int KB = 128 / ESZ;    // k-block elements (128 bytes)
   constexpr int CHUNK = 16 / ESZ;  // elements per 16-byte chunk
-  constexpr uint32_t kTmemCols = 2 * BN;
+  // two accumulators of BN columns; allocations are powers of two (192 -> 512)
+  constexpr uint32_t kTmemCols = 2 * BN > 256 ? 512u : (uint32_t)(2 * BN);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -992,6 +993,15 @@ int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w
     bn = d.k_stride > 128 ? 256 : (d.k_stride > 64 ? 128 : 64);
     // keep enough tiles in flight for the whole GPU
     while (bn > 64 && (long long)num_m * ((d.k_stride + bn - 1) / bn) < ctx->num_sms) bn /= 2;
+    if (bn == 256) {
+      // 192-wide tiles when they fill the last wave better: compare the
+      // busiest SM's output columns, ceil(tiles / SMs) x tile width
+      auto busiest = [&](int w) {
+        const long long tiles = (long long)num_m * ((d.k_stride + w - 1) / w);
+        return (tiles + ctx->num_sms - 1) / ctx->num_sms * w;
+      };
+      if (busiest(192) < busiest(256)) bn = 192;
+    }
   }
   // 64- and 128-wide tiles: the two-CTAs-per-SM configurations (see Occ)
   // when every SM gets more than one tile; otherwise each CTA runs alone on
@@ -999,10 +1009,10 @@ int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w
   if (!stages) {
     const long long tiles = (long long)num_m * ((d.k_stride + bn - 1) / bn);
     const bool pair = tiles > ctx->num_sms;
-    stages = bn == 256 ? 3 : (bn == 128 ? (pair ? 2 : 4) : (pair ? 3 : 8));
+    stages = bn >= 192 ? 3 : (bn == 128 ? (pair ? 2 : 4) : (pair ? 3 : 8));
   }
-  if (bn != 64 && bn != 128 && bn != 256)
-    return mdlc_set_error(ctx, MDLC_ERR_INVALID, "conv_tc: bn must be 64/128/256, got %d", bn);
+  if (bn != 64 && bn != 128 && bn != 192 && bn != 256)
+    return mdlc_set_error(ctx, MDLC_ERR_INVALID, "conv_tc: bn must be 64/128/192/256, got %d", bn);
 
   auto encode = get_encode_fn();
   if (!encode) return mdlc_set_error(ctx, MDLC_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
@@ -1148,6 +1158,7 @@ int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w
   MDLC_TC_CASE(64, 3)
   MDLC_TC_CASE(128, 2)
   MDLC_TC_CASE(256, 3)
+  MDLC_TC_CASE(192, 3)
   MDLC_TC_CASE(64, 8)
   MDLC_TC_CASE(128, 4)
 #undef MDLC_TC_ACT

@@ -28,10 +28,10 @@ import numpy as np
 
 from mdlc_b200 import _lib as L
 
-CONFIGS = ((64, 3), (128, 2), (256, 3), (64, 8), (128, 4))
+CONFIGS = ((64, 3), (128, 2), (256, 3), (192, 3), (64, 8), (128, 4))
 KERNEL_TAG = "conv_tc_v2"
 # resident CTAs per SM of each configuration (shared memory <= 113 KB: two)
-CTAS_PER_SM = {(64, 3): 2, (128, 2): 2, (256, 3): 1, (64, 8): 1, (128, 4): 1}
+CTAS_PER_SM = {(64, 3): 2, (128, 2): 2, (256, 3): 1, (192, 3): 1, (64, 8): 1, (128, 4): 1}
 # Cost-model constants, fitted to B200 measurements of this kernel (b=256
 # ResNet-18 layers, CUDA events): tensor-pipe cycles of one 128 x bn x 16 bf16
 # MMA with operands fresh from the stage ring; the cycles one CTA's issuing
@@ -40,7 +40,7 @@ CTAS_PER_SM = {(64, 3): 2, (128, 2): 2, (256, 3): 1, (64, 8): 1, (128, 4): 1}
 # of MMAs), which a second resident CTA overlaps; and the operand load latency
 # that bounds an SM's L2 -> shared-memory bandwidth to the bytes its stage
 # rings hold in flight (Little's law), up to a sustained maximum.
-MMA_CYCLES = {64: 63.0, 128: 64.0, 256: 128.0}
+MMA_CYCLES = {64: 63.0, 128: 64.0, 192: 96.0, 256: 128.0}
 ISSUE_GAP = 560.0
 LOAD_LATENCY = 2700.0
 L2_MAX_BYTES_PER_CYCLE = 64.0
@@ -109,7 +109,7 @@ def analytical_cost(shape: ConvShape, bn: int, stages: int, num_sms: int = 148) 
     occ = CTAS_PER_SM.get((bn, stages), 1)
     per_sm = -(-tiles // num_sms)
     conc = min(occ, per_sm)               # CTAs of this configuration busy on one SM
-    issue = 4 * MMA_CYCLES[bn] + (ISSUE_GAP if bn < 256 else 0.0)
+    issue = 4 * MMA_CYCLES[bn] + (ISSUE_GAP if bn <= 128 else 0.0)
     pipe = max(issue / conc, 4 * MMA_CYCLES[bn])
     stage_bytes = 128 * 128 + bn * 128
     bw = min(L2_MAX_BYTES_PER_CYCLE, conc * stages * stage_bytes / LOAD_LATENCY)

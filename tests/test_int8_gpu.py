@@ -116,3 +116,34 @@ def test_int8_resnet18_b1024_batch_invariance(resnet18_int8_b1):
             np.testing.assert_array_equal(out[i:i + 1], one, err_msg=f"row {i}")
     finally:
         exe.close()
+
+
+@pytest.mark.parametrize("shape", [(4, 256, 7, 7, 512, 3, 3, 1, 1), (2, 64, 20, 18, 200, 3, 3, 2, 1)],
+                         ids=["512ch-7x7", "ragged-k200-s2"])
+def test_int8_conv_same_bits_for_every_tile_config(shape):
+    """An int8 conv (u8 codes x s8 weights, int32 accumulation, fp32 dequantised
+    output) gives the same bits whichever tile configuration runs it, the
+    192-wide tiles and the two-CTAs-per-SM ones included: the integer sums are
+    exact and the epilogue is per element."""
+    from mdlc_b200 import _lib as L
+    from mdlc_b200.tuner import ConvShape, _Bench
+    ctx = L.Context(0)
+    b = _Bench(ctx, ConvShape(*shape, dtype=L.U8))
+    try:
+        d = b.d
+        rng = np.random.default_rng(7)
+        x = rng.integers(0, 256, (d.n, d.h, d.w, d.c_stride), dtype=np.uint8)
+        x[..., d.c:] = 0
+        ctx.upload(b.x, x)
+        outs = {}
+        for cfg in ((0, 0), (256, 3), (192, 3), (128, 2), (64, 3), (128, 4), (64, 8)):
+            b.run(L.TileCfg(bn=cfg[0], stages=cfg[1], flags=0) if cfg[0] else None)
+            ctx.sync()
+            outs[cfg] = ctx.download(b.y, (d.n * d.oh * d.ow, d.k_stride), np.float32)[:, :d.k]
+        ref = outs[(0, 0)]
+        assert np.isfinite(ref).all() and np.abs(ref).max() > 0
+        for cfg, y in outs.items():
+            np.testing.assert_array_equal(y, ref, err_msg=str(cfg))
+    finally:
+        b.close()
+        ctx.close()

@@ -125,7 +125,7 @@ def test_conv_bf16_tcgen05(ctx, case):
     check(got, want, 1e-2)
 
 
-@pytest.mark.parametrize("cfg", [(64, 3), (128, 2), (256, 3), (64, 8), (128, 4)])
+@pytest.mark.parametrize("cfg", [(64, 3), (128, 2), (256, 3), (192, 3), (64, 8), (128, 4)])
 def test_conv_bf16_tile_configs(ctx, cfg):
     """Every tile configuration the tuner may pick gives the same answer (odd M, k tail)."""
     rng = np.random.default_rng(7)
