@@ -610,71 +610,104 @@ __global__ void __launch_bounds__(256) to_s2d_kernel(const float* x, int c, int 
 }
 
 // The image-stem case of the above: at most 4 input channels into CS = 16 or
-// 32 output channels. One thread per output pixel reads one float2 (two
-// horizontally adjacent inputs) per (channel, row) -- coalesced across the
-// warp -- and writes the pixel's CS channels with full-width vector stores, so
-// the input is read once and every byte written is a whole 32-byte sector.
-template <int DT, int C, int CS>
-__global__ void __launch_bounds__(256) to_s2d16_kernel(const float* x, int h, int w, void* y, float inv_scale,
-                                                       int zp, int total) {
-  const int w2 = w >> 1, hw2 = (h >> 1) * w2;
-  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += gridDim.x * blockDim.x) {
-    const int img = idx / hw2;
-    const int p = idx - img * hw2;
-    const int Y = p / w2, X = p - Y * w2;
-    float v[16];
+// 32 output channels. One thread per PX horizontally adjacent output pixels
+// reads one 2*PX-float vector (float2 / float4) per (channel, row) --
+// coalesced across the warp -- and writes each pixel's CS channels with
+// full-width vector stores, so the input is read once and every byte written
+// is a whole 32-byte sector. PX = 2 (when the output row width is even)
+// halves the index arithmetic per pixel and doubles the bytes per load.
+template <int DT, int CS>
+MDLC_DEV void s2d_store_pixel(void* y, long long pix, const float (&v)[16], float inv_scale, int zp, int nvals) {
+  const long long o = pix * CS;
+  if constexpr (DT == MDLC_F32) {
+    float4* yo = reinterpret_cast<float4*>(static_cast<float*>(y) + o);
 #pragma unroll
-    for (int e = 0; e < 16; ++e) v[e] = 0.0f;
+    for (int j = 0; j < CS / 4; ++j)
+      yo[j] = j < 4 ? make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]) : make_float4(0, 0, 0, 0);
+  } else if constexpr (DT == MDLC_BF16) {
+    uint32_t u[8];
 #pragma unroll
-    for (int ci = 0; ci < C; ++ci)
+    for (int j = 0; j < 8; ++j) u[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
+    uint4* yo = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(y) + o);
+    yo[0] = make_uint4(u[0], u[1], u[2], u[3]);
+    yo[1] = make_uint4(u[4], u[5], u[6], u[7]);
 #pragma unroll
-      for (int dy = 0; dy < 2; ++dy) {
-        const float2 f = __ldg(reinterpret_cast<const float2*>(
-            x + (((long long)img * C + ci) * h + 2 * Y + dy) * w + 2 * X));
-        v[(2 * dy) * C + ci] = f.x;
-        v[(2 * dy + 1) * C + ci] = f.y;
-      }
-    const long long o = (long long)idx * CS;
-    if constexpr (DT == MDLC_F32) {
-      float4* yo = reinterpret_cast<float4*>(static_cast<float*>(y) + o);
+    for (int j = 2; j < CS / 8; ++j) yo[j] = make_uint4(0, 0, 0, 0);
+  } else {
+    uint32_t u[4] = {0, 0, 0, 0};
 #pragma unroll
-      for (int j = 0; j < CS / 4; ++j)
-        yo[j] = j < 4 ? make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]) : make_float4(0, 0, 0, 0);
-    } else if constexpr (DT == MDLC_BF16) {
-      uint32_t u[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) u[j] = pack_bf16x2(v[2 * j], v[2 * j + 1]);
-      uint4* yo = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(y) + o);
-      yo[0] = make_uint4(u[0], u[1], u[2], u[3]);
-      yo[1] = make_uint4(u[4], u[5], u[6], u[7]);
-#pragma unroll
-      for (int j = 2; j < CS / 8; ++j) yo[j] = make_uint4(0, 0, 0, 0);
-    } else {
-      uint32_t u[4] = {0, 0, 0, 0};
-#pragma unroll
-      for (int e = 0; e < 4 * C; ++e) {
+    for (int e = 0; e < 16; ++e) {
+      if (e < nvals) {
         int q = __float2int_rn(__fmul_rn(v[e], inv_scale)) + zp;
         q = DT == MDLC_S8 ? min(max(q, -128), 127) : min(max(q, 0), 255);
         u[e >> 2] |= (uint32_t)(q & 0xFF) << (8 * (e & 3));
       }
-      uint4* yo = reinterpret_cast<uint4*>(static_cast<uint8_t*>(y) + o);
-      yo[0] = make_uint4(u[0], u[1], u[2], u[3]);
-#pragma unroll
-      for (int j = 1; j < CS / 16; ++j) yo[j] = make_uint4(0, 0, 0, 0);
     }
+    uint4* yo = reinterpret_cast<uint4*>(static_cast<uint8_t*>(y) + o);
+    yo[0] = make_uint4(u[0], u[1], u[2], u[3]);
+#pragma unroll
+    for (int j = 1; j < CS / 16; ++j) yo[j] = make_uint4(0, 0, 0, 0);
+  }
+}
+
+template <int DT, int C, int CS, int PX>
+__global__ void __launch_bounds__(256) to_s2d16_kernel(const float* x, int h, int w, void* y, float inv_scale,
+                                                       int zp, int total) {
+  // total: output pixels / PX; a thread's pixels are (Y, PX*Xg .. PX*Xg + PX-1)
+  const int w2 = w >> 1, wg = w2 / PX, hwg = (h >> 1) * wg;
+  for (int idx = blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += gridDim.x * blockDim.x) {
+    const int img = idx / hwg;
+    const int p = idx - img * hwg;
+    const int Y = p / wg, Xg = p - Y * wg;
+    float v[PX][16];
+#pragma unroll
+    for (int q = 0; q < PX; ++q)
+#pragma unroll
+      for (int e = 0; e < 16; ++e) v[q][e] = 0.0f;
+#pragma unroll
+    for (int ci = 0; ci < C; ++ci)
+#pragma unroll
+      for (int dy = 0; dy < 2; ++dy) {
+        const float* src = x + (((long long)img * C + ci) * h + 2 * Y + dy) * w + 2 * PX * Xg;
+        if constexpr (PX == 2) {
+          const float4 f = __ldg(reinterpret_cast<const float4*>(src));
+          v[0][(2 * dy) * C + ci] = f.x;
+          v[0][(2 * dy + 1) * C + ci] = f.y;
+          v[1][(2 * dy) * C + ci] = f.z;
+          v[1][(2 * dy + 1) * C + ci] = f.w;
+        } else {
+          const float2 f = __ldg(reinterpret_cast<const float2*>(src));
+          v[0][(2 * dy) * C + ci] = f.x;
+          v[0][(2 * dy + 1) * C + ci] = f.y;
+        }
+      }
+    const long long pix0 = ((long long)img * (h >> 1) + Y) * w2 + (long long)PX * Xg;
+#pragma unroll
+    for (int q = 0; q < PX; ++q) s2d_store_pixel<DT, CS>(y, pix0 + q, v[q], inv_scale, zp, 4 * C);
+  }
+}
+
+template <int DT, int CS, int PX>
+void launch_s2d16_px(mdlc_ctx* ctx, const float* x, int c, int h, int w, void* y, float inv_scale, int zp,
+                     int total) {
+  const unsigned grid = grid_for(ctx, total);
+  switch (c) {
+    case 1: to_s2d16_kernel<DT, 1, CS, PX><<<grid, 256, 0, ctx->stream>>>(x, h, w, y, inv_scale, zp, total); break;
+    case 2: to_s2d16_kernel<DT, 2, CS, PX><<<grid, 256, 0, ctx->stream>>>(x, h, w, y, inv_scale, zp, total); break;
+    case 3: to_s2d16_kernel<DT, 3, CS, PX><<<grid, 256, 0, ctx->stream>>>(x, h, w, y, inv_scale, zp, total); break;
+    default: to_s2d16_kernel<DT, 4, CS, PX><<<grid, 256, 0, ctx->stream>>>(x, h, w, y, inv_scale, zp, total); break;
   }
 }
 
 template <int DT, int CS>
 void launch_s2d16(mdlc_ctx* ctx, const float* x, int c, int h, int w, void* y, float inv_scale, int zp,
                   int total) {
-  const unsigned grid = grid_for(ctx, total);
-  switch (c) {
-    case 1: to_s2d16_kernel<DT, 1, CS><<<grid, 256, 0, ctx->stream>>>(x, h, w, y, inv_scale, zp, total); break;
-    case 2: to_s2d16_kernel<DT, 2, CS><<<grid, 256, 0, ctx->stream>>>(x, h, w, y, inv_scale, zp, total); break;
-    case 3: to_s2d16_kernel<DT, 3, CS><<<grid, 256, 0, ctx->stream>>>(x, h, w, y, inv_scale, zp, total); break;
-    default: to_s2d16_kernel<DT, 4, CS><<<grid, 256, 0, ctx->stream>>>(x, h, w, y, inv_scale, zp, total); break;
-  }
+  // two pixels per thread when every thread's float4 is 16-byte aligned: rows
+  // of w floats with w % 4 == 0 (the output row width w / 2 is even)
+  if (w % 4 == 0 && reinterpret_cast<uintptr_t>(x) % 16 == 0)
+    launch_s2d16_px<DT, CS, 2>(ctx, x, c, h, w, y, inv_scale, zp, total / 2);
+  else
+    launch_s2d16_px<DT, CS, 1>(ctx, x, c, h, w, y, inv_scale, zp, total);
 }
 
 template <int DT>
