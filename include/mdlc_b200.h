@@ -115,7 +115,10 @@ typedef struct {
   int32_t flags;  /* bit 0: gather the A operand with cp.async even when the layer
                      qualifies for TMA loads; bit 1: per-tap TMA loads (im2col mode)
                      instead of the halo band of stride-1 layers; bit 2: load one halo band
-                     per tile for stride-1 layers instead of one load per tap */
+                     per tile for stride-1 layers instead of one load per tap; bits 8-15:
+                     split-K, the reduction cut into that many slices on different CTAs,
+                     the last one to finish a tile summing them in slice order (at most
+                     8 MiB of fp32 / int32 partials: tiles x slices x 128 x bn x 4 bytes) */
 } mdlc_tile_cfg;
 
 /* Pooling over NHWC (reference: ops.py:109-150). kind: 0 max, 1 average,

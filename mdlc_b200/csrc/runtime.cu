@@ -56,7 +56,10 @@ int mdlc_ctx_create(int device, mdlc_ctx** out) {
   if (cudaStreamCreateWithFlags(&ctx->stream, cudaStreamNonBlocking) != cudaSuccess ||
       cudaStreamCreateWithFlags(&ctx->copy_stream, cudaStreamNonBlocking) != cudaSuccess ||
       cudaMalloc(&ctx->d_err, 256) != cudaSuccess ||
-      cudaMemset(ctx->d_err, 0, 256) != cudaSuccess || cudaMalloc(&ctx->d_pad, 4096) != cudaSuccess) {
+      cudaMemset(ctx->d_err, 0, 256) != cudaSuccess || cudaMalloc(&ctx->d_pad, 4096) != cudaSuccess ||
+      cudaMalloc(&ctx->d_split_ws, kSplitWsBytes) != cudaSuccess ||
+      cudaMalloc(&ctx->d_split_cnt, kSplitCounters * sizeof(int)) != cudaSuccess ||
+      cudaMemset(ctx->d_split_cnt, 0, kSplitCounters * sizeof(int)) != cudaSuccess) {
     delete ctx;
     return MDLC_ERR_CUDA;
   }
@@ -86,6 +89,8 @@ int mdlc_ctx_destroy(mdlc_ctx* ctx) {
     if (ctx->fences[i]) cudaEventDestroy(ctx->fences[i]);
   cudaFree(ctx->d_err);
   cudaFree(ctx->d_pad);
+  cudaFree(ctx->d_split_ws);
+  cudaFree(ctx->d_split_cnt);
   cudaStreamDestroy(ctx->stream);
   if (ctx->copy_stream) cudaStreamDestroy(ctx->copy_stream);
   delete ctx;

@@ -123,8 +123,8 @@ def test_int8_resnet18_b1024_batch_invariance(resnet18_int8_b1):
 def test_int8_conv_same_bits_for_every_tile_config(shape):
     """An int8 conv (u8 codes x s8 weights, int32 accumulation, fp32 dequantised
     output) gives the same bits whichever tile configuration runs it, the
-    192-wide tiles and the two-CTAs-per-SM ones included: the integer sums are
-    exact and the epilogue is per element."""
+    192-wide tiles, the two-CTAs-per-SM ones and split-K (int32 partial sums)
+    included: the integer sums are exact and the epilogue is per element."""
     from mdlc_b200 import _lib as L
     from mdlc_b200.tuner import ConvShape, _Bench
     ctx = L.Context(0)
@@ -136,11 +136,14 @@ def test_int8_conv_same_bits_for_every_tile_config(shape):
         x[..., d.c:] = 0
         ctx.upload(b.x, x)
         outs = {}
-        for cfg in ((0, 0), (256, 3), (192, 3), (128, 2), (64, 3), (128, 4), (64, 8)):
-            b.run(L.TileCfg(bn=cfg[0], stages=cfg[1], flags=0) if cfg[0] else None)
+        # (bn, stages, flags): tile configurations, and split-K into 2 and 7
+        # slices (flags bits 8-15)
+        for cfg in ((0, 0, 0), (256, 3, 0), (192, 3, 0), (128, 2, 0), (64, 3, 0), (128, 4, 0), (64, 8, 0),
+                    (0, 0, 2 << 8), (64, 3, 7 << 8), (256, 3, 7 << 8)):
+            b.run(L.TileCfg(bn=cfg[0], stages=cfg[1], flags=cfg[2]) if any(cfg) else None)
             ctx.sync()
             outs[cfg] = ctx.download(b.y, (d.n * d.oh * d.ow, d.k_stride), np.float32)[:, :d.k]
-        ref = outs[(0, 0)]
+        ref = outs[(0, 0, 0)]
         assert np.isfinite(ref).all() and np.abs(ref).max() > 0
         for cfg, y in outs.items():
             np.testing.assert_array_equal(y, ref, err_msg=str(cfg))

@@ -244,6 +244,40 @@ def test_conv_halo_band_matches_per_tap_paths(ctx, case):
         np.testing.assert_array_equal(halo, per_tap)
 
 
+SPLIT_CASES = [
+    # n, c, h, w, k, r, stride, pad, splits
+    (1, 512, 7, 7, 512, 3, 1, 1, 9),      # ResNet-18 layer4 at b=1
+    (1, 256, 14, 14, 256, 3, 1, 1, 4),
+    (1, 96, 9, 9, 200, 3, 1, 1, 3),       # ragged k (200 of 256 columns) and M (81 rows)
+    (2, 64, 8, 8, 64, 3, 2, 1, 5),        # 9 k-blocks in 5 uneven slices, stride 2
+]
+
+
+@pytest.mark.parametrize("case", SPLIT_CASES, ids=[str(c) for c in SPLIT_CASES])
+def test_conv_split_k(ctx, case):
+    """Split-K: slices of the reduction on different CTAs, the tile's last one
+    summing them in slice order. Matches the unsplit kernel (bf16 rounding of a
+    differently ordered fp32 sum) and the oracle, and repeats bit for bit (the
+    arrival counters are left at zero)."""
+    n, c, h, w, k, r, st, pad, splits = case
+    rng = np.random.default_rng(500 + sum(case))
+    x = rng.standard_normal((n, c, h, w)).astype(np.float32)
+    wt = (rng.standard_normal((k, c, r, r)) * np.sqrt(2.0 / (c * r * r))).astype(np.float32)
+    b = (rng.standard_normal(k) * 0.1).astype(np.float32)
+    oh, ow = (h + 2 * pad - r) // st + 1, (w + 2 * pad - r) // st + 1
+    res = rng.standard_normal((n, k, oh, ow)).astype(np.float32)
+    split1 = run_conv(ctx, x, wt, b, stride=st, pad=pad, act=L.ACT_RELU, res=res, flags=splits << 8)
+    split2 = run_conv(ctx, x, wt, b, stride=st, pad=pad, act=L.ACT_RELU, res=res, flags=splits << 8)
+    whole = run_conv(ctx, x, wt, b, stride=st, pad=pad, act=L.ACT_RELU, res=res)
+    np.testing.assert_array_equal(split1, split2)
+    check(split1, whole, 1e-2)
+    check(split1, oracle_conv(x, wt, b, stride=st, pad=pad, act="Relu", res=res), 1e-2)
+    # fp32 output (the FC / logits form) through the same split
+    f1 = run_conv(ctx, x, wt, b, stride=st, pad=pad, act=L.ACT_RELU, out_f32=True, flags=splits << 8)
+    f0 = run_conv(ctx, x, wt, b, stride=st, pad=pad, act=L.ACT_RELU, out_f32=True)
+    check(f1, f0, 1e-4)
+
+
 @pytest.mark.parametrize("act,name", [(L.ACT_NONE, None), (L.ACT_CLIP, "Clip"), (L.ACT_SIGMOID, "Sigmoid"),
                                       (L.ACT_GELU, "Gelu"), (L.ACT_HARD_SWISH, "HardSwish"),
                                       (L.ACT_LEAKY_RELU, "LeakyRelu"), (L.ACT_TANH, "Tanh")])
@@ -394,7 +428,8 @@ def _s2d_ref(x):
 
 @pytest.mark.parametrize("dtype", [L.BF16, L.F32, L.U8, L.S8])
 @pytest.mark.parametrize("shape,cs", [((2, 3, 20, 18), 16), ((1, 4, 8, 6), 16), ((2, 1, 6, 4), 16),
-                                      ((2, 3, 20, 18), 32), ((2, 5, 10, 12), 24)])
+                                      ((2, 3, 20, 18), 32), ((2, 5, 10, 12), 24),
+                                      ((3, 3, 14, 28), 16), ((2, 3, 10, 24), 32)])   # two pixels per thread
 def test_space_to_depth_input(ctx, dtype, shape, cs):
     """fp32 NCHW -> 2x2 space-to-depth NHWC (16-channel stem kernel and the
     generic one), quantising for 8-bit types."""
