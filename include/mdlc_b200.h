@@ -210,6 +210,30 @@ int mdlc_conv_weight_bytes(const mdlc_conv_desc* desc, size_t* bytes);
  * layout the kernel for desc reads; int8 paths take already-quantised int8
  * values stored as float. Host-only. */
 int mdlc_pack_conv_weights(const mdlc_conv_desc* desc, const float* host_w_oihw, void* host_out);
+/* Split-K convolution that allocates nothing. No counterpart in the reference.
+ * For callers that cannot call cudaMalloc -- a plug-in that only borrows a
+ * stream from a host framework whose memory manager owns every device
+ * allocation, or a service whose device memory budget is fixed at start-up --
+ * and so cannot create an mdlc_ctx either. Runs mdlc_conv2d's tcgen05 kernel
+ * with the reduction cut into `splits` (2..255) slices, as tile-config flags
+ * bits 8-15 do, on `stream` (a cudaStream_t of the current device), with its
+ * scratch (per-slice partials, per-tile arrival counters, error word) in a
+ * fixed array of this library's device image: 8 MiB + 8 KiB, held by every GPU
+ * that loads the library until the process exits. Layers needing more partials
+ * than 8 MiB (tiles x splits x 128 x bn x 4 bytes) are rejected with
+ * MDLC_ERR_INVALID; only bf16 inputs and groups == 1. The first call on a device
+ * looks up the array's device address and should come before any stream
+ * capture; each call clears the counters and the error word with
+ * cudaMemsetAsync on `stream`. All calls on one GPU share that GPU's copy of
+ * the array, which keeps the last call's contents: calls whose work can overlap
+ * on the GPU (issued to different streams, or from host threads without
+ * ordering between them) race on it and must be serialised by the caller.
+ * Device-side errors (a bounded wait that ran out) are not reported.
+ * On failure `msg` (may be null) receives a message. */
+int mdlc_conv2d_splitk_noalloc(const mdlc_conv_desc* desc, const void* x, const void* w_packed,
+                               const void* bias, const void* residual, void* y, const mdlc_epilogue* epi,
+                               int splits, void* stream, char* msg, size_t msg_len);
+
 /* Depthwise convolution (groups == c == k): the entry point of
  * mdlc_conv2d's depthwise path with the shape checked. Replaces the grouped
  * conv host fallback (emit.py:175-180, ops.py:68-78). Weights packed by

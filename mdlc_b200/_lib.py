@@ -112,6 +112,8 @@ SIGNATURES = {
     "mdlc_pack_conv_weights": ([C.POINTER(ConvDesc), _P, _P], C.c_int),
     "mdlc_pool2d": ([_P, C.POINTER(PoolDesc), _P, _P], C.c_int),
     "mdlc_dwconv2d": ([_P, C.POINTER(ConvDesc), _P, _P, _P, _P, _P, C.POINTER(Epilogue)], C.c_int),
+    "mdlc_conv2d_splitk_noalloc": ([C.POINTER(ConvDesc), _P, _P, _P, _P, _P, C.POINTER(Epilogue), C.c_int, _P,
+                                    C.c_char_p, C.c_size_t], C.c_int),
     "mdlc_gemm_weight_bytes": ([C.POINTER(GemmDesc), C.POINTER(C.c_size_t)], C.c_int),
     "mdlc_pack_gemm_weights": ([C.POINTER(GemmDesc), _P, _P], C.c_int),
     "mdlc_gemm": ([_P, C.POINTER(GemmDesc), _P, _P, _P, _P, C.POINTER(Epilogue), C.POINTER(TileCfg)], C.c_int),
