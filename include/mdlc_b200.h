@@ -103,7 +103,9 @@ typedef struct {
   int32_t oh, ow;
   int32_t groups;
   int32_t in_type, out_type;    /* MDLC_BF16 -> MDLC_BF16|MDLC_F32; MDLC_F32 -> MDLC_F32;
-                                   MDLC_U8|MDLC_S8 -> MDLC_U8|MDLC_S8|MDLC_F32 */
+                                   MDLC_U8|MDLC_S8 -> MDLC_U8|MDLC_S8|MDLC_F32|MDLC_S32, where
+                                   MDLC_S32 writes the int32 accumulator + bias32 (no
+                                   requantisation, no residual; k_stride a multiple of 8) */
   int32_t res_stride;           /* residual channel stride (0: same as k_stride) */
   int32_t in_zp;                /* 8-bit input zero point: padded taps read this value */
 } mdlc_conv_desc;
@@ -223,16 +225,25 @@ int mdlc_pack_conv_weights(const mdlc_conv_desc* desc, const float* host_w_oihw,
  * than 8 MiB (tiles x splits x 128 x bn x 4 bytes) are rejected with
  * MDLC_ERR_INVALID; only bf16 inputs and groups == 1. The first call on a device
  * looks up the array's device address and should come before any stream
- * capture; each call clears the counters and the error word with
- * cudaMemsetAsync on `stream`. All calls on one GPU share that GPU's copy of
- * the array, which keeps the last call's contents: calls whose work can overlap
- * on the GPU (issued to different streams, or from host threads without
- * ordering between them) race on it and must be serialised by the caller.
- * Device-side errors (a bounded wait that ran out) are not reported.
+ * capture; each call clears the arrival counters it uses with cudaMemsetAsync
+ * on `stream`. All calls on one GPU share that GPU's copy of the array, which
+ * keeps the last call's contents: calls whose work can overlap on the GPU
+ * (issued to different streams, or from host threads without ordering between
+ * them) race on it and must be serialised by the caller. A device-side error
+ * (a bounded wait that ran out: the output is then incomplete) is kept in the
+ * array's error word, which mdlc_conv2d_splitk_noalloc_status reads. The
+ * array's device address is cached per device for the life of the process:
+ * after a device reset these entry points must not be called again.
  * On failure `msg` (may be null) receives a message. */
 int mdlc_conv2d_splitk_noalloc(const mdlc_conv_desc* desc, const void* x, const void* w_packed,
                                const void* bias, const void* residual, void* y, const mdlc_epilogue* epi,
                                int splits, void* stream, char* msg, size_t msg_len);
+/* Companion of mdlc_conv2d_splitk_noalloc, also allocation-free and with no
+ * reference counterpart: synchronises `stream`, then reads and clears the
+ * current device's error word into *flag (MDLC_DEVERR_* of the first
+ * device-side error any call on this device recorded since the last status
+ * call, or MDLC_DEVERR_NONE). */
+int mdlc_conv2d_splitk_noalloc_status(void* stream, int* flag, char* msg, size_t msg_len);
 
 /* Depthwise convolution (groups == c == k): the entry point of
  * mdlc_conv2d's depthwise path with the shape checked. Replaces the grouped
@@ -305,6 +316,10 @@ int mdlc_launch_count(mdlc_ctx* ctx, long long* count);
  * kernel records MDLC_DEVERR_WAIT_TIMEOUT in the error word and returns. Used
  * to test the bounded-wait path without faulting or hanging the GPU. */
 int mdlc_debug_timeout_probe(mdlc_ctx* ctx, int limit_us);
+/* Fills the context's split-K arrival counters with the byte `value` (on the
+ * stream), reproducing the state a split-K call that gave up on a bounded wait
+ * leaves behind, so tests can check that the next split-K call is unaffected. */
+int mdlc_debug_poison_split_counters(mdlc_ctx* ctx, int value);
 
 #ifdef __cplusplus
 }

@@ -114,6 +114,7 @@ SIGNATURES = {
     "mdlc_dwconv2d": ([_P, C.POINTER(ConvDesc), _P, _P, _P, _P, _P, C.POINTER(Epilogue)], C.c_int),
     "mdlc_conv2d_splitk_noalloc": ([C.POINTER(ConvDesc), _P, _P, _P, _P, _P, C.POINTER(Epilogue), C.c_int, _P,
                                     C.c_char_p, C.c_size_t], C.c_int),
+    "mdlc_conv2d_splitk_noalloc_status": ([_P, C.POINTER(C.c_int), C.c_char_p, C.c_size_t], C.c_int),
     "mdlc_gemm_weight_bytes": ([C.POINTER(GemmDesc), C.POINTER(C.c_size_t)], C.c_int),
     "mdlc_pack_gemm_weights": ([C.POINTER(GemmDesc), _P, _P], C.c_int),
     "mdlc_gemm": ([_P, C.POINTER(GemmDesc), _P, _P, _P, _P, C.POINTER(Epilogue), C.POINTER(TileCfg)], C.c_int),
@@ -130,6 +131,7 @@ SIGNATURES = {
     "mdlc_event_elapsed": ([_P, C.c_int, C.c_int, C.POINTER(C.c_float)], C.c_int),
     "mdlc_launch_count": ([_P, C.POINTER(C.c_longlong)], C.c_int),
     "mdlc_debug_timeout_probe": ([_P, C.c_int], C.c_int),
+    "mdlc_debug_poison_split_counters": ([_P, C.c_int], C.c_int),
 }
 
 _lib = None
@@ -336,6 +338,9 @@ class Context:
 
     def timeout_probe(self, limit_us: int) -> None:
         self.check(self.lib.mdlc_debug_timeout_probe(self.h, int(limit_us)), "timeout_probe")
+
+    def poison_split_counters(self, value: int) -> None:
+        self.check(self.lib.mdlc_debug_poison_split_counters(self.h, int(value)), "poison_split_counters")
 
     def close(self) -> None:
         if getattr(self, "h", None):

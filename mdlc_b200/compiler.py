@@ -13,8 +13,17 @@ that ``GpuExecutor(module).run(feeds, timing)`` executes
 ``graph`` is the passes-optimised IR — the reference's own ``Graph`` from
 ``default_pipeline()`` works by duck typing, as does
 :class:`mdlc_b200.ir.Graph` from :func:`mdlc_b200.passes.default_pipeline`.
-``schedule_fn`` (the reference codegen hook, ``emit.py:27,100``) is accepted
-as ``tuner``: a callable ``tuner(kind, geom) -> (bn, stages) | None``.
+Two schedule hooks: ``schedule_fn(node, (M, N, K)) -> GemmSchedule`` is the
+reference codegen's own hook (``emit.py:27,100``; a reference ``Tuner`` works
+as one), called with the same (M, N, K) per node, its output-channel tile
+mapped to this kernel's tile width (:func:`mdlc_b200.tuner.from_reference_schedule`);
+``tuner(kind, geom) -> (bn, stages) | None`` (:class:`mdlc_b200.tuner.Tuner`)
+searches this kernel's own tile configurations.
+
+``mem_plan`` (a reference ``MemoryPlan``, ``mdlc/runtime/memory_planner.py:30-41``,
+or its ``assignment`` dict) lays the arena out by the plan's tensor -> buffer
+sharing where that is safe for the backend's fused steps
+(:func:`mdlc_b200.memory.plan_from_reference`; ``report()`` lists what moved).
 
 Multi-GPU: ``devices=G`` shards the batch into G contiguous slices, one per
 GPU, with weights replicated and no collective; each device runs its slice
@@ -32,6 +41,7 @@ import numpy as np
 
 from mdlc_b200 import _lib as L
 from mdlc_b200 import lowering, memory
+from mdlc_b200 import tuner as tuner_mod
 from mdlc_b200 import shapes as S
 
 DTYPES = {"bf16": L.BF16, "fp32": L.F32, "f32": L.F32, "int8": L.U8}
@@ -67,7 +77,16 @@ class _Device:
         self.batch = batch
         lo = exe._lowered_for(batch)
         self.lo = lo
-        self.plan = memory.plan_arena(lo.steps, lo.tensors, lo.inputs, lo.outputs, reuse=not exe.keep_all)
+        ref_plan = exe.ref_mem_plan
+        if ref_plan is not None and not exe.keep_all:
+            # the reference MemoryPlan's tensor -> buffer assignment (or that dict itself)
+            assignment = getattr(ref_plan, "assignment", ref_plan)
+            self.plan = memory.plan_from_reference(lo.steps, lo.tensors, lo.inputs, lo.outputs, assignment)
+            bad = memory.conflicts(self.plan, lo.steps, lo.tensors, lo.inputs, lo.outputs)
+            if bad:
+                raise RuntimeError(f"internal: arena plan from mem_plan overlaps live tensors {bad[:3]}")
+        else:
+            self.plan = memory.plan_arena(lo.steps, lo.tensors, lo.inputs, lo.outputs, reuse=not exe.keep_all)
         self.q = exe.qplan
         self.arena = self.ctx.alloc(max(self.plan.total_bytes, 256))
         self.addr = {name: self.arena + off for name, off in self.plan.offsets.items()}
@@ -156,10 +175,15 @@ class _Device:
                         epi.out_zp = self.q.tensors[st.outputs[0]][1]
                         epi.qmin, epi.qmax = cq.qmin, cq.qmax
                 cfg = None
+                choice = None
                 if self.exe.tuner is not None:
                     choice = self.exe.tuner("conv", dict(geom, dtype=lo.dtype))
-                    if choice:
-                        cfg = L.TileCfg(bn=choice[0], stages=choice[1], flags=0)
+                elif self.exe.schedule_fn is not None:
+                    choice = tuner_mod.from_reference_schedule(self.exe.schedule_fn,
+                                                               self.exe.node_by_name.get(st.nodes[0]), geom)
+                if choice:
+                    cfg = L.TileCfg(bn=choice[0], stages=choice[1], flags=0)
+                    self.exe.schedules[st.params["weight"]] = tuple(choice)
                 calls.append(("conv", d, self.ptr(st.inputs[0]), self.wbuf[st.params["weight"]],
                               self.bbuf[st.params["weight"]],
                               self.ptr(st.params["residual"]) if st.params["residual"] else 0,
@@ -353,9 +377,14 @@ class Executable:
     """A compiled graph bound to one or more B200s."""
 
     def __init__(self, graph, *, dtype="bf16", batch=None, devices=1, tuner=None, mem_plan=None,
-                 keep_all=False, calib=None):
+                 keep_all=False, calib=None, schedule_fn=None):
         if dtype not in DTYPES:
             raise ValueError(f"dtype must be one of {sorted(DTYPES)}")
+        if tuner is not None and schedule_fn is not None:
+            raise ValueError("give either tuner= or schedule_fn=, not both")
+        self.schedule_fn = schedule_fn
+        self.schedules = {}   # weight name -> (bn, stages) chosen through a hook
+        self.node_by_name = {n.name: n for n in graph.nodes}
         self.graph = graph
         self.keep_all = keep_all
         self.qplan = None
@@ -535,9 +564,14 @@ def compile(graph, *, mem_plan=None, dtype: str = "bf16", batch=None, devices=1,
             schedule_fn=None, calib=None) -> Executable:
     """Compile a post-pass Graph IR for B200 execution (see module docstring).
 
+    ``mem_plan``: a reference ``MemoryPlan`` (or its tensor -> buffer id dict)
+    to lay the activation arena out by. ``schedule_fn``: the reference's
+    ``schedule_fn(node, (M, N, K))`` hook; ``tuner``: this backend's
+    ``tuner(kind, geom)`` hook (at most one of the two).
+
     ``dtype="int8"`` quantises the graph (:mod:`mdlc_b200.quant`): ``calib`` is
     either a dict of per-tensor (min, max) ranges, a list of feed dicts to
     calibrate on, or None for 32 seeded N(0, 1) batches of 4 images.
     """
-    return Executable(graph, dtype=dtype, batch=batch, devices=devices, tuner=tuner or schedule_fn,
+    return Executable(graph, dtype=dtype, batch=batch, devices=devices, tuner=tuner, schedule_fn=schedule_fn,
                       mem_plan=mem_plan, calib=calib)

@@ -363,7 +363,7 @@ Path path_of(const mdlc_conv_desc& d) {
   if (d.groups == 1) {
     if (d.in_type == MDLC_BF16 && (d.out_type == MDLC_BF16 || d.out_type == MDLC_F32)) return kPathTC;
     if ((d.in_type == MDLC_U8 || d.in_type == MDLC_S8) &&
-        (d.out_type == MDLC_U8 || d.out_type == MDLC_S8 || d.out_type == MDLC_F32))
+        (d.out_type == MDLC_U8 || d.out_type == MDLC_S8 || d.out_type == MDLC_F32 || d.out_type == MDLC_S32))
       return kPathTC;
     if (d.in_type == MDLC_F32 && d.out_type == MDLC_F32) return kPathF32;
     return kPathNone;
@@ -516,8 +516,10 @@ extern "C" int mdlc_conv2d(mdlc_ctx* ctx, const mdlc_conv_desc* d, const void* x
   cudaSetDevice(ctx->device);
   switch (path_of(*d)) {
     case kPathTC:
+      if (d->out_type == MDLC_S32 && res)
+        return mdlc_set_error(ctx, MDLC_ERR_INVALID, "conv int8: no residual with int32 accumulator output");
       if ((d->in_type == MDLC_U8 || d->in_type == MDLC_S8) && d->out_type != MDLC_F32 &&
-          (!epi || !epi->rq_scale))
+          d->out_type != MDLC_S32 && (!epi || !epi->rq_scale))
         return mdlc_set_error(ctx, MDLC_ERR_INVALID, "conv int8: requantisation scales required");
       if ((d->in_type == MDLC_U8 || d->in_type == MDLC_S8) && d->out_type == MDLC_F32 &&
           (!epi || !epi->deq_scale))

@@ -195,6 +195,17 @@ MDLC_DEV void store_chunk16(const TcArgs& a, int m, int nb0, const uint32_t (&v)
   } else {
     // int8 path: v holds int32 accumulators
     const int32_t* bias32 = static_cast<const int32_t*>(a.bias);
+    if (a.out_type == MDLC_S32) {
+      // the int32 accumulator itself (+ bias32), before any requantisation
+      int32_t* yi = static_cast<int32_t*>(a.y) + row;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const int ch = nb0 + e;
+        if (ch >= a.ks) continue;
+        yi[ch] = ch < a.k ? (int32_t)v[e] + (bias32 ? bias32[ch] : 0) : 0;
+      }
+      return;
+    }
     if (a.out_type == MDLC_F32) {
 #pragma unroll
       for (int e = 0; e < 16; ++e) {
@@ -1216,6 +1227,14 @@ int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w
       return mdlc_set_error(ctx, MDLC_ERR_INVALID,
                             "conv_tc: split-K needs %lld tiles x %d slices of %d x %d accumulators, over the "
                             "%zu-byte workspace", tiles, a.split, kBM, bn, kSplitWsBytes);
+    // The kernel leaves every counter at zero, except on a call whose CTAs gave
+    // up on a bounded wait: that tile's counter keeps its partial count, and
+    // the next split-K call would take a tile's last slice for early. So the
+    // counters this launch uses are cleared on the stream first.
+    if (a.split > 1) {
+      const cudaError_t e = cudaMemsetAsync(a.counters, 0, (size_t)tiles * sizeof(int), ctx->stream);
+      if (e != cudaSuccess) return mdlc_cuda_status(ctx, e, "conv_tc: clearing split-K counters");
+    }
   }
 
   // bf16 / 8-bit output: the epilogue stages 32x64 tiles in shared memory and

@@ -321,3 +321,11 @@ extern "C" int mdlc_debug_timeout_probe(mdlc_ctx* ctx, int limit_us) {
   mdlc_note_launch(ctx);
   return mdlc_cuda_status(ctx, cudaGetLastError(), "timeout probe launch");
 }
+
+extern "C" int mdlc_debug_poison_split_counters(mdlc_ctx* ctx, int value) {
+  if (!ctx || value < 0 || value > 255) return MDLC_ERR_INVALID;
+  cudaSetDevice(ctx->device);
+  return mdlc_cuda_status(
+      ctx, cudaMemsetAsync(ctx->d_split_cnt, value, kSplitCounters * sizeof(int), ctx->stream),
+      "poison split counters");
+}

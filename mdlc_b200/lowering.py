@@ -208,6 +208,16 @@ class _Lowerer:
                         oh=1, ow=1, groups=1)
         geom["flops"] = 2.0 * geom["n"] * geom["oh"] * geom["ow"] * geom["k"] * (geom["c"] // geom["groups"]) \
             * geom["r"] * geom["s"]   # algorithmic work of the node as written in the graph
+        # the (M, N, K) the reference codegen passes to its schedule hook for this
+        # node (mdlc/codegen/cuda/emit.py:202 conv: (OC, OH*OW, C/g*KH*KW) per
+        # image; :225 Gemm / :240 MatMul: (rows, out features, in features)),
+        # and which of M / N is the output-channel axis
+        if op in ("Conv", "FusedConvAct", "FusedConvBNAct"):
+            geom["ref_mnk"] = (geom["k"], geom["oh"] * geom["ow"], (geom["c"] // geom["groups"]) * geom["r"] * geom["s"])
+            geom["ref_channel_axis"] = "M"
+        else:
+            geom["ref_mnk"] = (geom["n"], geom["k"], geom["c"])
+            geom["ref_channel_axis"] = "N"
         bias = np.zeros(round_up(geom["k"], 16), np.float32)
         if b is not None:
             bias[:geom["k"]] = np.asarray(b, np.float32).reshape(-1)

@@ -264,3 +264,31 @@ def main():
 
 if __name__ == "__main__":
     raise SystemExit(main())
+
+
+TILE_WIDTHS = (64, 128, 192, 256)
+
+
+def from_reference_schedule(schedule_fn, node, geom):
+    """Tile choice for one conv from the reference's schedule hook.
+
+    The reference codegen calls ``schedule_fn(node, (M, N, K))``
+    (``mdlc/codegen/cuda/emit.py:27,100``; ``autotuner/tuner.py:164-174``'s
+    ``Tuner`` is such a callable) and tiles its GEMM with the returned
+    ``GemmSchedule`` (``mdlc/codegen/schedule.py:16-31``: ``BM x BN`` block
+    tile). Here the hook is called with the same (M, N, K) for the same node
+    (conv: (OC, OH*OW, C/g*KH*KW); Gemm / MatMul: (rows, out features, in
+    features)), and the schedule's tile along the output-channel axis (``BM``
+    for a conv, where the reference puts output channels on M; ``BN`` for a
+    GEMM) picks this kernel's tile width ``bn``: the smallest of 64 / 128 / 192
+    / 256 that covers it. The pipeline depth stays the library's choice for
+    that width. A hook returning a ``(bn, stages)`` tuple sets both directly;
+    ``None`` keeps the defaults. Returns ``(bn, stages)`` or None."""
+    sched = schedule_fn(node, tuple(geom["ref_mnk"]))
+    if sched is None:
+        return None
+    if isinstance(sched, tuple):
+        return int(sched[0]), int(sched[1])
+    width = int(getattr(sched, "BM" if geom["ref_channel_axis"] == "M" else "BN"))
+    bn = next((w for w in TILE_WIDTHS if w >= width), TILE_WIDTHS[-1])
+    return bn, 0

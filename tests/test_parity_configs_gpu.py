@@ -1,0 +1,239 @@
+"""Parity at the configurations BASELINE.json names, at its stated tolerances.
+
+* Config 1 (Conv+BN+ReLU sweep): Conv -> BatchNormalization -> Relu graphs at
+  (N, C=K, H=W) in {(32,64,56), (32,128,28), (32,256,14), (32,512,7)} plus the
+  three 1x1 stride-2 projections C -> 2C at 56 / 28 / 14, in fp32 and bf16.
+  The golden is the oracle on the *unfused* graph, as the reference's
+  ``test_conv_bn_fold_is_arithmetic_only`` does (``tests/test_passes.py:47-56``).
+  fp32 is held to FP32_REDUCTION (rtol 1e-4, atol 1e-4,
+  ``mdlc/testing/tolerances.py:51-54``); bf16 single layers to the literal
+  elementwise ``allclose(rtol=1e-2, atol=1e-3)`` against the oracle fed the
+  same bf16-rounded input and folded weights.
+* The headline graph: ResNet-18 at b=256, 224x224, compiled exactly as
+  ``bench.py`` compiles it; sampled images' logits equal, bit for bit, a b=1
+  run of the same images, whose logits are checked against the oracle.
+* The measured network-level deviation of bf16 logits (ResNet-18,
+  MobileNetV2, RepViT) from the fp32 oracle, with the fraction of logits
+  outside the literal bound.
+* INT8 int32 accumulators of every conv layer, bit for bit.
+"""
+
+import json
+
+import numpy as np
+import pytest
+
+from mdlc_b200 import _lib as L
+from mdlc_b200 import builders, compile, passes
+from oracle import quant as oq
+from oracle import reference as oref
+
+pytestmark = pytest.mark.gpu
+
+FP32_REDUCTION = dict(rtol=1e-4, atol=1e-4)
+BF16_LITERAL = dict(rtol=1e-2, atol=1e-3)
+
+SWEEP = [
+    # name, n, cin, cout, h, k, stride
+    ("3x3-64@56", 32, 64, 64, 56, 3, 1),
+    ("3x3-128@28", 32, 128, 128, 28, 3, 1),
+    ("3x3-256@14", 32, 256, 256, 14, 3, 1),
+    ("3x3-512@7", 32, 512, 512, 7, 3, 1),
+    ("1x1s2-64->128@56", 32, 64, 128, 56, 1, 2),
+    ("1x1s2-128->256@28", 32, 128, 256, 28, 1, 2),
+    ("1x1s2-256->512@14", 32, 256, 512, 14, 1, 2),
+]
+
+
+def _sweep_graph(n, cin, cout, h, k, stride):
+    raw = builders.conv_bn_relu(n=n, cin=cin, cout=cout, h=h, w=h, k=k, stride=stride, seed=cin + k)
+    feeds = builders.make_input(raw, seed=h)
+    return raw, passes.default_pipeline(builders.conv_bn_relu(n=n, cin=cin, cout=cout, h=h, w=h, k=k,
+                                                               stride=stride, seed=cin + k)), feeds
+
+
+@pytest.mark.parametrize("case", SWEEP, ids=[c[0] for c in SWEEP])
+def test_config1_sweep_fp32(case):
+    _, n, cin, cout, h, k, stride = case
+    raw, g, feeds = _sweep_graph(n, cin, cout, h, k, stride)
+    want = oref.run(raw, feeds)["y"]          # unfused Conv -> BN -> Relu
+    exe = compile(g, dtype="fp32")
+    try:
+        assert exe.fallbacks() == []
+        got = exe.run(feeds)["y"]
+    finally:
+        exe.close()
+    assert got.shape == want.shape
+    np.testing.assert_allclose(got, want, **FP32_REDUCTION)
+
+
+@pytest.mark.parametrize("case", SWEEP, ids=[c[0] for c in SWEEP])
+def test_config1_sweep_bf16_literal(case):
+    """Every element within rtol 1e-2 / atol 1e-3 of the oracle evaluated on
+    the same bf16-rounded operands (input and BN-folded weights; fp32 bias and
+    accumulation), and within the same bound of the unfused fp32 graph where
+    bf16 operand rounding allows (checked through the relative error norm)."""
+    _, n, cin, cout, h, k, stride = case
+    raw, g, feeds = _sweep_graph(n, cin, cout, h, k, stride)
+    same_ops = oref.run(g, feeds, bf16_emulation=True)["y"]
+    exe = compile(g, dtype="bf16")
+    try:
+        got = exe.run(feeds)["y"]
+    finally:
+        exe.close()
+    np.testing.assert_allclose(got, same_ops, **BF16_LITERAL)
+    ref = oref.run(raw, feeds)["y"]
+    rel = np.linalg.norm(got - ref) / np.linalg.norm(ref)
+    assert rel < 1e-2, f"bf16 vs fp32 unfused graph: relative error norm {rel:.2e}"
+
+
+def _same_weights(g_a, g_b):
+    assert set(g_a.initializers) == set(g_b.initializers)
+    for name, arr in g_a.initializers.items():
+        np.testing.assert_array_equal(np.asarray(arr), np.asarray(g_b.initializers[name]), err_msg=name)
+
+
+def test_headline_b256_graph_matches_b1_and_oracle():
+    """The benchmark's own graph (ResNet-18, 256 images of 224x224, bf16, the
+    tile configurations, two-CTAs-per-SM kernels, 192-wide tiles and
+    programmatic dependent launches that batch selects): four sampled images'
+    logits equal a b=1 executable's bit for bit, and those b=1 logits are
+    within the bf16 network bound of the fp32 oracle with the same top-1."""
+    import bench
+    g256 = passes.default_pipeline(builders.BUILDERS["resnet18"](batch=256, seed=0))
+    g1 = bench.g1_graph("resnet18")
+    _same_weights(g256, g1)
+    rng = np.random.default_rng(256)
+    x = rng.standard_normal((256, 3, 224, 224), dtype=np.float32)
+    exe = compile(g256, dtype="bf16", devices=[0])
+    try:
+        assert exe.fallbacks() == []
+        big = exe.run({"input": x})["logits"]
+    finally:
+        exe.close()
+    assert big.shape == (256, 1000) and np.isfinite(big).all()
+    exe1 = compile(g1, dtype="bf16", batch=1)
+    try:
+        for i in (0, 97, 170, 255):
+            one = exe1.run({"input": x[i:i + 1]})["logits"]
+            np.testing.assert_array_equal(big[i:i + 1], one, err_msg=f"image {i}")
+            want = oref.run(g1, {"input": x[i:i + 1]})["logits"]
+            scale = np.abs(want).max()
+            np.testing.assert_allclose(one, want, rtol=1e-2, atol=2e-2 * scale, err_msg=f"image {i}")
+            assert np.argmax(one) == np.argmax(want)
+    finally:
+        exe1.close()
+
+
+# Measured on a B200 with the four images below (seeded N(0,1), 224x224): the
+# bf16 executables' logits against the fp32 oracle. Each bound is the
+# measurement with about 2x headroom; the fraction is of logits outside the
+# literal elementwise bound |d| <= 1e-3 + 1e-2 |want|.
+# Measured: ResNet-18 0.0053 / 0.0038 / 0.236 (logit scale 26.9), MobileNetV2
+# 0.0196 / 0.0200 / 0.688 (scale 8.87), RepViT 0.0048 / 0.0041 / 0.160 (scale 2.69).
+NET_BOUNDS = {
+    # model: (max |d| / max |want|, relative error norm, fraction outside the literal bound)
+    "resnet18": (0.011, 0.008, 0.40),
+    "mobilenetv2": (0.04, 0.04, 0.85),
+    "repvit": (0.01, 0.009, 0.30),
+}
+
+
+@pytest.mark.parametrize("model", sorted(NET_BOUNDS))
+def test_network_bf16_deviation_measured(model):
+    """bf16 stores every activation with 8 mantissa bits, so whole-network
+    logits cannot meet an absolute 1e-3 bound at logit scale; this measures how
+    far they are from the fp32 oracle (printed as NETWORK_DEVIATION) and holds
+    them to the measured figures, with the same top-1 class on every image."""
+    g = passes.default_pipeline(builders.BUILDERS[model](batch=4, seed=0))
+    x = np.random.default_rng(4).standard_normal((4, 3, 224, 224), dtype=np.float32)
+    want = oref.run(g, {"input": x})["logits"]
+    exe = compile(g, dtype="bf16")
+    try:
+        got = exe.run({"input": x})["logits"]
+    finally:
+        exe.close()
+    d = np.abs(got - want)
+    scale = float(np.abs(want).max())
+    m = {"model": model, "images": 4, "logit_scale": scale, "max_abs": float(d.max()),
+         "max_abs_over_scale": float(d.max()) / scale,
+         "max_rel_elem": float((d / np.maximum(np.abs(want), 1e-3)).max()),
+         "rel_norm": float(np.linalg.norm(got - want) / np.linalg.norm(want)),
+         "frac_outside_literal": float(np.mean(d > 1e-3 + 1e-2 * np.abs(want))),
+         "top1_agree": int(np.sum(np.argmax(got, 1) == np.argmax(want, 1)))}
+    print("NETWORK_DEVIATION " + json.dumps(m))
+    b_abs, b_norm, b_frac = NET_BOUNDS[model]
+    assert m["max_abs_over_scale"] <= b_abs, m
+    assert m["rel_norm"] <= b_norm, m
+    assert m["frac_outside_literal"] <= b_frac, m
+    assert m["top1_agree"] == 4, m
+
+
+def _int8_accumulators(exe, g, feeds):
+    """Re-run every conv of an int8 executable's last forward with int32
+    accumulator output (acc + bias32) and compare with the integer oracle's
+    accumulators of the same layer, computed from the oracle's codes of the
+    layer input (which the per-layer test shows equal the device's)."""
+    want = oq.run_int8(g, exe.qplan, feeds)["__codes__"]
+    alias = {n.outputs[0]: n.inputs[0] for n in g.nodes if n.op_type in oq.ALIASES}
+
+    def src(name):
+        while name in alias:
+            name = alias[name]
+        return name
+
+    dev = exe.devices[0]
+    ctx = dev.ctx
+    nodes = {n.name: n for n in g.nodes}
+    checked = 0
+    for st, call in zip(dev.lo.steps, dev.calls):
+        if st.kind != "conv":
+            continue
+        _, d, x, w, b, _, _, _, cfg = call
+        cq = exe.qplan.convs[st.params["weight"]]
+        node = nodes[st.nodes[0]]
+        attrs = node.attrs if node.op_type not in ("Gemm", "FusedGemmAct", "MatMul") else {}
+        xq = np.asarray(want[src(cq.x)])
+        if xq.ndim == 2:
+            xq = xq.reshape(xq.shape[0], xq.shape[1], 1, 1)
+        zp_x = exe.qplan.tensors[src(cq.x)][1]
+        acc = oq.conv_int(xq, cq.w_q_orig, zp_x, attrs) + cq.bias32.astype(np.int64).reshape(1, -1, 1, 1)
+        assert acc.min() >= -(1 << 31) and acc.max() < (1 << 31)
+        d32 = L.ConvDesc(**{f: getattr(d, f) for f, _ in L.ConvDesc._fields_})
+        d32.out_type = L.S32
+        nbytes = d32.n * d32.oh * d32.ow * d32.k_stride * 4
+        y = ctx.alloc(nbytes)
+        try:
+            ctx.memset(y, 0xFF, nbytes)
+            ctx.conv2d(d32, x, w, b, 0, y, L.Epilogue(act=L.ACT_NONE), cfg)
+            ctx.sync()
+            got = ctx.download(y, (d32.n, d32.oh, d32.ow, d32.k_stride), np.int32)
+        finally:
+            ctx.free(y)
+        assert np.all(got[..., d32.k:] == 0)
+        got = got[..., :d32.k].transpose(0, 3, 1, 2).astype(np.int64)
+        bad = np.argwhere(got != acc.reshape(got.shape))
+        assert bad.size == 0, (f"{st.label()}: {len(bad)} of {got.size} int32 accumulators differ; "
+                               f"first {bad[0].tolist()}: device {got[tuple(bad[0])]} "
+                               f"oracle {acc.reshape(got.shape)[tuple(bad[0])]}")
+        checked += 1
+    return checked
+
+
+@pytest.mark.parametrize("name,kw", [("resnet18", dict(batch=2, image=64)), ("resnet18", dict(batch=1)),
+                                     ("conv_bn_relu", dict(n=2, cin=64, cout=80, h=17, w=15, stride=2))],
+                         ids=["resnet18-b2-64", "resnet18-b1-224", "conv-ragged-s2"])
+def test_int8_int32_accumulators_bit_exact(name, kw):
+    """BASELINE config 3 asks for bit-exact int32 accumulators: every conv
+    layer's (u8 codes x s8 weights) int32 sums, including the space-to-depth
+    stem, the stride-2 projections and the FC, equal the integer oracle's."""
+    from mdlc_b200.compiler import Executable
+    g = passes.default_pipeline(builders.BUILDERS[name](**kw))
+    n = g.value_info[g.runtime_inputs[0]].shape[0]
+    exe = Executable(g, dtype="int8", batch=n, keep_all=True)
+    try:
+        feeds = builders.make_input(g, seed=21)
+        exe.run(feeds)
+        assert _int8_accumulators(exe, g, feeds) >= 1
+    finally:
+        exe.close()

@@ -37,8 +37,9 @@ def _nhwc(x, cs):
 
 def test_splitk_noalloc_matches_conv2d_on_two_calls():
     """Two calls in a row of the allocation-free entry point (on the caller's
-    stream) give what mdlc_conv2d gives for the same split-K conv, within the
-    bf16 tolerance of the kernel tests."""
+    stream) give what mdlc_conv2d gives for the same split-K conv, and what the
+    oracle gives, within the bf16 tolerance of the kernel tests; the status
+    query reports no device-side error after each."""
     ctx = L.Context(0)
     lib = L.load()
     n, c, h, w, k, splits = 1, 512, 7, 7, 512, 9       # ResNet-18 layer4 at b=1, 8 k-blocks a slice
@@ -63,6 +64,9 @@ def test_splitk_noalloc_matches_conv2d_on_two_calls():
         ctx.conv2d(d, xd, wd, bd, rd, y_ref, epi, L.TileCfg(bn=0, stages=0, flags=splits << 8))
         ctx.sync()
         want = _from_bf16_bits(ctx.download(y_ref, (n, h, w, k), np.uint16))
+        xr, wr, rr = oref.round_bf16(x), oref.round_bf16(wt), oref.round_bf16(res)
+        oracle = oref.conv(xr, wr, b, strides=[1, 1], pads=[1, 1, 1, 1]) + rr
+        oracle = np.maximum(oracle, 0).transpose(0, 2, 3, 1)
         stream = C.c_void_p()
         assert lib.mdlc_get_stream(ctx.h, C.byref(stream)) == 0
         msg = C.create_string_buffer(256)
@@ -76,6 +80,12 @@ def test_splitk_noalloc_matches_conv2d_on_two_calls():
             got = _from_bf16_bits(ctx.download(y_new, (n, h, w, k), np.uint16))
             err = np.abs(got - want).max()
             assert err <= 1e-2 * np.abs(want).max(), f"call {call}: max err {err}"
+            # and directly against the oracle on the same bf16-rounded operands
+            err_o = np.abs(got - oracle).max()
+            assert err_o <= 1e-2 * np.abs(oracle).max(), f"call {call}: max err vs oracle {err_o}"
+            flag = C.c_int(-1)
+            assert lib.mdlc_conv2d_splitk_noalloc_status(stream, C.byref(flag), msg, len(msg)) == 0, msg.value
+            assert flag.value == 0, f"call {call}: device error word {flag.value}"
     finally:
         for p in bufs:
             ctx.free(p)
