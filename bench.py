@@ -110,61 +110,169 @@ def conv_flops(exe):
     return [lo.weights[st.params["weight"]][0]["flops"] for st in lo.steps if st.kind == "conv"]
 
 
-def conv_traffic():
-    """DRAM bytes per conv_tc_kernel launch from the committed ncu launch list of
-    this workload (profiles/conv_tc_resnet18_b256_dram.json), or None."""
+def conv_traffic(workload):
+    """DRAM bytes (read + write) per conv_tc_kernel launch of one forward of
+    ``workload``, from the committed single-kernel ncu captures
+    (profiles/conv_tc_<workload>_dram.json: every conv launch of one forward,
+    captured three launches per ncu run), averaged over the launches; or None."""
     try:
-        with open(os.path.join(ROOT, "profiles", "conv_tc_resnet18_b256_dram.json")) as f:
-            return json.load(f)["dram_bytes_per_launch"]
+        with open(os.path.join(ROOT, "profiles", f"conv_tc_{workload}_dram.json")) as f:
+            per = json.load(f)["dram_bytes_per_launch"]
+        return round(sum(per) / len(per)) if per else None
     except Exception:
         return None
 
 
-def timed_steps(exe, steps):
-    """`steps` forwards issued back to back between two CUDA events on the
-    device stream (inputs resident); returns the elapsed ms."""
-    dev = exe.devices[0]
-    ctx = dev.ctx
-    ctx.event_record(0)
-    for _ in range(steps):
-        dev.issue_forward()
-    ctx.event_record(1)
-    ctx.sync()
-    return ctx.event_elapsed(0, 1)
+def _esz(t):
+    from mdlc_b200 import _lib as L
+    return L.ELEM_BYTES[t]
 
 
-def conv_launch_times(exe, steps):
+def call_work(dev, call):
+    """(kernel class, roofline bound, algorithmic bytes, algorithmic FLOPs) of one
+    prepared call: bytes = every tensor the kernel must read or write, once, in
+    its stored layout (weights as packed); FLOPs = 2 x MACs of the graph node."""
+    from mdlc_b200 import _lib as L
+    kind = call[0]
+    if kind == "conv":
+        _, d, x, w, b, r, y, epi, cfg = call
+        ein, eout = _esz(d.in_type), _esz(d.out_type)
+        xb = d.n * d.h * d.w * d.c_stride * ein
+        yb = d.n * d.oh * d.ow * d.k_stride * eout
+        rb = d.n * d.oh * d.ow * (d.res_stride or d.k_stride) * eout if r else 0
+        wb = L.weight_bytes(d)
+        flops = 2.0 * d.n * d.oh * d.ow * d.k * (d.c // d.groups) * d.r * d.s
+        if d.groups == 1 and d.in_type != L.F32:
+            cls, bound = "conv_tc", "tensor"
+            if d.r == 1 and d.s == 1 and d.h * d.w == 1:
+                cls = "conv_tc(fc)"
+        elif d.groups == 1:
+            cls, bound = "conv_f32", "fp32 simt"
+        else:
+            cls, bound = "conv_dw", "hbm"
+        return cls, bound, xb + wb + yb + rb, flops
+    if kind == "pool":
+        d = call[1]
+        e = _esz(d.dtype)
+        cls = {0: "maxpool", 1: "avgpool", 2: "gap"}[d.kind]
+        return cls, "hbm", d.n * d.h * d.w * d.c_stride * e + d.n * d.oh * d.ow * d.c_stride * e, 0.0
+    prog = call[1]
+    e = _esz(prog.dtype)
+    full = prog.n * prog.hw * prog.c_stride * e
+    ins = sum({L.BC_FULL: full, L.BC_NC: prog.n * prog.c_stride * e, L.BC_C: prog.c_stride * 4,
+               L.BC_SCALAR: e}[prog.bcast[i]] for i in range(prog.n_inputs))
+    return "eltwise", "hbm", ins + prog.n_outputs * full, 0.0
+
+
+def io_work(dev):
+    """Work of the graph-boundary conversions of one forward: [(class, bytes)]."""
+    lo = dev.lo
+    out = []
+    for name in lo.inputs:
+        t = lo.tensors[name]
+        n = int(np.prod(lo.shapes[name]))
+        out.append(("to_s2d" if t.layout == "s2d2" else "to_nhwc", n * 4 + t.n * t.h * t.w * t.cs * _esz(t.dtype)))
+    for name in lo.outputs:
+        if dev.out_dev[name] is not None:
+            t = lo.tensors[name]
+            out.append(("to_nchw", int(np.prod(lo.shapes[name])) * 4 + t.n * t.h * t.w * t.cs * _esz(t.dtype)))
+    return out
+
+
+def launch_times(exe, steps):
     """A second timed pass of the same forwards with CUDA events recorded
-    around every conv launch (kept out of the region `value` is measured on,
-    since the extra event records cost the stream a little). Event slots are
-    finite, so at most ~2000 conv launches are instrumented. Returns
-    (pass_ms, conv_ms, conv_launches, forwards)."""
+    around every kernel launch (kept out of the region `value` is measured
+    on, since the extra event records cost the stream a little). Event slots
+    are finite, so at most ~2000 launches are instrumented. Returns
+    (pass_ms, {class: {launches, ms, bytes, flops, bound}}, forwards)."""
     dev = exe.devices[0]
     ctx = dev.ctx
-    per_fwd = sum(1 for c in dev.calls if c[0] == "conv")
+    io = io_work(dev)
+    per_fwd = len(dev.calls) + len(io)
     steps = max(1, min(steps, (4000 // 2) // max(per_fwd, 1)))
     slot = 3
-    conv_slots = []
+    marks = []   # (class, bound, bytes, flops, start slot)
+
+    def timed(cls, bound, nbytes, flops, fn):
+        nonlocal slot
+        ctx.event_record(slot)
+        fn()
+        ctx.event_record(slot + 1)
+        marks.append((cls, bound, nbytes, flops, slot))
+        slot += 2
+
+    n_in = len(dev.lo.inputs)
     ctx.event_record(0)
     for _ in range(steps):
-        dev.issue_inputs()
+        if n_in:   # one call converts every graph input
+            timed(io[0][0], "hbm", sum(b for _, b in io[:n_in]), 0.0, dev.issue_inputs)
         for c in dev.calls:
+            cls, bound, nbytes, flops = call_work(dev, c)
             if c[0] == "conv":
                 _, d, x, w, b, r, y, epi, cfg = c
-                ctx.event_record(slot)
-                ctx.conv2d(d, x, w, b, r, y, epi, cfg)
-                ctx.event_record(slot + 1)
-                conv_slots.append((slot, slot + 1))
-                slot += 2
+                timed(cls, bound, nbytes, flops, lambda: ctx.conv2d(d, x, w, b, r, y, epi, cfg))
             elif c[0] == "pool":
-                ctx.pool2d(c[1], c[2], c[3])
+                timed(cls, bound, nbytes, flops, lambda: ctx.pool2d(c[1], c[2], c[3]))
             else:
-                ctx.eltwise(c[1], c[2], c[3])
-        dev.issue_outputs()
+                timed(cls, bound, nbytes, flops, lambda: ctx.eltwise(c[1], c[2], c[3]))
+        if len(io) > n_in:
+            timed("to_nchw", "hbm", sum(b for _, b in io[n_in:]), 0.0, dev.issue_outputs)
+        else:
+            dev.issue_outputs()   # logits written by the FC epilogue: no conversion kernel
     ctx.event_record(1)
     ctx.sync()
-    conv_ms = sum(ctx.event_elapsed(a, b) for a, b in conv_slots)
-    return ctx.event_elapsed(0, 1), conv_ms, len(conv_slots), steps
+    table = {}
+    for cls, bound, nbytes, flops, a in marks:
+        e = table.setdefault(cls, {"launches": 0, "ms": 0.0, "bytes": 0, "flops": 0.0, "bound": bound})
+        e["launches"] += 1
+        e["ms"] += ctx.event_elapsed(a, a + 1)
+        e["bytes"] += nbytes
+        e["flops"] += flops
+    return ctx.event_elapsed(0, 1), table, steps
+
+
+def kernel_table(table, pass_ms, peak_tf, peak_gbs):
+    """Per kernel class: share of the instrumented pass, mean launch time, and
+    the achieved rate against its roofline (TFLOP/s against the measured bf16
+    tensor peak for tensor-bound classes, GB/s against the measured HBM copy
+    bandwidth for memory-bound ones; both figures are given for every class)."""
+    out = {}
+    for cls, e in sorted(table.items(), key=lambda kv: -kv[1]["ms"]):
+        s = e["ms"] / 1e3
+        tf = e["flops"] / s / 1e12 if e["flops"] else 0.0
+        gbs = e["bytes"] / s / 1e9
+        frac = tf / peak_tf if e["bound"] == "tensor" else gbs / peak_gbs
+        out[cls] = {"launches": e["launches"], "share": round(e["ms"] / pass_ms, 4),
+                    "avg_launch_us": round(1e3 * e["ms"] / e["launches"], 2), "bound": e["bound"],
+                    "achieved_tflops": round(tf, 1), "achieved_gbs": round(gbs, 1),
+                    "frac": round(frac, 4)}
+    return out
+
+
+def int8_peak_tops(device):
+    """Dense int8 tensor throughput measured on this GPU: torch._int_mm (a
+    cuBLASLt int8 x int8 -> int32 GEMM) at 8192^3, best of 10 launches timed
+    with CUDA events; the denominator for the int8 convs (the bf16 figure in
+    MEASURED_PEAKS.json is measured the same way with a bf16 GEMM)."""
+    import torch
+    dev = torch.device("cuda", device)
+    n = 8192
+    a = torch.randint(-127, 128, (n, n), dtype=torch.int8, device=dev)
+    b = torch.randint(-127, 128, (n, n), dtype=torch.int8, device=dev)
+    for _ in range(3):
+        torch._int_mm(a, b)
+    best = None
+    for _ in range(10):
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        torch._int_mm(a, b)
+        e1.record()
+        torch.cuda.synchronize(dev)
+        ms = e0.elapsed_time(e1)
+        best = ms if best is None else min(best, ms)
+    del a, b
+    torch.cuda.empty_cache()
+    return round(2.0 * n ** 3 / (best / 1e3) / 1e12, 1)
 
 
 def g1_graph(model):
@@ -276,14 +384,18 @@ def main() -> int:
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=100)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--batch", type=int, default=256, help="images per GPU")
+    ap.add_argument("--batch", type=int, default=None, help="images per GPU (default: the workload's)")
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--cpu-sample", type=int, default=12, help="b=1 oracle forwards for cpu_baseline")
     ap.add_argument("--workload", default=WORKLOAD, choices=sorted(WORKLOADS))
     ap.add_argument("--latency-iters", type=int, default=200, help="b=1 forwards for the p50 latency")
     ap.add_argument("--ref-procs", type=int, default=0, help="reference arm: host processes (0 = every core)")
+    ap.add_argument("--forwards-only", action="store_true",
+                    help="compile, stage the input and run --warmup forwards, then exit (no timing, no "
+                         "JSON line): the program profiled by the committed ncu captures")
     args = ap.parse_args()
-    args.warmup = max(args.warmup, 3)
+    if not args.forwards_only:
+        args.warmup = max(args.warmup, 3)
 
     from mdlc_b200 import dist as mdist
     dist = mdist.from_env()
@@ -298,7 +410,7 @@ def main() -> int:
     from mdlc_b200.compiler import compile as mdlc_compile
 
     model, dtype, default_batch = WORKLOADS[args.workload]
-    if args.workload != WORKLOAD and args.batch == 256:
+    if args.batch is None:
         args.batch = default_batch
     g = passes.default_pipeline(builders.BUILDERS[model](batch=args.batch, seed=0))
     exe = mdlc_compile(g, dtype=dtype, devices=[local])
@@ -315,6 +427,13 @@ def main() -> int:
     for _ in range(args.warmup):
         dev.issue_forward()
     exe.sync()
+    if args.forwards_only:
+        if rank == 0:
+            print(f"forwards-only: {args.workload} b={args.batch}, {1 + args.warmup} forwards of "
+                  f"{exe.launches_per_forward()} launches each", flush=True)
+        exe.close()
+        dist.close()
+        return 0
 
     # ---- timed: device-resident inputs
     barrier()
@@ -330,7 +449,7 @@ def main() -> int:
 
     # ---- per-kernel CUDA events for the roofline (a second timed pass)
     barrier()
-    inst_ms, conv_ms, nconv, inst_steps = conv_launch_times(exe, args.steps)
+    inst_ms, ktable, inst_steps = launch_times(exe, args.steps)
     barrier()
 
     # ---- e2e through the public host API: every step uploads its fp32 input
@@ -366,6 +485,20 @@ def main() -> int:
     logits = exe.wait(0)["logits"]
     assert np.isfinite(logits).all() and np.isfinite(exe.wait(1)["logits"]).all()
 
+    # ---- the whole job on the wall clock: from a common start (barrier) to
+    # every rank's logits gathered, per step: pinned H2D of the shard's
+    # images, forward, D2H of its logits, all-gather of all ranks' logits
+    exe.run_pinned()
+    dist.gather(outs["logits"])
+    barrier()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        exe.run_pinned()
+        gathered = dist.gather(outs["logits"])
+    job_s = max_over_ranks(time.perf_counter() - t0)
+    assert gathered.shape[0] == world * args.batch
+    barrier()
+
     latency = None
     if rank == 0 and args.latency_iters > 0:
         latency = b1_latency(g1_graph(model), dtype, local, args.latency_iters,
@@ -374,10 +507,15 @@ def main() -> int:
     if rank == 0:
         peak_tf, _, peak_kind = _peaks()
         if dtype == "int8":
-            peak_tf, peak_kind = 2 * peak_tf, f"2x {peak_kind}"     # int8 dense rate = 2x bf16
+            peak_tf, peak_kind = int8_peak_tops(local), "measured in this run (torch._int_mm) int8"
         conv_flops_step = sum(flops)
+        tc = [e for k, e in ktable.items() if k.startswith("conv_tc") or k == "conv_f32"]
+        conv_ms = sum(e["ms"] for e in tc)
+        nconv = sum(e["launches"] for e in tc)
         avg_launch_ms = conv_ms / nconv
-        achieved_tf = (conv_flops_step / len(flops)) / (avg_launch_ms / 1e3) / 1e12
+        achieved_tf = (sum(e["flops"] for e in tc) / nconv) / (avg_launch_ms / 1e3) / 1e12
+        _, peak_gbs, _ = _peaks()
+        kernels = kernel_table(ktable, inst_ms, peak_tf, peak_gbs)
         cpu = None
         if world == 1 and args.cpu_sample > 0 and model == "resnet18":
             ips, dt = cpu_baseline_sample(args.cpu_sample)
@@ -406,13 +544,26 @@ def main() -> int:
             "roofline": {"kernel": "conv_tc_kernel (tcgen05 implicit GEMM)", "bound": "tensor",
                          "achieved": round(achieved_tf, 1),
                          "peak": peak_tf, "unit": "TFLOP/s", "frac": round(achieved_tf / peak_tf, 4),
-                         "peak_kind": f"{peak_kind} bf16 (burst)", "traffic": conv_traffic() if args.workload == WORKLOAD else None,
+                         "peak_kind": peak_kind if dtype == "int8" else f"{peak_kind} bf16 (burst)", "traffic": conv_traffic(args.workload),
                          "traffic_unit": "bytes per launch (ncu dram read+write)",
                          "conv_share_of_step": round(conv_ms / inst_ms, 4) if inst_ms else None,
                          "flops_per_launch": round(conv_flops_step / len(flops)),
+                         "algorithmic_bytes_per_launch": round(sum(e["bytes"] for e in tc) / nconv),
                          "avg_launch_ms": round(avg_launch_ms, 5),
                          "how": f"CUDA events around each of the {nconv} conv launches of {inst_steps} "
                                 "forwards, in a timed pass after the one `value` is measured on"},
+            "kernels": kernels,
+            "kernels_how": f"per kernel class over {inst_steps} forwards of the instrumented pass: share of "
+                           "that pass, mean launch time, achieved TFLOP/s (algorithmic FLOPs of the graph "
+                           "nodes) and GB/s (algorithmic bytes: each tensor read or written once in its "
+                           "stored layout); frac against the measured bf16 tensor peak for tensor-bound "
+                           f"classes, the measured HBM copy bandwidth ({peak_gbs} GB/s) for the others",
+            "job": {"value": round(world * args.batch * args.steps / job_s, 1), "unit": "images/s",
+                    "ms_per_step": round(1e3 * job_s / args.steps, 4),
+                    "how": "host wall clock, max over ranks, from a common start (barrier) over "
+                           f"{args.steps} steps of: pinned H2D of each rank's {args.batch} images, forward, "
+                           "D2H of its logits, all-gather of every rank's logits (the final output "
+                           "gather); no overlap between steps"},
             "gpu_launches": launches,
             "network_tflops": round(world * conv_flops_step / (ms_per_step / 1e3) / 1e12, 1),
         }

@@ -66,6 +66,22 @@ class Dist:
         td.all_reduce(t, op=td.ReduceOp.SUM)
         return float(t.item())
 
+    def gather(self, arr):
+        """Concatenate every rank's ``arr`` (same shape and dtype on each) along
+        axis 0, in rank order, on every rank: the final output gather of a
+        batch-sharded run (one all-gather; through device memory on NCCL)."""
+        import numpy as np
+        arr = np.ascontiguousarray(arr)
+        if self.world == 1:
+            return arr.copy()
+        import torch
+        import torch.distributed as td
+        dev = torch.device("cuda", torch.cuda.current_device()) if self.backend == "nccl" else torch.device("cpu")
+        t = torch.from_numpy(arr).to(dev)
+        parts = [torch.empty_like(t) for _ in range(self.world)]
+        td.all_gather(parts, t)
+        return torch.cat(parts, 0).cpu().numpy()
+
     def close(self) -> None:
         if self.world > 1:
             import torch.distributed as td

@@ -173,22 +173,33 @@ def plan_from_reference(steps, tensors, inputs, outputs, assignment: dict) -> Ar
     input and the skip tensor and writes the add's output in one kernel), which
     can keep a tensor live longer than the IR order does. A tenant that would
     share its region with a tensor live at the same time is given a region of
-    its own, and each such move is recorded in the plan's notes. Tensors the
+    another (shared only among moved tenants, never live at the same time, best
+    fit by size), and each such move is recorded in the plan's notes. Tensors the
     reference plan does not pool (graph inputs, which it leaves to external
     storage) get regions of their own; zero-copy aliases share their source's."""
+    assignment = getattr(assignment, "assignment", assignment)   # a MemoryPlan or its dict
     live = liveness(steps, tensors, inputs, outputs)
     order = sorted(live, key=lambda s: (live[s][0], s))
     regions, region_of, notes = {}, {}, []
     for s in order:
         bid = assignment.get(s)
         key = ("ref", bid) if bid is not None and s not in inputs else ("own", s)
-        if key[0] == "ref":
-            f, l_ = live[s]
-            clash = [t for t in regions.get(key, []) if live[t][0] <= l_ and f <= live[t][1]]
-            if clash:
-                notes.append(f"mem_plan: {s!r} moved out of reference buffer {bid} "
-                             f"(live with {clash[0]!r} across the backend's fused steps)")
-                key = ("own", s)
+        f, l_ = live[s]
+
+        def clash(k):
+            return [t for t in regions.get(k, []) if live[t][0] <= l_ and f <= live[t][1]]
+
+        if key[0] == "ref" and clash(key):
+            other = clash(key)[0]
+            # best fit among the regions it can share: no tenant live at the same
+            # time, the smallest that holds it (else the largest)
+            need = _align(tensors[s].nbytes)
+            free = [k for k in regions if k[0] == "moved" and not clash(k)]
+            fits = [k for k in free if max(_align(tensors[t].nbytes) for t in regions[k]) >= need]
+            size = lambda k: max(_align(tensors[t].nbytes) for t in regions[k])   # noqa: E731
+            key = min(fits, key=size) if fits else (max(free, key=size) if free else ("moved", s))
+            notes.append(f"mem_plan: {s!r} moved out of reference buffer {bid} "
+                         f"(live with {other!r} across the backend's fused steps)")
         regions.setdefault(key, []).append(s)
         region_of[s] = key
     used_ref = {k[1] for k in regions if k[0] == "ref"}

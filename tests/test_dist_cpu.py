@@ -39,8 +39,11 @@ def _rank_main(rank, world, port, out):
         got_sum = d.sum(rank + 1)
         lo, hi = mdist.shard(512, world, rank)
         covered = d.sum(hi - lo)
+        import numpy as np
+        part = np.full((3, 4), rank, np.float32) + np.arange(12, dtype=np.float32).reshape(3, 4)
+        whole = d.gather(part)
         d.barrier()
-        out.put((rank, got_max, got_sum, lo, hi, covered))
+        out.put((rank, got_max, got_sum, lo, hi, covered, whole.tolist()))
     finally:
         d.close()
 
@@ -56,9 +59,13 @@ def test_gloo_two_ranks_max_and_shards():
     for p in procs:
         p.join(timeout=60)
         assert p.exitcode == 0
-    for rank, got_max, got_sum, lo, hi, covered in res:
+    import numpy as np
+    base = np.arange(12, dtype=np.float32).reshape(3, 4)
+    for rank, got_max, got_sum, lo, hi, covered, whole in res:
         assert got_max == 11.0 and got_sum == 3.0
         assert covered == 512
+        # the output gather: every rank's shard, in rank order, on every rank
+        np.testing.assert_array_equal(np.asarray(whole, np.float32), np.concatenate([base, base + 1]))
     assert [(r[3], r[4]) for r in res] == [(0, 256), (256, 512)]
 
 

@@ -188,3 +188,76 @@ def test_repvit_matches_oracle(batch, image):
             err_e = np.abs(got - emu).max()
             assert err_e <= 1e-2 * scale, f"bf16 vs bf16-emulating oracle: {err_e:.4g} (scale {scale:.4g})"
         exe.close()
+
+
+def test_reference_mem_plan_and_schedule_fn_through_compile():
+    """compile(mem_plan=<reference MemoryPlan assignment>) lays the arena out by
+    it and compile(schedule_fn=<reference-style hook>) picks tiles through it;
+    both give exactly the logits of the default executable."""
+    import json
+    import os
+    from dataclasses import dataclass
+
+    from conftest import GOLDEN
+
+    @dataclass(frozen=True)
+    class Sched:            # duck type of the reference GemmSchedule
+        BM: int
+        BN: int
+
+    with open(os.path.join(GOLDEN, "memplan.json")) as f:
+        ref_plan = json.load(f)["resnet18_b1"]
+    g, feeds = _case("resnet18", dict(batch=1, image=224))
+    exe = compile(g, dtype="bf16")
+    want = exe.run(feeds)["logits"]
+    exe.close()
+    seen = []
+
+    def schedule_fn(node, mnk):
+        seen.append(mnk)
+        return Sched(BM=128 if mnk[0] >= 128 else 64, BN=128)
+
+    exe = compile(g, dtype="bf16", mem_plan=ref_plan, schedule_fn=schedule_fn)
+    try:
+        assert "reference buffers honoured" in exe.report()
+        assert len(seen) == sum(1 for st in exe.lowered.steps if st.kind == "conv")
+        assert set(exe.schedules.values()) <= {(64, 0), (128, 0)}
+        np.testing.assert_array_equal(exe.run(feeds)["logits"], want)
+    finally:
+        exe.close()
+
+
+def _gpus():
+    from mdlc_b200 import _lib
+    try:
+        return _lib.device_count()
+    except Exception:
+        return 0
+
+
+@pytest.mark.skipif(_gpus() < 2, reason="needs 2 GPUs")
+def test_compile_devices_2_equals_devices_1():
+    """compile(devices=2): the batch split into two contiguous shards, one per
+    GPU, each on its own host thread, outputs gathered on the host -- the
+    logits equal a one-GPU executable's bit for bit."""
+    g, _ = _case("resnet18", dict(batch=8, image=224))
+    x = np.random.default_rng(88).standard_normal((8, 3, 224, 224), dtype=np.float32)
+    one = compile(g, dtype="bf16", devices=1)
+    try:
+        want = one.run({"input": x})["logits"]
+    finally:
+        one.close()
+    two = compile(g, dtype="bf16", devices=2)
+    try:
+        assert [d.ctx.device for d in two.devices] == [0, 1]
+        got = two.run({"input": x})["logits"]
+        np.testing.assert_array_equal(got, want)
+        # the serving calls too: pinned feeds per device, submit / wait
+        for i, d in enumerate(two.devices):
+            two.pinned_inputs(device=i)["input"][...] = x[4 * i:4 * i + 4]
+        two.submit(0)
+        two.wait(0)
+        for i in range(2):
+            np.testing.assert_array_equal(two.pinned_outputs(device=i)["logits"], want[4 * i:4 * i + 4])
+    finally:
+        two.close()
