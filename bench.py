@@ -123,6 +123,19 @@ def conv_traffic(workload):
         return None
 
 
+def timed_steps(exe, steps):
+    """`steps` forwards issued back to back between two CUDA events on the
+    device stream (inputs resident); returns the elapsed ms."""
+    dev = exe.devices[0]
+    ctx = dev.ctx
+    ctx.event_record(0)
+    for _ in range(steps):
+        dev.issue_forward()
+    ctx.event_record(1)
+    ctx.sync()
+    return ctx.event_elapsed(0, 1)
+
+
 def _esz(t):
     from mdlc_b200 import _lib as L
     return L.ELEM_BYTES[t]
@@ -390,6 +403,8 @@ def main() -> int:
     ap.add_argument("--workload", default=WORKLOAD, choices=sorted(WORKLOADS))
     ap.add_argument("--latency-iters", type=int, default=200, help="b=1 forwards for the p50 latency")
     ap.add_argument("--ref-procs", type=int, default=0, help="reference arm: host processes (0 = every core)")
+    ap.add_argument("--requant", default="fixed", choices=["fixed", "fp32"],
+                    help="int8 workloads: requantisation form of the 8-bit conv epilogues")
     ap.add_argument("--forwards-only", action="store_true",
                     help="compile, stage the input and run --warmup forwards, then exit (no timing, no "
                          "JSON line): the program profiled by the committed ncu captures")
@@ -413,7 +428,7 @@ def main() -> int:
     if args.batch is None:
         args.batch = default_batch
     g = passes.default_pipeline(builders.BUILDERS[model](batch=args.batch, seed=0))
-    exe = mdlc_compile(g, dtype=dtype, devices=[local])
+    exe = mdlc_compile(g, dtype=dtype, devices=[local], **({"requant": args.requant} if dtype == "int8" else {}))
     dev = exe.devices[0]
     ins, outs = exe.pinned_inputs(), exe.pinned_outputs()
     rng = np.random.default_rng(1234 + rank)
@@ -531,6 +546,7 @@ def main() -> int:
             "dtype": {"bf16": "bf16", "fp32": "f32", "int8": "u8 x s8 -> s32"}[dtype],
             "data": "synthetic (N(0,1) 3x224x224 images, random Kaiming weights)",
             "config": {"workload": args.workload, "model": model, "per_gpu_batch": args.batch,
+                       **({"requant": args.requant} if dtype == "int8" else {}),
                        "global_batch": args.batch * world, "image": 224, "parallelism": f"dp{world}",
                        "l2": "working set > 126 MB L2 (input 154 MB fp32 + activations), no flush needed"},
             "e2e": {"value": round(e2e_value, 1), "unit": "images/s", "h2d_bytes_per_step": in_bytes,

@@ -69,7 +69,14 @@ enum {
 
 /* Fused epilogue applied to every conv / GEMM output element:
  *   float path: y = act(acc + bias[k] (+ residual))
- *   int8 path : y = out_zp + clamp(rint(f), qmin - out_zp, qmax - out_zp) with
+ *   int8 path, fixed point (rq_mult set; the default of int8 executables):
+ *               y = out_zp + clamp(t, qmin - out_zp, qmax - out_zp) with
+ *               t = ((acc + bias32[k]) * rq_mult[k] (+ (residual - res_zp) * rq_res_mult[k])
+ *                    + 2^(rq_shift[k] - 1)) >> rq_shift[k]
+ *               in 64-bit integers, one rounding (half up): the single-rounding form of
+ *               TFLite's MultiplyByQuantizedMultiplier, the two products sharing the shift
+ *   int8 path, fp32 (rq_mult null, rq_scale set):
+ *               y = out_zp + clamp(rint(f), qmin - out_zp, qmax - out_zp) with
  *               f = fp32(acc + bias32[k]) * rq_scale[k] (+ fp32(residual - res_zp) * res_scale),
  *               every product and sum one IEEE fp32 rounding (no fused multiply-add),
  *               rint = round half to even; bias is int32 for the int8 path
@@ -88,6 +95,9 @@ typedef struct {
   int32_t res_signed;     /* int8 path: residual codes are signed int8 (else uint8) */
   const float* deq_scale; /* [k] (int8 path, float output) */
   const float* deq_bias;  /* [k] (int8 path, float output) */
+  const int32_t* rq_mult;     /* [k] fixed-point multipliers (int8 path, 8-bit output); null: fp32 form */
+  const int32_t* rq_res_mult; /* [k] residual multipliers sharing rq_shift (with a residual) */
+  const int32_t* rq_shift;    /* [k] right shifts, 1..62 */
 } mdlc_epilogue;
 
 /* 2-D convolution over NHWC tensors (groups == 1: implicit GEMM; groups == c

@@ -43,7 +43,8 @@ class Epilogue(C.Structure):
                 ("rq_scale", C.c_void_p),
                 ("out_zp", C.c_int32), ("qmin", C.c_int32), ("qmax", C.c_int32),
                 ("res_zp", C.c_int32), ("res_scale", C.c_float), ("res_signed", C.c_int32),
-                ("deq_scale", C.c_void_p), ("deq_bias", C.c_void_p)]
+                ("deq_scale", C.c_void_p), ("deq_bias", C.c_void_p),
+                ("rq_mult", C.c_void_p), ("rq_res_mult", C.c_void_p), ("rq_shift", C.c_void_p)]
 
 
 class ConvDesc(C.Structure):

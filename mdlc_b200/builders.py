@@ -173,6 +173,18 @@ def mlp(n=4, din=16, dh=32, dout=8, seed=2) -> Graph:
     return b.finish(b.fc(h, dh, dout, "fc2"), "y")
 
 
+def grouped_block(n=2, c=64, h=14, w=14, groups=8, width=2, seed=3) -> Graph:
+    """ResNeXt-style bottleneck with a grouped 3x3 conv (1 < groups < channels):
+    1x1 conv-bn-relu (c -> width*c), 3x3 grouped conv-bn-relu, 1x1 conv-bn, + skip, relu."""
+    b = _Builder("grouped_block", seed)
+    x = b.input("x", (n, c, h, w))
+    m = width * c
+    y = b.relu(b.bn(b.conv(x, c, m, 1, name="conv_in"), m, "bn_in"))
+    y = b.relu(b.bn(b.conv(y, m, m, 3, groups=groups, name="conv_g"), m, "bn_g"))
+    y = b.bn(b.conv(y, m, c, 1, name="conv_out"), c, "bn_out")
+    return b.finish(b.relu(b.node("Add", [y, x], None, "add")), "y")
+
+
 # --------------------------------------------------------------- MobileNetV2
 
 MBV2_SETTINGS = ((1, 16, 1, 1), (6, 24, 2, 2), (6, 32, 3, 2), (6, 64, 4, 2),
@@ -278,7 +290,8 @@ def repvit(batch: int = 1, seed: int = 0, image: int = 224, num_classes: int = 1
 
 
 BUILDERS = {"resnet18": resnet18, "mobilenetv2": mobilenetv2, "repvit": repvit,
-            "conv_bn_relu": conv_bn_relu, "residual_block": residual_block, "mlp": mlp}
+            "conv_bn_relu": conv_bn_relu, "residual_block": residual_block, "mlp": mlp,
+            "grouped_block": grouped_block}
 
 
 def make_input(graph: Graph, seed: int = 0) -> dict:

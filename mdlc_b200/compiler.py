@@ -102,6 +102,9 @@ class _Device:
                 self.wbuf[wname] = self.ctx.to_device(L.pack_weights(desc, cq.w_q))
                 self.bbuf[wname] = self.ctx.to_device(pad(cq.bias32, np.int32))
                 self.qbuf[wname] = {
+                    "mult": self.ctx.to_device(pad(cq.rq_mult, np.int32)) if cq.rq_mult is not None else 0,
+                    "res_mult": self.ctx.to_device(pad(cq.rq_res_mult, np.int32)) if cq.rq_mult is not None else 0,
+                    "shift": self.ctx.to_device(pad(cq.rq_shift, np.int32)) if cq.rq_mult is not None else 0,
                     "scale": self.ctx.to_device(pad(cq.rq_scale, np.float32)),
                     "deq_scale": self.ctx.to_device(pad(cq.deq_scale, np.float32)) if cq.deq_scale is not None else 0,
                     "deq_bias": self.ctx.to_device(pad(cq.deq_bias, np.float32)) if cq.deq_bias is not None else 0}
@@ -166,6 +169,8 @@ class _Device:
                     if yt.dtype != L.F32:
                         epi.act = L.ACT_NONE     # the activation is the integer clamp
                     epi.rq_scale = qb["scale"]
+                    if yt.dtype != L.F32 and qb["mult"]:
+                        epi.rq_mult, epi.rq_res_mult, epi.rq_shift = qb["mult"], qb["res_mult"], qb["shift"]
                     epi.deq_scale, epi.deq_bias = qb["deq_scale"] or None, qb["deq_bias"] or None
                     if cq.residual:
                         epi.res_zp = self.q.tensors[self._store(cq.residual)][1]
@@ -377,7 +382,7 @@ class Executable:
     """A compiled graph bound to one or more B200s."""
 
     def __init__(self, graph, *, dtype="bf16", batch=None, devices=1, tuner=None, mem_plan=None,
-                 keep_all=False, calib=None, schedule_fn=None):
+                 keep_all=False, calib=None, schedule_fn=None, requant="fixed"):
         if dtype not in DTYPES:
             raise ValueError(f"dtype must be one of {sorted(DTYPES)}")
         if tuner is not None and schedule_fn is not None:
@@ -419,7 +424,7 @@ class Executable:
                 ranges = quant.calibrate(graph, batches, device=devs[0])
             self.ranges = ranges
             lo_orig = lowering.lower(graph, S.infer(graph, self.shard), L.U8, s2d=False)
-            self.qplan = quant.build_plan(lo_orig, self.lowered, ranges, graph)
+            self.qplan = quant.build_plan(lo_orig, self.lowered, ranges, graph, requant=requant)
         self.devices = [_Device(self, d, self.shard) for d in devs]
 
     def _lowered_for(self, batch):
@@ -561,7 +566,7 @@ class Executable:
 
 
 def compile(graph, *, mem_plan=None, dtype: str = "bf16", batch=None, devices=1, tuner=None,
-            schedule_fn=None, calib=None) -> Executable:
+            schedule_fn=None, calib=None, requant: str = "fixed") -> Executable:
     """Compile a post-pass Graph IR for B200 execution (see module docstring).
 
     ``mem_plan``: a reference ``MemoryPlan`` (or its tensor -> buffer id dict)
@@ -571,7 +576,9 @@ def compile(graph, *, mem_plan=None, dtype: str = "bf16", batch=None, devices=1,
 
     ``dtype="int8"`` quantises the graph (:mod:`mdlc_b200.quant`): ``calib`` is
     either a dict of per-tensor (min, max) ranges, a list of feed dicts to
-    calibrate on, or None for 32 seeded N(0, 1) batches of 4 images.
+    calibrate on, or None for 32 seeded N(0, 1) batches of 4 images; ``requant``
+    selects the 8-bit conv requantisation: ``"fixed"`` (default; integer
+    multiplier and shift, one rounding) or ``"fp32"`` (an fp32 scale, rint).
     """
     return Executable(graph, dtype=dtype, batch=batch, devices=devices, tuner=tuner, schedule_fn=schedule_fn,
-                      mem_plan=mem_plan, calib=calib)
+                      mem_plan=mem_plan, calib=calib, requant=requant)

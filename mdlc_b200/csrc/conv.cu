@@ -319,6 +319,72 @@ __global__ void __launch_bounds__(128) conv_dw3_kernel(const DwArgs a, int strip
   }
 }
 
+// ------------------------------------------------------------ grouped
+// General grouped convolution (1 < groups < c; reference: the per-group loop
+// of mdlc/runtime/ops.py:68-78, which the reference GPU lowering sends to the
+// host, emit.py:175-180). One thread per (output pixel, output channel); the
+// threads of a warp take consecutive output channels of one pixel, so the
+// weights, packed [r*s][c/g][k_stride] fp32, are read coalesced and the
+// input channels of a group are broadcast to the threads of that group. fp32
+// accumulation over taps (row, column) then group channels in order.
+struct GroupedArgs {
+  const void* x;
+  const float* w;
+  const float* bias;
+  const void* res;
+  void* y;
+  int h, w_, cs, k, ks, icg, ocg, r, s, sh, sw, pt, pl, dh, dw, oh, ow, res_s;
+  long long total;  // M * ks
+  ActParams act;
+};
+
+template <typename T>
+MDLC_DEV float ld_f(const T* p);
+template <>
+MDLC_DEV float ld_f<float>(const float* p) { return __ldg(p); }
+template <>
+MDLC_DEV float ld_f<__nv_bfloat16>(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+template <typename T>
+MDLC_DEV void st_f(T* p, float v);
+template <>
+MDLC_DEV void st_f<float>(float* p, float v) { *p = v; }
+template <>
+MDLC_DEV void st_f<__nv_bfloat16>(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
+
+template <typename T>
+__global__ void __launch_bounds__(256) conv_grouped_kernel(const GroupedArgs a) {
+  const int ohw = a.oh * a.ow;
+  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < a.total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int o = (int)(idx % a.ks);
+    const long long m = idx / a.ks;
+    T* yp = static_cast<T*>(a.y) + m * a.ks + o;
+    if (o >= a.k) {
+      st_f<T>(yp, 0.0f);
+      continue;
+    }
+    const int img = (int)(m / ohw);
+    const int rem = (int)(m - (long long)img * ohw);
+    const int oy = rem / a.ow, ox = rem - (rem / a.ow) * a.ow;
+    const int c0 = (o / a.ocg) * a.icg;
+    float acc = a.bias ? __ldg(a.bias + o) : 0.0f;
+    const T* xb = static_cast<const T*>(a.x) + (long long)img * a.h * a.w_ * a.cs + c0;
+    for (int rr = 0; rr < a.r; ++rr) {
+      const int ih = oy * a.sh - a.pt + rr * a.dh;
+      if ((unsigned)ih >= (unsigned)a.h) continue;
+      for (int ss = 0; ss < a.s; ++ss) {
+        const int iw = ox * a.sw - a.pl + ss * a.dw;
+        if ((unsigned)iw >= (unsigned)a.w_) continue;
+        const T* xp = xb + ((long long)ih * a.w_ + iw) * a.cs;
+        const float* wp = a.w + (long long)(rr * a.s + ss) * a.icg * a.ks + o;
+        for (int c = 0; c < a.icg; ++c) acc = fmaf(ld_f<T>(xp + c), __ldg(wp + (long long)c * a.ks), acc);
+      }
+    }
+    if (a.res) acc += ld_f<T>(static_cast<const T*>(a.res) + m * a.res_s + o);
+    st_f<T>(yp, apply_act(acc, a.act));
+  }
+}
+
 ActParams act_of(const mdlc_epilogue* epi) {
   if (!epi) return ActParams{MDLC_ACT_NONE, 0.f, 0.f, -INFINITY, INFINITY};
   return ActParams{epi->act, epi->alpha, epi->beta, epi->clip_lo, epi->clip_hi};
@@ -357,7 +423,7 @@ int validate(mdlc_ctx* ctx, const mdlc_conv_desc* d) {
   return MDLC_OK;
 }
 
-enum Path { kPathTC, kPathF32, kPathDW, kPathNone };
+enum Path { kPathTC, kPathF32, kPathDW, kPathGrouped, kPathNone };
 
 Path path_of(const mdlc_conv_desc& d) {
   if (d.groups == 1) {
@@ -371,6 +437,9 @@ Path path_of(const mdlc_conv_desc& d) {
   if (d.groups == d.c && d.c == d.k && d.in_type == d.out_type &&
       (d.in_type == MDLC_BF16 || d.in_type == MDLC_F32))
     return kPathDW;
+  if (d.groups > 1 && d.c % d.groups == 0 && d.k % d.groups == 0 && d.in_type == d.out_type &&
+      (d.in_type == MDLC_BF16 || d.in_type == MDLC_F32))
+    return kPathGrouped;
   return kPathNone;
 }
 
@@ -431,6 +500,28 @@ int conv_dw(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const float* 
   return mdlc_cuda_status(ctx, cudaGetLastError(), "conv_dw launch");
 }
 
+int conv_grouped(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const float* w, const float* bias,
+                 const void* res, void* y, const mdlc_epilogue* epi) {
+  GroupedArgs a{};
+  a.x = x; a.w = w; a.bias = bias; a.res = res; a.y = y;
+  a.h = d.h; a.w_ = d.w; a.cs = d.c_stride; a.k = d.k; a.ks = d.k_stride;
+  a.icg = d.c / d.groups; a.ocg = d.k / d.groups;
+  a.r = d.r; a.s = d.s; a.sh = d.stride_h; a.sw = d.stride_w; a.pt = d.pad_t; a.pl = d.pad_l;
+  a.dh = d.dil_h; a.dw = d.dil_w; a.oh = d.oh; a.ow = d.ow;
+  a.res_s = d.res_stride ? d.res_stride : d.k_stride;
+  a.total = (long long)d.n * d.oh * d.ow * d.k_stride;
+  a.act = act_of(epi);
+  long long blocks = (a.total + 255) / 256;
+  const long long cap = (long long)ctx->num_sms * 16;
+  if (blocks > cap) blocks = cap;
+  if (d.in_type == MDLC_BF16)
+    conv_grouped_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, ctx->stream>>>(a);
+  else
+    conv_grouped_kernel<float><<<(unsigned)blocks, 256, 0, ctx->stream>>>(a);
+  mdlc_note_launch(ctx);
+  return mdlc_cuda_status(ctx, cudaGetLastError(), "conv_grouped launch");
+}
+
 }  // namespace mdlc
 
 using namespace mdlc;
@@ -450,6 +541,9 @@ extern "C" int mdlc_conv_weight_bytes(const mdlc_conv_desc* d, size_t* bytes) {
       return MDLC_OK;
     case kPathDW:
       *bytes = (size_t)d->r * d->s * d->c_stride * sizeof(float);
+      return MDLC_OK;
+    case kPathGrouped:
+      *bytes = (size_t)d->r * d->s * (d->c / d->groups) * d->k_stride * sizeof(float);
       return MDLC_OK;
     default:
       return MDLC_ERR_UNSUPPORTED;
@@ -498,6 +592,16 @@ extern "C" int mdlc_pack_conv_weights(const mdlc_conv_desc* d, const float* w, v
           for (int s = 0; s < S; ++s) o_[(r * S + s) * cs + c] = W(c, 0, r, s);
       return MDLC_OK;
     }
+    case kPathGrouped: {
+      // [r*s][c/g][k_stride]: output channel fastest (coalesced across a warp)
+      float* o_ = static_cast<float*>(out);
+      for (int o = 0; o < K; ++o)
+        for (int r = 0; r < R; ++r)
+          for (int s = 0; s < S; ++s)
+            for (int c = 0; c < icg; ++c)
+              o_[((long long)(r * S + s) * icg + c) * d->k_stride + o] = W(o, c, r, s);
+      return MDLC_OK;
+    }
     default:
       return MDLC_ERR_UNSUPPORTED;
   }
@@ -519,8 +623,11 @@ extern "C" int mdlc_conv2d(mdlc_ctx* ctx, const mdlc_conv_desc* d, const void* x
       if (d->out_type == MDLC_S32 && res)
         return mdlc_set_error(ctx, MDLC_ERR_INVALID, "conv int8: no residual with int32 accumulator output");
       if ((d->in_type == MDLC_U8 || d->in_type == MDLC_S8) && d->out_type != MDLC_F32 &&
-          d->out_type != MDLC_S32 && (!epi || !epi->rq_scale))
-        return mdlc_set_error(ctx, MDLC_ERR_INVALID, "conv int8: requantisation scales required");
+          d->out_type != MDLC_S32 && (!epi || (!epi->rq_scale && !epi->rq_mult)))
+        return mdlc_set_error(ctx, MDLC_ERR_INVALID, "conv int8: requantisation scales or multipliers required");
+      if (epi && epi->rq_mult && (!epi->rq_shift || (res && !epi->rq_res_mult)))
+        return mdlc_set_error(ctx, MDLC_ERR_INVALID,
+                              "conv int8: fixed-point requantisation needs rq_shift (and rq_res_mult with a residual)");
       if ((d->in_type == MDLC_U8 || d->in_type == MDLC_S8) && d->out_type == MDLC_F32 &&
           (!epi || !epi->deq_scale))
         return mdlc_set_error(ctx, MDLC_ERR_INVALID, "conv int8: deq_scale required for float output");
@@ -531,6 +638,8 @@ extern "C" int mdlc_conv2d(mdlc_ctx* ctx, const mdlc_conv_desc* d, const void* x
                       epi);
     case kPathDW:
       return conv_dw(ctx, *d, x, static_cast<const float*>(w), static_cast<const float*>(bias), res, y, epi);
+    case kPathGrouped:
+      return conv_grouped(ctx, *d, x, static_cast<const float*>(w), static_cast<const float*>(bias), res, y, epi);
     default:
       return mdlc_set_error(ctx, MDLC_ERR_UNSUPPORTED,
                             "conv: groups=%d in_type=%d out_type=%d not supported", d->groups, d->in_type,

@@ -16,4 +16,8 @@ int conv_f32(mdlc_ctx* ctx, const mdlc_conv_desc& d, const float* x, const float
 int conv_dw(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const float* w, const float* bias,
             const void* res, void* y, const mdlc_epilogue* epi);
 
+// grouped (1 < groups, not depthwise), bf16 or fp32 activations, fp32 weights
+int conv_grouped(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const float* w, const float* bias,
+                 const void* res, void* y, const mdlc_epilogue* epi);
+
 }  // namespace mdlc

@@ -78,6 +78,12 @@ struct TcArgs {
   int res_signed;
   const float* deq_scale;
   const float* deq_bias;
+  // fixed-point requantisation (8-bit output): per-channel multipliers of the
+  // accumulator and of the residual, sharing one right shift; null: fp32 form
+  const int32_t* rq_mult;
+  const int32_t* rq_res_mult;
+  const int32_t* rq_shift;
+  int rq_fixed;
   unsigned long long wait_cycles;
   int tma_epi;  // bf16 / 8-bit output staged in shared memory and written by TMA stores
   int tiles_x, tiles_y, halo_rows, cpb;  // halo mode: tile grid per image, band rows, channel blocks
@@ -102,8 +108,9 @@ struct Smem {
   static constexpr int kEBuf = 32 * 64 * ESZ;
   static constexpr int kE = kB + STAGES * kBBytes;
   // per-tile epilogue parameters, double-buffered by tile parity: the fp32
-  // bias (bf16), or the int32 bias and fp32 requantisation scale (8-bit)
-  static constexpr int kParamWords = ESZ == 2 ? 1 : 2;
+  // bias (bf16), or the int32 bias, the fp32 requantisation scale or the
+  // fixed-point multiplier, the residual multiplier and the shift (8-bit)
+  static constexpr int kParamWords = ESZ == 2 ? 1 : 4;
   static constexpr int kBias = kE + 4 * 2 * kEBuf;
   static constexpr int kBar = kBias + 2 * kParamWords * BN * 4;
   // barriers: fullA[S], fullB[S], empty[S], tfull[2], tempty[2], drain, resid[4 warps][2 buffers],
@@ -234,13 +241,20 @@ MDLC_DEV void store_chunk16(const TcArgs& a, int m, int nb0, const uint32_t (&v)
       int32_t q = 0;
       if (ch < a.k) {
         const int32_t acc = (int32_t)v[e] + (bias32 ? bias32[ch] : 0);
-        float f = __fmul_rn((float)acc, a.rq_scale[ch]);
-        if (a.res) {
-          const int32_t rq = a.res_signed ? (int32_t)(int8_t)a.res[(long long)m * a.res_s + ch]
+        const int32_t rq = !a.res ? 0
+                           : a.res_signed ? (int32_t)(int8_t)a.res[(long long)m * a.res_s + ch]
                                           : (int32_t)a.res[(long long)m * a.res_s + ch];
-          f = __fadd_rn(f, __fmul_rn((float)(rq - a.res_zp), a.res_scale));
+        if (a.rq_fixed) {
+          const int sh = a.rq_shift[ch];
+          long long t = (long long)acc * a.rq_mult[ch] + ((1ll << sh) >> 1);
+          if (a.res) t += (long long)(rq - a.res_zp) * a.rq_res_mult[ch];
+          t >>= sh;
+          q = (int32_t)(t < a.qlo ? a.qlo : (t > a.qhi ? a.qhi : t)) + a.out_zp;
+        } else {
+          float f = __fmul_rn((float)acc, a.rq_scale[ch]);
+          if (a.res) f = __fadd_rn(f, __fmul_rn((float)(rq - a.res_zp), a.res_scale));
+          q = min(max(__float2int_rn(f), a.qlo), a.qhi) + a.out_zp;
         }
-        q = min(max(__float2int_rn(f), a.qlo), a.qhi) + a.out_zp;
       }
       packed[e >> 2] |= ((uint32_t)(q & 0xFF)) << (8 * (e & 3));
     }
@@ -563,7 +577,8 @@ __global__ void __launch_bounds__(kThreads, (Occ<BN, STAGES, ESZ, AMODE>::value)
           tma_load_2d(dst, &tmap_r, c, m0 + ew * 32, bar);
       };
       float* sbias = reinterpret_cast<float*>(smem + L::kBias) + buf * BN;
-      int32_t* sq = reinterpret_cast<int32_t*>(smem + L::kBias) + buf * 2 * BN;  // 8-bit: bias32 | scale
+      // 8-bit: bias32 | fp32 scale or multiplier | residual multiplier | shift
+      int32_t* sq = reinterpret_cast<int32_t*>(smem + L::kBias) + buf * 4 * BN;
       if (tma_epi) {
         // stage this tile's epilogue parameters (and the first residual chunk) while the main loop runs
         if constexpr (ESZ == 2) {
@@ -573,7 +588,13 @@ __global__ void __launch_bounds__(kThreads, (Occ<BN, STAGES, ESZ, AMODE>::value)
           for (int i = etid; i < BN; i += 128) {
             const bool v = n0 + i < a.k;
             sq[i] = (v && a.bias) ? __ldg(static_cast<const int32_t*>(a.bias) + n0 + i) : 0;
-            sq[BN + i] = v ? __float_as_int(__ldg(a.rq_scale + n0 + i)) : 0;
+            if (a.rq_fixed) {
+              sq[BN + i] = v ? __ldg(a.rq_mult + n0 + i) : 0;
+              sq[2 * BN + i] = (v && a.rq_res_mult) ? __ldg(a.rq_res_mult + n0 + i) : 0;
+              sq[3 * BN + i] = v ? __ldg(a.rq_shift + n0 + i) : 1;
+            } else {
+              sq[BN + i] = v ? __float_as_int(__ldg(a.rq_scale + n0 + i)) : 0;
+            }
           }
         }
         if (a.res) {
@@ -654,15 +675,51 @@ __global__ void __launch_bounds__(kThreads, (Occ<BN, STAGES, ESZ, AMODE>::value)
               // this group's 16 int32 biases and fp32 scales as 128-bit loads
               const int col0 = c0 + 16 * q;
               int32_t bq[16];
-              float sc[16];
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
                 const int4 bb = *reinterpret_cast<const int4*>(sq + col0 + 4 * j);
-                const float4 ss = *reinterpret_cast<const float4*>(sq + BN + col0 + 4 * j);
                 bq[4 * j] = bb.x; bq[4 * j + 1] = bb.y; bq[4 * j + 2] = bb.z; bq[4 * j + 3] = bb.w;
-                sc[4 * j] = ss.x; sc[4 * j + 1] = ss.y; sc[4 * j + 2] = ss.z; sc[4 * j + 3] = ss.w;
               }
               const bool full = n0 + col0 + 16 <= a.k;  // group-uniform: no pad columns
+              int32_t t[16];
+              if (a.rq_fixed) {
+                // single-rounding fixed point: one 64-bit sum of the products
+                // with the multipliers and the rounding constant, one shift
+                int32_t m1[16], m2[16], sh[16];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  const int4 a4 = *reinterpret_cast<const int4*>(sq + BN + col0 + 4 * j);
+                  const int4 b4 = *reinterpret_cast<const int4*>(sq + 2 * BN + col0 + 4 * j);
+                  const int4 c4 = *reinterpret_cast<const int4*>(sq + 3 * BN + col0 + 4 * j);
+                  m1[4 * j] = a4.x; m1[4 * j + 1] = a4.y; m1[4 * j + 2] = a4.z; m1[4 * j + 3] = a4.w;
+                  m2[4 * j] = b4.x; m2[4 * j + 1] = b4.y; m2[4 * j + 2] = b4.z; m2[4 * j + 3] = b4.w;
+                  sh[4 * j] = c4.x; sh[4 * j + 1] = c4.y; sh[4 * j + 2] = c4.z; sh[4 * j + 3] = c4.w;
+                }
+                long long acc64[16];
+#pragma unroll
+                for (int e = 0; e < 16; ++e)
+                  acc64[e] = (long long)((int32_t)v[16 * q + e] + bq[e]) * m1[e] + ((1ll << sh[e]) >> 1);
+                if (a.res) {
+#pragma unroll
+                  for (int e = 0; e < 16; ++e) {
+                    const uint32_t byte = (rw[e >> 2] >> (8 * (e & 3))) & 0xFFu;
+                    const int32_t rq = a.res_signed ? (int32_t)(int8_t)byte : (int32_t)byte;
+                    acc64[e] += (long long)(rq - a.res_zp) * m2[e];
+                  }
+                }
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                  long long r = acc64[e] >> sh[e];
+                  r = r < a.qlo ? a.qlo : (r > a.qhi ? a.qhi : r);
+                  t[e] = (int32_t)r + a.out_zp;
+                }
+              } else {
+              float sc[16];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const float4 ss = *reinterpret_cast<const float4*>(sq + BN + col0 + 4 * j);
+                sc[4 * j] = ss.x; sc[4 * j + 1] = ss.y; sc[4 * j + 2] = ss.z; sc[4 * j + 3] = ss.w;
+              }
               // exact small-integer <-> float conversions without the conversion
               // unit: 1.5 * 2^23 in the exponent, value in the low mantissa bits
               // (|x| < 2^22; round-to-nearest-even like __float2int_rn)
@@ -684,10 +741,10 @@ __global__ void __launch_bounds__(kThreads, (Occ<BN, STAGES, ESZ, AMODE>::value)
                 }
               }
               // clamp then round == round then clamp (integer bounds)
-              int32_t t[16];
 #pragma unroll
               for (int e = 0; e < 16; ++e)
                 t[e] = __float_as_int(__fadd_rn(fminf(fmaxf(f[e], qlo_f), qhi_f), kMagic)) - kMagicBits + a.out_zp;
+              }
               if (!full) {
 #pragma unroll
                 for (int e = 0; e < 16; ++e)
@@ -1165,6 +1222,8 @@ int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w
     a.out_zp = epi->out_zp; a.qlo = epi->qmin - epi->out_zp; a.qhi = epi->qmax - epi->out_zp;
     a.res_zp = epi->res_zp; a.res_scale = epi->res_scale; a.res_signed = epi->res_signed;
     a.deq_scale = epi->deq_scale; a.deq_bias = epi->deq_bias;
+    a.rq_mult = epi->rq_mult; a.rq_res_mult = epi->rq_res_mult; a.rq_shift = epi->rq_shift;
+    a.rq_fixed = epi->rq_mult != nullptr;
   }
   if (int8) a.pad_src = ctx->d_pad + 16 * (d.in_zp & 0xFF);
 

@@ -166,8 +166,9 @@ class _Lowerer:
             group = a.get("group", 1)
             sh, sw = a.get("strides", [1, 1])
             dh, dw = a.get("dilations", [1, 1])
-            if group != 1 and not (group == xt.c == k and icg == 1):
-                raise LoweringError(f"{node.name}: grouped conv with group={group} (not depthwise)")
+            if group != 1 and (xt.c % group or k % group or icg * group != xt.c):
+                raise LoweringError(f"{node.name}: grouped conv with group={group} does not divide "
+                                    f"C={xt.c} / K={k}")
             wt = np.asarray(w, dtype=np.float32)
             geom = dict(n=xt.n, h=xt.h, w=xt.w, c=xt.c, k=k, r=r, s=s, sh=sh, sw=sw, pt=pt, pl=pl,
                         dh=dh, dw=dw, oh=oh, ow=ow, groups=group)

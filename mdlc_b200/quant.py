@@ -75,6 +75,40 @@ def quantize_multiplier(real: float):
     return q, shift
 
 
+def shared_shift_multipliers(real_acc, real_res=None):
+    """Per-channel fixed-point multipliers for ``t = (acc * M1 + r * M2 + 2^(S-1)) >> S``
+    (the single-rounding form of TFLite's MultiplyByQuantizedMultiplier, with
+    the residual term sharing the channel's shift so the sum is rounded once).
+
+    For channel k, S[k] = 31 - e with m = max(real_acc[k], real_res) = f * 2^e,
+    f in [0.5, 1): the larger multiplier gets 31 significant bits
+    (M in [2^30, 2^31)), the other as many as its ratio to the larger allows.
+    Returns int32 arrays (M1, M2, S); S is clamped to 62 (a multiplier below
+    2^-31 then rounds to 0)."""
+    real_acc = np.asarray(real_acc, np.float64)
+    rr = 0.0 if real_res is None else float(real_res)
+    k = real_acc.shape[0]
+    m1, m2, sh = np.zeros(k, np.int64), np.zeros(k, np.int64), np.zeros(k, np.int64)
+    for i in range(k):
+        big = max(float(real_acc[i]), rr)
+        if big <= 0.0:
+            sh[i] = 31
+            continue
+        _, e = math.frexp(big)
+        S = 31 - e
+        if S < 1:
+            raise ValueError(f"requantisation multiplier {big} too large for the fixed-point form")
+        S = min(S, 62)
+        a = int(round(float(real_acc[i]) * 2.0 ** S))
+        b = int(round(rr * 2.0 ** S))
+        if max(a, b) >= (1 << 31):      # rounded up to 2^31: one bit less
+            S -= 1
+            a = int(round(float(real_acc[i]) * 2.0 ** S))
+            b = int(round(rr * 2.0 ** S))
+        m1[i], m2[i], sh[i] = a, b, S
+    return m1.astype(np.int32), m2.astype(np.int32), sh.astype(np.int32)
+
+
 @dataclass
 class ConvQ:
     """Quantisation of one conv step (keyed by its weight name)."""
@@ -92,6 +126,9 @@ class ConvQ:
     res_scale: float = 0.0   # float32 residual scale: s_r / s_y (8-bit output), s_r (fp32 output)
     deq_scale: np.ndarray | None = None   # float32 [k] (fp32 output)
     deq_bias: np.ndarray | None = None    # float32 [k] (fp32 output)
+    rq_mult: np.ndarray | None = None     # int32 [k] fixed-point accumulator multipliers (8-bit output)
+    rq_res_mult: np.ndarray | None = None # int32 [k] residual multipliers (same shift)
+    rq_shift: np.ndarray | None = None    # int32 [k] right shifts
     act: str | None = None
     nodes: list = field(default_factory=list)
 
@@ -103,6 +140,7 @@ class QuantPlan:
     gap: dict                # output name -> (mult, shift, in_zp, out_zp)
     steps: list              # lowered steps (names, grouping), shared with the oracle
     signed: set = field(default_factory=set)   # tensors holding signed int8 codes
+    requant: str = "fixed"   # 8-bit conv outputs: "fixed" (integer multiplier + shift) or "fp32"
 
 
 def _act_range(act, attrs, s_y, zp_y):
@@ -119,7 +157,7 @@ def _act_range(act, attrs, s_y, zp_y):
     raise lowering.LoweringError(f"int8: activation {act!r} has no integer epilogue")
 
 
-def build_plan(lo_f32, lo_i8, ranges: dict, graph) -> QuantPlan:
+def build_plan(lo_f32, lo_i8, ranges: dict, graph, requant: str = "fixed") -> QuantPlan:
     """Quantisation plan for the int8 lowering ``lo_i8`` of ``graph``.
 
     ``ranges`` maps activation tensor names to (min, max) observed in fp32;
@@ -186,11 +224,18 @@ def build_plan(lo_f32, lo_i8, ranges: dict, graph) -> QuantPlan:
             q.bias32 = (np.rint(b / acc_scale).astype(np.int64) - zp_x * wsum).astype(np.int32)
             q.rq_scale = (acc_scale / np.float64(s_y)).astype(np.float32)
             q.qmin, q.qmax = _act_range(q.act, st.params["attrs"], s_y, zp_y)
+            real_res = None
             if q.residual:
                 s_r, _ = tensors[q.residual]
                 q.res_scale = float(np.float32(np.float64(s_r) / np.float64(s_y)))
+                real_res = np.float64(s_r) / np.float64(s_y)
+            if requant == "fixed":
+                q.rq_mult, q.rq_res_mult, q.rq_shift = shared_shift_multipliers(
+                    acc_scale / np.float64(s_y), real_res)
         convs[st.params["weight"]] = q
-    return QuantPlan(tensors, convs, gap, lo_i8.steps, signed)
+    if requant not in ("fixed", "fp32"):
+        raise ValueError(f"requant must be 'fixed' or 'fp32', not {requant!r}")
+    return QuantPlan(tensors, convs, gap, lo_i8.steps, signed, requant)
 
 
 def calibrate(graph, batches, *, device: int = 0) -> dict:

@@ -9,7 +9,12 @@ accumulation and IEEE float32 requantisation:
 * conv / GEMM: im2col of the uint8 codes padded with the input zero point, then
   an int64 ``einsum("ok,nkp->nop")`` — the reference's conv algorithm
   (``mdlc/runtime/ops.py:35-81``) on integers — plus the int32 bias;
-* conv requantisation in IEEE float32, one rounding per product and sum:
+* conv requantisation (8-bit outputs), as the plan says:
+  fixed point (the default), one rounding: ``zp + clip((acc*M1[k] [+ (res - zp_r)*M2[k]]
+  + 2^(S[k]-1)) >> S[k], qmin - zp, qmax - zp)`` in int64 -- the single-rounding
+  form of TFLite's MultiplyByQuantizedMultiplier (``TFLITE_SINGLE_ROUNDING``),
+  the residual product sharing the channel's shift; or IEEE float32, one
+  rounding per product and sum:
   ``zp + clip(rint(f32(acc + bias32) * r[k] [+ f32(res - zp_r) * r_res]), qmin - zp, qmax - zp)``;
 * global-average-pool requantisation in gemmlowp fixed point:
   SaturatingRoundingDoublingHighMul (truncating division by 2^31) followed by
@@ -147,6 +152,20 @@ def run_int8(graph, plan, feeds):
                 y = (y + (r - zp_r).astype(np.float32) * np.float32(cq.res_scale)).astype(np.float32)
             y = oref.activation(cq.act, y, node.attrs).astype(np.float32)
             env[st.outputs[0]] = y.reshape(y.shape[0], k) if node.op_type in ("Gemm", "FusedGemmAct", "MatMul") else y
+        elif getattr(cq, "rq_mult", None) is not None:
+            # single-rounding fixed point (TFLite MultiplyByQuantizedMultiplier,
+            # TFLITE_SINGLE_ROUNDING form): t = (acc*M1 + (r - zp_r)*M2 + 2^(S-1)) >> S
+            # in int64 (|acc*M1| < 2^62), arithmetic shift = floor, so ties round up
+            zp_y = plan.tensors[st.outputs[0]][1]
+            m1 = cq.rq_mult.astype(np.int64).reshape(1, k, 1, 1)
+            sh = cq.rq_shift.astype(np.int64).reshape(1, k, 1, 1)
+            v = acc.astype(np.int64) * m1 + (np.int64(1) << (sh - 1))
+            if cq.residual:
+                r = env[src(cq.residual)]
+                zp_r = plan.tensors[src(cq.residual)][1]
+                v = v + (np.asarray(r, np.int64) - zp_r) * cq.rq_res_mult.astype(np.int64).reshape(1, k, 1, 1)
+            t = np.clip(v >> sh, cq.qmin - zp_y, cq.qmax - zp_y) + zp_y
+            env[st.outputs[0]] = t.reshape(t.shape[0], k) if node.op_type in ("Gemm", "FusedGemmAct", "MatMul") else t
         else:
             zp_y = plan.tensors[st.outputs[0]][1]
             f = acc.astype(np.float32) * cq.rq_scale.astype(np.float32).reshape(1, k, 1, 1)

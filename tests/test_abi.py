@@ -29,15 +29,40 @@ def test_library_exports_every_declared_function():
     assert set(L.SIGNATURES) <= set(names)
 
 
-def test_struct_layouts_match_header():
-    # field counts mirror the header structs; sizes follow from int32/float/pointer fields
+STRUCTS = {"mdlc_epilogue": "Epilogue", "mdlc_conv_desc": "ConvDesc", "mdlc_tile_cfg": "TileCfg",
+           "mdlc_pool_desc": "PoolDesc", "mdlc_ew_instr": "EwInstr", "mdlc_ew_prog": "EwProg",
+           "mdlc_gemm_desc": "GemmDesc"}
+
+
+def test_struct_layouts_match_header(tmp_path):
+    """Every ctypes mirror has the size and field offsets the C compiler gives
+    the header's struct (a C program including include/mdlc_b200.h prints them)."""
     import ctypes as C
-    assert C.sizeof(L.ConvDesc) == 22 * 4
-    assert C.sizeof(L.PoolDesc) == 20 * 4
-    assert C.sizeof(L.TileCfg) == 12
-    assert C.sizeof(L.EwInstr) == 12
-    assert C.sizeof(L.EwProg) == 8 * 4 + 4 * 4 + 2 * 4 + 24 * 12
-    assert C.sizeof(L.Epilogue) == 5 * 4 + 4 + 8 + 4 * 4 + 4 + 4 + 2 * 8  # padding before the first pointer
+    import shutil
+    import subprocess
+    gcc = shutil.which("gcc") or shutil.which("cc")
+    if gcc is None:
+        pytest.skip("no C compiler")
+    lines = ["#include <stdio.h>", "#include <stddef.h>", '#include "mdlc_b200.h"', "int main(void) {"]
+    for cname, pname in STRUCTS.items():
+        lines.append(f'printf("{pname} size %zu\\n", sizeof({cname}));')
+        for field, _ in getattr(L, pname)._fields_:
+            lines.append(f'printf("{pname} {field} %zu\\n", offsetof({cname}, {field}));')
+    lines += ["return 0;", "}"]
+    src = tmp_path / "layout.c"
+    src.write_text("\n".join(lines))
+    exe = tmp_path / "layout"
+    inc = os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include")
+    subprocess.run([gcc, "-I", inc, str(src), "-o", str(exe)], check=True)
+    out = subprocess.run([str(exe)], check=True, capture_output=True, text=True).stdout.split("\n")
+    checked = 0
+    for line in filter(None, out):
+        pname, field, value = line.split()
+        cls = getattr(L, pname)
+        got = C.sizeof(cls) if field == "size" else getattr(cls, field).offset
+        assert got == int(value), f"{pname}.{field}: ctypes {got}, C {value}"
+        checked += 1
+    assert checked == sum(1 + len(getattr(L, p)._fields_) for p in STRUCTS.values())
 
 
 def test_version_and_no_device_here():

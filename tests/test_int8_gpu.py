@@ -1,7 +1,7 @@
 """INT8 executables on the B200 against the integer restatement (bit-exact).
 
 The device quantises the fp32 feeds, runs the tcgen05 ``kind::i8`` convs with
-the fp32 requantisation epilogue, max-pools codes, requantises the global
+the fixed-point (default) or fp32 requantisation epilogue, max-pools codes, requantises the global
 average pool in fixed point and dequantises the logits. Every stored code and the fp32
 logits must equal ``oracle.quant.run_int8`` evaluated under the executable's
 own quantisation plan (calibrated on the GPU).
@@ -57,11 +57,16 @@ def _compare(exe, g, feeds):
     return out, want, checked
 
 
+@pytest.mark.parametrize("requant", ["fixed", "fp32"])
 @pytest.mark.parametrize("name,kw", CASES, ids=[f"{n}-{i}" for i, (n, _) in enumerate(CASES)])
-def test_int8_bit_exact_per_layer(name, kw):
+def test_int8_bit_exact_per_layer(name, kw, requant):
+    """Every stored code and the logits, for both requantisation forms: the
+    fixed-point multiplier + shift (the default, BASELINE config 3's form) and
+    the fp32-scale opt-in."""
     g = _graph(name, kw)
     n = g.value_info[g.runtime_inputs[0]].shape[0]
-    exe = Executable(g, dtype="int8", batch=n, keep_all=True)
+    exe = Executable(g, dtype="int8", batch=n, keep_all=True, requant=requant)
+    assert exe.qplan.requant == requant
     try:
         assert exe.fallbacks() == []
         feeds = builders.make_input(g, seed=11)

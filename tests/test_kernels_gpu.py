@@ -366,6 +366,41 @@ def test_depthwise(ctx, dtype, case):
         np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4)
 
 
+GROUPED_CASES = [
+    # n, c, k, h, w, r, stride, pad, groups, residual
+    (2, 64, 64, 11, 13, 3, 1, 1, 2, False),
+    (2, 64, 96, 9, 9, 3, 2, 1, 4, True),       # k != c
+    (1, 128, 128, 7, 8, 3, 1, 1, 16, False),    # groups = C/8
+    (2, 24, 40, 10, 10, 1, 1, 0, 4, False),     # 1x1 grouped, ragged k stride
+    (2, 16, 32, 12, 12, 3, 1, 1, 16, False),    # depth multiplier 2 (groups = C, K = 2C)
+]
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+@pytest.mark.parametrize("case", GROUPED_CASES, ids=[str(c) for c in GROUPED_CASES])
+def test_grouped_conv(ctx, dtype, case):
+    """1 < groups < C (and channel multipliers) on the device: the reference
+    runs these per group on the host (ops.py:68-78, emit.py:175-180)."""
+    n, c, k, h, w, r, stride, pad, groups, with_res = case
+    rng = np.random.default_rng(77 + sum(case))
+    x = rng.standard_normal((n, c, h, w)).astype(np.float32)
+    wt = (rng.standard_normal((k, c // groups, r, r)) * np.sqrt(2.0 / (c // groups * r * r))).astype(np.float32)
+    b = (rng.standard_normal(k) * 0.1).astype(np.float32)
+    oh, ow = (h + 2 * pad - r) // stride + 1, (w + 2 * pad - r) // stride + 1
+    res = rng.standard_normal((n, k, oh, ow)).astype(np.float32) if with_res else None
+    got = run_conv(ctx, x, wt, b, stride=stride, pad=pad, groups=groups, dtype=dtype, act=L.ACT_RELU, res=res)
+    # grouped weights are kept in fp32; only activations are bf16
+    xr = oref.round_bf16(x) if dtype == "bf16" else x
+    y = oref.conv(xr, wt, b, strides=[stride] * 2, pads=[pad] * 4, group=groups)
+    if res is not None:
+        y = y + (oref.round_bf16(res) if dtype == "bf16" else res)
+    want = np.maximum(y, 0)
+    if dtype == "bf16":
+        np.testing.assert_allclose(got, want, rtol=1e-2, atol=1e-2)
+    else:
+        np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4)
+
+
 def _pool(ctx, x, kind, dtype, k=3, s=2, p=1):
     n, c, h, w = x.shape
     cs = _rnd8(c)

@@ -261,3 +261,26 @@ def test_compile_devices_2_equals_devices_1():
             np.testing.assert_array_equal(two.pinned_outputs(device=i)["logits"], want[4 * i:4 * i + 4])
     finally:
         two.close()
+
+
+@pytest.mark.parametrize("groups", [2, 4, 16])
+def test_grouped_block_matches_oracle(groups):
+    """A ResNeXt-style bottleneck whose 3x3 conv has 1 < groups < C compiles
+    with no host fallback and matches the oracle's grouped conv (the
+    reference's per-group loop, ops.py:68-78) in fp32 and bf16."""
+    g = passes.default_pipeline(builders.grouped_block(n=2, c=64, h=14, w=14, groups=groups))
+    feeds = builders.make_input(g, seed=groups)
+    want = oref.run(g, feeds)["y"]
+    emu = oref.run(g, feeds, bf16_emulation=True)["y"]
+    scale = np.abs(want).max()
+    for dtype in ("fp32", "bf16"):
+        exe = compile(g, dtype=dtype)
+        try:
+            assert exe.fallbacks() == []
+            got = exe.run(feeds)["y"]
+        finally:
+            exe.close()
+        if dtype == "fp32":
+            np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4)
+        else:
+            np.testing.assert_allclose(got, emu, rtol=1e-2, atol=1e-2 * scale)

@@ -121,3 +121,68 @@ def test_int8_oracle_tracks_fp32(name, kw):
         want = ref[o]
         rel = np.linalg.norm(y - want) / np.linalg.norm(want)
         assert rel < 0.1, f"int8 vs fp32 relative error {rel:.3f}"
+
+
+def test_shared_shift_multipliers():
+    """M1, M2 represent the real multipliers to 31 significant bits of the
+    larger one, with one shift per channel."""
+    rng = np.random.default_rng(3)
+    real = np.exp(rng.uniform(np.log(1e-6), np.log(0.9), 64))
+    for rres in (None, 0.013, 1.7):
+        m1, m2, sh = quant.shared_shift_multipliers(real, rres)
+        assert m1.dtype == np.int32 and sh.min() >= 1 and sh.max() <= 62
+        for k in range(64):
+            big = max(real[k], rres or 0.0)
+            assert (1 << 30) <= max(int(m1[k]), int(m2[k])) < (1 << 31)
+            assert abs(int(m1[k]) / 2.0 ** int(sh[k]) - real[k]) <= 0.5 / 2.0 ** int(sh[k])
+            if rres:
+                assert abs(int(m2[k]) / 2.0 ** int(sh[k]) - rres) <= 0.5 / 2.0 ** int(sh[k])
+            assert abs(max(int(m1[k]), int(m2[k])) / 2.0 ** int(sh[k]) - big) <= big * 2.0 ** -30
+
+
+def test_fixed_point_requant_is_one_rounding_of_the_exact_value():
+    """The oracle's fixed-point step equals floor(exact + 1/2) of the rational
+    (acc*M1 + r*M2) / 2^S computed with Python integers."""
+    from fractions import Fraction
+    g, plan = _plan("resnet18", dict(batch=1, image=64))
+    assert plan.requant == "fixed"
+    cq = next(c for c in plan.convs.values() if c.residual and c.rq_mult is not None)
+    rng = np.random.default_rng(5)
+    k = cq.rq_mult.shape[0]
+    acc = rng.integers(-(1 << 24), 1 << 24, (3, k), dtype=np.int64)
+    res = rng.integers(-128, 128, (3, k), dtype=np.int64)
+    m1, m2, sh = (cq.rq_mult.astype(np.int64), cq.rq_res_mult.astype(np.int64), cq.rq_shift.astype(np.int64))
+    got = (acc * m1 + res * m2 + (np.int64(1) << (sh - 1))) >> sh
+    for i in range(3):
+        for j in range(k):
+            exact = Fraction(int(acc[i, j]) * int(m1[j]) + int(res[i, j]) * int(m2[j]), 1 << int(sh[j]))
+            assert got[i, j] == math.floor(exact + Fraction(1, 2))
+
+
+@pytest.mark.parametrize("name,kw", [("residual_block", dict(n=2, c=16, h=16, w=16)),
+                                     ("resnet18", dict(batch=1, image=64))])
+def test_fixed_and_fp32_requant_agree_within_one_code(name, kw):
+    g = passes.default_pipeline(builders.BUILDERS[name](**kw))
+    _, plan_fx = _plan(name, kw)
+    shp = S.infer(g)
+    lo_i8 = lowering.lower(g, shp, L.U8, s2d=True)
+    for o in lo_i8.outputs:
+        prod = [st for st in lo_i8.steps if o in st.outputs]
+        if prod and prod[0].kind == "conv":
+            lo_i8.tensors[o].dtype = L.F32
+    lo_orig = lowering.lower(g, shp, L.U8, s2d=False)
+    ranges = {t: plan_fx.tensors[t] for t in plan_fx.tensors}
+    feeds = builders.make_input(g, seed=9)
+    # the same ranges -> same scales; only the requantisation arithmetic differs
+    env = oref.run(g, feeds, return_all=True)
+    rng_ = {kk: (float(np.asarray(v).min()), float(np.asarray(v).max())) for kk, v in env.items()
+            if kk not in g.initializers}
+    p_fx = quant.build_plan(lo_orig, lo_i8, rng_, g, requant="fixed")
+    p_fp = quant.build_plan(lo_orig, lo_i8, rng_, g, requant="fp32")
+    a = oq.run_int8(g, p_fx, feeds)["__codes__"]
+    b = oq.run_int8(g, p_fp, feeds)["__codes__"]
+    # the first requantised layer sees identical inputs: its codes differ by <= 1
+    first = next(st.outputs[0] for st in p_fx.steps if st.kind == "conv")
+    d = np.abs(np.asarray(a[first], np.int64) - np.asarray(b[first], np.int64))
+    assert d.max() <= 1 and d.mean() < 0.01
+    del ranges
