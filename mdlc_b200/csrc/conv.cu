@@ -471,6 +471,11 @@ int conv_dw(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const float* 
   a.oh = d.oh; a.ow = d.ow; a.res_s = d.res_stride ? d.res_stride : d.c_stride;
   a.total = (long long)d.n * d.oh * d.ow * (d.c_stride / 8);
   a.act = act_of(epi);
+  // 3x3 stride 1 / 2: the TMA halo-staged kernel (csrc/dwconv.cu)
+  {
+    const int st = conv_dw_tma(ctx, d, x, w, bias, res, y, epi);
+    if (st != MDLC_ERR_UNSUPPORTED) return st;
+  }
   const int strips = (d.oh + kDwStrip - 1) / kDwStrip;
   const long long strip_total = (long long)d.n * strips * d.ow * (d.c_stride / 8);
   if (d.r == 3 && d.s == 3 && d.dil_h == 1 && d.dil_w == 1 && d.stride_h == d.stride_w &&

@@ -1,6 +1,8 @@
 // Internal entry points of the convolution kernels (not part of the C ABI).
 #pragma once
 
+#include <cudaTypedefs.h>
+
 #include "mdlc_b200.h"
 #include "runtime.h"
 
@@ -19,5 +21,12 @@ int conv_dw(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const float* 
 // grouped (1 < groups, not depthwise), bf16 or fp32 activations, fp32 weights
 int conv_grouped(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const float* w, const float* bias,
                  const void* res, void* y, const mdlc_epilogue* epi);
+
+// depthwise 3x3 with TMA halo staging; MDLC_ERR_UNSUPPORTED when the layer
+// does not fit it (the caller then uses conv_dw)
+int conv_dw_tma(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const float* w, const float* bias,
+                const void* res, void* y, const mdlc_epilogue* epi);
+// cuTensorMapEncodeTiled from the driver (null when unavailable)
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 
 }  // namespace mdlc

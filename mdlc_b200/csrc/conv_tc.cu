@@ -108,9 +108,10 @@ struct Smem {
   static constexpr int kEBuf = 32 * 64 * ESZ;
   static constexpr int kE = kB + STAGES * kBBytes;
   // per-tile epilogue parameters, double-buffered by tile parity: the fp32
-  // bias (bf16), or the int32 bias, the fp32 requantisation scale or the
-  // fixed-point multiplier, the residual multiplier and the shift (8-bit)
-  static constexpr int kParamWords = ESZ == 2 ? 1 : 4;
+  // bias (bf16); the int32 bias and fp32 requantisation scale (8-bit, fp32
+  // form); or the multiplier, residual multiplier, packed shifts and the
+  // 64-bit constant bias32 * multiplier + rounding term (8-bit, fixed point)
+  static constexpr int kParamWords = ESZ == 2 ? 1 : 5;
   static constexpr int kBias = kE + 4 * 2 * kEBuf;
   static constexpr int kBar = kBias + 2 * kParamWords * BN * 4;
   // barriers: fullA[S], fullB[S], empty[S], tfull[2], tempty[2], drain, resid[4 warps][2 buffers],
@@ -577,8 +578,10 @@ __global__ void __launch_bounds__(kThreads, (Occ<BN, STAGES, ESZ, AMODE>::value)
           tma_load_2d(dst, &tmap_r, c, m0 + ew * 32, bar);
       };
       float* sbias = reinterpret_cast<float*>(smem + L::kBias) + buf * BN;
-      // 8-bit: bias32 | fp32 scale or multiplier | residual multiplier | shift
-      int32_t* sq = reinterpret_cast<int32_t*>(smem + L::kBias) + buf * 4 * BN;
+      // 8-bit, fp32 form: bias32 | fp32 scale; fixed point: multiplier |
+      // residual multiplier | shifts (min(S, 32) | max(S - 32, 0) << 8) |
+      // constant low word | constant high word
+      int32_t* sq = reinterpret_cast<int32_t*>(smem + L::kBias) + buf * 5 * BN;
       if (tma_epi) {
         // stage this tile's epilogue parameters (and the first residual chunk) while the main loop runs
         if constexpr (ESZ == 2) {
@@ -589,9 +592,14 @@ __global__ void __launch_bounds__(kThreads, (Occ<BN, STAGES, ESZ, AMODE>::value)
             const bool v = n0 + i < a.k;
             sq[i] = (v && a.bias) ? __ldg(static_cast<const int32_t*>(a.bias) + n0 + i) : 0;
             if (a.rq_fixed) {
-              sq[BN + i] = v ? __ldg(a.rq_mult + n0 + i) : 0;
-              sq[2 * BN + i] = (v && a.rq_res_mult) ? __ldg(a.rq_res_mult + n0 + i) : 0;
-              sq[3 * BN + i] = v ? __ldg(a.rq_shift + n0 + i) : 1;
+              const int32_t m1 = v ? __ldg(a.rq_mult + n0 + i) : 0;
+              const int sh = v ? __ldg(a.rq_shift + n0 + i) : 1;
+              const long long cst = (long long)sq[i] * m1 + (1ll << (sh - 1));
+              sq[i] = m1;
+              sq[BN + i] = (v && a.rq_res_mult) ? __ldg(a.rq_res_mult + n0 + i) : 0;
+              sq[2 * BN + i] = (sh < 32 ? sh : 32) | ((sh > 32 ? sh - 32 : 0) << 8);
+              sq[3 * BN + i] = (int32_t)(uint32_t)(unsigned long long)cst;
+              sq[4 * BN + i] = (int32_t)(cst >> 32);
             } else {
               sq[BN + i] = v ? __float_as_int(__ldg(a.rq_scale + n0 + i)) : 0;
             }
@@ -674,31 +682,34 @@ __global__ void __launch_bounds__(kThreads, (Occ<BN, STAGES, ESZ, AMODE>::value)
               const uint32_t rw[4] = {rr.x, rr.y, rr.z, rr.w};
               // this group's 16 int32 biases and fp32 scales as 128-bit loads
               const int col0 = c0 + 16 * q;
-              int32_t bq[16];
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const int4 bb = *reinterpret_cast<const int4*>(sq + col0 + 4 * j);
-                bq[4 * j] = bb.x; bq[4 * j + 1] = bb.y; bq[4 * j + 2] = bb.z; bq[4 * j + 3] = bb.w;
-              }
               const bool full = n0 + col0 + 16 <= a.k;  // group-uniform: no pad columns
               int32_t t[16];
               if (a.rq_fixed) {
-                // single-rounding fixed point: one 64-bit sum of the products
-                // with the multipliers and the rounding constant, one shift
-                int32_t m1[16], m2[16], sh[16];
+                // single-rounding fixed point: p = acc * M1 + (bias32 * M1 + 2^(S-1))
+                // [+ (res - zp) * M2] in 64 bits (one wide multiply-add each), then
+                // p >> S as a funnel shift of (hi, lo) by min(S, 32) and an
+                // arithmetic shift by max(S - 32, 0); exact in 32 bits because the
+                // host bounds |p >> S| below 2^30 for every possible 8-bit input
+                int32_t m1[16], m2[16], shp[16];
+                long long cst[16];
 #pragma unroll
                 for (int j = 0; j < 4; ++j) {
-                  const int4 a4 = *reinterpret_cast<const int4*>(sq + BN + col0 + 4 * j);
-                  const int4 b4 = *reinterpret_cast<const int4*>(sq + 2 * BN + col0 + 4 * j);
-                  const int4 c4 = *reinterpret_cast<const int4*>(sq + 3 * BN + col0 + 4 * j);
+                  const int4 a4 = *reinterpret_cast<const int4*>(sq + col0 + 4 * j);
+                  const int4 b4 = *reinterpret_cast<const int4*>(sq + BN + col0 + 4 * j);
+                  const int4 c4 = *reinterpret_cast<const int4*>(sq + 2 * BN + col0 + 4 * j);
+                  const int4 l4 = *reinterpret_cast<const int4*>(sq + 3 * BN + col0 + 4 * j);
+                  const int4 h4 = *reinterpret_cast<const int4*>(sq + 4 * BN + col0 + 4 * j);
                   m1[4 * j] = a4.x; m1[4 * j + 1] = a4.y; m1[4 * j + 2] = a4.z; m1[4 * j + 3] = a4.w;
                   m2[4 * j] = b4.x; m2[4 * j + 1] = b4.y; m2[4 * j + 2] = b4.z; m2[4 * j + 3] = b4.w;
-                  sh[4 * j] = c4.x; sh[4 * j + 1] = c4.y; sh[4 * j + 2] = c4.z; sh[4 * j + 3] = c4.w;
+                  shp[4 * j] = c4.x; shp[4 * j + 1] = c4.y; shp[4 * j + 2] = c4.z; shp[4 * j + 3] = c4.w;
+                  cst[4 * j] = ((long long)h4.x << 32) | (uint32_t)l4.x;
+                  cst[4 * j + 1] = ((long long)h4.y << 32) | (uint32_t)l4.y;
+                  cst[4 * j + 2] = ((long long)h4.z << 32) | (uint32_t)l4.z;
+                  cst[4 * j + 3] = ((long long)h4.w << 32) | (uint32_t)l4.w;
                 }
                 long long acc64[16];
 #pragma unroll
-                for (int e = 0; e < 16; ++e)
-                  acc64[e] = (long long)((int32_t)v[16 * q + e] + bq[e]) * m1[e] + ((1ll << sh[e]) >> 1);
+                for (int e = 0; e < 16; ++e) acc64[e] = (long long)(int32_t)v[16 * q + e] * m1[e] + cst[e];
                 if (a.res) {
 #pragma unroll
                   for (int e = 0; e < 16; ++e) {
@@ -709,11 +720,18 @@ __global__ void __launch_bounds__(kThreads, (Occ<BN, STAGES, ESZ, AMODE>::value)
                 }
 #pragma unroll
                 for (int e = 0; e < 16; ++e) {
-                  long long r = acc64[e] >> sh[e];
-                  r = r < a.qlo ? a.qlo : (r > a.qhi ? a.qhi : r);
-                  t[e] = (int32_t)r + a.out_zp;
+                  const int32_t r = (int32_t)__funnelshift_rc((uint32_t)(unsigned long long)acc64[e],
+                                                             (uint32_t)(acc64[e] >> 32), shp[e] & 0xFF) >>
+                                    (shp[e] >> 8);
+                  t[e] = min(max(r, a.qlo), a.qhi) + a.out_zp;
                 }
               } else {
+              int32_t bq[16];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const int4 bb = *reinterpret_cast<const int4*>(sq + col0 + 4 * j);
+                bq[4 * j] = bb.x; bq[4 * j + 1] = bb.y; bq[4 * j + 2] = bb.z; bq[4 * j + 3] = bb.w;
+              }
               float sc[16];
 #pragma unroll
               for (int j = 0; j < 4; ++j) {
@@ -1125,6 +1143,8 @@ int launch_tc(mdlc_ctx* ctx, const CUtensorMap& tmap, const CUtensorMap& tmap_y,
 }
 
 }  // namespace
+
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() { return get_encode_fn(); }
 
 int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w, const void* bias,
             const void* res, void* y, const mdlc_epilogue* epi, const mdlc_tile_cfg* cfg) {

@@ -232,6 +232,15 @@ def build_plan(lo_f32, lo_i8, ranges: dict, graph, requant: str = "fixed") -> Qu
             if requant == "fixed":
                 q.rq_mult, q.rq_res_mult, q.rq_shift = shared_shift_multipliers(
                     acc_scale / np.float64(s_y), real_res)
+                # the kernel keeps p >> S in 32 bits: bound it for every possible
+                # 8-bit input (|x| <= 255, |w| <= 127 over the whole reduction)
+                red = int(np.prod(w_q_orig.shape[1:]))
+                acc_max = red * 255 * 127 + np.abs(q.bias32.astype(np.int64))
+                top = (acc_max * q.rq_mult.astype(np.int64) + 255 * np.abs(q.rq_res_mult.astype(np.int64))
+                       ) >> q.rq_shift.astype(np.int64)
+                if top.max() >= (1 << 30):
+                    raise lowering.LoweringError(f"int8: fixed-point requantisation of {st.label()} "
+                                                 "could exceed 32 bits; use requant='fp32'")
         convs[st.params["weight"]] = q
     if requant not in ("fixed", "fp32"):
         raise ValueError(f"requant must be 'fixed' or 'fp32', not {requant!r}")

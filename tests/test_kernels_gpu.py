@@ -340,6 +340,10 @@ DW_CASES = [
     (1, 40, 35, 9, 3, 2, 1, False),      # 3 strips, ragged channel groups
     (2, 24, 20, 17, 3, 1, 0, True),      # no padding, residual
     (2, 32, 11, 10, 5, 1, 2, False),     # 5x5: generic kernel
+    (2, 144, 29, 31, 3, 1, 1, True),     # 48-channel blocks, tiles past both image edges
+    (1, 960, 9, 7, 3, 2, 1, False),      # 15 blocks of 64 channels, stride 2
+    (3, 56, 33, 17, 3, 2, 1, True),      # one 56-channel block, odd sizes, stride 2
+    (1, 24, 40, 40, 3, 1, 1, False),     # 24-channel pixels (48 bytes), several tiles
 ]
 
 
