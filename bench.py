@@ -156,13 +156,20 @@ def call_work(dev, call):
         wb = L.weight_bytes(d)
         flops = 2.0 * d.n * d.oh * d.ow * d.k * (d.c // d.groups) * d.r * d.s
         if d.groups == 1 and d.in_type != L.F32:
-            cls, bound = "conv_tc", "tensor"
+            # tensor- or HBM-bound by arithmetic intensity against the measured peaks
+            peak_tf, peak_gbs, _ = _peaks()
+            if flops / (xb + wb + yb + rb) >= peak_tf * 1e3 / peak_gbs:
+                cls, bound = "conv_tc", "tensor"
+            else:
+                cls, bound = "conv_tc(hbm-bound)", "hbm"
             if d.r == 1 and d.s == 1 and d.h * d.w == 1:
                 cls = "conv_tc(fc)"
         elif d.groups == 1:
-            cls, bound = "conv_f32", "fp32 simt"
-        else:
+            cls, bound = "conv_tc(3xtf32)", "tensor"
+        elif d.groups == d.c == d.k:
             cls, bound = "conv_dw", "hbm"
+        else:
+            cls, bound = "conv_grouped", "hbm"
         return cls, bound, xb + wb + yb + rb, flops
     if kind == "pool":
         d = call[1]
@@ -523,8 +530,11 @@ def main() -> int:
         peak_tf, _, peak_kind = _peaks()
         if dtype == "int8":
             peak_tf, peak_kind = int8_peak_tops(local), "measured in this run (torch._int_mm) int8"
+        elif dtype == "fp32":
+            # 3xTF32: three tf32 MMAs per fp32 product, each at half the bf16 rate
+            peak_tf, peak_kind = round(peak_tf / 6, 1), f"{peak_kind} bf16 / 6 (3xTF32 ceiling)"
         conv_flops_step = sum(flops)
-        tc = [e for k, e in ktable.items() if k.startswith("conv_tc") or k == "conv_f32"]
+        tc = [e for k, e in ktable.items() if k.startswith("conv_tc")]
         conv_ms = sum(e["ms"] for e in tc)
         nconv = sum(e["launches"] for e in tc)
         avg_launch_ms = conv_ms / nconv
@@ -560,7 +570,7 @@ def main() -> int:
             "roofline": {"kernel": "conv_tc_kernel (tcgen05 implicit GEMM)", "bound": "tensor",
                          "achieved": round(achieved_tf, 1),
                          "peak": peak_tf, "unit": "TFLOP/s", "frac": round(achieved_tf / peak_tf, 4),
-                         "peak_kind": peak_kind if dtype == "int8" else f"{peak_kind} bf16 (burst)", "traffic": conv_traffic(args.workload),
+                         "peak_kind": peak_kind if dtype != "bf16" else f"{peak_kind} bf16 (burst)", "traffic": conv_traffic(args.workload),
                          "traffic_unit": "bytes per launch (ncu dram read+write)",
                          "conv_share_of_step": round(conv_ms / inst_ms, 4) if inst_ms else None,
                          "flops_per_launch": round(conv_flops_step / len(flops)),

@@ -22,6 +22,18 @@ MDLC_DEV void record_error(int* err, int code) {
   if (err) atomicCAS(err, 0, code);
 }
 
+// Bounds checks of computed global-memory indices, compiled in only by the
+// checked build (-DMDLC_CHECK, libmdlc_b200_check.so): an index outside
+// [0, extent) records MDLC_DEVERR_BOUNDS in the error word and the access is
+// skipped; nothing traps. In the normal build the check is the constant true.
+#ifdef MDLC_CHECK
+#define MDLC_CHECK_IDX(err, idx, extent) \
+  (((unsigned long long)(idx) < (unsigned long long)(extent)) ? true \
+                                                              : (mdlc::record_error((err), MDLC_DEVERR_BOUNDS), false))
+#else
+#define MDLC_CHECK_IDX(err, idx, extent) true
+#endif
+
 MDLC_DEV uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
@@ -115,6 +127,15 @@ MDLC_DEV void tma_load_2d(uint32_t dst, const void* tmap, int32_t x, int32_t y, 
       "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes"
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(dst),
       "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar), "r"(x), "r"(y)
+      : "memory");
+}
+
+// 3-D tiled load into this CTA's shared memory.
+MDLC_DEV void tma_load_3d(uint32_t dst, const void* tmap, int32_t x, int32_t y, int32_t z, uint32_t bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%3, %4, %5}], [%2];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(tmap)), "r"(bar), "r"(x), "r"(y), "r"(z)
       : "memory");
 }
 
@@ -215,6 +236,10 @@ __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) |
          ((uint32_t)(M >> 4) << 24);
 }
+// Instruction descriptor, kind::tf32 (A and B tf32, format 2; fp32 accumulator).
+__host__ __device__ constexpr uint32_t idesc_tf32(int M, int N) {
+  return (1u << 4) | (2u << 7) | (2u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
 // Instruction descriptor, kind::i8 with int32 accumulator; a_signed/b_signed
 // select s8 (1) or u8 (0) operands.
 __host__ __device__ constexpr uint32_t idesc_i8(int M, int N, int a_signed, int b_signed) {
@@ -237,6 +262,15 @@ MDLC_DEV void umma_i8(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t 
       "{\n\t.reg .pred p;\n\t"
       "setp.ne.b32 p, %4, 0;\n\t"
       "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+MDLC_DEV void umma_tf32(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc,
+                        uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::tf32 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
       "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
       : "memory");
 }

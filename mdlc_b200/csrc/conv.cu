@@ -1,5 +1,5 @@
-// mdlc_conv2d dispatch, weight packing, the fp32 SIMT implicit GEMM and the
-// depthwise convolution kernel.
+// mdlc_conv2d dispatch, weight packing, and the depthwise (generic shapes) and
+// grouped convolution kernels.
 //
 // Reference semantics: mdlc/runtime/ops.py:56-81 (conv = im2col + einsum,
 // grouped conv per group), ops.py:84-92 (gemm). The reference lowering runs
@@ -14,100 +14,6 @@
 
 namespace mdlc {
 namespace {
-
-// ------------------------------------------------------------ fp32 SIMT GEMM
-// 64x64 output tile per 256-thread CTA, 16-deep k slices staged in shared
-// memory, 4x4 register micro-tile per thread. Implicit im2col: A elements are
-// gathered from the NHWC input on the fly (padding reads as zero).
-struct F32Args {
-  const float* x;
-  const float* w;  // [kg_pad][ks]
-  const float* bias;
-  const float* res;
-  float* y;
-  int h, w_, cs, k, ks, res_s, r, s, sh, sw, pt, pl, dh, dw, oh, ow, M, kg;
-  ActParams act;
-};
-
-__global__ void __launch_bounds__(256) conv_f32_kernel(const F32Args a) {
-  __shared__ float As[16][64 + 4];
-  __shared__ float Bs[16][64];
-  const int tid = threadIdx.x;
-  const int m0 = blockIdx.x * 64, n0 = blockIdx.y * 64;
-  const int kq = tid & 15;
-  int img[4], ih0[4], iw0[4];
-  const int ohw = a.oh * a.ow;
-#pragma unroll
-  for (int q = 0; q < 4; ++q) {
-    const int m = m0 + (tid >> 4) + 16 * q;
-    if (m < a.M) {
-      img[q] = m / ohw;
-      const int rem = m - img[q] * ohw;
-      const int oy = rem / a.ow;
-      ih0[q] = oy * a.sh - a.pt;
-      iw0[q] = (rem - oy * a.ow) * a.sw - a.pl;
-    } else {
-      img[q] = -1; ih0[q] = 0; iw0[q] = 0;
-    }
-  }
-  const int ty = tid >> 4, tx = tid & 15;
-  float acc[4][4] = {};
-  const int RS = a.r * a.s;
-  for (int k0 = 0; k0 < a.kg; k0 += 16) {
-    const int kk = k0 + kq;
-    const int tap = kk / a.cs;
-    const int c = kk - tap * a.cs;
-    const int rr = tap / a.s;
-    const int dy = rr * a.dh, dx = (tap - rr * a.s) * a.dw;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      float v = 0.0f;
-      const int ih = ih0[q] + dy, iw = iw0[q] + dx;
-      if (img[q] >= 0 && tap < RS && (unsigned)ih < (unsigned)a.h && (unsigned)iw < (unsigned)a.w_)
-        v = __ldg(a.x + ((long long)(img[q] * a.h + ih) * a.w_ + iw) * a.cs + c);
-      As[kq][(tid >> 4) + 16 * q] = v;
-    }
-#pragma unroll
-    for (int q = 0; q < 4; ++q) {
-      const int e = tid + 256 * q;
-      const int kr = e >> 6, nn = e & 63;
-      const int kg_i = k0 + kr;
-      Bs[kr][nn] = (n0 + nn < a.ks && kg_i < a.kg) ? __ldg(a.w + (long long)kg_i * a.ks + n0 + nn) : 0.0f;
-    }
-    __syncthreads();
-#pragma unroll
-    for (int t = 0; t < 16; ++t) {
-      float av[4], bv[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) av[i] = As[t][ty * 4 + i];
-#pragma unroll
-      for (int j = 0; j < 4; ++j) bv[j] = Bs[t][tx * 4 + j];
-#pragma unroll
-      for (int i = 0; i < 4; ++i)
-#pragma unroll
-        for (int j = 0; j < 4; ++j) acc[i][j] = fmaf(av[i], bv[j], acc[i][j]);
-    }
-    __syncthreads();
-  }
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int m = m0 + ty * 4 + i;
-    if (m >= a.M) continue;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int n = n0 + tx * 4 + j;
-      if (n >= a.ks) continue;
-      float v = 0.0f;
-      if (n < a.k) {
-        v = acc[i][j];
-        if (a.bias) v += a.bias[n];
-        if (a.res) v += a.res[(long long)m * a.res_s + n];
-        v = apply_act(v, a.act);
-      }
-      a.y[(long long)m * a.ks + n] = v;
-    }
-  }
-}
 
 // ------------------------------------------------------------ depthwise
 // One thread per (output pixel, 8-channel group): nine (or r*s) 16-byte
@@ -336,6 +242,8 @@ struct GroupedArgs {
   int h, w_, cs, k, ks, icg, ocg, r, s, sh, sw, pt, pl, dh, dw, oh, ow, res_s;
   long long total;  // M * ks
   ActParams act;
+  int* err;
+  long long x_elems, w_elems, res_elems;  // element extents (checked build)
 };
 
 template <typename T>
@@ -377,10 +285,14 @@ __global__ void __launch_bounds__(256) conv_grouped_kernel(const GroupedArgs a) 
         if ((unsigned)iw >= (unsigned)a.w_) continue;
         const T* xp = xb + ((long long)ih * a.w_ + iw) * a.cs;
         const float* wp = a.w + (long long)(rr * a.s + ss) * a.icg * a.ks + o;
+        if (!MDLC_CHECK_IDX(a.err, (xp + a.icg - 1) - static_cast<const T*>(a.x), a.x_elems) ||
+            !MDLC_CHECK_IDX(a.err, (wp - a.w) + (long long)(a.icg - 1) * a.ks, a.w_elems))
+          continue;
         for (int c = 0; c < a.icg; ++c) acc = fmaf(ld_f<T>(xp + c), __ldg(wp + (long long)c * a.ks), acc);
       }
     }
-    if (a.res) acc += ld_f<T>(static_cast<const T*>(a.res) + m * a.res_s + o);
+    if (a.res && MDLC_CHECK_IDX(a.err, m * a.res_s + o, a.res_elems))
+      acc += ld_f<T>(static_cast<const T*>(a.res) + m * a.res_s + o);
     st_f<T>(yp, apply_act(acc, a.act));
   }
 }
@@ -423,7 +335,7 @@ int validate(mdlc_ctx* ctx, const mdlc_conv_desc* d) {
   return MDLC_OK;
 }
 
-enum Path { kPathTC, kPathF32, kPathDW, kPathGrouped, kPathNone };
+enum Path { kPathTC, kPathDW, kPathGrouped, kPathNone };
 
 Path path_of(const mdlc_conv_desc& d) {
   if (d.groups == 1) {
@@ -431,7 +343,7 @@ Path path_of(const mdlc_conv_desc& d) {
     if ((d.in_type == MDLC_U8 || d.in_type == MDLC_S8) &&
         (d.out_type == MDLC_U8 || d.out_type == MDLC_S8 || d.out_type == MDLC_F32 || d.out_type == MDLC_S32))
       return kPathTC;
-    if (d.in_type == MDLC_F32 && d.out_type == MDLC_F32) return kPathF32;
+    if (d.in_type == MDLC_F32 && d.out_type == MDLC_F32) return kPathTC;  // 3xTF32
     return kPathNone;
   }
   if (d.groups == d.c && d.c == d.k && d.in_type == d.out_type &&
@@ -444,23 +356,6 @@ Path path_of(const mdlc_conv_desc& d) {
 }
 
 }  // namespace
-
-int conv_f32(mdlc_ctx* ctx, const mdlc_conv_desc& d, const float* x, const float* w, const float* bias,
-             const float* res, float* y, const mdlc_epilogue* epi) {
-  F32Args a{};
-  a.x = x; a.w = w; a.bias = bias; a.res = res; a.y = y;
-  a.h = d.h; a.w_ = d.w; a.cs = d.c_stride; a.k = d.k; a.ks = d.k_stride;
-  a.res_s = d.res_stride ? d.res_stride : d.k_stride;
-  a.r = d.r; a.s = d.s; a.sh = d.stride_h; a.sw = d.stride_w; a.pt = d.pad_t; a.pl = d.pad_l;
-  a.dh = d.dil_h; a.dw = d.dil_w; a.oh = d.oh; a.ow = d.ow;
-  a.M = d.n * d.oh * d.ow;
-  a.kg = d.r * d.s * d.c_stride;
-  a.act = act_of(epi);
-  dim3 grid((a.M + 63) / 64, (d.k_stride + 63) / 64);
-  conv_f32_kernel<<<grid, 256, 0, ctx->stream>>>(a);
-  mdlc_note_launch(ctx);
-  return mdlc_cuda_status(ctx, cudaGetLastError(), "conv_f32 launch");
-}
 
 int conv_dw(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const float* w, const float* bias,
             const void* res, void* y, const mdlc_epilogue* epi) {
@@ -516,6 +411,10 @@ int conv_grouped(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const fl
   a.res_s = d.res_stride ? d.res_stride : d.k_stride;
   a.total = (long long)d.n * d.oh * d.ow * d.k_stride;
   a.act = act_of(epi);
+  a.err = ctx->d_err;
+  a.x_elems = (long long)d.n * d.h * d.w * d.c_stride;
+  a.w_elems = (long long)d.r * d.s * a.icg * d.k_stride;
+  a.res_elems = (long long)d.n * d.oh * d.ow * a.res_s;
   long long blocks = (a.total + 255) / 256;
   const long long cap = (long long)ctx->num_sms * 16;
   if (blocks > cap) blocks = cap;
@@ -536,14 +435,12 @@ extern "C" int mdlc_conv_weight_bytes(const mdlc_conv_desc* d, size_t* bytes) {
   const long long kg = (long long)d->r * d->s * d->c_stride;
   switch (path_of(*d)) {
     case kPathTC: {
-      const int esz = (d->in_type == MDLC_BF16) ? 2 : 1;
+      const int esz = d->in_type == MDLC_BF16 ? 2 : (d->in_type == MDLC_F32 ? 4 : 1);
       const long long kb = 128 / esz;
-      *bytes = (size_t)(((kg + kb - 1) / kb) * 128) * (size_t)d->k;
+      // fp32: a tf32 hi matrix and a lo matrix
+      *bytes = (size_t)(((kg + kb - 1) / kb) * 128) * (size_t)d->k * (esz == 4 ? 2 : 1);
       return MDLC_OK;
     }
-    case kPathF32:
-      *bytes = (size_t)kg * d->k_stride * sizeof(float);
-      return MDLC_OK;
     case kPathDW:
       *bytes = (size_t)d->r * d->s * d->c_stride * sizeof(float);
       return MDLC_OK;
@@ -566,7 +463,7 @@ extern "C" int mdlc_pack_conv_weights(const mdlc_conv_desc* d, const float* w, v
   auto W = [&](int o, int c, int r, int s) { return w[(((long long)o * icg + c) * R + r) * S + s]; };
   switch (path_of(*d)) {
     case kPathTC: {
-      const int esz = (d->in_type == MDLC_BF16) ? 2 : 1;
+      const int esz = d->in_type == MDLC_BF16 ? 2 : (d->in_type == MDLC_F32 ? 4 : 1);
       const long long kb = 128 / esz;
       const long long kg_pad = ((1ll * R * S * cs + kb - 1) / kb) * kb;
       for (int o = 0; o < K; ++o)
@@ -574,20 +471,23 @@ extern "C" int mdlc_pack_conv_weights(const mdlc_conv_desc* d, const float* w, v
           for (int s = 0; s < S; ++s)
             for (int c = 0; c < C; ++c) {
               const long long idx = (long long)o * kg_pad + (long long)(r * S + s) * cs + c;
-              if (esz == 2)
-                static_cast<uint16_t*>(out)[idx] = f32_to_bf16_rne(W(o, c, r, s));
-              else
-                static_cast<int8_t*>(out)[idx] = (int8_t)lrintf(W(o, c, r, s));
+              const float v = W(o, c, r, s);
+              if (esz == 4) {
+                // tf32 split: hi keeps the top 10 mantissa bits (the rest cleared),
+                // lo = v - hi exactly; [hi matrix][lo matrix], each [k][kg_pad]
+                uint32_t u;
+                std::memcpy(&u, &v, 4);
+                u &= 0xFFFFE000u;
+                float hi;
+                std::memcpy(&hi, &u, 4);
+                static_cast<float*>(out)[idx] = hi;
+                static_cast<float*>(out)[(long long)K * kg_pad + idx] = v - hi;
+              } else if (esz == 2) {
+                static_cast<uint16_t*>(out)[idx] = f32_to_bf16_rne(v);
+              } else {
+                static_cast<int8_t*>(out)[idx] = (int8_t)lrintf(v);
+              }
             }
-      return MDLC_OK;
-    }
-    case kPathF32: {
-      float* o_ = static_cast<float*>(out);
-      for (int o = 0; o < K; ++o)
-        for (int r = 0; r < R; ++r)
-          for (int s = 0; s < S; ++s)
-            for (int c = 0; c < C; ++c)
-              o_[((long long)(r * S + s) * cs + c) * d->k_stride + o] = W(o, c, r, s);
       return MDLC_OK;
     }
     case kPathDW: {
@@ -637,10 +537,6 @@ extern "C" int mdlc_conv2d(mdlc_ctx* ctx, const mdlc_conv_desc* d, const void* x
           (!epi || !epi->deq_scale))
         return mdlc_set_error(ctx, MDLC_ERR_INVALID, "conv int8: deq_scale required for float output");
       return conv_tc(ctx, *d, x, w, bias, res, y, epi, cfg);
-    case kPathF32:
-      return conv_f32(ctx, *d, static_cast<const float*>(x), static_cast<const float*>(w),
-                      static_cast<const float*>(bias), static_cast<const float*>(res), static_cast<float*>(y),
-                      epi);
     case kPathDW:
       return conv_dw(ctx, *d, x, static_cast<const float*>(w), static_cast<const float*>(bias), res, y, epi);
     case kPathGrouped:

@@ -8,12 +8,9 @@
 
 namespace mdlc {
 
-// tcgen05 implicit GEMM (bf16 / int8), groups == 1
+// tcgen05 implicit GEMM (bf16, int8, fp32 as 3xTF32), groups == 1
 int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w, const void* bias,
             const void* res, void* y, const mdlc_epilogue* epi, const mdlc_tile_cfg* cfg);
-// fp32 SIMT implicit GEMM, groups == 1
-int conv_f32(mdlc_ctx* ctx, const mdlc_conv_desc& d, const float* x, const float* w, const float* bias,
-             const float* res, float* y, const mdlc_epilogue* epi);
 // depthwise (groups == c == k), bf16 or fp32 activations, fp32 weights
 int conv_dw(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const float* w, const float* bias,
             const void* res, void* y, const mdlc_epilogue* epi);

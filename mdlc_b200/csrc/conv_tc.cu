@@ -39,6 +39,9 @@ namespace mdlc {
 namespace {
 
 constexpr int kThreads = 320;
+// fp32 (3xTF32) adds four warps that split every A stage into tf32 hi and lo parts
+template <int ESZ>
+constexpr int threads_for() { return ESZ == 4 ? 448 : kThreads; }
 constexpr int kBM = 128;
 constexpr int kABytes = kBM * 128;  // one A stage: 128 rows x 128 bytes
 
@@ -94,29 +97,35 @@ struct TcArgs {
   // (counted in `counters`, left at zero) sums the slices in slice order and
   // runs the epilogue
   int split, kps;
+  // element extents of x, y and the residual (checked build only)
+  long long x_elems, y_elems, res_elems;
   uint32_t* ws;
   int* counters;
 };
 
 template <int BN, int STAGES, int ESZ, int AMODE>
 struct Smem {
-  static constexpr int kBBytes = BN * 128;
+  // B stage: the packed weights' k-block (fp32: its tf32 hi tile, then its lo tile)
+  static constexpr int kBBytes = (ESZ == 4 ? 2 : 1) * BN * 128;
   static constexpr int kA = 0;
-  static constexpr int kB = AMODE == 4 ? kHaloStages * kHaloBytes : STAGES * kABytes;
+  // fp32: the lo parts of the A stages, written by the split warps
+  static constexpr int kALo = AMODE == 4 ? kHaloStages * kHaloBytes : STAGES * kABytes;
+  static constexpr int kB = kALo + (ESZ == 4 ? STAGES * kABytes : 0);
   // epilogue staging: 4 warps x 2 buffers x (32 rows x 64 columns), rows of
-  // 128 bytes (bf16, 128-byte swizzle) or 64 bytes (8-bit, 64-byte swizzle)
-  static constexpr int kEBuf = 32 * 64 * ESZ;
+  // 128 bytes (bf16, 128-byte swizzle) or 64 bytes (8-bit, 64-byte swizzle);
+  // none for fp32 (direct stores)
+  static constexpr int kEBuf = ESZ == 4 ? 0 : 32 * 64 * ESZ;
   static constexpr int kE = kB + STAGES * kBBytes;
   // per-tile epilogue parameters, double-buffered by tile parity: the fp32
   // bias (bf16); the int32 bias and fp32 requantisation scale (8-bit, fp32
   // form); or the multiplier, residual multiplier, packed shifts and the
   // 64-bit constant bias32 * multiplier + rounding term (8-bit, fixed point)
-  static constexpr int kParamWords = ESZ == 2 ? 1 : 5;
+  static constexpr int kParamWords = ESZ == 1 ? 5 : 1;
   static constexpr int kBias = kE + 4 * 2 * kEBuf;
   static constexpr int kBar = kBias + 2 * kParamWords * BN * 4;
   // barriers: fullA[S], fullB[S], empty[S], tfull[2], tempty[2], drain, resid[4 warps][2 buffers],
-  // band full[2], band empty[2]
-  static constexpr int kNumBars = 3 * STAGES + 13 + 2 * kHaloStages;
+  // band full[2], band empty[2], split[S] (fp32: A stage split into hi / lo)
+  static constexpr int kNumBars = 4 * STAGES + 13 + 2 * kHaloStages;
   static constexpr int kMisc = kBar + kNumBars * 8;
   static constexpr int kBytes = kMisc + 16;
   static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
@@ -133,14 +142,20 @@ struct Smem {
 // for at most 96 registers per thread (2 x 320 threads).
 template <int BN, int STAGES, int ESZ, int AMODE>
 struct Occ {
-  static constexpr int value = Smem<BN, STAGES, ESZ, AMODE>::kAlloc <= 113 * 1024 ? 2 : 1;
+  static constexpr int value = ESZ != 4 && Smem<BN, STAGES, ESZ, AMODE>::kAlloc <= 113 * 1024 ? 2 : 1;
 };
 
 // ---------------------------------------------------------------- epilogue
 template <int ESZ>
 MDLC_DEV void store_chunk16(const TcArgs& a, int m, int nb0, const uint32_t (&v)[16]) {
   const long long row = (long long)m * a.ks;
-  if constexpr (ESZ == 2) {
+  // the 16 output elements (and their residual) stay inside the tensors
+  if (!MDLC_CHECK_IDX(a.err, row + (nb0 + 16 <= a.ks ? nb0 + 15 : a.ks - 1), a.y_elems)) return;
+  if (a.res && !MDLC_CHECK_IDX(a.err, (long long)m * a.res_s + (nb0 + 16 <= a.k ? nb0 + 15 : a.k - 1),
+                               a.res_elems))
+    return;
+  if constexpr (ESZ != 1) {
+    // float path: bf16 (ESZ 2) or fp32 (ESZ 4) residual
     float f[16];
 #pragma unroll
     for (int e = 0; e < 16; ++e) f[e] = __uint_as_float(v[e]);
@@ -153,7 +168,14 @@ MDLC_DEV void store_chunk16(const TcArgs& a, int m, int nb0, const uint32_t (&v)
           f[4 * q] += bb.x; f[4 * q + 1] += bb.y; f[4 * q + 2] += bb.z; f[4 * q + 3] += bb.w;
         }
       }
-      if (a.res) {
+      if (a.res && ESZ == 4) {
+        const float4* r4 = reinterpret_cast<const float4*>(a.res + ((long long)m * a.res_s + nb0) * 4);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 rr = __ldg(r4 + q);
+          f[4 * q] += rr.x; f[4 * q + 1] += rr.y; f[4 * q + 2] += rr.z; f[4 * q + 3] += rr.w;
+        }
+      } else if (a.res) {
         const uint4* r4 = reinterpret_cast<const uint4*>(a.res + ((long long)m * a.res_s + nb0) * 2);
 #pragma unroll
         for (int q = 0; q < 2; ++q) {
@@ -188,7 +210,9 @@ MDLC_DEV void store_chunk16(const TcArgs& a, int m, int nb0, const uint32_t (&v)
         if (ch < a.k) {
           val = f[e];
           if (a.bias) val += static_cast<const float*>(a.bias)[ch];
-          if (a.res) {
+          if (a.res && ESZ == 4) {
+            val += *reinterpret_cast<const float*>(a.res + ((long long)m * a.res_s + ch) * 4);
+          } else if (a.res) {
             const uint16_t rb = *reinterpret_cast<const uint16_t*>(a.res + ((long long)m * a.res_s + ch) * 2);
             val += __uint_as_float((uint32_t)rb << 16);
           }
@@ -272,7 +296,7 @@ MDLC_DEV void store_chunk16(const TcArgs& a, int m, int nb0, const uint32_t (&v)
 
 // ---------------------------------------------------------------- kernel
 template <int BN, int STAGES, int ESZ, int ACT, int AMODE>
-__global__ void __launch_bounds__(kThreads, (Occ<BN, STAGES, ESZ, AMODE>::value))
+__global__ void __launch_bounds__(threads_for<ESZ>(), (Occ<BN, STAGES, ESZ, AMODE>::value))
     conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_y,
                    const __grid_constant__ CUtensorMap tmap_r, const __grid_constant__ CUtensorMap tmap_x,
                    const TcArgs a) {
@@ -295,6 +319,8 @@ __global__ void __launch_bounds__(kThreads, (Occ<BN, STAGES, ESZ, AMODE>::value)
   auto resid = [&](int w, int b) { return sbar + 8u * (3 * STAGES + 5 + 2 * w + b); };
   auto hfull = [&](int i) { return sbar + 8u * (3 * STAGES + 13 + i); };
   auto hempty = [&](int i) { return sbar + 8u * (3 * STAGES + 13 + kHaloStages + i); };
+  auto splitA = [&](int i) { return sbar + 8u * (3 * STAGES + 13 + 2 * kHaloStages + i); };
+  const uint32_t sALo = sbase + L::kALo;
   // halo mode: tile -> (image, tile row, tile column)
   auto halo_tile = [&](int mt, int& img, int& ty, int& tx) {
     tx = mt % a.tiles_x;
@@ -329,6 +355,7 @@ __global__ void __launch_bounds__(kThreads, (Occ<BN, STAGES, ESZ, AMODE>::value)
       mbar_init(hfull(i), 1);
       mbar_init(hempty(i), 1);
     }
+    for (int i = 0; i < STAGES; ++i) mbar_init(splitA(i), 128);
     *abort_flag = 0;
     fence_mbar_init();
   }
@@ -414,9 +441,10 @@ __global__ void __launch_bounds__(kThreads, (Occ<BN, STAGES, ESZ, AMODE>::value)
         for (int i = 0; i < 8; ++i) {
           const int ih = ih0[i] + dy, iw = iw0[i] + dx;
           const bool v = kvalid && (unsigned)ih < (unsigned)a.h && (unsigned)iw < (unsigned)a.w;
-          const uint8_t* src =
-              v ? a.x + ((long long)((nb[i] + ih) * a.w + iw) * a.cs + c) * ESZ : pad;
-          cp_async_16(dst0 + i * 2048u, src, v ? 16u : pad_bytes);
+          const long long e = (long long)((nb[i] + ih) * a.w + iw) * a.cs + c;
+          const bool in = v && MDLC_CHECK_IDX(a.err, e + CHUNK - 1, a.x_elems);
+          const uint8_t* src = in ? a.x + e * ESZ : pad;
+          cp_async_16(dst0 + i * 2048u, src, in ? 16u : pad_bytes);
         }
         // the barrier phase completes when all 128 producers' copies have landed
         cp_async_mbar_arrive_noinc(fullA(st));
@@ -517,6 +545,8 @@ __global__ void __launch_bounds__(kThreads, (Occ<BN, STAGES, ESZ, AMODE>::value)
         tc_fence_after();
         const uint32_t tacc = tmem + lane_base + (uint32_t)(buf * BN);
         const size_t row = (size_t)(ew * 32 + lane);
+        // (checked build: a workspace row out of range is recorded and not written)
+        const bool ws_ok = MDLC_CHECK_IDX(a.err, ((size_t)u * kBM + row + 1) * BN - 1, kSplitWsBytes / 4);
         uint4* dst = reinterpret_cast<uint4*>(a.ws + ((size_t)u * kBM + row) * BN);
 #pragma unroll 1
         for (int c = 0; c < BN; c += 16) {
@@ -525,7 +555,7 @@ __global__ void __launch_bounds__(kThreads, (Occ<BN, STAGES, ESZ, AMODE>::value)
           tmem_ld_wait();
 #pragma unroll
           for (int q = 0; q < 4; ++q)
-            __stcg(dst + c / 4 + q, make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
+            if (ws_ok) __stcg(dst + c / 4 + q, make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
         }
         __threadfence();
         asm volatile("bar.sync 1, 128;" ::: "memory");
@@ -908,7 +938,10 @@ __global__ void __launch_bounds__(kThreads, (Occ<BN, STAGES, ESZ, AMODE>::value)
             break;
           }
           mbar_arrive_expect_tx(fullA(st), L::kBBytes);
-          tma_load_2d(sB + st * L::kBBytes, &tmap_w, kb * KB, n0, fullA(st));
+          if constexpr (ESZ == 4)  // the k-block of the hi and of the lo weight matrix in one load
+            tma_load_3d(sB + st * L::kBBytes, &tmap_w, kb * KB, n0, 0, fullA(st));
+          else
+            tma_load_2d(sB + st * L::kBBytes, &tmap_w, kb * KB, n0, fullA(st));
         }
       }
       if (!ok) {
@@ -976,7 +1009,8 @@ __global__ void __launch_bounds__(kThreads, (Occ<BN, STAGES, ESZ, AMODE>::value)
         mbar_wait(drain, 0, nullptr, a.err, 1000000ull);
       }
     } else if (lane == 0) {
-      const uint32_t idesc = ESZ == 2 ? idesc_bf16(kBM, BN) : idesc_i8(kBM, BN, a.a_signed, 1);
+      const uint32_t idesc =
+          ESZ == 4 ? idesc_tf32(kBM, BN) : (ESZ == 2 ? idesc_bf16(kBM, BN) : idesc_i8(kBM, BN, a.a_signed, 1));
       int it = 0, local = 0;
       bool ok = true;
       for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++local) {
@@ -991,28 +1025,42 @@ __global__ void __launch_bounds__(kThreads, (Occ<BN, STAGES, ESZ, AMODE>::value)
         for (int kb = kb0; kb < kb_end(u); ++kb, ++it) {
           const int st = it % STAGES;
           const uint32_t par = (it / STAGES) & 1;
-          if (!mbar_wait(fullA(st), par, abort_flag, a.err, a.wait_cycles)) {
+          // fp32: wait for the split warps (the stage's A and B have landed and A
+          // is split into hi / lo parts)
+          if (!mbar_wait(ESZ == 4 ? splitA(st) : fullA(st), par, abort_flag, a.err, a.wait_cycles)) {
             ok = false;
             break;
           }
-          // cp.async writes A through the generic proxy: order them before the
-          // async-proxy operand reads of tcgen05.mma. TMA-written operands are
-          // ordered by the mbarrier completion itself.
-          if constexpr (AMODE == 0) {
+          // cp.async (and the split warps' stores) write A through the generic
+          // proxy: order them before the async-proxy operand reads of
+          // tcgen05.mma. TMA-written operands are ordered by the mbarrier
+          // completion itself.
+          if constexpr (AMODE == 0 || ESZ == 4) {
             fence_proxy_async_smem();
             tc_fence_after();
           }
           const uint32_t ab = sA + st * kABytes, bb = sB + st * L::kBBytes;
+          auto adesc = [&](uint32_t base, int kq) {
+            return AMODE == 2   ? umma_desc_k(base + kq * (kABytes / 4), 256, 6)
+                   : AMODE == 3 ? umma_desc_k(base + (kq >> 1) * (kABytes / 2) + (kq & 1) * 32, 512, 4)
+                                : umma_desc_sw128(base + kq * 32);
+          };
 #pragma unroll
           for (int kq = 0; kq < 4; ++kq) {
-            const uint64_t ad = AMODE == 2   ? umma_desc_k(ab + kq * (kABytes / 4), 256, 6)
-                                : AMODE == 3 ? umma_desc_k(ab + (kq >> 1) * (kABytes / 2) + (kq & 1) * 32, 512, 4)
-                                             : umma_desc_sw128(ab + kq * 32);
+            const uint64_t ad = adesc(ab, kq);
             const uint64_t bd = umma_desc_sw128(bb + kq * 32);
-            if constexpr (ESZ == 2)
+            if constexpr (ESZ == 4) {
+              // 3xTF32: a*b ~ ahi*bhi + ahi*blo + alo*bhi (alo*blo ~ 2^-22 |ab| dropped)
+              const uint64_t ad_lo = adesc(sALo + st * kABytes, kq);
+              const uint64_t bd_lo = umma_desc_sw128(bb + BN * 128 + kq * 32);
+              umma_tf32(d, ad, bd, idesc, (kb != kb0) || kq != 0);
+              umma_tf32(d, ad, bd_lo, idesc, 1);
+              umma_tf32(d, ad_lo, bd, idesc, 1);
+            } else if constexpr (ESZ == 2) {
               umma_bf16(d, ad, bd, idesc, (kb != kb0) || kq != 0);
-            else
+            } else {
               umma_i8(d, ad, bd, idesc, (kb != kb0) || kq != 0);
+            }
           }
           umma_commit(empty(st));
         }
@@ -1021,6 +1069,42 @@ __global__ void __launch_bounds__(kThreads, (Occ<BN, STAGES, ESZ, AMODE>::value)
       if (!ok) {
         umma_commit(drain);
         mbar_wait(drain, 0, nullptr, a.err, 1000000ull);
+      }
+    }
+  } else if (ESZ == 4 && warp >= 10) {
+    // ---------------- A split (fp32 operands): each landed A stage becomes its
+    // tf32 high part (low 13 mantissa bits cleared, in place) and the exact
+    // remainder a - hi (the lo stage); the MMA issuer sums hi*hi + hi*lo + lo*hi.
+    // Layout-agnostic (element for element in place), so every A mode works.
+    const int sid = tid - 320;           // 0..127
+    const int j = sid & 7, row0 = sid >> 3;
+    int it = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+      for (int kb = kb_begin(u); kb < kb_end(u); ++kb, ++it) {
+        const int st = it % STAGES;
+        if (!mbar_wait(fullA(st), (it / STAGES) & 1, abort_flag, a.err, a.wait_cycles)) {
+          ok = false;
+          break;
+        }
+        uint8_t* hi_p = smem + L::kA + st * kABytes;
+        uint8_t* lo_p = smem + L::kALo + st * kABytes;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int off = (row0 + 16 * i) * 128 + j * 16;
+          const uint4 x4 = *reinterpret_cast<const uint4*>(hi_p + off);
+          const uint4 h4 = make_uint4(x4.x & 0xFFFFE000u, x4.y & 0xFFFFE000u, x4.z & 0xFFFFE000u,
+                                      x4.w & 0xFFFFE000u);
+          const float4 l4 = make_float4(__uint_as_float(x4.x) - __uint_as_float(h4.x),
+                                        __uint_as_float(x4.y) - __uint_as_float(h4.y),
+                                        __uint_as_float(x4.z) - __uint_as_float(h4.z),
+                                        __uint_as_float(x4.w) - __uint_as_float(h4.w));
+          *reinterpret_cast<uint4*>(hi_p + off) = h4;
+          *reinterpret_cast<float4*>(lo_p + off) = l4;
+        }
+        // generic-proxy writes, read next by tcgen05.mma (async proxy)
+        fence_proxy_async_smem();
+        mbar_arrive(splitA(st));
       }
     }
   }
@@ -1103,7 +1187,8 @@ int encode_im2col(CUtensorMap* m, const mdlc_conv_desc& d, const void* x, int es
   const int lower[2] = {lower_w, lower_h};
   const int upper[2] = {upper_w, upper_h};
   const cuuint32_t estride[4] = {1, (cuuint32_t)d.stride_w, (cuuint32_t)d.stride_h, 1};
-  const bool ok = fn(m, esz == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 4,
+  const bool ok = fn(m, esz == 2 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16
+                                 : (esz == 4 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_UINT8), 4,
                      const_cast<void*>(x), gdim, gstride, lower, upper, (cuuint32_t)cpp, (cuuint32_t)kBM, estride,
                      CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
@@ -1129,7 +1214,7 @@ int launch_tc(mdlc_ctx* ctx, const CUtensorMap& tmap, const CUtensorMap& tmap_y,
   // set-up while the previous conv kernel drains (see griddepcontrol.wait)
   cudaLaunchConfig_t lc = {};
   lc.gridDim = dim3(grid);
-  lc.blockDim = dim3(kThreads);
+  lc.blockDim = dim3(threads_for<ESZ>());
   lc.dynamicSmemBytes = L::kAlloc;
   lc.stream = ctx->stream;
   cudaLaunchAttribute attr[1];
@@ -1149,7 +1234,8 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() { return get_encode_fn();
 int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w, const void* bias,
             const void* res, void* y, const mdlc_epilogue* epi, const mdlc_tile_cfg* cfg) {
   const bool int8 = d.in_type == MDLC_U8 || d.in_type == MDLC_S8;
-  const int esz = int8 ? 1 : 2;
+  const bool fp32 = d.in_type == MDLC_F32;  // 3xTF32 on kind::tf32
+  const int esz = int8 ? 1 : (fp32 ? 4 : 2);
   const int kb_elems = 128 / esz;
   const long long kg = (long long)d.r * d.s * d.c_stride;
   const int num_kb = (int)((kg + kb_elems - 1) / kb_elems);
@@ -1168,7 +1254,7 @@ int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w
   const bool halo = out_tma && band_px && d.stride_h == 1 && d.stride_w == 1 && d.dil_h == 1 && d.dil_w == 1 &&
                     d.r * d.s > 1 && d.r <= kHaloMaxR && d.s <= kHaloSlots - kHaloTW + 1 && d.oh >= 14 &&
                     d.ow >= 14 && (!int8 || d.in_zp == 0) && !(cfg && (cfg->flags & 3)) && cfg &&
-                    (cfg->flags & 4);
+                    (cfg->flags & 4) && !fp32;
   const int tiles_x = (d.ow + kHaloTW - 1) / kHaloTW, tiles_y = (d.oh + kHaloTH - 1) / kHaloTH;
 
   int bn = cfg && cfg->bn ? cfg->bn : 0;
@@ -1176,6 +1262,11 @@ int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w
   const long long num_m_ll = halo ? (long long)d.n * tiles_x * tiles_y : (M + kBM - 1) / kBM;
   if (num_m_ll > (1ll << 30)) return mdlc_set_error(ctx, MDLC_ERR_INVALID, "conv: too many tiles");
   const int num_m = (int)num_m_ll;
+  if (!bn && fp32) {
+    // fp32 tiles: 64, 128 or 256 wide (shared memory holds hi and lo stages)
+    bn = d.k_stride > 128 ? 256 : (d.k_stride > 64 ? 128 : 64);
+    while (bn > 64 && (long long)num_m * ((d.k_stride + bn - 1) / bn) < ctx->num_sms) bn /= 2;
+  }
   if (!bn) {
     bn = d.k_stride > 128 ? 256 : (d.k_stride > 64 ? 128 : 64);
     // keep enough tiles in flight for the whole GPU
@@ -1193,24 +1284,32 @@ int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w
   // 64- and 128-wide tiles: the two-CTAs-per-SM configurations (see Occ)
   // when every SM gets more than one tile; otherwise each CTA runs alone on
   // its SM and the deep single-CTA pipelines are faster
+  if (!stages && fp32) stages = bn == 64 ? 3 : 2;
   if (!stages) {
     const long long tiles = (long long)num_m * ((d.k_stride + bn - 1) / bn);
     const bool pair = tiles > ctx->num_sms;
     stages = bn >= 192 ? 3 : (bn == 128 ? (pair ? 2 : 4) : (pair ? 3 : 8));
   }
+  if (fp32 && !((bn == 64 && stages == 3) || (bn == 128 && stages == 2) || (bn == 256 && stages == 2)))
+    return mdlc_set_error(ctx, MDLC_ERR_UNSUPPORTED,
+                          "conv_tc fp32: tile configurations (64, 3), (128, 2), (256, 2) only, got (%d, %d)", bn,
+                          stages);
   if (bn != 64 && bn != 128 && bn != 192 && bn != 256)
     return mdlc_set_error(ctx, MDLC_ERR_INVALID, "conv_tc: bn must be 64/128/192/256, got %d", bn);
 
   auto encode = get_encode_fn();
   if (!encode) return mdlc_set_error(ctx, MDLC_ERR_CUDA, "cuTensorMapEncodeTiled unavailable");
   CUtensorMap tmap;
-  const cuuint64_t gdim[2] = {(cuuint64_t)num_kb * kb_elems, (cuuint64_t)d.k};
-  const cuuint64_t gstride[1] = {(cuuint64_t)num_kb * 128};
-  const cuuint32_t box[2] = {(cuuint32_t)kb_elems, (cuuint32_t)bn};
-  const cuuint32_t estride[2] = {1, 1};
-  CUresult cr = encode(&tmap, int8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
-                       const_cast<void*>(w), gdim, gstride, box, estride, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                       CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+  const cuuint64_t gdim[3] = {(cuuint64_t)num_kb * kb_elems, (cuuint64_t)d.k, 2};
+  const cuuint64_t gstride[2] = {(cuuint64_t)num_kb * 128, (cuuint64_t)num_kb * 128 * d.k};
+  const cuuint32_t box[3] = {(cuuint32_t)kb_elems, (cuuint32_t)bn, 2};
+  const cuuint32_t estride[3] = {1, 1, 1};
+  // fp32: the packed weights are the tf32 hi matrix then the lo matrix ([2][k][k_pad]);
+  // one 3-D box brings a k-block of both, hi tile then lo tile
+  const auto wdt = int8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                        : (fp32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16);
+  CUresult cr = encode(&tmap, wdt, fp32 ? 3 : 2, const_cast<void*>(w), gdim, gstride, box, estride,
+                       CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                        CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (cr != CUDA_SUCCESS) return mdlc_set_error(ctx, MDLC_ERR_INVALID, "weight tensor map: CUresult %d", (int)cr);
 
@@ -1226,6 +1325,9 @@ int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w
   a.r = d.r; a.s = d.s; a.sh = d.stride_h; a.sw = d.stride_w; a.pt = d.pad_t; a.pl = d.pad_l;
   a.dh = d.dil_h; a.dw = d.dil_w; a.oh = d.oh; a.ow = d.ow;
   a.M = (int)M;
+  a.x_elems = (long long)d.n * d.h * d.w * d.c_stride;
+  a.y_elems = M * d.k_stride;
+  a.res_elems = M * (d.res_stride ? d.res_stride : d.k_stride);
   a.num_kb = num_kb;
   a.num_m_tiles = num_m;
   a.tiles_x = tiles_x; a.tiles_y = tiles_y;
@@ -1250,7 +1352,7 @@ int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w
   // A operand: im2col-mode TMA when the layer qualifies (zero padding only, so
   // not for int8 inputs with a non-zero zero point), else the cp.async gather
   CUtensorMap tmap_x = tmap;
-  const auto dt = int8 ? CU_TENSOR_MAP_DATA_TYPE_UINT8 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+  const auto dt = wdt;
   int amode = 0;
   if (halo) {
     // the input band of a tile: one channel block (band_px bytes) x kHaloSlots
@@ -1366,6 +1468,22 @@ int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w
   return launch_tc<BN_, ST_, E_, A_, 0>(ctx, tmap, tmap_y, tmap_r, tmap_x, a);
 #define MDLC_TC_ACT(BN_, ST_, A_) \
   if (act_t == A_) { MDLC_TC_LAUNCH(BN_, ST_, 2, A_) }
+// fp32 (3xTF32): no halo mode
+#define MDLC_TC_LAUNCH_F32(BN_, ST_)                                                            \
+  switch (amode) {                                                                            \
+    case 1: return launch_tc<BN_, ST_, 4, -1, 1>(ctx, tmap, tmap_y, tmap_r, tmap_x, a);       \
+    case 5: return launch_tc<BN_, ST_, 4, -1, 5>(ctx, tmap, tmap_y, tmap_r, tmap_x, a);       \
+    case 2: if (BN_ <= 128) return launch_tc<BN_, ST_, 4, -1, 2>(ctx, tmap, tmap_y, tmap_r, tmap_x, a); break; \
+    case 3: if (BN_ <= 128) return launch_tc<BN_, ST_, 4, -1, 3>(ctx, tmap, tmap_y, tmap_r, tmap_x, a); break; \
+    default: break;                                                                           \
+  }                                                                                           \
+  return launch_tc<BN_, ST_, 4, -1, 0>(ctx, tmap, tmap_y, tmap_r, tmap_x, a);
+  if (fp32) {
+    if (bn == 64) { MDLC_TC_LAUNCH_F32(64, 3) }
+    if (bn == 128) { MDLC_TC_LAUNCH_F32(128, 2) }
+    MDLC_TC_LAUNCH_F32(256, 2)
+  }
+#undef MDLC_TC_LAUNCH_F32
 #define MDLC_TC_CASE(BN_, ST_)                                                               \
   if (bn == BN_ && stages == ST_) {                                                         \
     if (int8) { MDLC_TC_LAUNCH(BN_, ST_, 1, -1) }                                           \

@@ -1,8 +1,8 @@
 // GEMM and depthwise entry points of the C ABI, expressed on the convolution
 // kernels. A GEMM y[m, n] = a[m, k] . op(b) is a 1x1 convolution over m
 // images of one pixel with k input and n output channels, so it runs on the
-// tcgen05 implicit-GEMM kernel (a loaded as a plain 2-D tile) for bf16 / 8-bit
-// and on the SIMT kernel for fp32. Reference: the Gemm / MatMul lowering of
+// tcgen05 implicit-GEMM kernel (a loaded as a plain 2-D tile): bf16, 8-bit, and
+// fp32 as 3xTF32. Reference: the Gemm / MatMul lowering of
 // mdlc/codegen/cuda/emit.py:211-244 and ops.gemm (mdlc/runtime/ops.py:84-92).
 #include <cstring>
 #include <vector>

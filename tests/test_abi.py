@@ -101,7 +101,13 @@ def test_weight_packing_layouts(path):
         want[:, :72] = np.pad(round_bf16(w).transpose(0, 2, 3, 1), ((0, 0), (0, 0), (0, 0), (0, 5))).reshape(k, 72)
         np.testing.assert_array_equal(f, want)
     else:
-        q = p.view(np.float32).reshape(72, 16)
-        want = np.zeros((72, 16), np.float32)
-        want[:, :k] = np.pad(w.transpose(2, 3, 1, 0), ((0, 0), (0, 0), (0, 5), (0, 0))).reshape(72, k)
-        np.testing.assert_array_equal(q, want)
+        # fp32 (3xTF32): [hi matrix][lo matrix], each [k][kg_pad] with 32-element k-blocks
+        kg_pad = 96   # 72 -> three 32-element k-blocks
+        q = p.view(np.float32).reshape(2, k, kg_pad)
+        full = np.zeros((k, kg_pad), np.float32)
+        full[:, :72] = np.pad(w.transpose(0, 2, 3, 1), ((0, 0), (0, 0), (0, 0), (0, 5))).reshape(k, 72)
+        hi = (full.view(np.uint32) & np.uint32(0xFFFFE000)).view(np.float32)
+        np.testing.assert_array_equal(q[0], hi)
+        np.testing.assert_array_equal(q[1], full - hi)
+        assert np.all((q[0].view(np.uint32) & 0x1FFF) == 0)              # hi is exactly a tf32 value
+        np.testing.assert_array_equal(q[0].astype(np.float64) + q[1], full.astype(np.float64))  # split is exact
