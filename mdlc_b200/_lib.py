@@ -14,7 +14,9 @@ import os
 import numpy as np
 
 HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(HERE, "libmdlc_b200.so")
+# MDLC_B200_LIB=check selects the bounds-checked build (python -m mdlc_b200.build --check)
+LIB_PATH = os.path.join(HERE, "libmdlc_b200_check.so" if os.environ.get("MDLC_B200_LIB") == "check"
+                        else "libmdlc_b200.so")
 
 OK, ERR_INVALID, ERR_CUDA, ERR_UNSUPPORTED, ERR_TIMEOUT, ERR_DEVICE, ERR_NOMEM = 0, -1, -2, -3, -4, -5, -6
 STREAM_COMPUTE, STREAM_COPY = 0, 1

@@ -1,6 +1,11 @@
 """Build ``libmdlc_b200.so`` (all CUDA kernels, sm_100a) in-tree.
 
-    python -m mdlc_b200.build [--verbose]
+    python -m mdlc_b200.build [--verbose] [--check]
+
+``--check`` builds the bounds-checked variant ``libmdlc_b200_check.so``
+(``-DMDLC_CHECK``: computed global-memory indices are checked against the
+tensors' extents; a violation records ``MDLC_DEVERR_BOUNDS`` and skips the
+access). ``_lib`` loads it when ``MDLC_B200_LIB=check``.
 
 Each ``csrc/*.cu`` is compiled by nvcc in parallel into ``_build/`` and linked
 into ``mdlc_b200/libmdlc_b200.so`` next to this file, which is where
@@ -23,6 +28,8 @@ CSRC = os.path.join(HERE, "csrc")
 INCLUDE = os.path.join(ROOT, "include")
 BUILD = os.path.join(ROOT, "_build")
 LIB = os.path.join(HERE, "libmdlc_b200.so")
+CHECK_BUILD = os.path.join(ROOT, "_build_check")
+CHECK_LIB = os.path.join(HERE, "libmdlc_b200_check.so")
 NVCC = os.environ.get("NVCC", "/usr/local/cuda/bin/nvcc")
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
@@ -39,20 +46,23 @@ def _deps():
         glob.glob(os.path.join(INCLUDE, "*.h"))
 
 
-def up_to_date() -> bool:
-    if not os.path.exists(LIB):
+def up_to_date(lib: str = LIB) -> bool:
+    if not os.path.exists(lib):
         return False
-    t = os.path.getmtime(LIB)
+    t = os.path.getmtime(lib)
     return all(os.path.getmtime(p) <= t for p in _deps())
 
 
-def build(force: bool = False, verbose: bool = False, extra=()) -> str:
-    if not force and up_to_date():
-        return LIB
-    os.makedirs(BUILD, exist_ok=True)
+def build(force: bool = False, verbose: bool = False, extra=(), check: bool = False) -> str:
+    lib, bdir = (CHECK_LIB, CHECK_BUILD) if check else (LIB, BUILD)
+    if check:
+        extra = (*extra, "-DMDLC_CHECK")
+    if not force and up_to_date(lib):
+        return lib
+    os.makedirs(bdir, exist_ok=True)
 
     def compile_one(src):
-        obj = os.path.join(BUILD, os.path.basename(src) + ".o")
+        obj = os.path.join(bdir, os.path.basename(src) + ".o")
         cmd = [NVCC, *ARCH, *FLAGS, *extra, "-c", src, "-o", obj]
         if verbose:
             cmd += ["-Xptxas", "-v"]
@@ -66,22 +76,23 @@ def build(force: bool = False, verbose: bool = False, extra=()) -> str:
     if verbose:
         for _, log in results:
             sys.stderr.write(log)
-    tmp = LIB + ".tmp"
+    tmp = lib + ".tmp"
     cmd = [NVCC, *ARCH, "-shared", "-o", tmp, *[o for o, _ in results], "-lcudart_static", "-ldl", "-lrt",
            "-lpthread"]
     r = subprocess.run(cmd, capture_output=True, text=True)
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stderr}")
-    os.replace(tmp, LIB)
-    return LIB
+    os.replace(tmp, lib)
+    return lib
 
 
 def main() -> int:
     ap = argparse.ArgumentParser()
     ap.add_argument("--force", action="store_true")
     ap.add_argument("--verbose", action="store_true", help="print ptxas register/smem usage")
+    ap.add_argument("--check", action="store_true", help="the bounds-checked variant (-DMDLC_CHECK)")
     args = ap.parse_args()
-    print(build(force=args.force, verbose=args.verbose))
+    print(build(force=args.force, verbose=args.verbose, check=args.check))
     return 0
 
 

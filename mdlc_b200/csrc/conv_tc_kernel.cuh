@@ -1,0 +1,1177 @@
+// The tcgen05 implicit-GEMM convolution kernel template, shared by the
+// translation units that instantiate it (one per element type, bf16 in two
+// halves, so nvcc compiles them in parallel) and by the host dispatcher
+// in conv_tc.cu.
+//
+// Implicit-GEMM convolution / GEMM on the sm_100a tensor cores (tcgen05).
+//
+// GEMM view: D[M x N] = A[M x K] * B[N x K]^T with
+//   M = n*oh*ow output pixels (NHWC row order),
+//   N = output channels,
+//   K = r*s*c_stride (tap-major, channel-minor), padded to the k-block.
+// A is never materialised (no im2col buffer): four producer warps gather each
+// 128-pixel x 128-byte k-block straight from the NHWC input with 16-byte
+// cp.async (zero-fill, or a zero-point pattern for int8, at padded taps) and
+// write it in the 128-byte-swizzled K-major layout UMMA reads; completion is
+// signalled asynchronously (cp.async.mbarrier.arrive.noinc), so each producer
+// keeps up to STAGES k-blocks in flight. B (the packed
+// weights, [N][K_pad]) arrives by 2-D TMA with the same swizzle. One thread
+// issues tcgen05.mma (kind::f16 for bf16, kind::i8 for int8) into a TMEM
+// accumulator of 128 lanes x BN columns; four epilogue warps read it back
+// with tcgen05.ld and apply bias / residual / activation or the int8
+// requantisation before storing NHWC.
+//
+// The kernel is persistent: each CTA walks tiles (m-tile major, n-tile
+// minor) with a STAGES-deep shared-memory ring that runs across tiles and two
+// TMEM accumulators, so the epilogue of one tile overlaps the main loop of the
+// next. Warp roles (320 threads):
+//   warps 0-3  A producers (cp.async gather)
+//   warps 4-7  epilogue (warp w reads TMEM lanes 32*(w%4) .. +31)
+//   warp 8     B producer (TMA), lane 0
+//   warp 9     TMEM allocator + MMA issuer, lane 0
+// Every mbarrier wait is bounded; on expiry the CTA records
+// MDLC_DEVERR_WAIT_TIMEOUT, drains its in-flight copies and MMAs, frees TMEM
+// and exits.
+#pragma once
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "conv.h"
+#include "runtime.h"
+
+namespace mdlc {
+
+constexpr int kThreads = 320;
+// fp32 (3xTF32) adds four warps that split every A stage into tf32 hi and lo parts
+template <int ESZ>
+constexpr int threads_for() { return ESZ == 4 ? 448 : kThreads; }
+constexpr int kBM = 128;
+constexpr int kABytes = kBM * 128;  // one A stage: 128 rows x 128 bytes
+
+// Halo mode (AMODE 4, stride-1 convs): a tile is kHaloTH output rows x
+// kHaloTW output columns of one image (M = 128). For each channel block the
+// padded input band of the tile -- (kHaloTH + r - 1) rows of kHaloSlots
+// pixel slots of P bytes (P = 32 or 64: the whole pixel, 32/64-byte swizzle;
+// P = 128: one 128-byte channel block, 128-byte swizzle) -- is loaded by ONE
+// tiled TMA and every filter tap (ty, tx) reads it in place: A row (oy, ox) of
+// tap (ty, tx) is band pixel (oy + ty, ox + tx), i.e. the operand starts at
+// band row ty, column tx, with 8-row groups (one output row each)
+// kHaloSlots * P bytes apart (a multiple of the swizzle repeat, 8 * P). Each
+// input byte crosses into shared memory once per tile instead of once per tap.
+constexpr int kHaloTW = 8, kHaloTH = 16, kHaloSlots = 16, kHaloMaxR = 5;
+constexpr int kHaloRowBytes = kHaloSlots * 128;  // band row stride at P = 128
+constexpr int kHaloBytes = (kHaloTH + kHaloMaxR - 1) * kHaloRowBytes;
+constexpr int kHaloStages = 2;
+static_assert(kHaloTW * kHaloTH == kBM, "a halo tile is one M tile");
+static_assert(kHaloSlots % 8 == 0, "band rows must keep the swizzle phase");
+
+struct TcArgs {
+  const uint8_t* x;
+  void* y;
+  const void* bias;      // float[k] (bf16 path) or int32[k] (int8 path); may be null
+  const uint8_t* res;    // residual NHWC, may be null
+  const uint8_t* pad_src;  // 16-byte pad pattern (int8 zero point) or null for zero fill
+  int* err;
+  int n, h, w, cs;
+  int k, ks, res_s;
+  int r, s, sh, sw, pt, pl, dh, dw, oh, ow;
+  int M, num_kb, num_m_tiles, num_n_tiles;
+  int out_type, a_signed;
+  ActParams act;
+  const float* rq_scale;
+  int out_zp, qlo, qhi, res_zp;  // qlo / qhi: clamp bounds relative to out_zp
+  float res_scale;
+  int res_signed;
+  const float* deq_scale;
+  const float* deq_bias;
+  // fixed-point requantisation (8-bit output): per-channel multipliers of the
+  // accumulator and of the residual, sharing one right shift; null: fp32 form
+  const int32_t* rq_mult;
+  const int32_t* rq_res_mult;
+  const int32_t* rq_shift;
+  int rq_fixed;
+  unsigned long long wait_cycles;
+  int tma_epi;  // bf16 / 8-bit output staged in shared memory and written by TMA stores
+  int tiles_x, tiles_y, halo_rows, cpb;  // halo mode: tile grid per image, band rows, channel blocks
+  int band_px;                           // halo mode: bytes per band pixel slot (32, 64 or 128)
+  // split-K: each tile's k-blocks are cut into `split` slices of `kps`; every
+  // (tile, slice) unit writes its raw accumulators to `ws` (fp32, or int32 for
+  // 8-bit operands: 128 rows x BN per unit), and the tile's last unit to finish
+  // (counted in `counters`, left at zero) sums the slices in slice order and
+  // runs the epilogue
+  int split, kps;
+  // element extents of x, y and the residual (checked build only)
+  long long x_elems, y_elems, res_elems;
+  uint32_t* ws;
+  int* counters;
+};
+
+// One kernel launch, as the host dispatcher prepared it: tensor maps, the
+// kernel arguments, and the template choices (tile width, pipeline depth, A
+// operand mode, compile-time activation of the bf16 TMA epilogue or -1).
+struct TcLaunch {
+  const CUtensorMap* tmap_w;
+  const CUtensorMap* tmap_y;
+  const CUtensorMap* tmap_r;
+  const CUtensorMap* tmap_x;
+  const TcArgs* args;
+  int bn, stages, amode, act;
+};
+// Launchers, each in its own translation unit: bf16 tiles (64, 3), (128, 2),
+// (256, 3) / (192, 3), (64, 8), (128, 4); 8-bit; fp32 (3xTF32).
+int launch_tc_bf16_a(mdlc_ctx* ctx, const TcLaunch& l);
+int launch_tc_bf16_b(mdlc_ctx* ctx, const TcLaunch& l);
+int launch_tc_i8(mdlc_ctx* ctx, const TcLaunch& l);
+int launch_tc_f32(mdlc_ctx* ctx, const TcLaunch& l);
+
+namespace {
+
+template <int BN, int STAGES, int ESZ, int AMODE>
+struct Smem {
+  // B stage: the packed weights' k-block (fp32: its tf32 hi tile, then its lo tile)
+  static constexpr int kBBytes = (ESZ == 4 ? 2 : 1) * BN * 128;
+  static constexpr int kA = 0;
+  // fp32: the lo parts of the A stages, written by the split warps
+  static constexpr int kALo = AMODE == 4 ? kHaloStages * kHaloBytes : STAGES * kABytes;
+  static constexpr int kB = kALo + (ESZ == 4 ? STAGES * kABytes : 0);
+  // epilogue staging: 4 warps x 2 buffers x (32 rows x 64 columns), rows of
+  // 128 bytes (bf16, 128-byte swizzle) or 64 bytes (8-bit, 64-byte swizzle);
+  // none for fp32 (direct stores)
+  static constexpr int kEBuf = ESZ == 4 ? 0 : 32 * 64 * ESZ;
+  static constexpr int kE = kB + STAGES * kBBytes;
+  // per-tile epilogue parameters, double-buffered by tile parity: the fp32
+  // bias (bf16); the int32 bias and fp32 requantisation scale (8-bit, fp32
+  // form); or the multiplier, residual multiplier, packed shifts and the
+  // 64-bit constant bias32 * multiplier + rounding term (8-bit, fixed point)
+  static constexpr int kParamWords = ESZ == 1 ? 5 : 1;
+  static constexpr int kBias = kE + 4 * 2 * kEBuf;
+  static constexpr int kBar = kBias + 2 * kParamWords * BN * 4;
+  // barriers: fullA[S], fullB[S], empty[S], tfull[2], tempty[2], drain, resid[4 warps][2 buffers],
+  // band full[2], band empty[2], split[S] (fp32: A stage split into hi / lo)
+  static constexpr int kNumBars = 4 * STAGES + 13 + 2 * kHaloStages;
+  static constexpr int kMisc = kBar + kNumBars * 8;
+  static constexpr int kBytes = kMisc + 16;
+  static constexpr int kAlloc = kBytes + 1024;  // slack for 1024-byte alignment
+};
+
+// Resident CTAs per SM. A single thread issues every tcgen05.mma of a CTA,
+// and between k-blocks it also waits on the stage's full barrier (~100 cycles
+// even when the phase is already complete) and commits the stage's empty
+// barrier (~40 cycles); the issue queue is too shallow to cover that with
+// N <= 128 instructions (measured: one issuer sustains one 128x128x16 MMA per
+// ~96 cycles with a wait and commit per k-block, two issuers the full rate of
+// one per 64). So configurations whose shared memory allows it run two CTAs
+// per SM, whose issuers fill each other's gaps; the kernel is then compiled
+// for at most 96 registers per thread (2 x 320 threads).
+template <int BN, int STAGES, int ESZ, int AMODE>
+struct Occ {
+  static constexpr int value = ESZ != 4 && Smem<BN, STAGES, ESZ, AMODE>::kAlloc <= 113 * 1024 ? 2 : 1;
+};
+
+// ---------------------------------------------------------------- epilogue
+template <int ESZ>
+MDLC_DEV void store_chunk16(const TcArgs& a, int m, int nb0, const uint32_t (&v)[16]) {
+  const long long row = (long long)m * a.ks;
+  // the 16 output elements (and their residual) stay inside the tensors
+  if (!MDLC_CHECK_IDX(a.err, row + (nb0 + 16 <= a.ks ? nb0 + 15 : a.ks - 1), a.y_elems)) return;
+  if (a.res && !MDLC_CHECK_IDX(a.err, (long long)m * a.res_s + (nb0 + 16 <= a.k ? nb0 + 15 : a.k - 1),
+                               a.res_elems))
+    return;
+  if constexpr (ESZ != 1) {
+    // float path: bf16 (ESZ 2) or fp32 (ESZ 4) residual
+    float f[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) f[e] = __uint_as_float(v[e]);
+    if (nb0 + 16 <= a.k) {
+      if (a.bias) {
+        const float4* b4 = reinterpret_cast<const float4*>(static_cast<const float*>(a.bias) + nb0);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 bb = __ldg(b4 + q);
+          f[4 * q] += bb.x; f[4 * q + 1] += bb.y; f[4 * q + 2] += bb.z; f[4 * q + 3] += bb.w;
+        }
+      }
+      if (a.res && ESZ == 4) {
+        const float4* r4 = reinterpret_cast<const float4*>(a.res + ((long long)m * a.res_s + nb0) * 4);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float4 rr = __ldg(r4 + q);
+          f[4 * q] += rr.x; f[4 * q + 1] += rr.y; f[4 * q + 2] += rr.z; f[4 * q + 3] += rr.w;
+        }
+      } else if (a.res) {
+        const uint4* r4 = reinterpret_cast<const uint4*>(a.res + ((long long)m * a.res_s + nb0) * 2);
+#pragma unroll
+        for (int q = 0; q < 2; ++q) {
+          const uint4 rr = __ldg(r4 + q);
+          const uint32_t u[4] = {rr.x, rr.y, rr.z, rr.w};
+#pragma unroll
+          for (int t = 0; t < 4; ++t) {
+            f[8 * q + 2 * t] += bf16_lo(u[t]);
+            f[8 * q + 2 * t + 1] += bf16_hi(u[t]);
+          }
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 16; ++e) f[e] = apply_act(f[e], a.act);
+      if (a.out_type == MDLC_F32) {
+        float4* y4 = reinterpret_cast<float4*>(static_cast<float*>(a.y) + row + nb0);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) y4[q] = make_float4(f[4 * q], f[4 * q + 1], f[4 * q + 2], f[4 * q + 3]);
+      } else {
+        uint4* y4 = reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(a.y) + row + nb0);
+#pragma unroll
+        for (int q = 0; q < 2; ++q)
+          y4[q] = make_uint4(pack_bf16x2(f[8 * q], f[8 * q + 1]), pack_bf16x2(f[8 * q + 2], f[8 * q + 3]),
+                             pack_bf16x2(f[8 * q + 4], f[8 * q + 5]), pack_bf16x2(f[8 * q + 6], f[8 * q + 7]));
+      }
+    } else {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const int ch = nb0 + e;
+        if (ch >= a.ks) continue;
+        float val = 0.0f;
+        if (ch < a.k) {
+          val = f[e];
+          if (a.bias) val += static_cast<const float*>(a.bias)[ch];
+          if (a.res && ESZ == 4) {
+            val += *reinterpret_cast<const float*>(a.res + ((long long)m * a.res_s + ch) * 4);
+          } else if (a.res) {
+            const uint16_t rb = *reinterpret_cast<const uint16_t*>(a.res + ((long long)m * a.res_s + ch) * 2);
+            val += __uint_as_float((uint32_t)rb << 16);
+          }
+          val = apply_act(val, a.act);
+        }
+        if (a.out_type == MDLC_F32)
+          static_cast<float*>(a.y)[row + ch] = val;
+        else
+          static_cast<__nv_bfloat16*>(a.y)[row + ch] = __float2bfloat16_rn(val);
+      }
+    }
+  } else {
+    // int8 path: v holds int32 accumulators
+    const int32_t* bias32 = static_cast<const int32_t*>(a.bias);
+    if (a.out_type == MDLC_S32) {
+      // the int32 accumulator itself (+ bias32), before any requantisation
+      int32_t* yi = static_cast<int32_t*>(a.y) + row;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const int ch = nb0 + e;
+        if (ch >= a.ks) continue;
+        yi[ch] = ch < a.k ? (int32_t)v[e] + (bias32 ? bias32[ch] : 0) : 0;
+      }
+      return;
+    }
+    if (a.out_type == MDLC_F32) {
+#pragma unroll
+      for (int e = 0; e < 16; ++e) {
+        const int ch = nb0 + e;
+        if (ch >= a.ks) continue;
+        float val = 0.0f;
+        if (ch < a.k) {
+          const int32_t acc = (int32_t)v[e] + (bias32 ? bias32[ch] : 0);
+          val = __fmul_rn((float)acc, a.deq_scale[ch]);
+          if (a.deq_bias) val = __fadd_rn(val, a.deq_bias[ch]);
+          if (a.res) {
+            const int32_t rq = a.res_signed ? (int32_t)(int8_t)a.res[(long long)m * a.res_s + ch]
+                                            : (int32_t)a.res[(long long)m * a.res_s + ch];
+            val = __fadd_rn(val, __fmul_rn((float)(rq - a.res_zp), a.res_scale));
+          }
+          val = apply_act(val, a.act);
+        }
+        static_cast<float*>(a.y)[row + ch] = val;
+      }
+      return;
+    }
+    uint32_t packed[4] = {0, 0, 0, 0};
+#pragma unroll
+    for (int e = 0; e < 16; ++e) {
+      const int ch = nb0 + e;
+      int32_t q = 0;
+      if (ch < a.k) {
+        const int32_t acc = (int32_t)v[e] + (bias32 ? bias32[ch] : 0);
+        const int32_t rq = !a.res ? 0
+                           : a.res_signed ? (int32_t)(int8_t)a.res[(long long)m * a.res_s + ch]
+                                          : (int32_t)a.res[(long long)m * a.res_s + ch];
+        if (a.rq_fixed) {
+          const int sh = a.rq_shift[ch];
+          long long t = (long long)acc * a.rq_mult[ch] + ((1ll << sh) >> 1);
+          if (a.res) t += (long long)(rq - a.res_zp) * a.rq_res_mult[ch];
+          t >>= sh;
+          q = (int32_t)(t < a.qlo ? a.qlo : (t > a.qhi ? a.qhi : t)) + a.out_zp;
+        } else {
+          float f = __fmul_rn((float)acc, a.rq_scale[ch]);
+          if (a.res) f = __fadd_rn(f, __fmul_rn((float)(rq - a.res_zp), a.res_scale));
+          q = min(max(__float2int_rn(f), a.qlo), a.qhi) + a.out_zp;
+        }
+      }
+      packed[e >> 2] |= ((uint32_t)(q & 0xFF)) << (8 * (e & 3));
+    }
+    uint8_t* yb = static_cast<uint8_t*>(a.y) + row + nb0;
+    if (nb0 + 16 <= a.ks) {
+      *reinterpret_cast<uint4*>(yb) = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+    } else {
+#pragma unroll
+      for (int e = 0; e < 16; ++e)
+        if (nb0 + e < a.ks) yb[e] = (uint8_t)(packed[e >> 2] >> (8 * (e & 3)));
+    }
+  }
+}
+
+// ---------------------------------------------------------------- kernel
+template <int BN, int STAGES, int ESZ, int ACT, int AMODE>
+__global__ void __launch_bounds__(threads_for<ESZ>(), (Occ<BN, STAGES, ESZ, AMODE>::value))
+    conv_tc_kernel(const __grid_constant__ CUtensorMap tmap_w, const __grid_constant__ CUtensorMap tmap_y,
+                   const __grid_constant__ CUtensorMap tmap_r, const __grid_constant__ CUtensorMap tmap_x,
+                   const TcArgs a) {
+  using L = Smem<BN, STAGES, ESZ, AMODE>;
+  constexpr int KB = 128 / ESZ;    // k-block elements (128 bytes)
+  constexpr int CHUNK = 16 / ESZ;  // elements per 16-byte chunk
+  // two accumulators of BN columns; allocations are powers of two (192 -> 512)
+  constexpr uint32_t kTmemCols = 2 * BN > 256 ? 512u : (uint32_t)(2 * BN);
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const uint32_t sbase = smem_u32(smem);
+  const uint32_t sA = sbase + L::kA, sB = sbase + L::kB, sbar = sbase + L::kBar;
+  auto fullA = [&](int i) { return sbar + 8u * i; };
+  auto fullB = [&](int i) { return sbar + 8u * (STAGES + i); };
+  auto empty = [&](int i) { return sbar + 8u * (2 * STAGES + i); };
+  auto tfull = [&](int i) { return sbar + 8u * (3 * STAGES + i); };
+  auto tempty = [&](int i) { return sbar + 8u * (3 * STAGES + 2 + i); };
+  const uint32_t drain = sbar + 8u * (3 * STAGES + 4);
+  auto resid = [&](int w, int b) { return sbar + 8u * (3 * STAGES + 5 + 2 * w + b); };
+  auto hfull = [&](int i) { return sbar + 8u * (3 * STAGES + 13 + i); };
+  auto hempty = [&](int i) { return sbar + 8u * (3 * STAGES + 13 + kHaloStages + i); };
+  auto splitA = [&](int i) { return sbar + 8u * (3 * STAGES + 13 + 2 * kHaloStages + i); };
+  const uint32_t sALo = sbase + L::kALo;
+  // halo mode: tile -> (image, tile row, tile column)
+  auto halo_tile = [&](int mt, int& img, int& ty, int& tx) {
+    tx = mt % a.tiles_x;
+    const int t = mt / a.tiles_x;
+    ty = t % a.tiles_y;
+    img = t / a.tiles_y;
+  };
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(smem + L::kMisc);
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 4);
+
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    for (int i = 0; i < STAGES; ++i) {
+      // fullA completes a stage (A and B landed): A arrives from 128 gathering
+      // threads (AMODE 0), from one TMA issuer per k-block (AMODE 1) or from one
+      // issuer per tap of the k-block (AMODE 2 / 3); B adds one arrival. Halo
+      // mode signals B on fullB and the band on hfull instead.
+      mbar_init(fullA(i), AMODE == 4 ? 1 : 1 + (AMODE == 0 ? 128 : (AMODE == 2 ? 4 : (AMODE == 3 ? 2 : 1))));
+      mbar_init(fullB(i), 1);
+      mbar_init(empty(i), 1);
+    }
+    for (int i = 0; i < 2; ++i) {
+      mbar_init(tfull(i), 1);
+      mbar_init(tempty(i), 128);
+    }
+    mbar_init(drain, 1);
+    for (int i = 0; i < 4; ++i) {
+      mbar_init(resid(i, 0), 1);
+      mbar_init(resid(i, 1), 1);
+    }
+    for (int i = 0; i < kHaloStages; ++i) {
+      mbar_init(hfull(i), 1);
+      mbar_init(hempty(i), 1);
+    }
+    for (int i = 0; i < STAGES; ++i) mbar_init(splitA(i), 128);
+    *abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 9) {
+    tmem_alloc(smem_u32(tmem_slot), kTmemCols);
+    tmem_relinquish();
+  }
+  if (warp == 8 && lane == 0) {
+    tma_prefetch_desc(&tmap_w);
+    if (AMODE) tma_prefetch_desc(&tmap_x);
+    if (a.tma_epi) {
+      tma_prefetch_desc(&tmap_y);
+      if (a.res) tma_prefetch_desc(&tmap_r);
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  // Programmatic dependent launch: the set-up above (barriers, TMEM, descriptor
+  // prefetch) may run while the previous kernel in the stream finishes;
+  // nothing below reads or writes global memory before that kernel has
+  // completed and its writes are visible. Dependents may then be scheduled.
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  const uint32_t tmem = *tmem_slot;
+
+  const int num_tiles = a.num_m_tiles * a.num_n_tiles;
+  const int RS = a.r * a.s;
+  // work units: (tile, K slice); without split-K a unit is a tile
+  const int S = a.split;
+  const int num_units = num_tiles * S;
+  auto kb_begin = [&](int u) { return (u % S) * a.kps; };
+  auto kb_end = [&](int u) {
+    const int e = (u % S + 1) * a.kps;
+    return e < a.num_kb ? e : a.num_kb;
+  };
+
+  if (warp < 4 && AMODE == 0) {
+    // ---------------- A producers: implicit im2col gather
+    const int j = tid & 7;     // 16-byte chunk within the 128-byte row
+    const int row0 = tid >> 3; // rows row0 + 16*i, i = 0..7
+    const uint32_t row_off = (uint32_t)row0 * 128u + (uint32_t)((j ^ (row0 & 7)) << 4);
+    const uint8_t* pad = a.pad_src ? a.pad_src : a.x;
+    const uint32_t pad_bytes = a.pad_src ? 16u : 0u;
+    const int ohw = a.oh * a.ow;
+    int it = 0;  // global k-block counter (stage ring position)
+    bool ok = true;
+    for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+      const int tile = u / S;
+      const int m0 = (tile / a.num_n_tiles) * kBM;
+      int ih0[8], iw0[8], nb[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        const int m = m0 + row0 + 16 * i;
+        if (m < a.M) {
+          const int img = m / ohw;
+          const int rem = m - img * ohw;
+          const int oy = rem / a.ow;
+          const int ox = rem - oy * a.ow;
+          ih0[i] = oy * a.sh - a.pt;
+          iw0[i] = ox * a.sw - a.pl;
+          nb[i] = img * a.h;
+        } else {
+          ih0[i] = -(1 << 29);
+          iw0[i] = 0;
+          nb[i] = 0;
+        }
+      }
+      for (int kb = kb_begin(u); kb < kb_end(u); ++kb, ++it) {
+        const int st = it % STAGES;
+        if (!mbar_wait(empty(st), ((it / STAGES) & 1) ^ 1, abort_flag, a.err, a.wait_cycles)) {
+          ok = false;
+          break;
+        }
+        const int kk = kb * KB + j * CHUNK;
+        const int tap = kk / a.cs;
+        const int c = kk - tap * a.cs;
+        const bool kvalid = tap < RS;
+        const int rr = tap / a.s;
+        const int dy = rr * a.dh, dx = (tap - rr * a.s) * a.dw;
+        const uint32_t dst0 = sA + st * kABytes + row_off;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int ih = ih0[i] + dy, iw = iw0[i] + dx;
+          const bool v = kvalid && (unsigned)ih < (unsigned)a.h && (unsigned)iw < (unsigned)a.w;
+          const long long e = (long long)((nb[i] + ih) * a.w + iw) * a.cs + c;
+          const bool in = v && MDLC_CHECK_IDX(a.err, e + CHUNK - 1, a.x_elems);
+          const uint8_t* src = in ? a.x + e * ESZ : pad;
+          cp_async_16(dst0 + i * 2048u, src, in ? 16u : pad_bytes);
+        }
+        // the barrier phase completes when all 128 producers' copies have landed
+        cp_async_mbar_arrive_noinc(fullA(st));
+      }
+    }
+    cp_async_wait_all();
+  } else if (warp < 4 && ((AMODE >= 1 && AMODE <= 3) || AMODE == 5)) {
+    // ---------------- A producers (TMA), lane 0 of warps 0-3. Each issuing
+    // thread sustains about one TMA load per few hundred cycles, so the loads
+    // are spread: AMODE 1 deals stages to warps (stage st belongs to warp
+    // st % min(4, STAGES), so every use of a stage is issued -- and its empty
+    // barrier awaited -- by one thread in order, which the parity waits need);
+    // AMODE 2 / 3 (4 / 2 taps per k-block) give warp j tap j of every k-block.
+    constexpr int TPB = AMODE == 2 ? 4 : (AMODE == 3 ? 2 : 1);
+    constexpr bool kWhole = AMODE == 1 || AMODE == 5;  // one load per k-block
+    constexpr int kAIssuers = kWhole ? (STAGES < 4 ? STAGES : 4) : TPB;
+    if (lane == 0 && warp < kAIssuers) {
+      constexpr uint32_t kTapBytes = kABytes / TPB;
+      int it = 0, last = -1;
+      bool ok = true;
+      const int cpb = a.cs / KB;  // k-blocks per filter tap (AMODE 1: cs % KB == 0)
+      const int ohw = a.oh * a.ow;
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+        const int tile = u / S;
+        const int m0 = (tile / a.num_n_tiles) * kBM;
+        const int xn = m0 / ohw;
+        const int rem = m0 - xn * ohw;
+        const int oy = rem / a.ow;
+        const int xh = oy * a.sh - a.pt;
+        const int xw = (rem - oy * a.ow) * a.sw - a.pl;
+        for (int kb = kb_begin(u); kb < kb_end(u); ++kb, ++it) {
+          if (kWhole && (it % STAGES) % kAIssuers != warp) continue;
+          const int st = it % STAGES;
+          if (!mbar_wait(empty(st), ((it / STAGES) & 1) ^ 1, abort_flag, a.err, a.wait_cycles)) {
+            ok = false;
+            break;
+          }
+          if (AMODE == 5) {
+            // 1x1 / stride 1 / no padding: A is the [M, cs] activation matrix itself
+            mbar_arrive_expect_tx(fullA(st), kABytes);
+            tma_load_2d(sA + st * kABytes, &tmap_x, kb * KB, m0, fullA(st));
+          } else if (AMODE == 1) {
+            const int tap = kb / cpb;
+            const int c0 = (kb - tap * cpb) * KB;
+            const int rr = tap / a.s;
+            mbar_arrive_expect_tx(fullA(st), kABytes);
+            tma_load_im2col_4d(sA + st * kABytes, &tmap_x, c0, xw, xh, xn, (uint16_t)((tap - rr * a.s) * a.dw),
+                               (uint16_t)(rr * a.dh), fullA(st));
+          } else {
+            // AMODE 2: 32-byte pixels (bf16 cs 16 / int8 cs 32); AMODE 3: 64-byte
+            // pixels (bf16 cs 32 / int8 cs 64). Taps past the end of the filter
+            // re-load tap 0: their weights are zero, so finite data adds nothing.
+            const int tap = kb * TPB + warp;
+            const int rr = tap / a.s;
+            const bool real = tap < RS;
+            mbar_arrive_expect_tx(fullA(st), kTapBytes);
+            tma_load_im2col_4d(sA + st * kABytes + warp * kTapBytes, &tmap_x, 0, xw, xh, xn,
+                               (uint16_t)(real ? (tap - rr * a.s) * a.dw : 0), (uint16_t)(real ? rr * a.dh : 0),
+                               fullA(st));
+          }
+          last = it;
+        }
+      }
+      if (!ok) {
+        // let this thread's loads land before the CTA's shared memory is released
+        for (int q = last; q >= 0 && q > last - STAGES; --q)
+          if (!kWhole || (q % STAGES) % kAIssuers == warp)
+            mbar_wait(fullA(q % STAGES), (q / STAGES) & 1, nullptr, a.err, 2000000ull);
+      }
+    }
+  } else if (warp >= 4 && warp < 8) {
+    // ---------------- epilogue
+    const int ew = warp - 4;
+    const int etid = tid - 128;
+    const uint32_t lane_base = (uint32_t)(ew * 32) << 16;
+    constexpr int kEBuf = L::kEBuf;
+    const uint32_t stage0 = sbase + L::kE + ew * 2 * kEBuf;
+    uint8_t* stage_ptr0 = smem + L::kE + ew * 2 * kEBuf;
+    const bool tma_epi = a.tma_epi;
+    int local = 0, chunk_i = 0;
+    uint32_t res_use0 = 0, res_use1 = 0;  // completed loads per residual buffer (phase parity)
+    int res_pending = -1;                 // residual buffer with a load in flight not yet awaited
+    uint32_t res_pending_par = 0;
+    volatile int* last_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 8);
+    for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++local) {
+      const int tile = u / S;
+      const int buf = local & 1;
+      const int m0 = (tile / a.num_n_tiles) * kBM;
+      const int n0 = (tile % a.num_n_tiles) * BN;
+      // split-K: every unit writes its raw accumulators to the workspace; a
+      // unit that is not its tile's last releases the accumulator and moves
+      // on, the last one sums all slices (in slice order) back into its own
+      // accumulator and runs the epilogue below on it
+      bool acc_ready = false;
+      if (S > 1) {
+        const bool okp = mbar_wait(tfull(buf), (local >> 1) & 1, abort_flag, a.err, a.wait_cycles);
+        if (!__all_sync(0xffffffffu, okp)) break;
+        tc_fence_after();
+        const uint32_t tacc = tmem + lane_base + (uint32_t)(buf * BN);
+        const size_t row = (size_t)(ew * 32 + lane);
+        // (checked build: a workspace row out of range is recorded and not written)
+        const bool ws_ok = MDLC_CHECK_IDX(a.err, ((size_t)u * kBM + row + 1) * BN - 1, kSplitWsBytes / 4);
+        uint4* dst = reinterpret_cast<uint4*>(a.ws + ((size_t)u * kBM + row) * BN);
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+          uint32_t v[16];
+          tmem_ld16(tacc + c, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int q = 0; q < 4; ++q)
+            if (ws_ok) __stcg(dst + c / 4 + q, make_uint4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]));
+        }
+        __threadfence();
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (etid == 0) *last_flag = atomicAdd(a.counters + tile, 1) == S - 1;
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+        if (!*last_flag) {
+          tc_fence_before();
+          mbar_arrive(tempty(buf));
+          continue;
+        }
+        __threadfence();
+        if (etid == 0) a.counters[tile] = 0;  // zero again for the next call
+        const uint4* src = reinterpret_cast<const uint4*>(a.ws + ((size_t)tile * S * kBM + row) * BN);
+        const size_t slice = (size_t)kBM * BN / 4;  // uint4 per slice
+#pragma unroll 1
+        for (int c = 0; c < BN; c += 16) {
+          uint32_t v[16];
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            uint4 s4 = __ldcg(src + c / 4 + q);
+            for (int sl = 1; sl < S; ++sl) {
+              const uint4 p4 = __ldcg(src + sl * slice + c / 4 + q);
+              if constexpr (ESZ == 1) {
+                s4 = make_uint4((uint32_t)((int)s4.x + (int)p4.x), (uint32_t)((int)s4.y + (int)p4.y),
+                                (uint32_t)((int)s4.z + (int)p4.z), (uint32_t)((int)s4.w + (int)p4.w));
+              } else {
+                s4 = make_uint4(__float_as_uint(__uint_as_float(s4.x) + __uint_as_float(p4.x)),
+                                __float_as_uint(__uint_as_float(s4.y) + __uint_as_float(p4.y)),
+                                __float_as_uint(__uint_as_float(s4.z) + __uint_as_float(p4.z)),
+                                __float_as_uint(__uint_as_float(s4.w) + __uint_as_float(p4.w)));
+              }
+            }
+            v[4 * q] = s4.x; v[4 * q + 1] = s4.y; v[4 * q + 2] = s4.z; v[4 * q + 3] = s4.w;
+          }
+          tmem_st16(tacc + c, v);
+        }
+        tmem_st_wait();
+        acc_ready = true;
+      }
+      int hx = 0, hy = 0, himg = 0;
+      if constexpr (AMODE == 4) {
+        halo_tile(tile / a.num_n_tiles, himg, hy, hx);
+        hx *= kHaloTW;
+        hy = hy * kHaloTH + ew * (32 / kHaloTW);
+      }
+      auto load_res = [&](uint32_t dst, int c, uint32_t bar) {
+        if constexpr (AMODE == 4)
+          tma_load_4d(dst, &tmap_r, c, hx, hy, himg, bar);
+        else
+          tma_load_2d(dst, &tmap_r, c, m0 + ew * 32, bar);
+      };
+      float* sbias = reinterpret_cast<float*>(smem + L::kBias) + buf * BN;
+      // 8-bit, fp32 form: bias32 | fp32 scale; fixed point: multiplier |
+      // residual multiplier | shifts (min(S, 32) | max(S - 32, 0) << 8) |
+      // constant low word | constant high word
+      int32_t* sq = reinterpret_cast<int32_t*>(smem + L::kBias) + buf * 5 * BN;
+      if (tma_epi) {
+        // stage this tile's epilogue parameters (and the first residual chunk) while the main loop runs
+        if constexpr (ESZ == 2) {
+          for (int i = etid; i < BN; i += 128)
+            sbias[i] = (a.bias && n0 + i < a.k) ? __ldg(static_cast<const float*>(a.bias) + n0 + i) : 0.0f;
+        } else {
+          for (int i = etid; i < BN; i += 128) {
+            const bool v = n0 + i < a.k;
+            sq[i] = (v && a.bias) ? __ldg(static_cast<const int32_t*>(a.bias) + n0 + i) : 0;
+            if (a.rq_fixed) {
+              const int32_t m1 = v ? __ldg(a.rq_mult + n0 + i) : 0;
+              const int sh = v ? __ldg(a.rq_shift + n0 + i) : 1;
+              const long long cst = (long long)sq[i] * m1 + (1ll << (sh - 1));
+              sq[i] = m1;
+              sq[BN + i] = (v && a.rq_res_mult) ? __ldg(a.rq_res_mult + n0 + i) : 0;
+              sq[2 * BN + i] = (sh < 32 ? sh : 32) | ((sh > 32 ? sh - 32 : 0) << 8);
+              sq[3 * BN + i] = (int32_t)(uint32_t)(unsigned long long)cst;
+              sq[4 * BN + i] = (int32_t)(cst >> 32);
+            } else {
+              sq[BN + i] = v ? __float_as_int(__ldg(a.rq_scale + n0 + i)) : 0;
+            }
+          }
+        }
+        if (a.res) {
+          const int sbuf = chunk_i & 1;
+          if (lane == 0) {
+            bulk_wait_read<0>();
+            mbar_arrive_expect_tx(resid(ew, sbuf), kEBuf);
+            load_res(stage0 + sbuf * kEBuf, n0, resid(ew, sbuf));
+          }
+          res_pending = sbuf;
+          res_pending_par = (sbuf ? res_use1 : res_use0) & 1;
+        }
+        asm volatile("bar.sync 1, 128;" ::: "memory");
+      }
+      bool ok = true;
+      if (!acc_ready) {
+        ok = mbar_wait(tfull(buf), (local >> 1) & 1, abort_flag, a.err, a.wait_cycles);
+        ok = __all_sync(0xffffffffu, ok);
+        if (!ok) break;
+        tc_fence_after();
+      }
+      const int m = m0 + ew * 32 + lane;
+      const uint32_t taddr = tmem + lane_base + (uint32_t)(buf * BN);
+      if (tma_epi) {
+        // 64-column chunks: TMEM -> registers -> (+bias, +residual tile, act) ->
+        // bf16 in a 128B-swizzled staging tile (8-bit: requantised codes in a
+        // 64B-swizzled tile) -> TMA store
+        const int sw = ESZ == 2 ? (lane & 7) : ((lane >> 1) & 3);
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 64) {
+          if (n0 + c0 >= a.ks) break;  // warp-uniform
+          const int sbuf = chunk_i & 1;
+          const uint32_t sb = stage0 + sbuf * kEBuf;
+          uint8_t* sp = stage_ptr0 + sbuf * kEBuf + lane * (64 * ESZ);
+          if (a.res) {
+            const uint32_t use = sbuf ? res_use1++ : res_use0++;
+            const bool rok = mbar_wait(resid(ew, sbuf), use & 1, abort_flag, a.err, a.wait_cycles);
+            if (!__all_sync(0xffffffffu, rok)) {
+              ok = false;
+              break;
+            }
+            res_pending = -1;
+            if (c0 + 64 < BN && n0 + c0 + 64 < a.ks) {
+              // prefetch the next residual chunk into the other buffer once its store has read it
+              if (lane == 0) {
+                bulk_wait_read<0>();
+                mbar_arrive_expect_tx(resid(ew, sbuf ^ 1), kEBuf);
+                load_res(stage0 + (sbuf ^ 1) * kEBuf, n0 + c0 + 64, resid(ew, sbuf ^ 1));
+              }
+              res_pending = sbuf ^ 1;
+              res_pending_par = (sbuf ^ 1 ? res_use1 : res_use0) & 1;
+            }
+          } else {
+            if (lane == 0) bulk_wait_read<1>();  // the store issued two chunks ago has read this buffer
+          }
+          __syncwarp();
+          // Cheap activations: the whole 64-column chunk is loaded and its eight
+          // 8-column groups unrolled. Expensive ones (GELU, sigmoid, the run-time
+          // switch) keep the loop rolled over 16-column loads, so the inlined
+          // activation is not copied 64 times into the instruction stream.
+          constexpr bool kHeavy =
+              ESZ == 2 && (ACT == MDLC_ACT_GELU || ACT == MDLC_ACT_SIGMOID || ACT == -1);
+          uint32_t v[64];
+          if constexpr (!kHeavy) {
+            tmem_ld16(taddr + c0, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
+            tmem_ld16(taddr + c0 + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
+            tmem_ld16(taddr + c0 + 32, *reinterpret_cast<uint32_t(*)[16]>(&v[32]));
+            tmem_ld16(taddr + c0 + 48, *reinterpret_cast<uint32_t(*)[16]>(&v[48]));
+            tmem_ld_wait();
+          }
+          if constexpr (ESZ == 1) {
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {  // 16-column (16-byte) groups
+              uint4* qp = reinterpret_cast<uint4*>(sp + ((q ^ sw) << 4));
+              uint4 rr = make_uint4(0, 0, 0, 0);
+              if (a.res) rr = *qp;
+              const uint32_t rw[4] = {rr.x, rr.y, rr.z, rr.w};
+              // this group's 16 int32 biases and fp32 scales as 128-bit loads
+              const int col0 = c0 + 16 * q;
+              const bool full = n0 + col0 + 16 <= a.k;  // group-uniform: no pad columns
+              int32_t t[16];
+              if (a.rq_fixed) {
+                // single-rounding fixed point: p = acc * M1 + (bias32 * M1 + 2^(S-1))
+                // [+ (res - zp) * M2] in 64 bits (one wide multiply-add each), then
+                // p >> S as a funnel shift of (hi, lo) by min(S, 32) and an
+                // arithmetic shift by max(S - 32, 0); exact in 32 bits because the
+                // host bounds |p >> S| below 2^30 for every possible 8-bit input
+                int32_t m1[16], m2[16], shp[16];
+                long long cst[16];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                  const int4 a4 = *reinterpret_cast<const int4*>(sq + col0 + 4 * j);
+                  const int4 b4 = *reinterpret_cast<const int4*>(sq + BN + col0 + 4 * j);
+                  const int4 c4 = *reinterpret_cast<const int4*>(sq + 2 * BN + col0 + 4 * j);
+                  const int4 l4 = *reinterpret_cast<const int4*>(sq + 3 * BN + col0 + 4 * j);
+                  const int4 h4 = *reinterpret_cast<const int4*>(sq + 4 * BN + col0 + 4 * j);
+                  m1[4 * j] = a4.x; m1[4 * j + 1] = a4.y; m1[4 * j + 2] = a4.z; m1[4 * j + 3] = a4.w;
+                  m2[4 * j] = b4.x; m2[4 * j + 1] = b4.y; m2[4 * j + 2] = b4.z; m2[4 * j + 3] = b4.w;
+                  shp[4 * j] = c4.x; shp[4 * j + 1] = c4.y; shp[4 * j + 2] = c4.z; shp[4 * j + 3] = c4.w;
+                  cst[4 * j] = ((long long)h4.x << 32) | (uint32_t)l4.x;
+                  cst[4 * j + 1] = ((long long)h4.y << 32) | (uint32_t)l4.y;
+                  cst[4 * j + 2] = ((long long)h4.z << 32) | (uint32_t)l4.z;
+                  cst[4 * j + 3] = ((long long)h4.w << 32) | (uint32_t)l4.w;
+                }
+                long long acc64[16];
+#pragma unroll
+                for (int e = 0; e < 16; ++e) acc64[e] = (long long)(int32_t)v[16 * q + e] * m1[e] + cst[e];
+                if (a.res) {
+#pragma unroll
+                  for (int e = 0; e < 16; ++e) {
+                    const uint32_t byte = (rw[e >> 2] >> (8 * (e & 3))) & 0xFFu;
+                    const int32_t rq = a.res_signed ? (int32_t)(int8_t)byte : (int32_t)byte;
+                    acc64[e] += (long long)(rq - a.res_zp) * m2[e];
+                  }
+                }
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                  const int32_t r = (int32_t)__funnelshift_rc((uint32_t)(unsigned long long)acc64[e],
+                                                             (uint32_t)(acc64[e] >> 32), shp[e] & 0xFF) >>
+                                    (shp[e] >> 8);
+                  t[e] = min(max(r, a.qlo), a.qhi) + a.out_zp;
+                }
+              } else {
+              int32_t bq[16];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const int4 bb = *reinterpret_cast<const int4*>(sq + col0 + 4 * j);
+                bq[4 * j] = bb.x; bq[4 * j + 1] = bb.y; bq[4 * j + 2] = bb.z; bq[4 * j + 3] = bb.w;
+              }
+              float sc[16];
+#pragma unroll
+              for (int j = 0; j < 4; ++j) {
+                const float4 ss = *reinterpret_cast<const float4*>(sq + BN + col0 + 4 * j);
+                sc[4 * j] = ss.x; sc[4 * j + 1] = ss.y; sc[4 * j + 2] = ss.z; sc[4 * j + 3] = ss.w;
+              }
+              // exact small-integer <-> float conversions without the conversion
+              // unit: 1.5 * 2^23 in the exponent, value in the low mantissa bits
+              // (|x| < 2^22; round-to-nearest-even like __float2int_rn)
+              constexpr float kMagic = 12582912.0f;
+              constexpr int32_t kMagicBits = 0x4B400000;
+              const float qlo_f = (float)a.qlo, qhi_f = (float)a.qhi;
+              // each stage over all 16 elements before the next, so their
+              // dependency chains interleave
+              float f[16];
+#pragma unroll
+              for (int e = 0; e < 16; ++e) f[e] = __fmul_rn(__int2float_rn((int32_t)v[16 * q + e] + bq[e]), sc[e]);
+              if (a.res) {
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                  const uint32_t byte = (rw[e >> 2] >> (8 * (e & 3))) & 0xFFu;
+                  const int32_t rq = a.res_signed ? (int32_t)(int8_t)byte : (int32_t)byte;
+                  const float rf = __fsub_rn(__int_as_float(rq - a.res_zp + kMagicBits), kMagic);
+                  f[e] = __fadd_rn(f[e], __fmul_rn(rf, a.res_scale));
+                }
+              }
+              // clamp then round == round then clamp (integer bounds)
+#pragma unroll
+              for (int e = 0; e < 16; ++e)
+                t[e] = __float_as_int(__fadd_rn(fminf(fmaxf(f[e], qlo_f), qhi_f), kMagic)) - kMagicBits + a.out_zp;
+              }
+              if (!full) {
+#pragma unroll
+                for (int e = 0; e < 16; ++e)
+                  if (n0 + col0 + e >= a.k) t[e] = 0;
+              }
+              uint32_t packed[4] = {0, 0, 0, 0};
+#pragma unroll
+              for (int e = 0; e < 16; ++e) packed[e >> 2] |= ((uint32_t)t[e] & 0xFFu) << (8 * (e & 3));
+              *qp = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+            }
+          } else {
+          // one 8-column (16-byte) group: + bias (+ residual), activation, bf16
+          auto group = [&](int q, const uint32_t* vv) {
+            uint4* qp = reinterpret_cast<uint4*>(sp + ((q ^ sw) << 4));
+            const float4 b0 = *reinterpret_cast<const float4*>(sbias + c0 + 8 * q);
+            const float4 b1 = *reinterpret_cast<const float4*>(sbias + c0 + 8 * q + 4);
+            float f[8] = {__uint_as_float(vv[0]) + b0.x, __uint_as_float(vv[1]) + b0.y,
+                          __uint_as_float(vv[2]) + b0.z, __uint_as_float(vv[3]) + b0.w,
+                          __uint_as_float(vv[4]) + b1.x, __uint_as_float(vv[5]) + b1.y,
+                          __uint_as_float(vv[6]) + b1.z, __uint_as_float(vv[7]) + b1.w};
+            if (a.res) {
+              const uint4 r = *qp;
+              f[0] += bf16_lo(r.x); f[1] += bf16_hi(r.x); f[2] += bf16_lo(r.y); f[3] += bf16_hi(r.y);
+              f[4] += bf16_lo(r.z); f[5] += bf16_hi(r.z); f[6] += bf16_lo(r.w); f[7] += bf16_hi(r.w);
+            }
+            const int nb0 = n0 + c0 + 8 * q;
+            if constexpr (ACT == MDLC_ACT_GELU) {
+              gelu8(f);
+            } else if constexpr (ACT == MDLC_ACT_SIGMOID) {
+              sigmoid8(f);
+            } else {
+#pragma unroll
+              for (int e = 0; e < 8; ++e) f[e] = act_fn<ACT>(f[e], a.act);
+            }
+#pragma unroll
+            for (int e = 0; e < 8; ++e) f[e] = (nb0 + e < a.k) ? f[e] : 0.0f;
+            *qp = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
+                             pack_bf16x2(f[6], f[7]));
+          };
+          if constexpr (kHeavy) {
+            // two 16-column register buffers: the next load is in flight while
+            // the current columns are computed
+            uint32_t va[16], vb[16];
+            tmem_ld16(taddr + c0, va);
+            tmem_ld_wait();
+#pragma unroll 1
+            for (int j = 0; j < 4; j += 2) {
+              tmem_ld16(taddr + c0 + 16 * (j + 1), vb);
+              group(2 * j, va);
+              group(2 * j + 1, va + 8);
+              tmem_ld_wait();
+              if (j + 2 < 4) tmem_ld16(taddr + c0 + 16 * (j + 2), va);
+              group(2 * j + 2, vb);
+              group(2 * j + 3, vb + 8);
+              tmem_ld_wait();
+            }
+          } else {
+#pragma unroll
+            for (int q = 0; q < 8; ++q) group(q, v + 8 * q);
+          }
+          }
+          fence_proxy_async_smem();
+          __syncwarp();
+          if (lane == 0) {
+            if constexpr (AMODE == 4)
+              tma_store_4d(&tmap_y, n0 + c0, hx, hy, himg, sb);
+            else
+              tma_store_2d(&tmap_y, n0 + c0, m0 + ew * 32, sb);
+            bulk_commit();
+          }
+          ++chunk_i;
+        }
+        if (!ok) break;
+      } else {
+#pragma unroll 1
+        for (int c0 = 0; c0 < BN; c0 += 16) {
+          if (n0 + c0 >= a.ks) break;  // warp-uniform
+          uint32_t v[16];
+          tmem_ld16(taddr + c0, v);
+          tmem_ld_wait();
+          if (m < a.M) store_chunk16<ESZ>(a, m, n0 + c0, v);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(tempty(buf));
+    }
+    // a residual load still in flight (the loop was left on an abort) must land
+    // before the CTA's shared memory is released
+    if (res_pending >= 0 && lane == 0)
+      mbar_wait(resid(ew, res_pending), res_pending_par, nullptr, a.err, 2000000ull);
+    if (lane == 0) bulk_wait<0>();
+  } else if (warp == 8) {
+    // ---------------- B producer (TMA); with AMODE >= 1 also the A operand by TMA
+    if (lane == 0 && AMODE == 4) {
+      // halo mode: one band per (tile, channel block), then the weights of every tap
+      int it = 0, hit = 0;
+      bool ok = true;
+      const uint32_t band_bytes = (uint32_t)a.halo_rows * kHaloSlots * a.band_px;
+      // k-blocks per band: one per tap (128-byte channel blocks, weight k-block
+      // tap * cpb + cb), or every k-block of the filter (whole-pixel bands)
+      const int kpb = a.band_px == 128 ? RS : a.num_kb;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
+        const int n0 = (tile % a.num_n_tiles) * BN;
+        int img, ty, tx;
+        halo_tile(tile / a.num_n_tiles, img, ty, tx);
+        for (int cb = 0; cb < a.cpb && ok; ++cb, ++hit) {
+          const int hs = hit % kHaloStages;
+          if (!mbar_wait(hempty(hs), ((hit / kHaloStages) & 1) ^ 1, abort_flag, a.err, a.wait_cycles)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(hfull(hs), band_bytes);
+          tma_load_4d(sA + hs * kHaloBytes, &tmap_x, cb * KB, tx * kHaloTW - a.pl, ty * kHaloTH - a.pt, img,
+                      hfull(hs));
+          for (int j = 0; j < kpb; ++j, ++it) {
+            const int st = it % STAGES;
+            if (!mbar_wait(empty(st), ((it / STAGES) & 1) ^ 1, abort_flag, a.err, a.wait_cycles)) {
+              ok = false;
+              break;
+            }
+            mbar_arrive_expect_tx(fullB(st), L::kBBytes);
+            tma_load_2d(sB + st * L::kBBytes, &tmap_w, (a.band_px == 128 ? j * a.cpb + cb : j) * KB, n0, fullB(st));
+          }
+        }
+      }
+      if (!ok) {
+        // let the loads already issued land before the CTA's shared memory is released
+        for (int q = it - 1; q >= 0 && q >= it - STAGES; --q)
+          mbar_wait(fullB(q % STAGES), (q / STAGES) & 1, nullptr, a.err, 2000000ull);
+        for (int q = hit - 1; q >= 0 && q >= hit - kHaloStages; --q)
+          mbar_wait(hfull(q % kHaloStages), (q / kHaloStages) & 1, nullptr, a.err, 2000000ull);
+      }
+    } else if (lane == 0) {
+      // weights only: the A operand comes from warps 0-3 (gather or TMA)
+      int it = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+        const int n0 = (u / S % a.num_n_tiles) * BN;
+        for (int kb = kb_begin(u); kb < kb_end(u); ++kb, ++it) {
+          const int st = it % STAGES;
+          if (!mbar_wait(empty(st), ((it / STAGES) & 1) ^ 1, abort_flag, a.err, a.wait_cycles)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(fullA(st), L::kBBytes);
+          if constexpr (ESZ == 4)  // the k-block of the hi and of the lo weight matrix in one load
+            tma_load_3d(sB + st * L::kBBytes, &tmap_w, kb * KB, n0, 0, fullA(st));
+          else
+            tma_load_2d(sB + st * L::kBBytes, &tmap_w, kb * KB, n0, fullA(st));
+        }
+      }
+      if (!ok) {
+        // let the loads already issued land before the CTA's shared memory is released
+        for (int q = it - 1; q >= 0 && q >= it - STAGES; --q)
+          mbar_wait(fullA(q % STAGES), (q / STAGES) & 1, nullptr, a.err, 2000000ull);
+      }
+    }
+  } else if (warp == 9) {
+    // ---------------- MMA issuer (warps 0-3 idle here when A arrives by TMA)
+    if (lane == 0 && AMODE == 4) {
+      const uint32_t idesc = ESZ == 2 ? idesc_bf16(kBM, BN) : idesc_i8(kBM, BN, a.a_signed, 1);
+      int it = 0, hit = 0, local = 0;
+      bool ok = true;
+      for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x, ++local) {
+        const int buf = local & 1;
+        if (!mbar_wait(tempty(buf), ((local >> 1) & 1) ^ 1, abort_flag, a.err, a.wait_cycles)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(buf * BN);
+        for (int cb = 0; cb < a.cpb && ok; ++cb, ++hit) {
+          const int hs = hit % kHaloStages;
+          if (!mbar_wait(hfull(hs), (hit / kHaloStages) & 1, abort_flag, a.err, a.wait_cycles)) {
+            ok = false;
+            break;
+          }
+          const uint32_t band = sA + hs * kHaloBytes;
+          const int P = a.band_px;
+          const int kpb = P == 128 ? RS : a.num_kb;
+          const uint32_t sbo = (uint32_t)(kHaloSlots * P);
+          const uint32_t layout = P == 32 ? 6u : (P == 64 ? 4u : 2u);
+          for (int j = 0; j < kpb; ++j, ++it) {
+            const int st = it % STAGES;
+            if (!mbar_wait(fullB(st), (it / STAGES) & 1, abort_flag, a.err, a.wait_cycles)) {
+              ok = false;
+              break;
+            }
+            const uint32_t bb = sB + st * L::kBBytes;
+#pragma unroll
+            for (int kq = 0; kq < 4; ++kq) {
+              // the 32 K bytes of this MMA: tap and byte offset inside the band pixel;
+              // taps past the end of the filter have zero weights and re-read tap 0
+              const int kbyte = P == 128 ? j * P + kq * 32 : (j * 4 + kq) * 32;
+              int tap = kbyte / P;
+              if (tap >= RS) tap = 0;
+              const int ty = tap / a.s, tx = tap - ty * a.s;
+              const uint32_t a0 = band + (uint32_t)(ty * kHaloSlots + tx) * (uint32_t)P + (uint32_t)(kbyte % P);
+              const uint64_t ad = umma_desc_k(a0, sbo, layout);
+              const uint64_t bd = umma_desc_sw128(bb + kq * 32);
+              if constexpr (ESZ == 2)
+                umma_bf16(d, ad, bd, idesc, (cb | j | kq) != 0);
+              else
+                umma_i8(d, ad, bd, idesc, (cb | j | kq) != 0);
+            }
+            umma_commit(empty(st));
+          }
+          if (ok) umma_commit(hempty(hs));  // the band is free once its MMAs have read it
+        }
+        if (ok) umma_commit(tfull(buf));
+      }
+      if (!ok) {
+        umma_commit(drain);
+        mbar_wait(drain, 0, nullptr, a.err, 1000000ull);
+      }
+    } else if (lane == 0) {
+      const uint32_t idesc =
+          ESZ == 4 ? idesc_tf32(kBM, BN) : (ESZ == 2 ? idesc_bf16(kBM, BN) : idesc_i8(kBM, BN, a.a_signed, 1));
+      int it = 0, local = 0;
+      bool ok = true;
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++local) {
+        const int buf = local & 1;
+        if (!mbar_wait(tempty(buf), ((local >> 1) & 1) ^ 1, abort_flag, a.err, a.wait_cycles)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t d = tmem + (uint32_t)(buf * BN);
+        const int kb0 = kb_begin(u);
+        for (int kb = kb0; kb < kb_end(u); ++kb, ++it) {
+          const int st = it % STAGES;
+          const uint32_t par = (it / STAGES) & 1;
+          // fp32: wait for the split warps (the stage's A and B have landed and A
+          // is split into hi / lo parts)
+          if (!mbar_wait(ESZ == 4 ? splitA(st) : fullA(st), par, abort_flag, a.err, a.wait_cycles)) {
+            ok = false;
+            break;
+          }
+          // cp.async (and the split warps' stores) write A through the generic
+          // proxy: order them before the async-proxy operand reads of
+          // tcgen05.mma. TMA-written operands are ordered by the mbarrier
+          // completion itself.
+          if constexpr (AMODE == 0 || ESZ == 4) {
+            fence_proxy_async_smem();
+            tc_fence_after();
+          }
+          const uint32_t ab = sA + st * kABytes, bb = sB + st * L::kBBytes;
+          auto adesc = [&](uint32_t base, int kq) {
+            return AMODE == 2   ? umma_desc_k(base + kq * (kABytes / 4), 256, 6)
+                   : AMODE == 3 ? umma_desc_k(base + (kq >> 1) * (kABytes / 2) + (kq & 1) * 32, 512, 4)
+                                : umma_desc_sw128(base + kq * 32);
+          };
+#pragma unroll
+          for (int kq = 0; kq < 4; ++kq) {
+            const uint64_t ad = adesc(ab, kq);
+            const uint64_t bd = umma_desc_sw128(bb + kq * 32);
+            if constexpr (ESZ == 4) {
+              // 3xTF32: a*b ~ ahi*bhi + ahi*blo + alo*bhi (alo*blo ~ 2^-22 |ab| dropped)
+              const uint64_t ad_lo = adesc(sALo + st * kABytes, kq);
+              const uint64_t bd_lo = umma_desc_sw128(bb + BN * 128 + kq * 32);
+              umma_tf32(d, ad, bd, idesc, (kb != kb0) || kq != 0);
+              umma_tf32(d, ad, bd_lo, idesc, 1);
+              umma_tf32(d, ad_lo, bd, idesc, 1);
+            } else if constexpr (ESZ == 2) {
+              umma_bf16(d, ad, bd, idesc, (kb != kb0) || kq != 0);
+            } else {
+              umma_i8(d, ad, bd, idesc, (kb != kb0) || kq != 0);
+            }
+          }
+          umma_commit(empty(st));
+        }
+        if (ok) umma_commit(tfull(buf));
+      }
+      if (!ok) {
+        umma_commit(drain);
+        mbar_wait(drain, 0, nullptr, a.err, 1000000ull);
+      }
+    }
+  } else if (ESZ == 4 && warp >= 10) {
+    // ---------------- A split (fp32 operands): each landed A stage becomes its
+    // tf32 high part (low 13 mantissa bits cleared, in place) and the exact
+    // remainder a - hi (the lo stage); the MMA issuer sums hi*hi + hi*lo + lo*hi.
+    // Layout-agnostic (element for element in place), so every A mode works.
+    const int sid = tid - 320;           // 0..127
+    const int j = sid & 7, row0 = sid >> 3;
+    int it = 0;
+    bool ok = true;
+    for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+      for (int kb = kb_begin(u); kb < kb_end(u); ++kb, ++it) {
+        const int st = it % STAGES;
+        if (!mbar_wait(fullA(st), (it / STAGES) & 1, abort_flag, a.err, a.wait_cycles)) {
+          ok = false;
+          break;
+        }
+        uint8_t* hi_p = smem + L::kA + st * kABytes;
+        uint8_t* lo_p = smem + L::kALo + st * kABytes;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const int off = (row0 + 16 * i) * 128 + j * 16;
+          const uint4 x4 = *reinterpret_cast<const uint4*>(hi_p + off);
+          const uint4 h4 = make_uint4(x4.x & 0xFFFFE000u, x4.y & 0xFFFFE000u, x4.z & 0xFFFFE000u,
+                                      x4.w & 0xFFFFE000u);
+          const float4 l4 = make_float4(__uint_as_float(x4.x) - __uint_as_float(h4.x),
+                                        __uint_as_float(x4.y) - __uint_as_float(h4.y),
+                                        __uint_as_float(x4.z) - __uint_as_float(h4.z),
+                                        __uint_as_float(x4.w) - __uint_as_float(h4.w));
+          *reinterpret_cast<uint4*>(hi_p + off) = h4;
+          *reinterpret_cast<float4*>(lo_p + off) = l4;
+        }
+        // generic-proxy writes, read next by tcgen05.mma (async proxy)
+        fence_proxy_async_smem();
+        mbar_arrive(splitA(st));
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 9) {
+    __syncwarp();
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
+}
+
+template <int BN, int STAGES, int ESZ, int ACT, int AMODE>
+int launch_tc(mdlc_ctx* ctx, const CUtensorMap& tmap, const CUtensorMap& tmap_y, const CUtensorMap& tmap_r,
+              const CUtensorMap& tmap_x, const TcArgs& args) {
+  using L = Smem<BN, STAGES, ESZ, AMODE>;
+  static_assert(L::kAlloc <= 232448, "shared memory budget");
+  auto kern = conv_tc_kernel<BN, STAGES, ESZ, ACT, AMODE>;
+  static bool attr_set[64] = {};
+  if (!attr_set[ctx->device & 63]) {
+    cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::kAlloc);
+    if (e != cudaSuccess) return mdlc_cuda_status(ctx, e, "conv_tc smem attribute");
+    attr_set[ctx->device & 63] = true;
+  }
+  const int tiles = args.num_m_tiles * args.num_n_tiles * args.split;  // work units
+  const int slots = ctx->num_sms * Occ<BN, STAGES, ESZ, AMODE>::value;
+  const int grid = tiles < slots ? tiles : slots;
+  // launched with programmatic stream serialization: the kernel starts its
+  // set-up while the previous conv kernel drains (see griddepcontrol.wait)
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = dim3(grid);
+  lc.blockDim = dim3(threads_for<ESZ>());
+  lc.dynamicSmemBytes = L::kAlloc;
+  lc.stream = ctx->stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  const cudaError_t e = cudaLaunchKernelEx(&lc, kern, tmap, tmap_y, tmap_r, tmap_x, args);
+  mdlc_note_launch(ctx);
+  return mdlc_cuda_status(ctx, e != cudaSuccess ? e : cudaGetLastError(), "conv_tc launch");
+}
+
+}  // namespace
+}  // namespace mdlc

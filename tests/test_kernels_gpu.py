@@ -320,8 +320,23 @@ def test_conv_bf16_fp32_output(ctx):
     check(got, want, 2e-3)   # no output rounding: only accumulation order differs
 
 
-@pytest.mark.parametrize("case", [(2, 3, 11, 11, 16, 3, 1, 1), (1, 64, 9, 9, 64, 3, 2, 1), (3, 40, 6, 6, 24, 1, 1, 0)])
-def test_conv_fp32_simt(ctx, case):
+F32_CASES = [
+    # n, c, h, w, k, r, stride, pad
+    (2, 3, 11, 11, 16, 3, 1, 1),       # small: cp.async gather
+    (1, 64, 9, 9, 64, 3, 2, 1),
+    (3, 40, 6, 6, 24, 1, 1, 0),        # ragged channels
+    (4, 64, 32, 32, 64, 3, 1, 1),      # im2col TMA, 32-channel (128-byte) blocks
+    (8, 8, 40, 40, 64, 3, 1, 1),       # 32-byte pixels (c = 8)
+    (6, 16, 33, 31, 128, 3, 2, 1),     # 64-byte pixels (c = 16), stride 2
+    (4, 128, 20, 20, 256, 1, 1, 0),    # pointwise 2-D TMA, 256-wide tiles
+    (2, 256, 7, 7, 512, 3, 1, 1),      # deep reduction (2304)
+]
+
+
+@pytest.mark.parametrize("case", F32_CASES, ids=[str(c) for c in F32_CASES])
+def test_conv_fp32_3xtf32(ctx, case):
+    """fp32 convolutions on the tensor cores (3xTF32) meet the reference's
+    FP32_REDUCTION tier against the fp32 oracle."""
     n, c, h, w, k, r, st, pad = case
     rng = np.random.default_rng(5)
     x = rng.standard_normal((n, c, h, w)).astype(np.float32)
@@ -331,6 +346,18 @@ def test_conv_fp32_simt(ctx, case):
     got = run_conv(ctx, x, wt, b, stride=st, pad=pad, dtype="f32", act=L.ACT_RELU, res=res)
     want = oracle_conv(x, wt, b, stride=st, pad=pad, act="Relu", res=res, bf16=False)
     np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4)   # FP32_REDUCTION tier
+
+
+def test_conv_fp32_split_k(ctx):
+    """3xTF32 with split-K: fp32 partial sums summed in slice order."""
+    n, c, h, w, k, r, st, pad = 1, 512, 7, 7, 512, 3, 1, 1
+    rng = np.random.default_rng(15)
+    x = rng.standard_normal((n, c, h, w)).astype(np.float32)
+    wt = (rng.standard_normal((k, c, r, r)) * 0.02).astype(np.float32)
+    b = (rng.standard_normal(k) * 0.1).astype(np.float32)
+    got = run_conv(ctx, x, wt, b, stride=st, pad=pad, dtype="f32", act=L.ACT_RELU, flags=6 << 8)
+    want = oracle_conv(x, wt, b, stride=st, pad=pad, act="Relu", bf16=False)
+    np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4)
 
 
 DW_CASES = [
