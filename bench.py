@@ -176,6 +176,12 @@ def call_work(dev, call):
         e = _esz(d.dtype)
         cls = {0: "maxpool", 1: "avgpool", 2: "gap"}[d.kind]
         return cls, "hbm", d.n * d.h * d.w * d.c_stride * e + d.n * d.oh * d.ow * d.c_stride * e, 0.0
+    if kind in ("copy", "softmax"):
+        d = call[1]
+        e = _esz(d.dtype)
+        dims = list(d.out_dims) + [d.out_cs] if kind == "copy" else list(d.dims) + [d.cs]
+        n = dims[0] * dims[2] * dims[3] * dims[4]
+        return kind, "hbm", 2 * n * e, 0.0
     prog = call[1]
     e = _esz(prog.dtype)
     full = prog.n * prog.hw * prog.c_stride * e
@@ -233,6 +239,10 @@ def launch_times(exe, steps):
                 timed(cls, bound, nbytes, flops, lambda: ctx.conv2d(d, x, w, b, r, y, epi, cfg))
             elif c[0] == "pool":
                 timed(cls, bound, nbytes, flops, lambda: ctx.pool2d(c[1], c[2], c[3]))
+            elif c[0] == "copy":
+                timed(cls, bound, nbytes, flops, lambda: ctx.copy4d(c[1], c[2], c[3]))
+            elif c[0] == "softmax":
+                timed(cls, bound, nbytes, flops, lambda: ctx.softmax(c[1], c[2], c[3]))
             else:
                 timed(cls, bound, nbytes, flops, lambda: ctx.eltwise(c[1], c[2], c[3]))
         if len(io) > n_in:

@@ -307,6 +307,43 @@ int mdlc_nhwc_to_nchw(mdlc_ctx* ctx, const void* x, int n, int c, int h, int w, 
 int mdlc_nchw_to_s2d(mdlc_ctx* ctx, const float* x, int n, int c, int h, int w, void* y, int cs, int dtype,
                      float inv_scale, int zp);
 
+/* Data-movement ops over NHWC tensors addressed by their logical 4-D index
+ * (n, c, h, w) (rank-2 [n, c] and rank-3 [n, c, h] tensors use h = w = 1 / w = 1).
+ * Replaces the Transpose / Concat / Pad host bounces of the reference GPU
+ * executor (mdlc/codegen/cuda/emit.py:32-35; semantics mdlc/runtime/ops.py:229-255).
+ * Gather (mode 0): every output element, padding channels included, reads the
+ * source element whose index along source dimension src_dim[i] is
+ * out_index[i] - offset[i]; an index outside the source is filled per
+ * pad_mode: 0 constant (value), 1 edge (clamped), 2 reflect (no edge repeat).
+ * Scatter (mode 1): every source element is written to the output element at
+ * index + offset (src_dim must be the identity); other output elements are
+ * left as they are. Transpose = gather with src_dim = the inverse permutation;
+ * Pad = gather with offset = the leading pads; Concat = gather of the first
+ * input (zero fill) then a scatter of each other input at its offset. */
+typedef struct {
+  int32_t dtype;        /* MDLC_F32 | MDLC_BF16 */
+  int32_t in_dims[4];   /* logical n, c, h, w of the source */
+  int32_t in_cs;        /* source channel stride */
+  int32_t out_dims[4];
+  int32_t out_cs;
+  int32_t src_dim[4];
+  int32_t offset[4];
+  int32_t mode, pad_mode;
+  float value;
+} mdlc_copy_desc;
+int mdlc_copy4d(mdlc_ctx* ctx, const mdlc_copy_desc* desc, const void* x, void* y);
+
+/* Softmax along one logical axis (0..3 of n, c, h, w) of an NHWC tensor:
+ * y = exp(x - max) / sum(exp(x - max)) over that axis, fp32 arithmetic.
+ * Replaces the Softmax host bounce (reference ops.py:188-191). */
+typedef struct {
+  int32_t dtype;   /* MDLC_F32 | MDLC_BF16 */
+  int32_t dims[4]; /* logical n, c, h, w */
+  int32_t cs;      /* channel stride of x and y */
+  int32_t axis;
+} mdlc_softmax_desc;
+int mdlc_softmax(mdlc_ctx* ctx, const mdlc_softmax_desc* desc, const void* x, void* y);
+
 /* ---- CUDA graph capture of a whole run (b=1 latency) ------------------- */
 int mdlc_graph_begin(mdlc_ctx* ctx);
 int mdlc_graph_end(mdlc_ctx* ctx);    /* instantiates the captured graph */

@@ -85,6 +85,16 @@ class EwProg(C.Structure):
                 ("out_reg", C.c_int32 * EW_MAX_OUTPUTS), ("code", EwInstr * EW_MAX_INSTR)]
 
 
+class CopyDesc(C.Structure):
+    _fields_ = [("dtype", C.c_int32), ("in_dims", C.c_int32 * 4), ("in_cs", C.c_int32),
+                ("out_dims", C.c_int32 * 4), ("out_cs", C.c_int32), ("src_dim", C.c_int32 * 4),
+                ("offset", C.c_int32 * 4), ("mode", C.c_int32), ("pad_mode", C.c_int32), ("value", C.c_float)]
+
+
+class SoftmaxDesc(C.Structure):
+    _fields_ = [("dtype", C.c_int32), ("dims", C.c_int32 * 4), ("cs", C.c_int32), ("axis", C.c_int32)]
+
+
 # exported symbol -> (argtypes, restype); the CPU test suite checks every
 # function declared in include/mdlc_b200.h is exported and listed here.
 _P, _I, _S = C.c_void_p, C.c_int, C.c_size_t
@@ -125,6 +135,8 @@ SIGNATURES = {
     "mdlc_nchw_to_nhwc": ([_P, _P, _I, _I, _I, _I, _P, _I, _I, C.c_float, _I], C.c_int),
     "mdlc_nhwc_to_nchw": ([_P, _P, _I, _I, _I, _I, _I, _I, _P, C.c_float, _I], C.c_int),
     "mdlc_nchw_to_s2d": ([_P, _P, _I, _I, _I, _I, _P, _I, _I, C.c_float, _I], C.c_int),
+    "mdlc_copy4d": ([_P, C.POINTER(CopyDesc), _P, _P], C.c_int),
+    "mdlc_softmax": ([_P, C.POINTER(SoftmaxDesc), _P, _P], C.c_int),
     "mdlc_graph_begin": ([_P], C.c_int),
     "mdlc_graph_end": ([_P], C.c_int),
     "mdlc_graph_launch": ([_P], C.c_int),
@@ -292,6 +304,12 @@ class Context:
         outs = (C.c_void_p * EW_MAX_OUTPUTS)(*([C.c_void_p(p) for p in outputs] +
                                               [C.c_void_p(0)] * (EW_MAX_OUTPUTS - len(outputs))))
         self.check(self.lib.mdlc_eltwise(self.h, C.byref(prog), ins, outs), "eltwise")
+
+    def copy4d(self, desc: CopyDesc, x, y) -> None:
+        self.check(self.lib.mdlc_copy4d(self.h, C.byref(desc), C.c_void_p(x), C.c_void_p(y)), "copy4d")
+
+    def softmax(self, desc: SoftmaxDesc, x, y) -> None:
+        self.check(self.lib.mdlc_softmax(self.h, C.byref(desc), C.c_void_p(x), C.c_void_p(y)), "softmax")
 
     def to_nhwc(self, x, n, c, h, w, y, cs, dtype, inv_scale=1.0, zp=0) -> None:
         self.check(self.lib.mdlc_nchw_to_nhwc(self.h, C.c_void_p(x), n, c, h, w, C.c_void_p(y), cs, dtype,

@@ -61,8 +61,18 @@ def build(force: bool = False, verbose: bool = False, extra=(), check: bool = Fa
         return lib
     os.makedirs(bdir, exist_ok=True)
 
+    headers = [p for p in _deps() if not p.endswith(".cu")]
+    newest_header = max((os.path.getmtime(p) for p in headers), default=0.0)
+    flags_file = os.path.join(bdir, "flags.txt")
+    flags = " ".join([*ARCH, *FLAGS, *extra])
+    same_flags = os.path.exists(flags_file) and open(flags_file).read() == flags
+
     def compile_one(src):
         obj = os.path.join(bdir, os.path.basename(src) + ".o")
+        # incremental: an object newer than its source and every header is reused
+        if (not force and same_flags and os.path.exists(obj) and
+                os.path.getmtime(obj) >= max(os.path.getmtime(src), newest_header)):
+            return obj, ""
         cmd = [NVCC, *ARCH, *FLAGS, *extra, "-c", src, "-o", obj]
         if verbose:
             cmd += ["-Xptxas", "-v"]
@@ -73,6 +83,8 @@ def build(force: bool = False, verbose: bool = False, extra=(), check: bool = Fa
 
     with ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 4)) as ex:
         results = list(ex.map(compile_one, _sources()))
+    with open(flags_file, "w") as f:
+        f.write(flags)
     if verbose:
         for _, log in results:
             sys.stderr.write(log)

@@ -193,6 +193,26 @@ class _Device:
                               self.bbuf[st.params["weight"]],
                               self.ptr(st.params["residual"]) if st.params["residual"] else 0,
                               self.ptr(st.outputs[0]), epi, cfg))
+            elif st.kind == "copy":
+                yt = lo.tensors[st.outputs[0]]
+                for part in st.params["parts"]:
+                    xt = lo.tensors[part["src"]]
+                    d = L.CopyDesc(dtype=yt.dtype, in_cs=xt.cs, out_cs=yt.cs, mode=part["mode"],
+                                   pad_mode=part["pad_mode"], value=part["value"])
+                    for i, v in enumerate((xt.n, xt.c, xt.h, xt.w)):
+                        d.in_dims[i] = v
+                    for i, v in enumerate((yt.n, yt.c, yt.h, yt.w)):
+                        d.out_dims[i] = v
+                    for i in range(4):
+                        d.src_dim[i] = part["src_dim"][i]
+                        d.offset[i] = part["offset"][i]
+                    calls.append(("copy", d, self.ptr(part["src"]), self.ptr(st.outputs[0])))
+            elif st.kind == "softmax":
+                t = lo.tensors[st.inputs[0]]
+                d = L.SoftmaxDesc(dtype=t.dtype, cs=t.cs, axis=st.params["axis"])
+                for i, v in enumerate((t.n, t.c, t.h, t.w)):
+                    d.dims[i] = v
+                calls.append(("softmax", d, self.ptr(st.inputs[0]), self.ptr(st.outputs[0])))
             elif st.kind == "pool":
                 xt, yt = lo.tensors[st.inputs[0]], lo.tensors[st.outputs[0]]
                 p = st.params
@@ -229,6 +249,10 @@ class _Device:
                 ctx.conv2d(d, x, w, b, r, y, epi, cfg)
             elif c[0] == "pool":
                 ctx.pool2d(c[1], c[2], c[3])
+            elif c[0] == "copy":
+                ctx.copy4d(c[1], c[2], c[3])
+            elif c[0] == "softmax":
+                ctx.softmax(c[1], c[2], c[3])
             else:
                 ctx.eltwise(c[1], c[2], c[3])
 
@@ -416,6 +440,10 @@ class Executable:
         self.shard = self.batch // ndev
         self._lowered = {}
         self.lowered = self._lowered_for(self.shard)   # validates the graph (raises on gaps)
+        mixing = [st.label() for st in self.lowered.steps if st.params.get("batch_mixing")]
+        if ndev > 1 and mixing:
+            raise lowering.LoweringError(f"{mixing[0]} mixes images across the batch axis, which "
+                                         f"devices={ndev} shards; compile it for one device")
         if self.dtype == L.U8:
             from mdlc_b200 import quant
             ranges = calib

@@ -181,7 +181,14 @@ class _Lowerer:
                 alpha, beta = 1.0, 1.0
             else:
                 if a.get("transA", 0):
-                    raise LoweringError(f"{node.name}: Gemm transA=1 is not supported")
+                    # the activation is [K, M]: a transpose step makes it [M, K]
+                    k_, m_ = (int(v) for v in self.shapes[x])
+                    xT = f"{node.name}.A_T"
+                    self.shapes[xT] = (m_, k_)
+                    self.steps.append(self.transpose_step(f"{node.name}.transA", x, xT, [1, 0]))
+                    self.tensor(xT)
+                    x = xT
+                    xt = self.tensor(xT)
                 B = self.const(node.inputs[1])
                 if B is None:
                     raise LoweringError(f"{node.name}: Gemm weight must be constant")
@@ -486,6 +493,26 @@ class _Lowerer:
                 self.tensor(node.inputs[0])
                 self.tensor(node.outputs[0])
                 self.steps.append(Step("pool", [node.inputs[0]], [node.outputs[0]], [node.name], dict(kind=2)))
+            elif op == "BatchNormalization":
+                self.steps.append(self.batchnorm_step(node))
+            elif op == "Softmax":
+                rank = len(self.shapes[node.inputs[0]])
+                self.tensor(node.inputs[0])
+                self.tensor(node.outputs[0])
+                axis = int(node.attrs.get("axis", -1)) % rank
+                self.steps.append(Step("softmax", [node.inputs[0]], [node.outputs[0]], [node.name],
+                                       dict(axis=axis, batch_mixing=axis == 0)))
+            elif op == "Transpose":
+                x = node.inputs[0]
+                rank = len(self.shapes[x])
+                perm = [int(v) for v in node.attrs.get("perm", list(range(rank))[::-1])]
+                self.tensor(x)
+                self.tensor(node.outputs[0])
+                self.steps.append(self.transpose_step(node.name, x, node.outputs[0], perm))
+            elif op == "Pad":
+                self.steps.append(self.pad_step(node))
+            elif op == "Concat":
+                self.steps.append(self.concat_step(node))
             elif op in ALIAS_OPS:
                 src = self.tensor(node.inputs[0])
                 out_shape = tuple(self.shapes[node.outputs[0]])
@@ -509,6 +536,87 @@ class _Lowerer:
             raise LoweringError("internal: unplaced fused step")
         return Lowered(self.steps, self.tensors, self.weights, self.consts, list(self.g.runtime_inputs),
                        list(self.g.outputs), self.shapes, self.dtype)
+
+    # ---------------------------------------------------------- data movement
+    def transpose_step(self, name, x, y, perm):
+        """out axis i reads source axis perm[i] (ONNX Transpose, ops.py:229-230);
+        the axes past the tensor's rank (h, w of a 2-D one) stay in place."""
+        rank = len(perm)
+        if rank > 4 or sorted(perm) != list(range(rank)):
+            raise LoweringError(f"{name}: Transpose perm {perm} is not a permutation of rank <= 4")
+        src_dim = list(perm) + list(range(rank, 4))
+        part = dict(src=x, mode=0, src_dim=src_dim, offset=[0, 0, 0, 0], pad_mode=0, value=0.0)
+        return Step("copy", [x], [y], [name], dict(parts=[part], batch_mixing=perm[0] != 0))
+
+    def pad_step(self, node):
+        """ONNX Pad (ops.py:249-255): constant / edge / reflect over up to 4 axes."""
+        x, y = node.inputs[0], node.outputs[0]
+        rank = len(self.shapes[x])
+        pads = self.const(node.inputs[1]) if len(node.inputs) > 1 and node.inputs[1] else node.attrs.get("pads")
+        if pads is None:
+            raise LoweringError(f"{node.name}: Pad needs constant pads")
+        pads = [int(v) for v in np.asarray(pads).ravel()]
+        val = self.const(node.inputs[2]) if len(node.inputs) > 2 and node.inputs[2] else node.attrs.get("value", 0.0)
+        if len(node.inputs) > 2 and node.inputs[2] and val is None:
+            raise LoweringError(f"{node.name}: Pad value must be constant")
+        mode = node.attrs.get("mode", "constant")
+        if isinstance(mode, bytes):
+            mode = mode.decode()
+        if mode not in ("constant", "edge", "reflect") or len(pads) != 2 * rank or rank > 4:
+            raise LoweringError(f"{node.name}: Pad mode {mode!r} / pads {pads} not supported")
+        self.tensor(x)
+        self.tensor(y)
+        begin = pads[:rank] + [0] * (4 - rank)
+        part = dict(src=x, mode=0, src_dim=[0, 1, 2, 3], offset=begin,
+                    pad_mode={"constant": 0, "edge": 1, "reflect": 2}[mode],
+                    value=float(np.asarray(0.0 if val is None else val).item()))
+        return Step("copy", [x], [y], [node.name], dict(parts=[part], batch_mixing=pads[0] != 0 or pads[rank] != 0))
+
+    def concat_step(self, node):
+        """ONNX Concat (ops.py:233-234): the first input gathered into the output
+        (zero elsewhere), every other one scattered at its offset along the axis."""
+        ins, y = [i for i in node.inputs if i], node.outputs[0]
+        rank = len(self.shapes[y])
+        axis = int(node.attrs.get("axis", 0)) % rank
+        if rank > 4:
+            raise LoweringError(f"{node.name}: Concat of rank {rank}")
+        for i in ins:
+            if self.const(i) is not None:
+                raise LoweringError(f"{node.name}: Concat of a constant operand")
+            self.tensor(i)
+        self.tensor(y)
+        parts, off = [], 0
+        for k, i in enumerate(ins):
+            offset = [0, 0, 0, 0]
+            offset[axis] = off
+            parts.append(dict(src=i, mode=0 if k == 0 else 1, src_dim=[0, 1, 2, 3], offset=offset,
+                              pad_mode=0, value=0.0))
+            off += int(self.shapes[i][axis])
+        return Step("copy", list(ins), [y], [node.name], dict(parts=parts, batch_mixing=axis == 0))
+
+    def batchnorm_step(self, node):
+        """Inference BatchNormalization (ops.py:95-106) not folded into a conv:
+        y = x * s + t per channel, s = scale / sqrt(var + eps), t = bias - mean * s."""
+        x, y = node.inputs[0], node.outputs[0]
+        prm = [self.const(i) for i in node.inputs[1:5]]
+        if any(p is None for p in prm):
+            raise LoweringError(f"{node.name}: BatchNormalization parameters must be constant")
+        scale, bias, mean, var = (np.asarray(p, np.float64).reshape(-1) for p in prm)
+        eps = float(node.attrs.get("epsilon", 1e-5))
+        sc = scale / np.sqrt(var + eps)
+        sh = bias - mean * sc
+        xt = self.tensor(x)
+        self.tensor(y)
+        names = []
+        for tag, arr in (("scale", sc), ("shift", sh)):
+            padded = np.zeros(xt.cs, np.float32)
+            padded[:xt.c] = arr.astype(np.float32)
+            cname = f"{node.name}.{tag}"
+            self.consts[cname] = padded
+            names.append(cname)
+        code = [(L.EW_MUL, 3, 0, 1, 0.0, 0.0), (L.EW_ADD, 3, 3, 2, 0.0, 0.0)]
+        return Step("eltwise", [x], [y], [node.name],
+                    dict(code=code, operands=[x] + names, bcast=[L.BC_FULL, L.BC_C, L.BC_C], out_regs=[3]))
 
     def _reduce_axes(self, node):
         axes = node.attrs.get("axes")

@@ -125,6 +125,24 @@ def node_shapes(node, shape_of, const_of):
         return [local[o] for o in node.outputs]
     if op in ("Add", "Sub", "Mul", "Div"):
         return [broadcast(shape_of(ins[0]), shape_of(ins[1]))]
+    if op == "BatchNormalization":
+        return [shape_of(ins[0])]
+    if op == "Transpose":
+        xs = shape_of(ins[0])
+        perm = a.get("perm", list(range(len(xs)))[::-1])
+        return [tuple(xs[int(p)] for p in perm)]
+    if op == "Pad":
+        xs = shape_of(ins[0])
+        pads = const_of(ins[1]) if len(ins) > 1 and ins[1] else a.get("pads")
+        pads = [int(v) for v in np.asarray(pads).ravel()]
+        r = len(xs)
+        return [tuple(xs[i] + pads[i] + pads[i + r] for i in range(r))]
+    if op == "Concat":
+        parts = [shape_of(i) for i in ins if i]
+        axis = int(a.get("axis", 0)) % len(parts[0])
+        out = list(parts[0])
+        out[axis] = sum(p[axis] for p in parts)
+        return [tuple(out)]
     if op in ("Relu", "Clip", "Sigmoid", "Tanh", "HardSwish", "HardSigmoid", "LeakyRelu", "Erf",
               "Gelu", "Softmax"):
         return [shape_of(ins[0])]

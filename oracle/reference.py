@@ -268,6 +268,17 @@ def exec_node(node, env, bf16_emulation=False):
         return [np.transpose(ins[0], a.get("perm"))]
     if op == "Concat":
         return [np.concatenate([x for x in ins if x is not None], axis=a.get("axis", 0))]
+    if op == "Pad":   # ops.py:249-255: pads = [begin..., end...], constant / reflect / edge
+        pads = ins[1] if len(ins) > 1 and ins[1] is not None else a.get("pads")
+        pads = [int(p) for p in np.asarray(pads).ravel()]
+        val = ins[2] if len(ins) > 2 and ins[2] is not None else a.get("value", 0.0)
+        half = len(pads) // 2
+        width = [(pads[i], pads[i + half]) for i in range(half)]
+        mode = a.get("mode", "constant")
+        mode = mode.decode() if isinstance(mode, bytes) else mode
+        if mode == "constant":
+            return [np.pad(ins[0], width, mode="constant", constant_values=float(np.asarray(val).item()))]
+        return [np.pad(ins[0], width, mode={"reflect": "reflect", "edge": "edge"}.get(mode, "constant"))]
     if op == "Squeeze":
         axes = ins[1] if len(ins) > 1 and ins[1] is not None else a.get("axes")
         return [np.squeeze(ins[0]) if axes is None
