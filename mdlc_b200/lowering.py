@@ -682,6 +682,62 @@ def space_to_depth_stem(lo: Lowered) -> None:
         st.params["s2d"] = True
 
 
+def pair_weights(wt: np.ndarray, cs: int, pad_l: int):
+    """Re-index a stride-1 conv's OIHW weights for column pairing.
+
+    The input [N, H, W, cs] is read as [N, H, W/2, 2cs] (super-pixels of two
+    horizontally adjacent pixels: the same bytes) and the output [N, OH, OW, K]
+    as [N, OH, OW/2, 2K]: output super-pixel p holds output columns 2p + q,
+    q in {0, 1}. Output column 2p + q, tap s reads input column 2p + q + s - pad_l,
+    i.e. super-pixel p + s' - pad_l' half `sub` with 2 s' - 2 pad_l' + sub =
+    q + s - pad_l, so the paired conv has S' = floor((S - pad_l) / 2) +
+    ceil(pad_l / 2) + 1 taps, left padding pad_l' = ceil(pad_l / 2) and
+    W'[q K + o, sub cs + c, r, s'] = w[o, c, r, 2 s' - 2 pad_l' + sub - q + pad_l]
+    where that tap exists (zero elsewhere, and for the padding channels
+    c >= C). Returns (W', S', pad_l')."""
+    k, c, R, S = wt.shape
+    pl2 = -(-pad_l // 2)
+    S2 = (S - pad_l) // 2 + pl2 + 1
+    out = np.zeros((2 * k, 2 * cs, R, S2), np.float32)
+    for q in range(2):
+        for s2 in range(S2):
+            for sub in range(2):
+                s_ = 2 * s2 - 2 * pl2 + sub - q + pad_l
+                if 0 <= s_ < S:
+                    out[q * k:(q + 1) * k, sub * cs:sub * cs + c, :, s2] = wt[:, :, :, s_]
+    return out, S2, pl2
+
+
+def pair_stem_columns(lo: Lowered) -> None:
+    """Compute the space-to-depth stem two output columns per GEMM row.
+
+    After the space-to-depth rewrite the stem is a 4x4 stride-1 conv over
+    16-channel (32-byte) pixels with 64 outputs: its A operand arrives as 16
+    small per-tap TMA loads per 128-pixel tile and its MMAs are only 64 wide.
+    Paired (see pair_weights), the same bytes are a 4x3 conv over 32-channel
+    super-pixels with 128 outputs: 64-byte taps, 128-wide MMAs, 12 loads per
+    256 output pixels instead of 32. Float dtypes; the output keeps its tensor
+    (identical bytes)."""
+    for st in lo.steps:
+        if st.kind != "conv" or not st.params.get("s2d") or st.params.get("residual"):
+            continue
+        if lo.dtype not in (L.BF16, L.F32):
+            continue
+        geom, wt, bias = lo.weights[st.params["weight"]]
+        k = geom["k"]
+        if (geom["sh"], geom["sw"], geom["dh"], geom["dw"]) != (1, 1, 1, 1) or geom["w"] % 2 or geom["ow"] % 2 \
+                or k % 8 or geom["groups"] != 1:
+            continue
+        cs = geom["cs"]
+        w2, s2, pl2 = pair_weights(wt, cs, geom["pl"])
+        b2 = np.zeros(round_up(2 * k, 16), np.float32)
+        b2[:k] = bias[:k]
+        b2[k:2 * k] = bias[:k]
+        g2 = dict(geom, w=geom["w"] // 2, c=2 * cs, cs=2 * cs, k=2 * k, s=s2, pl=pl2, ow=geom["ow"] // 2)
+        lo.weights[st.params["weight"]] = (g2, w2, b2)
+        st.params["paired"] = True
+
+
 def lower(graph, shapes: dict, dtype: int, s2d: bool = True) -> Lowered:
     """Lower a post-pass graph to backend steps. For 8-bit lowering the graph
     inputs are signed (symmetric int8, zero point 0: padded taps read real
