@@ -748,4 +748,5 @@ def lower(graph, shapes: dict, dtype: int, s2d: bool = True) -> Lowered:
             lo.tensors[name].dtype = L.S8
     if s2d:
         space_to_depth_stem(lo)
+        pair_stem_columns(lo)
     return lo
