@@ -98,7 +98,13 @@ class _Device:
             if self.q is not None:
                 cq = self.q.convs[wname]
                 ks = desc.k_stride
-                pad = lambda a, dt: np.concatenate([np.asarray(a, dt), np.zeros(ks - len(a), dt)])
+                # a paired stem computes two output columns per row: its per-channel
+                # parameters repeat for the second column
+                rep = 2 if geom.get("paired") else 1
+
+                def pad(a, dt):
+                    a = np.tile(np.asarray(a, dt), rep)
+                    return np.concatenate([a, np.zeros(ks - len(a), dt)])
                 self.wbuf[wname] = self.ctx.to_device(L.pack_weights(desc, cq.w_q))
                 self.bbuf[wname] = self.ctx.to_device(pad(cq.bias32, np.int32))
                 self.qbuf[wname] = {

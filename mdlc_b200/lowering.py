@@ -716,12 +716,11 @@ def pair_stem_columns(lo: Lowered) -> None:
     small per-tap TMA loads per 128-pixel tile and its MMAs are only 64 wide.
     Paired (see pair_weights), the same bytes are a 4x3 conv over 32-channel
     super-pixels with 128 outputs: 64-byte taps, 128-wide MMAs, 12 loads per
-    256 output pixels instead of 32. Float dtypes; the output keeps its tensor
-    (identical bytes)."""
+    256 output pixels instead of 32. The output keeps its tensor (identical
+    bytes); per-channel epilogue parameters are duplicated for the two output
+    columns (int8: by the executable, the quantisation plan keeps the graph's K)."""
     for st in lo.steps:
         if st.kind != "conv" or not st.params.get("s2d") or st.params.get("residual"):
-            continue
-        if lo.dtype not in (L.BF16, L.F32):
             continue
         geom, wt, bias = lo.weights[st.params["weight"]]
         k = geom["k"]
@@ -733,7 +732,8 @@ def pair_stem_columns(lo: Lowered) -> None:
         b2 = np.zeros(round_up(2 * k, 16), np.float32)
         b2[:k] = bias[:k]
         b2[k:2 * k] = bias[:k]
-        g2 = dict(geom, w=geom["w"] // 2, c=2 * cs, cs=2 * cs, k=2 * k, s=s2, pl=pl2, ow=geom["ow"] // 2)
+        g2 = dict(geom, w=geom["w"] // 2, c=2 * cs, cs=2 * cs, k=2 * k, s=s2, pl=pl2, ow=geom["ow"] // 2,
+                  paired=True, cs_unpaired=cs, pl_unpaired=geom["pl"], k_unpaired=k)
         lo.weights[st.params["weight"]] = (g2, w2, b2)
         st.params["paired"] = True
 

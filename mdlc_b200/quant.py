@@ -203,6 +203,8 @@ def build_plan(lo_f32, lo_i8, ranges: dict, graph, requant: str = "fixed") -> Qu
         w_q_orig = np.clip(np.rint(w_orig / s_w.reshape(k, 1, 1, 1)), -127, 127).astype(np.float32)
         if st.params.get("s2d"):
             w_q, _, _ = lowering.s2d_weights(w_q_orig, geom["pt_orig"], geom["pl_orig"])
+            if geom.get("paired"):   # two output columns per row: the same codes, re-indexed
+                w_q, _, _ = lowering.pair_weights(w_q, geom["cs_unpaired"], geom["pl_unpaired"])
         else:
             w_q = w_q_orig
         acc_scale = (np.float64(s_x) * s_w.astype(np.float64))

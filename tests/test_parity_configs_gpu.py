@@ -211,7 +211,10 @@ def _int8_accumulators(exe, g, feeds):
         finally:
             ctx.free(y)
         assert np.all(got[..., d32.k:] == 0)
-        got = got[..., :d32.k].transpose(0, 3, 1, 2).astype(np.int64)
+        got = got[..., :d32.k]
+        if st.params.get("paired"):   # [n, oh, ow/2, 2k] holds [n, oh, ow, k]
+            got = got.reshape(d32.n, d32.oh, 2 * d32.ow, d32.k // 2)
+        got = got.transpose(0, 3, 1, 2).astype(np.int64)
         bad = np.argwhere(got != acc.reshape(got.shape))
         assert bad.size == 0, (f"{st.label()}: {len(bad)} of {got.size} int32 accumulators differ; "
                                f"first {bad[0].tolist()}: device {got[tuple(bad[0])]} "

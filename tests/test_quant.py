@@ -99,9 +99,11 @@ def test_plan_structure_resnet18():
         assert cq.bias32.dtype == np.int32 and cq.rq_scale.dtype == np.float32
         if cq.deq_scale is None:
             assert np.all(cq.rq_scale > 0) and np.all(np.isfinite(cq.rq_scale))
-    # the stem's space-to-depth weights hold the same codes
+    # the stem's space-to-depth, column-paired weights hold the same codes, once
+    # for each of the two output columns of a row
     stem = next(c for w, c in plan.convs.items() if w.startswith("conv1"))
-    assert stem.w_q.shape[1] == 12 and np.abs(stem.w_q).sum() == np.abs(stem.w_q_orig).sum()
+    assert stem.w_q.shape[:2] == (128, 64) and np.abs(stem.w_q).sum() == 2 * np.abs(stem.w_q_orig).sum()
+    assert stem.bias32.shape == (64,)     # per-channel parameters keep the graph's K
 
 
 @pytest.mark.parametrize("name,kw", [("conv_bn_relu", dict(n=2, cin=3, cout=16, h=12, w=12)),

@@ -49,4 +49,6 @@ def test_resnet18_stem_is_paired_space_to_depth():
     assert (geom["w"], geom["ow"], geom["pl"]) == (16, 16, 1)
     assert geom["flops"] == 2.0 * 2 * 32 * 32 * 64 * 3 * 49     # algorithmic work of the 7x7 node
     lo8 = lowering.lower(g, S.infer(g, None), L.U8)
-    assert lo8.steps[0].params.get("s2d") and not lo8.steps[0].params.get("paired")
+    assert lo8.steps[0].params.get("s2d") and lo8.steps[0].params.get("paired")
+    g8 = lo8.weights[lo8.steps[0].params["weight"]][0]
+    assert (g8["cs"], g8["k"], g8["s"]) == (64, 128, 3)      # 32-byte int8 pixels -> 64-byte super-pixels
