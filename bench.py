@@ -422,6 +422,9 @@ def main() -> int:
     ap.add_argument("--ref-procs", type=int, default=0, help="reference arm: host processes (0 = every core)")
     ap.add_argument("--requant", default="fixed", choices=["fixed", "fp32"],
                     help="int8 workloads: requantisation form of the 8-bit conv epilogues")
+    ap.add_argument("--tune", default=None, metavar="CACHE",
+                    help="time every tile configuration of each conv shape the cache lacks on this GPU "
+                         "(mdlc_b200.tuner) and write the cache to CACHE")
     ap.add_argument("--forwards-only", action="store_true",
                     help="compile, stage the input and run --warmup forwards, then exit (no timing, no "
                          "JSON line): the program profiled by the committed ncu captures")
@@ -445,7 +448,17 @@ def main() -> int:
     if args.batch is None:
         args.batch = default_batch
     g = passes.default_pipeline(builders.BUILDERS[model](batch=args.batch, seed=0))
-    exe = mdlc_compile(g, dtype=dtype, devices=[local], **({"requant": args.requant} if dtype == "int8" else {}))
+    kw = {"requant": args.requant} if dtype == "int8" else {}
+    if args.tune:
+        from mdlc_b200 import _lib as L
+        from mdlc_b200 import tuner as T
+        tctx = L.Context(local)
+        cache = T.TuneCache(args.tune)
+        kw["tuner"] = T.Tuner(cache, ctx=tctx)
+    exe = mdlc_compile(g, dtype=dtype, devices=[local], **kw)
+    if args.tune:
+        cache.save()
+        tctx.close()
     dev = exe.devices[0]
     ins, outs = exe.pinned_inputs(), exe.pinned_outputs()
     rng = np.random.default_rng(1234 + rank)

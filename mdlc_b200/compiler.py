@@ -415,8 +415,14 @@ class Executable:
                  keep_all=False, calib=None, schedule_fn=None, requant="fixed"):
         if dtype not in DTYPES:
             raise ValueError(f"dtype must be one of {sorted(DTYPES)}")
-        if tuner is not None and schedule_fn is not None:
+        if tuner not in (None, False) and schedule_fn is not None:
             raise ValueError("give either tuner= or schedule_fn=, not both")
+        if tuner is None and schedule_fn is None:
+            # the shipped per-shape cache of measured tile configurations
+            # (mdlc_b200/tune_cache.json); shapes it lacks keep the library heuristic
+            tuner = tuner_mod.Tuner(model=False)
+        elif tuner is False:
+            tuner = None
         self.schedule_fn = schedule_fn
         self.schedules = {}   # weight name -> (bn, stages) chosen through a hook
         self.node_by_name = {n.name: n for n in graph.nodes}

@@ -29,9 +29,11 @@ import numpy as np
 from mdlc_b200 import _lib as L
 
 CONFIGS = ((64, 3), (128, 2), (256, 3), (192, 3), (64, 8), (128, 4))
-KERNEL_TAG = "conv_tc_v2"
+# fp32 (3xTF32) keeps hi and lo stages: its own tile set
+CONFIGS_F32 = ((64, 3), (128, 2), (256, 2))
+KERNEL_TAG = "conv_tc_v3"
 # resident CTAs per SM of each configuration (shared memory <= 113 KB: two)
-CTAS_PER_SM = {(64, 3): 2, (128, 2): 2, (256, 3): 1, (192, 3): 1, (64, 8): 1, (128, 4): 1}
+CTAS_PER_SM = {(64, 3): 2, (128, 2): 2, (256, 3): 1, (192, 3): 1, (64, 8): 1, (128, 4): 1, (256, 2): 1}
 # Cost-model constants, fitted to B200 measurements of this kernel (b=256
 # ResNet-18 layers, CUDA events): tensor-pipe cycles of one 128 x bn x 16 bf16
 # MMA with operands fresh from the stage ring; the cycles one CTA's issuing
@@ -41,6 +43,10 @@ CTAS_PER_SM = {(64, 3): 2, (128, 2): 2, (256, 3): 1, (192, 3): 1, (64, 8): 1, (1
 # that bounds an SM's L2 -> shared-memory bandwidth to the bytes its stage
 # rings hold in flight (Little's law), up to a sustained maximum.
 MMA_CYCLES = {64: 63.0, 128: 64.0, 192: 96.0, 256: 128.0}
+
+
+def configs_for(dtype) -> tuple:
+    return CONFIGS_F32 if dtype == L.F32 else CONFIGS
 ISSUE_GAP = 560.0
 LOAD_LATENCY = 2700.0
 L2_MAX_BYTES_PER_CYCLE = 64.0
@@ -192,12 +198,12 @@ def tune(shape: ConvShape, ctx: L.Context | None = None, iters: int = 10):
     """Best (bn, stages) for ``shape``: measured on ``ctx`` if given, else modeled."""
     ranking = []
     if ctx is None:
-        for bn, st in CONFIGS:
+        for bn, st in configs_for(shape.dtype):
             ranking.append(((bn, st), analytical_cost(shape, bn, st)))
     else:
         bench = _Bench(ctx, shape)
         try:
-            for bn, st in CONFIGS:
+            for bn, st in configs_for(shape.dtype):
                 try:
                     ranking.append(((bn, st), bench.time_ms(bn, st, iters=iters)))
                 except L.MdlcError as e:
@@ -211,12 +217,19 @@ def tune(shape: ConvShape, ctx: L.Context | None = None, iters: int = 10):
 
 
 class Tuner:
-    """Cache-backed tile-config oracle, callable as ``tuner(kind, geom)``."""
+    """Cache-backed tile-config oracle, callable as ``tuner(kind, geom)``.
 
-    def __init__(self, cache: TuneCache | None = None, ctx: L.Context | None = None, iters: int = 10):
+    A shape in the cache gets its cached configuration. Otherwise: with a
+    context, every configuration is timed on the device and the best cached;
+    without one, the cost model ranks them (``model=True``) or the library's
+    own heuristic decides (``None`` is returned)."""
+
+    def __init__(self, cache: TuneCache | None = None, ctx: L.Context | None = None, iters: int = 10,
+                 model: bool = True):
         self.cache = cache or TuneCache()
         self.ctx = ctx
         self.iters = iters
+        self.model = model
 
     def __call__(self, kind, geom):
         if kind != "conv" or geom.get("groups", 1) != 1:
@@ -228,9 +241,39 @@ class Tuner:
         cached = self.cache.get(shape.key())
         if cached:
             return cached
+        if self.ctx is None and not self.model:
+            return None
         cfg, metric, _ = tune(shape, self.ctx, self.iters)
         self.cache.put(shape.key(), cfg, metric, self.ctx is not None)
         return cfg
+
+
+TILE_WIDTHS = (64, 128, 192, 256)
+
+
+def from_reference_schedule(schedule_fn, node, geom):
+    """Tile choice for one conv from the reference's schedule hook.
+
+    The reference codegen calls ``schedule_fn(node, (M, N, K))``
+    (``mdlc/codegen/cuda/emit.py:27,100``; ``autotuner/tuner.py:164-174``'s
+    ``Tuner`` is such a callable) and tiles its GEMM with the returned
+    ``GemmSchedule`` (``mdlc/codegen/schedule.py:16-31``: ``BM x BN`` block
+    tile). Here the hook is called with the same (M, N, K) for the same node
+    (conv: (OC, OH*OW, C/g*KH*KW); Gemm / MatMul: (rows, out features, in
+    features)), and the schedule's tile along the output-channel axis (``BM``
+    for a conv, where the reference puts output channels on M; ``BN`` for a
+    GEMM) picks this kernel's tile width ``bn``: the smallest of 64 / 128 / 192
+    / 256 that covers it. The pipeline depth stays the library's choice for
+    that width. A hook returning a ``(bn, stages)`` tuple sets both directly;
+    ``None`` keeps the defaults. Returns ``(bn, stages)`` or None."""
+    sched = schedule_fn(node, tuple(geom["ref_mnk"]))
+    if sched is None:
+        return None
+    if isinstance(sched, tuple):
+        return int(sched[0]), int(sched[1])
+    width = int(getattr(sched, "BM" if geom["ref_channel_axis"] == "M" else "BN"))
+    bn = next((w for w in TILE_WIDTHS if w >= width), TILE_WIDTHS[-1])
+    return bn, 0
 
 
 def main():
@@ -265,30 +308,3 @@ def main():
 if __name__ == "__main__":
     raise SystemExit(main())
 
-
-TILE_WIDTHS = (64, 128, 192, 256)
-
-
-def from_reference_schedule(schedule_fn, node, geom):
-    """Tile choice for one conv from the reference's schedule hook.
-
-    The reference codegen calls ``schedule_fn(node, (M, N, K))``
-    (``mdlc/codegen/cuda/emit.py:27,100``; ``autotuner/tuner.py:164-174``'s
-    ``Tuner`` is such a callable) and tiles its GEMM with the returned
-    ``GemmSchedule`` (``mdlc/codegen/schedule.py:16-31``: ``BM x BN`` block
-    tile). Here the hook is called with the same (M, N, K) for the same node
-    (conv: (OC, OH*OW, C/g*KH*KW); Gemm / MatMul: (rows, out features, in
-    features)), and the schedule's tile along the output-channel axis (``BM``
-    for a conv, where the reference puts output channels on M; ``BN`` for a
-    GEMM) picks this kernel's tile width ``bn``: the smallest of 64 / 128 / 192
-    / 256 that covers it. The pipeline depth stays the library's choice for
-    that width. A hook returning a ``(bn, stages)`` tuple sets both directly;
-    ``None`` keeps the defaults. Returns ``(bn, stages)`` or None."""
-    sched = schedule_fn(node, tuple(geom["ref_mnk"]))
-    if sched is None:
-        return None
-    if isinstance(sched, tuple):
-        return int(sched[0]), int(sched[1])
-    width = int(getattr(sched, "BM" if geom["ref_channel_axis"] == "M" else "BN"))
-    bn = next((w for w in TILE_WIDTHS if w >= width), TILE_WIDTHS[-1])
-    return bn, 0
