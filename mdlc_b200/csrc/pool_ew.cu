@@ -474,6 +474,96 @@ extern "C" int mdlc_pool2d(mdlc_ctx* ctx, const mdlc_pool_desc* d, const void* x
   return mdlc_cuda_status(ctx, cudaGetLastError(), "pool launch");
 }
 
+namespace mdlc {
+namespace {
+
+// Fast path of the interpreter for out = [unary](in0 (op) in1): two inputs, in0
+// full, in1 broadcast per the given mode, one binary instruction and at most
+// one unary one after it (the squeeze-excite multiply, a residual add + act
+// not absorbed into a conv). Values stay in registers (the interpreter's
+// register file is indexed at run time and lives in local memory).
+template <typename T, int BC>
+__global__ void __launch_bounds__(256) eltwise_binary_kernel(const mdlc_ew_prog p, const void* in0, const void* in1,
+                                                             void* out0, int bop, int uop, float u0, float u1,
+                                                             long long total) {
+  const int G = p.c_stride >> 3;
+  const long long hwG = (long long)p.hw * G;
+  float bs = 0.0f;
+  if (BC == MDLC_BC_SCALAR)
+    bs = (sizeof(T) == 2) ? __bfloat162float(*static_cast<const __nv_bfloat16*>(in1)) : *static_cast<const float*>(in1);
+  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int g = (int)(idx % G);
+    float a[8], b[8];
+    V8<T>::load(static_cast<const char*>(in0) + idx * 8 * V8<T>::kBytes, a);
+    if (BC == MDLC_BC_SCALAR) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) b[e] = bs;
+    } else {
+      const long long off = BC == MDLC_BC_FULL ? idx * 8 : (BC == MDLC_BC_NC ? (idx / hwG) * p.c_stride + g * 8 : g * 8);
+      V8<T>::load(static_cast<const char*>(in1) + off * V8<T>::kBytes, b);
+    }
+    float r[8];
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      switch (bop) {
+        case MDLC_EW_ADD: r[e] = a[e] + b[e]; break;
+        case MDLC_EW_SUB: r[e] = a[e] - b[e]; break;
+        case MDLC_EW_MUL: r[e] = a[e] * b[e]; break;
+        case MDLC_EW_DIV: r[e] = a[e] / b[e]; break;
+        case MDLC_EW_MAX: r[e] = fmaxf(a[e], b[e]); break;
+        default: r[e] = fminf(a[e], b[e]); break;
+      }
+    }
+    if (uop >= 0) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) r[e] = ew_unary(uop, r[e], u0, u1);
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) r[e] = (g * 8 + e < p.c) ? r[e] : 0.0f;
+    V8<T>::store(static_cast<char*>(out0) + idx * 8 * V8<T>::kBytes, r);
+  }
+}
+
+bool is_binary(int op) { return op <= MDLC_EW_DIV || op == MDLC_EW_MAX || op == MDLC_EW_MIN; }
+
+// Runs the program on the fast path when it has that shape; false otherwise.
+template <typename T>
+bool eltwise_fast(mdlc_ctx* ctx, const mdlc_ew_prog* p, const void* const* in, void* const* out, long long total) {
+  if (p->n_inputs != 2 || p->n_outputs != 1 || p->bcast[0] != MDLC_BC_FULL || p->n_instr < 1 || p->n_instr > 2)
+    return false;
+  const mdlc_ew_instr& b = p->code[0];
+  if (!is_binary(b.op) || b.src0 != 0 || b.src1 != 1 || b.dst < 2) return false;
+  int uop = -1;
+  float u0 = 0.0f, u1 = 0.0f;
+  int last = b.dst;
+  if (p->n_instr == 2) {
+    const mdlc_ew_instr& u = p->code[1];
+    if (is_binary(u.op) || u.src0 != b.dst) return false;
+    uop = u.op, u0 = u.imm0, u1 = u.imm1, last = u.dst;
+  }
+  if (p->out_reg[0] != last) return false;
+  const unsigned grid = grid_for(ctx, total);
+  switch (p->bcast[1]) {
+    case MDLC_BC_FULL:
+      eltwise_binary_kernel<T, MDLC_BC_FULL><<<grid, 256, 0, ctx->stream>>>(*p, in[0], in[1], out[0], b.op, uop, u0, u1, total);
+      break;
+    case MDLC_BC_NC:
+      eltwise_binary_kernel<T, MDLC_BC_NC><<<grid, 256, 0, ctx->stream>>>(*p, in[0], in[1], out[0], b.op, uop, u0, u1, total);
+      break;
+    case MDLC_BC_C:
+      eltwise_binary_kernel<T, MDLC_BC_C><<<grid, 256, 0, ctx->stream>>>(*p, in[0], in[1], out[0], b.op, uop, u0, u1, total);
+      break;
+    default:
+      eltwise_binary_kernel<T, MDLC_BC_SCALAR><<<grid, 256, 0, ctx->stream>>>(*p, in[0], in[1], out[0], b.op, uop, u0, u1, total);
+      break;
+  }
+  return true;
+}
+
+}  // namespace
+}  // namespace mdlc
+
 extern "C" int mdlc_eltwise(mdlc_ctx* ctx, const mdlc_ew_prog* p, const void* const* inputs,
                             void* const* outputs) {
   if (!ctx) return MDLC_ERR_INVALID;
@@ -502,6 +592,11 @@ extern "C" int mdlc_eltwise(mdlc_ctx* ctx, const mdlc_ew_prog* p, const void* co
   }
   cudaSetDevice(ctx->device);
   const long long total = (long long)p->n * p->hw * (p->c_stride / 8);
+  if ((p->dtype == MDLC_BF16 && eltwise_fast<__nv_bfloat16>(ctx, p, in, out, total)) ||
+      (p->dtype == MDLC_F32 && eltwise_fast<float>(ctx, p, in, out, total))) {
+    mdlc_note_launch(ctx);
+    return mdlc_cuda_status(ctx, cudaGetLastError(), "eltwise launch");
+  }
   if (p->dtype == MDLC_BF16)
     eltwise_kernel<__nv_bfloat16><<<grid_for(ctx, total), 256, 0, ctx->stream>>>(*p, in[0], in[1], in[2], in[3],
                                                                                  out[0], out[1], total);

@@ -584,6 +584,57 @@ def test_eltwise_program(ctx, dtype):
     check(outs[1], want1, 1e-2 if dt == L.BF16 else 1e-6)
 
 
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+@pytest.mark.parametrize("mode,op,post", [(L.BC_FULL, L.EW_ADD, L.EW_RELU), (L.BC_NC, L.EW_MUL, None),
+                                          (L.BC_C, L.EW_SUB, L.EW_SIGMOID), (L.BC_SCALAR, L.EW_MUL, L.EW_CLIP)])
+def test_eltwise_binary_fast_path(ctx, dtype, mode, op, post):
+    """Programs of the form [unary](in0 (op) in1), in1 broadcast full / per (n, c)
+    / per c / scalar, take the register-resident fast path; same results."""
+    rng = np.random.default_rng(19 + mode)
+    n, c, h, w = 3, 44, 6, 5
+    cs = _rnd8(c)
+    dt = L.BF16 if dtype == "bf16" else L.F32
+    a = rng.standard_normal((n, c, h, w)).astype(np.float32)
+    bshape = {L.BC_FULL: (n, c, h, w), L.BC_NC: (n, c, 1, 1), L.BC_C: (1, c, 1, 1), L.BC_SCALAR: (1, 1, 1, 1)}[mode]
+    b = rng.standard_normal(bshape).astype(np.float32)
+    conv = (lambda t: bf16_bits(t)) if dt == L.BF16 else (lambda t: t)
+    ad = ctx.to_device(conv(nhwc(a, cs)))
+    if mode == L.BC_SCALAR:
+        bd = ctx.to_device(conv(b.reshape(1)))
+    elif mode == L.BC_C:
+        bd = ctx.to_device(conv(nhwc(b, cs)).reshape(-1))
+    else:
+        bd = ctx.to_device(conv(nhwc(b, cs)))
+    eb = 2 if dt == L.BF16 else 4
+    yd = ctx.alloc(n * h * w * cs * eb)
+    ctx.memset(yd, 0xFF, n * h * w * cs * eb)
+    prog = L.EwProg(n=n, hw=h * w, c=c, c_stride=cs, dtype=dt, n_inputs=2, n_outputs=1,
+                    n_instr=1 if post is None else 2)
+    prog.bcast[0], prog.bcast[1] = L.BC_FULL, mode
+    prog.code[0] = L.EwInstr(op=op, dst=2, src0=0, src1=1)
+    if post is not None:
+        prog.code[1] = L.EwInstr(op=post, dst=3, src0=2, src1=0, imm0=-0.5, imm1=0.75)
+    prog.out_reg[0] = 2 if post is None else 3
+    ctx.eltwise(prog, [ad, bd], [yd])
+    ctx.sync()
+    y = ctx.download(yd, (n, h, w, cs), np.uint16 if dt == L.BF16 else np.float32)
+    y = from_bf16_bits(y) if dt == L.BF16 else y
+    assert np.all(y[..., c:] == 0)
+    got = y[..., :c].transpose(0, 3, 1, 2)
+    if dt == L.BF16:
+        a, b = oref.round_bf16(a), oref.round_bf16(b)
+    r = {L.EW_ADD: a + b, L.EW_MUL: a * b, L.EW_SUB: a - b}[op]
+    if post == L.EW_RELU:
+        r = np.maximum(r, 0)
+    elif post == L.EW_SIGMOID:
+        r = 1 / (1 + np.exp(-r))
+    elif post == L.EW_CLIP:
+        r = np.clip(r, -0.5, 0.75)
+    check(got, r, 1e-2 if dt == L.BF16 else 1e-6)
+    for p_ in (ad, bd, yd):
+        ctx.free(p_)
+
+
 @pytest.mark.parametrize("dtype", [L.BF16, L.F32])
 def test_layout_roundtrip(ctx, dtype):
     rng = np.random.default_rng(19)
