@@ -47,6 +47,14 @@ from mdlc_b200 import shapes as S
 DTYPES = {"bf16": L.BF16, "fp32": L.F32, "f32": L.F32, "int8": L.U8}
 
 
+def _bf16_bits(a: np.ndarray) -> np.ndarray:
+    """fp32 -> bf16 bit patterns, round to nearest even (NaN stays a quiet NaN)."""
+    u = np.ascontiguousarray(a, np.float32).view(np.uint32)
+    r = (u + (((u >> 16) & 1) + 0x7FFF)) >> 16
+    r = np.where(np.isnan(a), 0x7FC0, r)
+    return r.astype(np.uint16)
+
+
 def _has_static_shapes(graph) -> bool:
     vi = graph.value_info
     for n in graph.nodes:
@@ -118,7 +126,9 @@ class _Device:
                 packed = L.pack_weights(desc, wt)
                 self.wbuf[wname] = self.ctx.to_device(packed)
                 self.bbuf[wname] = self.ctx.to_device(bias)
-        self.cbuf = {name: self.ctx.to_device(arr) for name, arr in lo.consts.items()}
+        # elementwise constant operands are read in the tensors' own dtype
+        self.cbuf = {name: self.ctx.to_device(_bf16_bits(arr) if lo.dtype == L.BF16 else arr)
+                     for name, arr in lo.consts.items()}
         # staging: fp32 NCHW feeds / outputs on device and pinned on the host, in
         # two slots (slot 1 allocated on first use) so that one slot's upload can
         # overlap the other slot's forward

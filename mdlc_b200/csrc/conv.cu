@@ -71,7 +71,7 @@ __global__ void __launch_bounds__(256) conv_dw_kernel(const DwArgs a) {
     float acc[8];
     if (a.bias) {
 #pragma unroll
-      for (int e = 0; e < 8; ++e) acc[e] = __ldg(a.bias + c0 + e);
+      for (int e = 0; e < 8; ++e) acc[e] = c0 + e < a.c ? __ldg(a.bias + c0 + e) : 0.0f;
     } else {
 #pragma unroll
       for (int e = 0; e < 8; ++e) acc[e] = 0.0f;
@@ -153,7 +153,7 @@ __global__ void __launch_bounds__(128) conv_dw3_kernel(const DwArgs a, int strip
     for (int tap = 0; tap < 9; ++tap) Vec8<float>::load(a.w + tap * a.cs + c0, w[tap]);
     float bias[8];
 #pragma unroll
-    for (int e = 0; e < 8; ++e) bias[e] = a.bias ? __ldg(a.bias + c0 + e) : 0.0f;
+    for (int e = 0; e < 8; ++e) bias[e] = (a.bias && c0 + e < a.c) ? __ldg(a.bias + c0 + e) : 0.0f;
     const int iw0 = ox * a.sw - a.pl;
     const bool cv0 = (unsigned)iw0 < (unsigned)a.w_, cv1 = (unsigned)(iw0 + 1) < (unsigned)a.w_,
                cv2 = (unsigned)(iw0 + 2) < (unsigned)a.w_;

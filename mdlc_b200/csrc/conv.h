@@ -23,6 +23,12 @@ int conv_grouped(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const fl
 // does not fit it (the caller then uses conv_dw)
 int conv_dw_tma(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const float* w, const float* bias,
                 const void* res, void* y, const mdlc_epilogue* epi);
+// its tile for one layer: channel block (elements), threads as quads x column
+// pairs x row groups, rows per thread, output tile, input window, stage ring
+struct DwTileChoice {
+  int cb, quads, pairs, groups, rows, th, tw, ih, iw, stage_bytes, stages;
+};
+DwTileChoice choose_dw_tile(int c_stride, int esz, int oh, int ow, int n, int sh);
 // cuTensorMapEncodeTiled from the driver (null when unavailable)
 PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder();
 

@@ -256,6 +256,8 @@ int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w
   // default. Not in halo mode.
   a.split = 1;
   a.kps = num_kb;
+  // fp32: promote the accumulator every 4 k-blocks (128 reduction elements)
+  a.kchunk = esz == 4 ? 4 : 0;
   a.ws = ctx->d_split_ws;
   a.counters = ctx->d_split_cnt;
   if (cfg && ((cfg->flags >> 8) & 0xFF) > 1) {

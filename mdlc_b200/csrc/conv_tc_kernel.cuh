@@ -100,6 +100,13 @@ struct TcArgs {
   // (counted in `counters`, left at zero) sums the slices in slice order and
   // runs the epilogue
   int split, kps;
+  // fp32 (3xTF32) accumulator promotion every `kchunk` k-blocks (0: none). The
+  // tensor cores add each MMA's products into their fp32 accumulator with
+  // truncation, so over a deep reduction the error grows with the
+  // accumulator's magnitude. With promotion every chunk is accumulated from
+  // zero in a TMEM slot, and the epilogue warps add the chunks, in order, into
+  // a running sum (another TMEM region) with round-to-nearest fp32 adds.
+  int kchunk;
   // element extents of x, y and the residual (checked build only)
   long long x_elems, y_elems, res_elems;
   uint32_t* ws;
@@ -326,8 +333,17 @@ __global__ void __launch_bounds__(threads_for<ESZ>(), (Occ<BN, STAGES, ESZ, AMOD
   using L = Smem<BN, STAGES, ESZ, AMODE>;
   constexpr int KB = 128 / ESZ;    // k-block elements (128 bytes)
   constexpr int CHUNK = 16 / ESZ;  // elements per 16-byte chunk
-  // two accumulators of BN columns; allocations are powers of two (192 -> 512)
-  constexpr uint32_t kTmemCols = 2 * BN > 256 ? 512u : (uint32_t)(2 * BN);
+  // Accumulator slots of BN columns, used round-robin by units (or, with fp32
+  // promotion, by k-chunks): two, or one for fp32 at BN = 256. fp32 adds the
+  // running sum of the promoted chunks after them. Allocations are powers of
+  // two (192 -> 256, 384 -> 512).
+  constexpr int kSlots = (ESZ == 4 && BN > 128) ? 1 : 2;
+  constexpr uint32_t kRunCol = (uint32_t)(kSlots * BN);
+  constexpr int kUsedCols = (kSlots + (ESZ == 4 ? 1 : 0)) * BN;
+  constexpr uint32_t kTmemCols = kUsedCols > 256 ? 512u : (kUsedCols > 128 ? 256u : (uint32_t)kUsedCols);
+  static_assert(kUsedCols <= 512, "TMEM holds 512 columns");
+  // k-blocks per accumulator use: a chunk (fp32 promotion) or the whole unit
+  const int kchunk = (ESZ == 4 && a.kchunk > 0) ? a.kchunk : (1 << 30);
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -552,21 +568,67 @@ __global__ void __launch_bounds__(threads_for<ESZ>(), (Occ<BN, STAGES, ESZ, AMOD
     int res_pending = -1;                 // residual buffer with a load in flight not yet awaited
     uint32_t res_pending_par = 0;
     volatile int* last_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 8);
+    int lc = 0;  // accumulator slot uses so far (the MMA issuer counts the same way)
     for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++local) {
       const int tile = u / S;
-      const int buf = local & 1;
+      const int buf = local & 1;  // parity of the per-tile shared-memory parameters
       const int m0 = (tile / a.num_n_tiles) * kBM;
       const int n0 = (tile % a.num_n_tiles) * BN;
+      // the unit's accumulator: its slot (one use), or with fp32 promotion
+      // over several chunks the running sum they are added into here
+      const int nchunks = (kb_end(u) - kb_begin(u) + kchunk - 1) / kchunk;
+      const int slot = lc % kSlots;
+      const uint32_t slot_par = (uint32_t)(lc / kSlots) & 1;
+      uint32_t acc_col = (uint32_t)(slot * BN);
+      bool acc_ready = false, promoted = false;
+      if (ESZ == 4 && nchunks > 1) {
+        const uint32_t run = tmem + lane_base + kRunCol;
+        bool okc = true;
+        for (int q = 0; q < nchunks; ++q, ++lc) {
+          const int cslot = lc % kSlots;
+          okc = mbar_wait(tfull(cslot), (uint32_t)(lc / kSlots) & 1, abort_flag, a.err, a.wait_cycles);
+          if (!__all_sync(0xffffffffu, okc)) {
+            okc = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t part = tmem + lane_base + (uint32_t)(cslot * BN);
+#pragma unroll 1
+          for (int c = 0; c < BN; c += 16) {
+            uint32_t v[16];
+            tmem_ld16(part + c, v);
+            if (q > 0) {
+              uint32_t r[16];
+              tmem_ld16(run + c, r);
+              tmem_ld_wait();
+#pragma unroll
+              for (int e = 0; e < 16; ++e) v[e] = __float_as_uint(__fadd_rn(__uint_as_float(r[e]), __uint_as_float(v[e])));
+            } else {
+              tmem_ld_wait();
+            }
+            tmem_st16(run + c, v);
+          }
+          tmem_st_wait();
+          tc_fence_before();
+          mbar_arrive(tempty(cslot));  // the slot takes the next chunk
+        }
+        if (!okc) break;
+        acc_col = kRunCol;
+        acc_ready = promoted = true;
+      } else {
+        ++lc;
+      }
       // split-K: every unit writes its raw accumulators to the workspace; a
       // unit that is not its tile's last releases the accumulator and moves
       // on, the last one sums all slices (in slice order) back into its own
       // accumulator and runs the epilogue below on it
-      bool acc_ready = false;
       if (S > 1) {
-        const bool okp = mbar_wait(tfull(buf), (local >> 1) & 1, abort_flag, a.err, a.wait_cycles);
-        if (!__all_sync(0xffffffffu, okp)) break;
-        tc_fence_after();
-        const uint32_t tacc = tmem + lane_base + (uint32_t)(buf * BN);
+        if (!promoted) {
+          const bool okp = mbar_wait(tfull(slot), slot_par, abort_flag, a.err, a.wait_cycles);
+          if (!__all_sync(0xffffffffu, okp)) break;
+          tc_fence_after();
+        }
+        const uint32_t tacc = tmem + lane_base + acc_col;
         const size_t row = (size_t)(ew * 32 + lane);
         // (checked build: a workspace row out of range is recorded and not written)
         const bool ws_ok = MDLC_CHECK_IDX(a.err, ((size_t)u * kBM + row + 1) * BN - 1, kSplitWsBytes / 4);
@@ -585,8 +647,10 @@ __global__ void __launch_bounds__(threads_for<ESZ>(), (Occ<BN, STAGES, ESZ, AMOD
         if (etid == 0) *last_flag = atomicAdd(a.counters + tile, 1) == S - 1;
         asm volatile("bar.sync 1, 128;" ::: "memory");
         if (!*last_flag) {
-          tc_fence_before();
-          mbar_arrive(tempty(buf));
+          if (!promoted) {
+            tc_fence_before();
+            mbar_arrive(tempty(slot));
+          }
           continue;
         }
         __threadfence();
@@ -672,13 +736,13 @@ __global__ void __launch_bounds__(threads_for<ESZ>(), (Occ<BN, STAGES, ESZ, AMOD
       }
       bool ok = true;
       if (!acc_ready) {
-        ok = mbar_wait(tfull(buf), (local >> 1) & 1, abort_flag, a.err, a.wait_cycles);
+        ok = mbar_wait(tfull(slot), slot_par, abort_flag, a.err, a.wait_cycles);
         ok = __all_sync(0xffffffffu, ok);
         if (!ok) break;
         tc_fence_after();
       }
       const int m = m0 + ew * 32 + lane;
-      const uint32_t taddr = tmem + lane_base + (uint32_t)(buf * BN);
+      const uint32_t taddr = tmem + lane_base + acc_col;
       if (tma_epi) {
         // 64-column chunks: TMEM -> registers -> (+bias, +residual tile, act) ->
         // bf16 in a 128B-swizzled staging tile (8-bit: requantised codes in a
@@ -899,8 +963,10 @@ __global__ void __launch_bounds__(threads_for<ESZ>(), (Occ<BN, STAGES, ESZ, AMOD
           if (m < a.M) store_chunk16<ESZ>(a, m, n0 + c0, v);
         }
       }
-      tc_fence_before();
-      mbar_arrive(tempty(buf));
+      if (!promoted) {
+        tc_fence_before();
+        mbar_arrive(tempty(slot));
+      }
     }
     // a residual load still in flight (the loop was left on an abort) must land
     // before the CTA's shared memory is released
@@ -1034,60 +1100,64 @@ __global__ void __launch_bounds__(threads_for<ESZ>(), (Occ<BN, STAGES, ESZ, AMOD
     } else if (lane == 0) {
       const uint32_t idesc =
           ESZ == 4 ? idesc_tf32(kBM, BN) : (ESZ == 2 ? idesc_bf16(kBM, BN) : idesc_i8(kBM, BN, a.a_signed, 1));
-      int it = 0, local = 0;
+      int it = 0, lc = 0;
       bool ok = true;
-      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x, ++local) {
-        const int buf = local & 1;
-        if (!mbar_wait(tempty(buf), ((local >> 1) & 1) ^ 1, abort_flag, a.err, a.wait_cycles)) {
-          ok = false;
-          break;
-        }
-        tc_fence_after();
-        const uint32_t d = tmem + (uint32_t)(buf * BN);
-        const int kb0 = kb_begin(u);
-        for (int kb = kb0; kb < kb_end(u); ++kb, ++it) {
-          const int st = it % STAGES;
-          const uint32_t par = (it / STAGES) & 1;
-          // fp32: wait for the split warps (the stage's A and B have landed and A
-          // is split into hi / lo parts)
-          if (!mbar_wait(ESZ == 4 ? splitA(st) : fullA(st), par, abort_flag, a.err, a.wait_cycles)) {
+      for (int u = blockIdx.x; u < num_units && ok; u += gridDim.x) {
+        const int kb_last = kb_end(u);
+        // one accumulator slot use per chunk of k-blocks (per unit without fp32 promotion)
+        for (int kb0 = kb_begin(u); kb0 < kb_last && ok; kb0 += kchunk, ++lc) {
+          const int slot = lc % kSlots;
+          if (!mbar_wait(tempty(slot), ((uint32_t)(lc / kSlots) & 1) ^ 1, abort_flag, a.err, a.wait_cycles)) {
             ok = false;
             break;
           }
-          // cp.async (and the split warps' stores) write A through the generic
-          // proxy: order them before the async-proxy operand reads of
-          // tcgen05.mma. TMA-written operands are ordered by the mbarrier
-          // completion itself.
-          if constexpr (AMODE == 0 || ESZ == 4) {
-            fence_proxy_async_smem();
-            tc_fence_after();
-          }
-          const uint32_t ab = sA + st * kABytes, bb = sB + st * L::kBBytes;
-          auto adesc = [&](uint32_t base, int kq) {
-            return AMODE == 2   ? umma_desc_k(base + kq * (kABytes / 4), 256, 6)
-                   : AMODE == 3 ? umma_desc_k(base + (kq >> 1) * (kABytes / 2) + (kq & 1) * 32, 512, 4)
-                                : umma_desc_sw128(base + kq * 32);
-          };
-#pragma unroll
-          for (int kq = 0; kq < 4; ++kq) {
-            const uint64_t ad = adesc(ab, kq);
-            const uint64_t bd = umma_desc_sw128(bb + kq * 32);
-            if constexpr (ESZ == 4) {
-              // 3xTF32: a*b ~ ahi*bhi + ahi*blo + alo*bhi (alo*blo ~ 2^-22 |ab| dropped)
-              const uint64_t ad_lo = adesc(sALo + st * kABytes, kq);
-              const uint64_t bd_lo = umma_desc_sw128(bb + BN * 128 + kq * 32);
-              umma_tf32(d, ad, bd, idesc, (kb != kb0) || kq != 0);
-              umma_tf32(d, ad, bd_lo, idesc, 1);
-              umma_tf32(d, ad_lo, bd, idesc, 1);
-            } else if constexpr (ESZ == 2) {
-              umma_bf16(d, ad, bd, idesc, (kb != kb0) || kq != 0);
-            } else {
-              umma_i8(d, ad, bd, idesc, (kb != kb0) || kq != 0);
+          tc_fence_after();
+          const uint32_t d = tmem + (uint32_t)(slot * BN);
+          const int kb1 = kb_last - kb0 > kchunk ? kb0 + kchunk : kb_last;
+          for (int kb = kb0; kb < kb1; ++kb, ++it) {
+            const int st = it % STAGES;
+            const uint32_t par = (it / STAGES) & 1;
+            // fp32: wait for the split warps (the stage's A and B have landed and A
+            // is split into hi / lo parts)
+            if (!mbar_wait(ESZ == 4 ? splitA(st) : fullA(st), par, abort_flag, a.err, a.wait_cycles)) {
+              ok = false;
+              break;
             }
+            // cp.async (and the split warps' stores) write A through the generic
+            // proxy: order them before the async-proxy operand reads of
+            // tcgen05.mma. TMA-written operands are ordered by the mbarrier
+            // completion itself.
+            if constexpr (AMODE == 0 || ESZ == 4) {
+              fence_proxy_async_smem();
+              tc_fence_after();
+            }
+            const uint32_t ab = sA + st * kABytes, bb = sB + st * L::kBBytes;
+            auto adesc = [&](uint32_t base, int kq) {
+              return AMODE == 2   ? umma_desc_k(base + kq * (kABytes / 4), 256, 6)
+                     : AMODE == 3 ? umma_desc_k(base + (kq >> 1) * (kABytes / 2) + (kq & 1) * 32, 512, 4)
+                                  : umma_desc_sw128(base + kq * 32);
+            };
+#pragma unroll
+            for (int kq = 0; kq < 4; ++kq) {
+              const uint64_t ad = adesc(ab, kq);
+              const uint64_t bd = umma_desc_sw128(bb + kq * 32);
+              if constexpr (ESZ == 4) {
+                // 3xTF32: a*b ~ ahi*bhi + ahi*blo + alo*bhi (alo*blo ~ 2^-22 |ab| dropped)
+                const uint64_t ad_lo = adesc(sALo + st * kABytes, kq);
+                const uint64_t bd_lo = umma_desc_sw128(bb + BN * 128 + kq * 32);
+                umma_tf32(d, ad, bd, idesc, (kb != kb0) || kq != 0);
+                umma_tf32(d, ad, bd_lo, idesc, 1);
+                umma_tf32(d, ad_lo, bd, idesc, 1);
+              } else if constexpr (ESZ == 2) {
+                umma_bf16(d, ad, bd, idesc, (kb != kb0) || kq != 0);
+              } else {
+                umma_i8(d, ad, bd, idesc, (kb != kb0) || kq != 0);
+              }
+            }
+            umma_commit(empty(st));
           }
-          umma_commit(empty(st));
+          if (ok) umma_commit(tfull(slot));
         }
-        if (ok) umma_commit(tfull(buf));
       }
       if (!ok) {
         umma_commit(drain);

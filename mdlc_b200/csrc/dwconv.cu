@@ -1,41 +1,38 @@
-// Depthwise 3x3 convolution with the input halo staged in shared memory by TMA.
+// Depthwise 3x3 convolution with the input window staged in shared memory by TMA.
 //
 // Reference semantics: the grouped conv of mdlc/runtime/ops.py:68-78 with
 // groups == C == K, which the reference GPU lowering runs on the host
 // (mdlc/codegen/cuda/emit.py:175-180).
 //
 // HBM-bound (9 multiply-adds per output element against 2 bytes read and 2
-// written in bf16), so the design is about keeping enough bytes in flight:
-// persistent CTAs, one per SM, walk output tiles (16 x 16 pixels at stride 1,
-// 8 x 8 at stride 2) x channel blocks of up to 128 bytes per pixel. One thread
-// issues ONE tiled 4-D TMA load per tile for the tile's padded input window
-// ((TH-1)*S+3 rows x (TW-1)*S+3 columns x the channel block); out-of-image
-// pixels arrive as zeros, so padding costs nothing. Three shared-memory
-// stages: two windows load while the current one is computed. Each thread
-// owns one 8-channel vector of one output column and walks a run of output
-// rows with a register ring of the three input rows it needs (one or two new
-// rows per output row, unpacked to fp32 once), weights and bias in registers,
-// paired fp32 multiply-adds (fma.rn.f32x2), fused bias + residual +
-// activation, 16-byte stores.
+// written in bf16), so the kernel has two jobs: keep enough bytes in flight
+// to stream HBM, and spend few enough instructions per output that the SM's
+// issue rate is not the limit. Bytes in flight come from TMA: persistent
+// CTAs (one per SM, 12 warps) walk tiles of TH x TW output pixels x one
+// channel block, and one thread keeps up to four tile windows ((TH-1)*S+3 x
+// (TW-1)*S+3 input pixels x the block; out-of-image pixels arrive as zeros,
+// so padding costs nothing) loading into shared memory while the current one
+// is computed. Instructions: each thread owns four channels of TWO adjacent
+// output columns and walks R output rows of the tile with a register ring of
+// the input rows they need (per output row, one new input row of four pixels
+// at stride 1: 2 new input pixels per output instead of 3), weights and bias
+// in registers as fp32 pairs, paired fp32 multiply-adds (fma.rn.f32x2: 4.5
+// per output), and for bf16 outputs the clamp activations (none / ReLU /
+// ReLU6-style clip) applied to the packed bf16 pairs (max/min.bf16x2).
+// The host picks the channel block, the tile and R per layer so that a layer
+// of any spatial size keeps most threads on real pixels.
+#include <cmath>
+
 #include "common.cuh"
 #include "conv.h"
 
 namespace mdlc {
 namespace {
 
-constexpr int kDwThreads = 256;
-constexpr int kDwMaxBlockBytes = 128;  // channel block per pixel in shared memory
-
-template <int SH>
-struct DwTile {
-  static constexpr int TH = SH == 1 ? 16 : 8;
-  static constexpr int TW = SH == 1 ? 16 : 8;
-  static constexpr int IH = (TH - 1) * SH + 3;  // input window rows
-  static constexpr int IW = (TW - 1) * SH + 3;  // input window columns
-  static constexpr int kStage = IH * IW * kDwMaxBlockBytes;
-  static constexpr int kStages = 3;                     // input windows in flight per CTA
-  static constexpr int kSmem = kStages * kStage + 64 + 128;  // + barriers, alignment slack
-};
+constexpr int kDwThreads = 384;
+constexpr int kDwMaxStages = 4;
+constexpr int kDwSmemBudget = 200 * 1024;  // stage ring (one CTA per SM)
+constexpr int kDwMaxStageBytes = 64 * 1024;
 
 struct DwTmaArgs {
   const float* w;  // [9][cs] fp32
@@ -44,11 +41,16 @@ struct DwTmaArgs {
   void* y;
   int* err;
   int cs, c, res_s, oh, ow, pt, pl;
-  int cb_elems, vecs, cblocks;  // channel block (elements), 8-channel vectors in it, blocks per pixel
-  int tiles_x, tiles_y, total;  // tiles per image row / column, total tiles
-  long long y_elems, res_elems; // element extents (checked build)
+  int cb_elems, cblocks;            // channel block (elements), blocks per pixel
+  int quads, pairs, groups, rows;   // threads: quads x column pairs x row groups; rows per thread
+  int th, tw, ih, iw;               // output tile and input window extents
+  int stage_bytes, stages;
+  int tiles_x, tiles_y, total;      // tiles per image row / column, total tiles
+  long long y_elems, res_elems;     // element extents (checked build)
   unsigned long long wait_cycles;
   ActParams act;
+  int act_kind;                     // 0 identity, 1 clamp to [lo, hi], 2 general (apply_act)
+  uint32_t lo2, hi2;                // bf16 output: the clamp bounds as bf16 pairs
 };
 
 // Paired fp32 multiply-add (one fma.rn.f32x2: two IEEE fmas), on float2 kept
@@ -61,62 +63,92 @@ MDLC_DEV void ffma2(float2& d, const float2 a, const float2 b) {
   d = *reinterpret_cast<float2*>(&dd);
 }
 
-// 8 channels of one pixel from shared memory, as four fp32 pairs
+// 4 channels of one pixel from shared memory, as two fp32 pairs
 template <typename T>
-MDLC_DEV void lds8(const uint8_t* p, float2 (&f)[4]);
+MDLC_DEV void lds4(const uint8_t* p, float2 (&f)[2]);
 template <>
-MDLC_DEV void lds8<__nv_bfloat16>(const uint8_t* p, float2 (&f)[4]) {
-  const uint4 v = *reinterpret_cast<const uint4*>(p);
+MDLC_DEV void lds4<__nv_bfloat16>(const uint8_t* p, float2 (&f)[2]) {
+  const uint2 v = *reinterpret_cast<const uint2*>(p);
   f[0] = make_float2(bf16_lo(v.x), bf16_hi(v.x));
   f[1] = make_float2(bf16_lo(v.y), bf16_hi(v.y));
-  f[2] = make_float2(bf16_lo(v.z), bf16_hi(v.z));
-  f[3] = make_float2(bf16_lo(v.w), bf16_hi(v.w));
 }
 template <>
-MDLC_DEV void lds8<float>(const uint8_t* p, float2 (&f)[4]) {
-  const float4 a = reinterpret_cast<const float4*>(p)[0], b = reinterpret_cast<const float4*>(p)[1];
-  f[0] = make_float2(a.x, a.y); f[1] = make_float2(a.z, a.w);
-  f[2] = make_float2(b.x, b.y); f[3] = make_float2(b.z, b.w);
+MDLC_DEV void lds4<float>(const uint8_t* p, float2 (&f)[2]) {
+  const float4 v = *reinterpret_cast<const float4*>(p);
+  f[0] = make_float2(v.x, v.y);
+  f[1] = make_float2(v.z, v.w);
 }
 
+// 4 channels of a global tensor as two fp32 pairs (the residual)
 template <typename T>
-MDLC_DEV void load8(const T* p, float (&f)[8]);
+MDLC_DEV void ldg4(const T* p, float2 (&f)[2]);
 template <>
-MDLC_DEV void load8<__nv_bfloat16>(const __nv_bfloat16* p, float (&f)[8]) {
-  const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
-  f[0] = bf16_lo(u.x); f[1] = bf16_hi(u.x); f[2] = bf16_lo(u.y); f[3] = bf16_hi(u.y);
-  f[4] = bf16_lo(u.z); f[5] = bf16_hi(u.z); f[6] = bf16_lo(u.w); f[7] = bf16_hi(u.w);
+MDLC_DEV void ldg4<__nv_bfloat16>(const __nv_bfloat16* p, float2 (&f)[2]) {
+  const uint2 v = __ldg(reinterpret_cast<const uint2*>(p));
+  f[0] = make_float2(bf16_lo(v.x), bf16_hi(v.x));
+  f[1] = make_float2(bf16_lo(v.y), bf16_hi(v.y));
 }
 template <>
-MDLC_DEV void load8<float>(const float* p, float (&f)[8]) {
-  const float4 a = __ldg(reinterpret_cast<const float4*>(p)), b = __ldg(reinterpret_cast<const float4*>(p) + 1);
-  f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
-}
-template <typename T>
-MDLC_DEV void store8(T* p, const float (&f)[8]);
-template <>
-MDLC_DEV void store8<__nv_bfloat16>(__nv_bfloat16* p, const float (&f)[8]) {
-  *reinterpret_cast<uint4*>(p) = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]),
-                                            pack_bf16x2(f[4], f[5]), pack_bf16x2(f[6], f[7]));
-}
-template <>
-MDLC_DEV void store8<float>(float* p, const float (&f)[8]) {
-  reinterpret_cast<float4*>(p)[0] = make_float4(f[0], f[1], f[2], f[3]);
-  reinterpret_cast<float4*>(p)[1] = make_float4(f[4], f[5], f[6], f[7]);
+MDLC_DEV void ldg4<float>(const float* p, float2 (&f)[2]) {
+  const float4 v = __ldg(reinterpret_cast<const float4*>(p));
+  f[0] = make_float2(v.x, v.y);
+  f[1] = make_float2(v.z, v.w);
 }
 
-template <typename T, int SH>
+MDLC_DEV uint32_t clamp_bf16x2(uint32_t v, uint32_t lo2, uint32_t hi2) {
+  asm("max.bf16x2 %0, %0, %1;" : "+r"(v) : "r"(lo2));
+  asm("min.bf16x2 %0, %0, %1;" : "+r"(v) : "r"(hi2));
+  return v;
+}
+
+// bias + taps (+ residual) of 4 channels -> activation -> 4 output elements;
+// channels at or past c (the padding of the channel stride) are written as 0
+template <typename T, bool GEN>
+MDLC_DEV void store4(const DwTmaArgs& a, T* yp, float2 (&f)[2], bool full, int c0) {
+  if constexpr (sizeof(T) == 4) {
+    float v[4] = {f[0].x, f[0].y, f[1].x, f[1].y};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      if constexpr (GEN) v[e] = apply_act(v[e], a.act);
+      else if (a.act_kind == 1) v[e] = fminf(fmaxf(v[e], a.act.lo), a.act.hi);
+      if (!full && c0 + e >= a.c) v[e] = 0.0f;
+    }
+    *reinterpret_cast<float4*>(yp) = make_float4(v[0], v[1], v[2], v[3]);
+    return;
+  }
+  if constexpr (GEN) {
+    f[0] = make_float2(apply_act(f[0].x, a.act), apply_act(f[0].y, a.act));
+    f[1] = make_float2(apply_act(f[1].x, a.act), apply_act(f[1].y, a.act));
+  }
+  if (!full) {
+    f[0] = make_float2(c0 < a.c ? f[0].x : 0.0f, c0 + 1 < a.c ? f[0].y : 0.0f);
+    f[1] = make_float2(c0 + 2 < a.c ? f[1].x : 0.0f, c0 + 3 < a.c ? f[1].y : 0.0f);
+  }
+  uint32_t w0 = pack_bf16x2(f[0].x, f[0].y), w1 = pack_bf16x2(f[1].x, f[1].y);
+  // clamp bounds are exact in bf16 (the host checks), and rounding is
+  // monotonic, so clamping the rounded pair equals rounding the clamped one;
+  // a zero padding channel stays zero as every clamp range holds 0
+  if (!GEN && a.act_kind == 1) {
+    w0 = clamp_bf16x2(w0, a.lo2, a.hi2);
+    w1 = clamp_bf16x2(w1, a.lo2, a.hi2);
+  }
+  *reinterpret_cast<uint2*>(yp) = make_uint2(w0, w1);
+}
+
+// GEN: the activation is not a clamp (apply_act per element)
+template <typename T, int SH, bool GEN>
 __global__ void __launch_bounds__(kDwThreads, 1)
     conv_dw3_tma_kernel(const __grid_constant__ CUtensorMap tmap, const DwTmaArgs a) {
-  using Tl = DwTile<SH>;
-  constexpr int TH = Tl::TH, TW = Tl::TW, IW = Tl::IW, NS = Tl::kStages;
+  constexpr int NC = SH == 1 ? 4 : 5;  // input columns under a thread's two output columns
+  constexpr int esz = (int)sizeof(T);
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~uintptr_t(127));
   const uint32_t sbase = smem_u32(smem);
-  const uint32_t bar0 = sbase + NS * Tl::kStage;
-  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + NS * Tl::kStage + 8 * NS + 8);
+  const int NS = a.stages;
+  const int ring_bytes = NS * a.stage_bytes;
+  const uint32_t bar0 = sbase + ring_bytes;
+  volatile int* abort_flag = reinterpret_cast<volatile int*>(smem + ring_bytes + 8 * kDwMaxStages);
   const int tid = threadIdx.x;
-  const int esz = (int)sizeof(T);
   const int cb_bytes = a.cb_elems * esz;
   const int per_img = a.tiles_x * a.tiles_y;
   const int per_cb = a.total / a.cblocks;  // tiles of one channel block
@@ -132,9 +164,9 @@ __global__ void __launch_bounds__(kDwThreads, 1)
     int cb, img, ty, tx;
     decode(tile, cb, img, ty, tx);
     const uint32_t bar = bar0 + 8u * stage;
-    mbar_arrive_expect_tx(bar, (uint32_t)(Tl::IH * IW * cb_bytes));
-    tma_load_4d(sbase + stage * Tl::kStage, &tmap, cb * a.cb_elems, tx * TW * SH - a.pl, ty * TH * SH - a.pt, img,
-                bar);
+    mbar_arrive_expect_tx(bar, (uint32_t)(a.ih * a.iw * cb_bytes));
+    tma_load_4d(sbase + stage * a.stage_bytes, &tmap, cb * a.cb_elems, tx * a.tw * SH - a.pl,
+                ty * a.th * SH - a.pt, img, bar);
   };
   if (tid == 0) {
     for (int q = 0; q < NS; ++q) mbar_init(bar0 + 8u * q, 1);
@@ -148,14 +180,14 @@ __global__ void __launch_bounds__(kDwThreads, 1)
     for (int q = 0; q < NS - 1; ++q)
       if ((int)blockIdx.x + q * (int)gridDim.x < a.total) issue(blockIdx.x + q * gridDim.x, q);
 
-  // thread -> (8-channel vector, output column, run of output rows)
-  const int V = a.vecs;
-  const int groups = kDwThreads / (V * TW);           // row groups (>= 2 for V <= 8)
-  const int rpt = (TH + groups - 1) / groups;         // output rows per thread
-  const int v = tid % V, col = (tid / V) % TW, rg = tid / (V * TW);
-  const bool active = rg < groups;
-  const int oy0 = rg * rpt, oy1 = min(oy0 + rpt, TH);
-  float2 w[9][4], bias[4];
+  // thread -> (4-channel quad, output column pair, row group of R rows)
+  const int Q = a.quads, P = a.pairs;
+  const int qd = tid % Q, pr = (tid / Q) % P, rg = tid / (Q * P);
+  const bool active = rg < a.groups;
+  const int ox = 2 * pr;            // tile-local first output column
+  const int oy0 = rg * a.rows;      // tile-local first output row
+  const int row_bytes = a.iw * cb_bytes;
+  float2 w[9][2], bias[2];
   int cur_cb = -1;
   int i = 0;
   for (int tile = blockIdx.x; tile < a.total; tile += gridDim.x, ++i) {
@@ -170,80 +202,85 @@ __global__ void __launch_bounds__(kDwThreads, 1)
     if (__syncthreads_or(!ok)) break;  // a timed-out wait ends every thread's loop together
     int cb, img, ty, tx;
     decode(tile, cb, img, ty, tx);
-    const int c0 = cb * a.cb_elems + v * 8;
-    if (active && oy0 < oy1) {
+    const int c0 = cb * a.cb_elems + qd * 4;
+    const int gx = tx * a.tw + ox;
+    const int gy0 = ty * a.th + oy0;
+    if (active && gx < a.ow && gy0 < a.oh) {
       if (cb != cur_cb) {
 #pragma unroll
         for (int tap = 0; tap < 9; ++tap) {
-          const float4 w0 = __ldg(reinterpret_cast<const float4*>(a.w + tap * a.cs + c0));
-          const float4 w1 = __ldg(reinterpret_cast<const float4*>(a.w + tap * a.cs + c0) + 1);
-          w[tap][0] = make_float2(w0.x, w0.y); w[tap][1] = make_float2(w0.z, w0.w);
-          w[tap][2] = make_float2(w1.x, w1.y); w[tap][3] = make_float2(w1.z, w1.w);
+          const float4 w4 = __ldg(reinterpret_cast<const float4*>(a.w + tap * a.cs + c0));
+          w[tap][0] = make_float2(w4.x, w4.y);
+          w[tap][1] = make_float2(w4.z, w4.w);
         }
-        if (a.bias) {
-          const float4 b0 = __ldg(reinterpret_cast<const float4*>(a.bias + c0));
-          const float4 b1 = __ldg(reinterpret_cast<const float4*>(a.bias + c0) + 1);
-          bias[0] = make_float2(b0.x, b0.y); bias[1] = make_float2(b0.z, b0.w);
-          bias[2] = make_float2(b1.x, b1.y); bias[3] = make_float2(b1.z, b1.w);
-        } else {
+        // bias holds c floats (not necessarily the padded stride)
+        float b4[4];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) bias[e] = make_float2(0.0f, 0.0f);
-        }
+        for (int e = 0; e < 4; ++e) b4[e] = (a.bias && c0 + e < a.c) ? __ldg(a.bias + c0 + e) : 0.0f;
+        bias[0] = make_float2(b4[0], b4[1]);
+        bias[1] = make_float2(b4[2], b4[3]);
         cur_cb = cb;
       }
-      const uint8_t* st = smem + stage * Tl::kStage + v * 8 * esz;
-      auto px_at = [&](int r, int c) { return st + (r * IW + c) * cb_bytes; };
-      float2 p[3][3][4];  // the three input rows of the current output row, unpacked
-      const int c_in = col * SH;
+      const bool full = c0 + 4 <= a.c;
+      const bool v1 = gx + 1 < a.ow;
+      const uint8_t* colp = smem + stage * a.stage_bytes + (ox * SH) * cb_bytes + qd * 4 * esz;
+      float2 x[3][NC][2];  // the input rows under the current output row, unpacked
+      auto load_row = [&](int wr, float2 (&dst)[NC][2]) {
+        const uint8_t* rp = colp + wr * row_bytes;
 #pragma unroll
-      for (int r = 0; r < 3; ++r)
+        for (int c = 0; c < NC; ++c) lds4<T>(rp + c * cb_bytes, dst[c]);
+      };
 #pragma unroll
-        for (int c = 0; c < 3; ++c) lds8<T>(px_at(oy0 * SH + r, c_in + c), p[r][c]);
-      const int gx = tx * TW + col;
-      for (int oy = oy0; oy < oy1; ++oy) {
-        float2 acc[4] = {bias[0], bias[1], bias[2], bias[3]};
+      for (int r = 0; r < 3; ++r) load_row(oy0 * SH + r, x[r]);
+      const int nrows = min(a.rows, a.oh - gy0);
+      const long long m0 = ((long long)img * a.oh + gy0) * a.ow + gx;
+      // output row r from the ring (xa, xb, xc) = its input rows; then the
+      // oldest slot(s) take the next row's new input rows. The row loop is
+      // unrolled by three with the slots rotated, so the ring never moves.
+      auto step = [&](float2 (&xa)[NC][2], float2 (&xb)[NC][2], float2 (&xc)[NC][2], int r) {
+        float2 acc[2][2] = {{bias[0], bias[1]}, {bias[0], bias[1]}};
 #pragma unroll
-        for (int r = 0; r < 3; ++r)
+        for (int kx = 0; kx < 3; ++kx)
 #pragma unroll
-          for (int c = 0; c < 3; ++c)
+          for (int j = 0; j < 2; ++j)
 #pragma unroll
-            for (int e = 0; e < 4; ++e) ffma2(acc[e], p[r][c][e], w[r * 3 + c][e]);
-        const int gy = ty * TH + oy;
-        const long long m = ((long long)img * a.oh + gy) * a.ow + gx;
-        if (gy < a.oh && gx < a.ow && MDLC_CHECK_IDX(a.err, m * a.cs + c0 + 7, a.y_elems) &&
-            (!a.res || MDLC_CHECK_IDX(a.err, m * a.res_s + c0 + 7, a.res_elems))) {
-          float f[8] = {acc[0].x, acc[0].y, acc[1].x, acc[1].y, acc[2].x, acc[2].y, acc[3].x, acc[3].y};
+            for (int e = 0; e < 2; ++e) {
+              ffma2(acc[j][e], xa[j * SH + kx][e], w[kx][e]);
+              ffma2(acc[j][e], xb[j * SH + kx][e], w[3 + kx][e]);
+              ffma2(acc[j][e], xc[j * SH + kx][e], w[6 + kx][e]);
+            }
+        const long long m = m0 + (long long)r * a.ow;
+#pragma unroll
+        for (int j = 0; j < 2; ++j) {
+          if (j == 1 && !v1) break;
+          const long long mj = m + j;
+          if (!MDLC_CHECK_IDX(a.err, mj * a.cs + c0 + 3, a.y_elems)) continue;
           if (a.res) {
-            float rv[8];
-            load8<T>(static_cast<const T*>(a.res) + m * a.res_s + c0, rv);
-#pragma unroll
-            for (int e = 0; e < 8; ++e) f[e] += rv[e];
+            if (!MDLC_CHECK_IDX(a.err, mj * a.res_s + c0 + 3, a.res_elems)) continue;
+            float2 rv[2];
+            ldg4<T>(static_cast<const T*>(a.res) + mj * a.res_s + c0, rv);
+            const float2 one = make_float2(1.0f, 1.0f);
+            ffma2(acc[j][0], rv[0], one);
+            ffma2(acc[j][1], rv[1], one);
           }
-#pragma unroll
-          for (int e = 0; e < 8; ++e) f[e] = (c0 + e < a.c) ? apply_act(f[e], a.act) : 0.0f;
-          store8<T>(static_cast<T*>(a.y) + m * a.cs + c0, f);
+          store4<T, GEN>(a, static_cast<T*>(a.y) + mj * a.cs + c0, acc[j], full, c0);
         }
-        if (oy + 1 < oy1) {
-          if (SH == 1) {
-#pragma unroll
-            for (int c = 0; c < 3; ++c) {
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                p[0][c][e] = p[1][c][e];
-                p[1][c][e] = p[2][c][e];
-              }
-              lds8<T>(px_at(oy + 3, c_in + c), p[2][c]);
-            }
-          } else {
-#pragma unroll
-            for (int c = 0; c < 3; ++c) {
-#pragma unroll
-              for (int e = 0; e < 4; ++e) p[0][c][e] = p[2][c][e];
-              lds8<T>(px_at(oy * 2 + 3, c_in + c), p[1][c]);
-              lds8<T>(px_at(oy * 2 + 4, c_in + c), p[2][c]);
-            }
-          }
+        if (r + 1 >= nrows) return false;
+        const int oy = oy0 + r;
+        if (SH == 1) {
+          load_row(oy + 3, xa);  // next: (xb, xc, xa)
+        } else {
+          load_row(oy * 2 + 3, xa);  // next: (xc, xa, xb)
+          load_row(oy * 2 + 4, xb);
         }
+        return true;
+      };
+      if (SH == 1) {
+        for (int r = 0;; r += 3)
+          if (!step(x[0], x[1], x[2], r) || !step(x[1], x[2], x[0], r + 1) || !step(x[2], x[0], x[1], r + 2)) break;
+      } else {
+        for (int r = 0;; r += 3)
+          if (!step(x[0], x[1], x[2], r) || !step(x[2], x[0], x[1], r + 1) || !step(x[1], x[2], x[0], r + 2)) break;
       }
     }
     __syncthreads();  // every thread is done with this stage before it is reloaded
@@ -258,10 +295,58 @@ __global__ void __launch_bounds__(kDwThreads, 1)
   }
 }
 
-}  // namespace
-}  // namespace mdlc
+uint16_t bf16_bits_rn(float f) {
+  uint32_t u;
+  memcpy(&u, &f, 4);
+  if (std::isnan(f)) return 0x7FC0;
+  return (uint16_t)((u + 0x7FFFu + ((u >> 16) & 1u)) >> 16);
+}
 
-namespace mdlc {
+}  // namespace
+
+// Tile choice for one layer (host): channel block, column pairs, rows per
+// thread. Score = the fraction of threads on real output pixels (and of
+// enough tiles to occupy every SM) over a per-output instruction estimate:
+// 4.5 paired FMAs + ~2 for the epilogue + the ring loads (an input row of
+// NC pixels is 5 instructions a pixel in bf16 -- one shared load, four
+// unpacks -- and a thread loads R + 2 rows at stride 1, 2R + 1 at stride 2,
+// for 8 outputs a row) + ~100 instructions of per-tile overhead (barrier,
+// tile decode) spread over the thread's 8R outputs.
+DwTileChoice choose_dw_tile(int c_stride, int esz, int oh, int ow, int n, int sh) {
+  DwTileChoice best{};
+  double best_score = -1.0;
+  for (int cbb = 256; cbb >= 16; cbb -= 16) {  // channel block bytes
+    const int cb = cbb / esz;
+    if (cb % 4 || c_stride % cb) continue;
+    const int Q = cb / 4;
+    for (int P = 8; P >= 2; --P) {
+      if (Q * P > kDwThreads) continue;
+      const int G = kDwThreads / (Q * P);
+      for (int R = 8; R >= 1; --R) {
+        const int th = G * R, tw = 2 * P;
+        const int ih = (th - 1) * sh + 3, iw = (tw - 1) * sh + 3;
+        if (ih > 256 || iw > 256) continue;
+        const int stage = (ih * iw * cbb + 127) / 128 * 128;
+        if (stage > kDwMaxStageBytes) continue;
+        int stages = kDwSmemBudget / stage;
+        if (stages > kDwMaxStages) stages = kDwMaxStages;
+        if (stages < 2) continue;
+        const long long tx = (ow + tw - 1) / tw, ty = (oh + th - 1) / th;
+        const double used = (double)oh * ow / ((double)tx * tw * ty * th) * (double)(Q * P * G) / kDwThreads;
+        const double load = sh == 1 ? (R + 2.0) / R * 2.5 : (2.0 * R + 1.0) / R * 3.125;
+        const double cost = 6.5 + load + 100.0 / (8.0 * R);
+        const long long tiles = (long long)(c_stride / cb) * n * tx * ty;
+        const double spread = tiles >= 4 * 148 ? 1.0 : (double)tiles / (4 * 148);
+        const double score = used * spread / cost;
+        if (score > best_score + 1e-9) {
+          best_score = score;
+          best = DwTileChoice{cb, Q, P, G, R, th, tw, ih, iw, stage, stages};
+        }
+      }
+    }
+  }
+  return best;
+}
 
 int conv_dw_tma(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const float* w, const float* bias,
                 const void* res, void* y, const mdlc_epilogue* epi) {
@@ -270,26 +355,18 @@ int conv_dw_tma(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const flo
     return MDLC_ERR_UNSUPPORTED;
   const bool bf = d.in_type == MDLC_BF16;
   const int esz = bf ? 2 : 4;
-  // channel block: the largest multiple of 8 channels of at most 128 bytes dividing the stride
-  int cb = 0;
-  for (int c = kDwMaxBlockBytes / esz; c >= 8; c -= 8)
-    if (d.c_stride % c == 0) {
-      cb = c;
-      break;
-    }
   auto encode = tensor_map_encoder();
-  if (!cb || !encode) return MDLC_ERR_UNSUPPORTED;
   const int SH = d.stride_h;
-  const int TH = SH == 1 ? DwTile<1>::TH : DwTile<2>::TH, TW = SH == 1 ? DwTile<1>::TW : DwTile<2>::TW;
-  const int IH = SH == 1 ? DwTile<1>::IH : DwTile<2>::IH, IW = SH == 1 ? DwTile<1>::IW : DwTile<2>::IW;
-  const long long tiles_x = (d.ow + TW - 1) / TW, tiles_y = (d.oh + TH - 1) / TH;
-  const long long total = (long long)(d.c_stride / cb) * d.n * tiles_x * tiles_y;
+  const DwTileChoice t = choose_dw_tile(d.c_stride, esz, d.oh, d.ow, d.n, SH);
+  if (!t.cb || !encode) return MDLC_ERR_UNSUPPORTED;
+  const long long tiles_x = (d.ow + t.tw - 1) / t.tw, tiles_y = (d.oh + t.th - 1) / t.th;
+  const long long total = (long long)(d.c_stride / t.cb) * d.n * tiles_x * tiles_y;
   if (total >= (1ll << 31)) return MDLC_ERR_UNSUPPORTED;
   CUtensorMap tmap;
   const cuuint64_t gd[4] = {(cuuint64_t)d.c_stride, (cuuint64_t)d.w, (cuuint64_t)d.h, (cuuint64_t)d.n};
   const cuuint64_t gs[3] = {(cuuint64_t)d.c_stride * esz, (cuuint64_t)d.w * d.c_stride * esz,
                             (cuuint64_t)d.h * d.w * d.c_stride * esz};
-  const cuuint32_t box[4] = {(cuuint32_t)cb, (cuuint32_t)IW, (cuuint32_t)IH, 1};
+  const cuuint32_t box[4] = {(cuuint32_t)t.cb, (cuuint32_t)t.iw, (cuuint32_t)t.ih, 1};
   const cuuint32_t es[4] = {1, 1, 1, 1};
   if (encode(&tmap, bf ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 4, const_cast<void*>(x),
              gd, gs, box, es, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE,
@@ -299,30 +376,55 @@ int conv_dw_tma(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const flo
   a.w = w; a.bias = bias; a.res = res; a.y = y; a.err = ctx->d_err;
   a.cs = d.c_stride; a.c = d.c; a.res_s = d.res_stride ? d.res_stride : d.c_stride;
   a.oh = d.oh; a.ow = d.ow; a.pt = d.pad_t; a.pl = d.pad_l;
-  a.cb_elems = cb; a.vecs = cb / 8; a.cblocks = d.c_stride / cb;
+  a.cb_elems = t.cb; a.cblocks = d.c_stride / t.cb;
+  a.quads = t.quads; a.pairs = t.pairs; a.groups = t.groups; a.rows = t.rows;
+  a.th = t.th; a.tw = t.tw; a.ih = t.ih; a.iw = t.iw;
+  a.stage_bytes = t.stage_bytes; a.stages = t.stages;
   a.tiles_x = (int)tiles_x; a.tiles_y = (int)tiles_y; a.total = (int)total;
   a.y_elems = (long long)d.n * d.oh * d.ow * d.c_stride;
   a.res_elems = (long long)d.n * d.oh * d.ow * a.res_s;
   a.wait_cycles = 2 * kWaitLimitNs;
   a.act = epi ? ActParams{epi->act, epi->alpha, epi->beta, epi->clip_lo, epi->clip_hi}
               : ActParams{MDLC_ACT_NONE, 0.f, 0.f, -INFINITY, INFINITY};
-  const long long slots = (long long)ctx->num_sms;  // one CTA per SM (register budget)
+  // activations that are a clamp: none (kind 0), ReLU, and clip with bounds
+  // exact in the output type
+  a.act_kind = 2;
+  if (a.act.act == MDLC_ACT_NONE) {
+    a.act_kind = 0;
+  } else if (a.act.act == MDLC_ACT_RELU || a.act.act == MDLC_ACT_CLIP) {
+    const float lo = a.act.act == MDLC_ACT_RELU ? 0.0f : a.act.lo;
+    const float hi = a.act.act == MDLC_ACT_RELU ? INFINITY : a.act.hi;
+    const uint16_t lb = bf16_bits_rn(lo), hb = bf16_bits_rn(hi);
+    uint32_t lu, hu;
+    memcpy(&lu, &lo, 4);
+    memcpy(&hu, &hi, 4);
+    const bool exact = !bf || (((uint32_t)lb << 16) == lu && ((uint32_t)hb << 16) == hu);
+    if (exact && lo <= 0.0f && hi >= 0.0f && !std::isnan(lo) && !std::isnan(hi)) {
+      a.act_kind = 1;
+      a.act.lo = lo;
+      a.act.hi = hi;
+      a.lo2 = (uint32_t)lb | ((uint32_t)lb << 16);
+      a.hi2 = (uint32_t)hb | ((uint32_t)hb << 16);
+    }
+  }
+  const long long slots = (long long)ctx->num_sms;  // one CTA per SM
   const unsigned grid = (unsigned)(total < slots ? total : slots);
   void (*kern)(const CUtensorMap, const DwTmaArgs);
-  int smem;
+  const bool gen = a.act_kind == 2;
   if (SH == 1) {
-    kern = bf ? conv_dw3_tma_kernel<__nv_bfloat16, 1> : conv_dw3_tma_kernel<float, 1>;
-    smem = DwTile<1>::kSmem;
+    if (bf) kern = gen ? conv_dw3_tma_kernel<__nv_bfloat16, 1, true> : conv_dw3_tma_kernel<__nv_bfloat16, 1, false>;
+    else kern = gen ? conv_dw3_tma_kernel<float, 1, true> : conv_dw3_tma_kernel<float, 1, false>;
   } else {
-    kern = bf ? conv_dw3_tma_kernel<__nv_bfloat16, 2> : conv_dw3_tma_kernel<float, 2>;
-    smem = DwTile<2>::kSmem;
+    if (bf) kern = gen ? conv_dw3_tma_kernel<__nv_bfloat16, 2, true> : conv_dw3_tma_kernel<__nv_bfloat16, 2, false>;
+    else kern = gen ? conv_dw3_tma_kernel<float, 2, true> : conv_dw3_tma_kernel<float, 2, false>;
   }
-  static bool attr_set[64][4] = {};
-  const int which = (SH - 1) * 2 + (bf ? 1 : 0);
-  if (!attr_set[ctx->device & 63][which]) {
+  const int smem = t.stages * t.stage_bytes + 8 * kDwMaxStages + 16 + 128;  // + barriers, flag, alignment slack
+  static int attr_set[64][8] = {};
+  const int which = (SH - 1) * 4 + (bf ? 2 : 0) + (gen ? 1 : 0);
+  if (attr_set[ctx->device & 63][which] < smem) {
     const cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e != cudaSuccess) return mdlc_cuda_status(ctx, e, "conv_dw3_tma smem attribute");
-    attr_set[ctx->device & 63][which] = true;
+    attr_set[ctx->device & 63][which] = smem;
   }
   kern<<<grid, kDwThreads, smem, ctx->stream>>>(tmap, a);
   mdlc_note_launch(ctx);

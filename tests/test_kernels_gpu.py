@@ -371,6 +371,12 @@ DW_CASES = [
     (1, 960, 9, 7, 3, 2, 1, False),      # 15 blocks of 64 channels, stride 2
     (3, 56, 33, 17, 3, 2, 1, True),      # one 56-channel block, odd sizes, stride 2
     (1, 24, 40, 40, 3, 1, 1, False),     # 24-channel pixels (48 bytes), several tiles
+    (1, 20, 15, 15, 3, 1, 1, False),     # c % 4 != 0: the last 4-channel quad is ragged
+    (2, 32, 112, 112, 3, 1, 1, False),   # MobileNetV2 block 1 (tall tiles, 64-byte pixels)
+    (2, 96, 112, 112, 3, 2, 1, False),   # MobileNetV2 first stride-2 layer
+    (2, 384, 14, 14, 3, 1, 1, True),     # late-stage layer, residual
+    (2, 576, 14, 14, 3, 2, 1, False),
+    (4, 960, 7, 7, 3, 1, 1, False),
 ]
 
 
@@ -395,6 +401,37 @@ def test_depthwise(ctx, dtype, case):
         check(got, want, 1e-2)
     else:
         np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4)
+
+
+DW_ACTS = [
+    # activation, clip bounds, oracle
+    (L.ACT_NONE, (0.0, 6.0), lambda y: y),
+    (L.ACT_RELU, (0.0, 6.0), lambda y: np.maximum(y, 0.0)),
+    (L.ACT_CLIP, (-1.0, 2.5), lambda y: np.clip(y, -1.0, 2.5)),   # bounds exact in bf16
+    (L.ACT_CLIP, (0.1, 6.0), lambda y: np.clip(y, 0.1, 6.0)),     # 0.1 is not: per-element path
+    (L.ACT_SIGMOID, (0.0, 6.0), lambda y: 1.0 / (1.0 + np.exp(-y))),
+]
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+@pytest.mark.parametrize("act", range(len(DW_ACTS)))
+def test_depthwise_activations(ctx, dtype, act):
+    """Depthwise epilogue activations: clamps folded into packed bf16 pairs,
+    or per element (general activations, or clip bounds not exact in bf16)."""
+    code, clip, fn = DW_ACTS[act]
+    n, c, h, w = 2, 44, 19, 23
+    rng = np.random.default_rng(31 + act)
+    x = rng.standard_normal((n, c, h, w)).astype(np.float32)
+    wt = (rng.standard_normal((c, 1, 3, 3)) * 0.4).astype(np.float32)
+    b = (rng.standard_normal(c) * 0.1).astype(np.float32)
+    for stride in (1, 2):
+        got = run_conv(ctx, x, wt, b, stride=stride, pad=1, groups=c, dtype=dtype, act=code, clip=clip)
+        xr = oref.round_bf16(x) if dtype == "bf16" else x
+        want = fn(oref.conv(xr, wt, b, strides=[stride] * 2, pads=[1] * 4, group=c))
+        if dtype == "bf16":
+            check(got, want, 1e-2)
+        else:
+            np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4)
 
 
 GROUPED_CASES = [

@@ -80,3 +80,15 @@ def test_batch_mixing_ops_refuse_sharding():
     g2 = passes.default_pipeline(ops_graph("transpose"))
     lo2 = lowering.lower(g2, S.infer(g2, None), L.BF16)
     assert not any(st.params.get("batch_mixing") for st in lo2.steps)
+
+
+def test_bf16_constant_bits_round_to_nearest_even():
+    """Elementwise constants of bf16 graphs are uploaded as bf16 bit patterns (RNE)."""
+    import torch
+    from mdlc_b200.compiler import _bf16_bits
+    rng = np.random.default_rng(3)
+    a = np.concatenate([rng.standard_normal(4096).astype(np.float32) * 100,
+                        np.array([0.0, -0.0, 1.0 + 2 ** -8, 1.0 + 3 * 2 ** -8, np.inf, -np.inf], np.float32)])
+    want = torch.from_numpy(a).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
+    np.testing.assert_array_equal(_bf16_bits(a), want)
+    assert _bf16_bits(np.array([np.nan], np.float32))[0] & 0x7FC0 == 0x7FC0
