@@ -257,7 +257,10 @@ int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w
   a.split = 1;
   a.kps = num_kb;
   // fp32: promote the accumulator every 4 k-blocks (128 reduction elements)
-  a.kchunk = esz == 4 ? 4 : 0;
+  // when the reduction is deeper than 1152: the truncation error of the
+  // tensor cores' accumulation grows like K^1.5, and at K <= 1152 it stays
+  // near the fp32 rounding error of the sum itself
+  a.kchunk = (esz == 4 && num_kb > 36) ? 4 : 0;
   a.ws = ctx->d_split_ws;
   a.counters = ctx->d_split_cnt;
   if (cfg && ((cfg->flags >> 8) & 0xFF) > 1) {

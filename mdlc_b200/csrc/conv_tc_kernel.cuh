@@ -593,20 +593,26 @@ __global__ void __launch_bounds__(threads_for<ESZ>(), (Occ<BN, STAGES, ESZ, AMOD
           }
           tc_fence_after();
           const uint32_t part = tmem + lane_base + (uint32_t)(cslot * BN);
+          // 32 columns per round trip: four loads in flight behind one wait
 #pragma unroll 1
-          for (int c = 0; c < BN; c += 16) {
-            uint32_t v[16];
-            tmem_ld16(part + c, v);
+          for (int c = 0; c < BN; c += 32) {
+            uint32_t v[2][16], r[2][16];
+            tmem_ld16(part + c, v[0]);
+            tmem_ld16(part + c + 16, v[1]);
             if (q > 0) {
-              uint32_t r[16];
-              tmem_ld16(run + c, r);
-              tmem_ld_wait();
-#pragma unroll
-              for (int e = 0; e < 16; ++e) v[e] = __float_as_uint(__fadd_rn(__uint_as_float(r[e]), __uint_as_float(v[e])));
-            } else {
-              tmem_ld_wait();
+              tmem_ld16(run + c, r[0]);
+              tmem_ld16(run + c + 16, r[1]);
             }
-            tmem_st16(run + c, v);
+            tmem_ld_wait();
+            if (q > 0) {
+#pragma unroll
+              for (int h = 0; h < 2; ++h)
+#pragma unroll
+                for (int e = 0; e < 16; ++e)
+                  v[h][e] = __float_as_uint(__fadd_rn(__uint_as_float(r[h][e]), __uint_as_float(v[h][e])));
+            }
+            tmem_st16(run + c, v[0]);
+            tmem_st16(run + c + 16, v[1]);
           }
           tmem_st_wait();
           tc_fence_before();

@@ -23,7 +23,7 @@ def test_kernel_shapes_under_bounds_checks():
     probe = subprocess.run([sys.executable, "-c", "from mdlc_b200 import _lib; print(_lib.load()._name)"],
                            cwd=ROOT, env=env, capture_output=True, text=True, timeout=300)
     assert probe.returncode == 0 and probe.stdout.strip().endswith("libmdlc_b200_check.so"), probe.stderr
-    r = subprocess.run([sys.executable, "-m", "pytest", "tests/test_kernels_gpu.py", "-q", "-x", "-p",
+    r = subprocess.run([sys.executable, "-m", "pytest", "tests/test_kernels_gpu.py", "-x", "-p",
                         "no:cacheprovider", "-k",
                         "conv_bf16_tcgen05 or tile_configs or split_k or im2col or pointwise or depthwise "
                         "or grouped or fp32 or gemm or pools or eltwise"],

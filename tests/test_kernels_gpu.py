@@ -621,14 +621,17 @@ def test_eltwise_program(ctx, dtype):
     check(outs[1], want1, 1e-2 if dt == L.BF16 else 1e-6)
 
 
+@pytest.mark.parametrize("shape", [(3, 44, 6, 5), (8, 128, 56, 56)], ids=["padded", "multi-trip"])
 @pytest.mark.parametrize("dtype", ["bf16", "f32"])
 @pytest.mark.parametrize("mode,op,post", [(L.BC_FULL, L.EW_ADD, L.EW_RELU), (L.BC_NC, L.EW_MUL, None),
                                           (L.BC_C, L.EW_SUB, L.EW_SIGMOID), (L.BC_SCALAR, L.EW_MUL, L.EW_CLIP)])
-def test_eltwise_binary_fast_path(ctx, dtype, mode, op, post):
+def test_eltwise_binary_fast_path(ctx, dtype, mode, op, post, shape):
     """Programs of the form [unary](in0 (op) in1), in1 broadcast full / per (n, c)
-    / per c / scalar, take the register-resident fast path; same results."""
+    / per c / scalar, take the register-resident fast path; same results. The
+    second shape has no padding channels and more vectors than one grid-stride
+    trip of the launch covers."""
     rng = np.random.default_rng(19 + mode)
-    n, c, h, w = 3, 44, 6, 5
+    n, c, h, w = shape
     cs = _rnd8(c)
     dt = L.BF16 if dtype == "bf16" else L.F32
     a = rng.standard_normal((n, c, h, w)).astype(np.float32)
