@@ -409,6 +409,22 @@ MDLC_DEV uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 MDLC_DEV float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }
+// Paired fp32 add (add.rn.f32x2: two IEEE round-to-nearest adds in one
+// instruction) on a float2 kept in a 64-bit register pair.
+MDLC_DEV void fadd2(float2& d, const float2 b) {
+  unsigned long long dd = *reinterpret_cast<unsigned long long*>(&d);
+  asm("add.rn.f32x2 %0, %0, %1;" : "+l"(dd) : "l"(*reinterpret_cast<const unsigned long long*>(&b)));
+  d = *reinterpret_cast<float2*>(&dd);
+}
+// Clamp both halves of a bf16 pair to [lo, hi] (given as bf16 pairs). With
+// bounds exact in bf16, clamping after rounding to bf16 equals rounding after
+// clamping in fp32 (rounding is monotonic); NaN becomes lo, as with
+// fminf(fmaxf(x, lo), hi).
+MDLC_DEV uint32_t clamp_bf16x2(uint32_t v, uint32_t lo2, uint32_t hi2) {
+  asm("max.bf16x2 %0, %0, %1;" : "+r"(v) : "r"(lo2));
+  asm("min.bf16x2 %0, %0, %1;" : "+r"(v) : "r"(hi2));
+  return v;
+}
 MDLC_DEV float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
 
 // ------------------------------------------------------------ int8 requant

@@ -4,6 +4,8 @@
 // then the launcher of the element type's translation unit.
 #include <cudaTypedefs.h>
 
+#include <cmath>
+#include <cstring>
 #include <mutex>
 
 #include "conv_tc_kernel.cuh"
@@ -48,6 +50,15 @@ PFN_cuTensorMapEncodeIm2col_v12000 get_im2col_fn() {
 // stride not a multiple of the block, corners outside [-128, 127], traversal
 // stride above 8, offsets of 128 or more) or is small (< 128 KiB), in which
 // case the kernel gathers A with cp.async instead.
+// v as a bf16 pair (both halves) when v is exactly representable in bf16
+bool bf16_pair_exact(float v, uint32_t* pair) {
+  uint32_t u;
+  memcpy(&u, &v, 4);
+  if ((u & 0xFFFFu) != 0 || v != v) return false;
+  *pair = (u >> 16) | (u & 0xFFFF0000u);
+  return true;
+}
+
 int encode_im2col(CUtensorMap* m, const mdlc_conv_desc& d, const void* x, int esz) {
   const int kb_elems = 128 / esz;
   // mode 1: 128-byte channel blocks; modes 2/3: the whole pixel (bf16 cs 16 / 32) per load
@@ -322,6 +333,17 @@ int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w
   const int act_t = (!int8 && !fp32 && a.tma_epi &&
                      (act == MDLC_ACT_NONE || act == MDLC_ACT_RELU || act == MDLC_ACT_CLIP ||
                       act == MDLC_ACT_GELU || act == MDLC_ACT_SIGMOID)) ? act : -1;
+  // none / ReLU / clip with bounds exact in bf16: applied to packed bf16 pairs
+  if (act_t == MDLC_ACT_NONE || act_t == MDLC_ACT_RELU || act_t == MDLC_ACT_CLIP) {
+    const float lo = act_t == MDLC_ACT_CLIP ? a.act.lo : (act_t == MDLC_ACT_RELU ? 0.0f : -INFINITY);
+    const float hi = act_t == MDLC_ACT_CLIP ? a.act.hi : INFINITY;
+    uint32_t lo2 = 0, hi2 = 0;
+    if (bf16_pair_exact(lo, &lo2) && bf16_pair_exact(hi, &hi2) && lo <= hi) {
+      a.act_packed = 1;
+      a.act_lo2 = lo2;
+      a.act_hi2 = hi2;
+    }
+  }
   const TcLaunch l{&tmap, &tmap_y, &tmap_r, &tmap_x, &a, bn, stages, amode, act_t};
   if (fp32) return launch_tc_f32(ctx, l);
   if (int8) return launch_tc_i8(ctx, l);

@@ -92,6 +92,10 @@ struct TcArgs {
   int rq_fixed;
   unsigned long long wait_cycles;
   int tma_epi;  // bf16 / 8-bit output staged in shared memory and written by TMA stores
+  // bf16 output with a none / ReLU / clip activation whose bounds are exact in
+  // bf16: the activation is applied to the packed bf16 pairs (bounds below)
+  int act_packed;
+  uint32_t act_lo2, act_hi2;
   int tiles_x, tiles_y, halo_rows, cpb;  // halo mode: tile grid per image, band rows, channel blocks
   int band_px;                           // halo mode: bytes per band pixel slot (32, 64 or 128)
   // split-K: each tile's k-blocks are cut into `split` slices of `kps`; every
@@ -897,33 +901,57 @@ __global__ void __launch_bounds__(threads_for<ESZ>(), (Occ<BN, STAGES, ESZ, AMOD
               *qp = make_uint4(packed[0], packed[1], packed[2], packed[3]);
             }
           } else {
-          // one 8-column (16-byte) group: + bias (+ residual), activation, bf16
+          // one 8-column (16-byte) group: + bias (+ residual), activation, bf16.
+          // Paired fp32 adds; clamp-type activations on the packed bf16 pairs;
+          // padding columns (only in a chunk that reaches past k) zeroed last.
+          constexpr bool kClampAct = ACT == MDLC_ACT_NONE || ACT == MDLC_ACT_RELU || ACT == MDLC_ACT_CLIP;
+          const bool full = n0 + c0 + 64 <= a.k;
           auto group = [&](int q, const uint32_t* vv) {
             uint4* qp = reinterpret_cast<uint4*>(sp + ((q ^ sw) << 4));
             const float4 b0 = *reinterpret_cast<const float4*>(sbias + c0 + 8 * q);
             const float4 b1 = *reinterpret_cast<const float4*>(sbias + c0 + 8 * q + 4);
-            float f[8] = {__uint_as_float(vv[0]) + b0.x, __uint_as_float(vv[1]) + b0.y,
-                          __uint_as_float(vv[2]) + b0.z, __uint_as_float(vv[3]) + b0.w,
-                          __uint_as_float(vv[4]) + b1.x, __uint_as_float(vv[5]) + b1.y,
-                          __uint_as_float(vv[6]) + b1.z, __uint_as_float(vv[7]) + b1.w};
+            float2 f2[4] = {make_float2(__uint_as_float(vv[0]), __uint_as_float(vv[1])),
+                            make_float2(__uint_as_float(vv[2]), __uint_as_float(vv[3])),
+                            make_float2(__uint_as_float(vv[4]), __uint_as_float(vv[5])),
+                            make_float2(__uint_as_float(vv[6]), __uint_as_float(vv[7]))};
+            fadd2(f2[0], make_float2(b0.x, b0.y));
+            fadd2(f2[1], make_float2(b0.z, b0.w));
+            fadd2(f2[2], make_float2(b1.x, b1.y));
+            fadd2(f2[3], make_float2(b1.z, b1.w));
             if (a.res) {
               const uint4 r = *qp;
-              f[0] += bf16_lo(r.x); f[1] += bf16_hi(r.x); f[2] += bf16_lo(r.y); f[3] += bf16_hi(r.y);
-              f[4] += bf16_lo(r.z); f[5] += bf16_hi(r.z); f[6] += bf16_lo(r.w); f[7] += bf16_hi(r.w);
+              fadd2(f2[0], make_float2(bf16_lo(r.x), bf16_hi(r.x)));
+              fadd2(f2[1], make_float2(bf16_lo(r.y), bf16_hi(r.y)));
+              fadd2(f2[2], make_float2(bf16_lo(r.z), bf16_hi(r.z)));
+              fadd2(f2[3], make_float2(bf16_lo(r.w), bf16_hi(r.w)));
             }
-            const int nb0 = n0 + c0 + 8 * q;
-            if constexpr (ACT == MDLC_ACT_GELU) {
-              gelu8(f);
-            } else if constexpr (ACT == MDLC_ACT_SIGMOID) {
-              sigmoid8(f);
+            uint32_t w[4];
+            if (kClampAct && a.act_packed) {
+#pragma unroll
+              for (int i = 0; i < 4; ++i) {
+                w[i] = pack_bf16x2(f2[i].x, f2[i].y);
+                if constexpr (ACT != MDLC_ACT_NONE) w[i] = clamp_bf16x2(w[i], a.act_lo2, a.act_hi2);
+              }
             } else {
+              float f[8] = {f2[0].x, f2[0].y, f2[1].x, f2[1].y, f2[2].x, f2[2].y, f2[3].x, f2[3].y};
+              if constexpr (ACT == MDLC_ACT_GELU) {
+                gelu8(f);
+              } else if constexpr (ACT == MDLC_ACT_SIGMOID) {
+                sigmoid8(f);
+              } else {
 #pragma unroll
-              for (int e = 0; e < 8; ++e) f[e] = act_fn<ACT>(f[e], a.act);
+                for (int e = 0; e < 8; ++e) f[e] = act_fn<ACT>(f[e], a.act);
+              }
+#pragma unroll
+              for (int i = 0; i < 4; ++i) w[i] = pack_bf16x2(f[2 * i], f[2 * i + 1]);
             }
+            if (!full) {
+              const int nb0 = n0 + c0 + 8 * q;
 #pragma unroll
-            for (int e = 0; e < 8; ++e) f[e] = (nb0 + e < a.k) ? f[e] : 0.0f;
-            *qp = make_uint4(pack_bf16x2(f[0], f[1]), pack_bf16x2(f[2], f[3]), pack_bf16x2(f[4], f[5]),
-                             pack_bf16x2(f[6], f[7]));
+              for (int i = 0; i < 4; ++i)
+                w[i] = (nb0 + 2 * i < a.k ? (w[i] & 0xFFFFu) : 0u) | (nb0 + 2 * i + 1 < a.k ? (w[i] & 0xFFFF0000u) : 0u);
+            }
+            *qp = make_uint4(w[0], w[1], w[2], w[3]);
           };
           if constexpr (kHeavy) {
             // two 16-column register buffers: the next load is in flight while

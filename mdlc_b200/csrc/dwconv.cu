@@ -95,12 +95,6 @@ MDLC_DEV void ldg4<float>(const float* p, float2 (&f)[2]) {
   f[1] = make_float2(v.z, v.w);
 }
 
-MDLC_DEV uint32_t clamp_bf16x2(uint32_t v, uint32_t lo2, uint32_t hi2) {
-  asm("max.bf16x2 %0, %0, %1;" : "+r"(v) : "r"(lo2));
-  asm("min.bf16x2 %0, %0, %1;" : "+r"(v) : "r"(hi2));
-  return v;
-}
-
 // bias + taps (+ residual) of 4 channels -> activation -> 4 output elements;
 // channels at or past c (the padding of the channel stride) are written as 0
 template <typename T, bool GEN>

@@ -125,6 +125,37 @@ def test_conv_bf16_tcgen05(ctx, case):
     check(got, want, 1e-2)
 
 
+EPI_ACTS = [
+    # activation code, clip bounds, oracle activation name
+    (L.ACT_NONE, (0.0, 6.0), None),
+    (L.ACT_RELU, (0.0, 6.0), "Relu"),
+    (L.ACT_CLIP, (0.0, 6.0), "Clip"),      # ReLU6: bounds exact in bf16 -> packed-pair clamp
+    (L.ACT_CLIP, (-0.75, 1.5), "Clip"),    # exact, lower bound below zero
+    (L.ACT_CLIP, (0.1, 2.0), "Clip"),      # 0.1 is not a bf16 value -> per-element fp32 clamp
+    (L.ACT_GELU, (0.0, 6.0), "Gelu"),
+]
+
+
+@pytest.mark.parametrize("k", [40, 72, 128])
+@pytest.mark.parametrize("act", range(len(EPI_ACTS)))
+def test_conv_bf16_epilogue_activations(ctx, act, k):
+    """bf16 epilogue: bias + residual by paired fp32 adds, clamp activations on
+    packed bf16 pairs (or per element when a bound is not exact in bf16), padding
+    columns of a chunk past k zeroed (k = 40, 72: ragged 64-column chunks)."""
+    code, clip, name = EPI_ACTS[act]
+    n, c, h, w = 2, 32, 9, 10
+    rng = np.random.default_rng(300 + 7 * act + k)
+    x = rng.standard_normal((n, c, h, w)).astype(np.float32)
+    wt = (rng.standard_normal((k, c, 3, 3)) * np.sqrt(2.0 / (c * 9))).astype(np.float32)
+    b = (rng.standard_normal(k) * 0.2).astype(np.float32)
+    res = rng.standard_normal((n, k, h, w)).astype(np.float32)
+    got = run_conv(ctx, x, wt, b, stride=1, pad=1, act=code, res=res, clip=clip)
+    want = oracle_conv(x, wt, b, stride=1, pad=1, act=name, res=res, clip=clip)
+    check(got, want, 1e-2)
+    if code == L.ACT_CLIP:
+        assert got.min() >= clip[0] - 1e-6 and got.max() <= clip[1] + 1e-6
+
+
 @pytest.mark.parametrize("cfg", [(64, 3), (128, 2), (256, 3), (192, 3), (64, 8), (128, 4)])
 def test_conv_bf16_tile_configs(ctx, cfg):
     """Every tile configuration the tuner may pick gives the same answer (odd M, k tail)."""
