@@ -313,6 +313,31 @@ struct ActParams {
 
 MDLC_DEV float apply_act(float v, const ActParams& p);
 
+// Paired fp32 arithmetic (add / mul / fma .rn.f32x2: two IEEE
+// round-to-nearest operations in one instruction) on float2 values kept in
+// 64-bit register pairs.
+MDLC_DEV unsigned long long f2_bits(const float2 v) { return *reinterpret_cast<const unsigned long long*>(&v); }
+MDLC_DEV float2 f2_from(unsigned long long b) { return *reinterpret_cast<float2*>(&b); }
+MDLC_DEV void fadd2(float2& d, const float2 b) {
+  unsigned long long dd = f2_bits(d);
+  asm("add.rn.f32x2 %0, %0, %1;" : "+l"(dd) : "l"(f2_bits(b)));
+  d = f2_from(dd);
+}
+MDLC_DEV float2 fmul2(const float2 a, const float2 b) {
+  unsigned long long d;
+  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));
+  return f2_from(d);
+}
+// a * b + c
+MDLC_DEV float2 fma2(const float2 a, const float2 b, const float2 c) {
+  unsigned long long d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)), "l"(f2_bits(c)));
+  return f2_from(d);
+}
+// d += a * b
+MDLC_DEV void ffma2(float2& d, const float2 a, const float2 b) { d = fma2(a, b, d); }
+MDLC_DEV float2 splat2(float v) { return make_float2(v, v); }
+
 // GELU(x) = x * Phi(x) = 0.5 x (1 + erf(x / sqrt 2)), branch-free so the
 // independent elements of an epilogue chunk interleave (erff branches on |x|,
 // which left the epilogue one latency chain at a time). erfc(z), z >= 0, is the
@@ -339,40 +364,50 @@ MDLC_DEV float gelu_f(float x) {
 // before the next, so the eight dependency chains interleave (one epilogue
 // warp per scheduler has no other warps to hide their latency).
 MDLC_DEV void gelu8(float (&x)[8]) {
-  float z[8], t[8], p[8];
+  // the same evaluation as gelu_f, two elements per instruction where the
+  // operation pairs (f32x2 multiply / fma), scalar for reciprocal and exp2
+  constexpr float kC[10] = {0.17087277f, -0.82215223f, 1.48851587f, -1.13520398f, 0.27886807f,
+                            -0.18628806f, 0.09678418f, 0.37409196f, 1.00002368f, -1.26551223f};
+  float2 z[4], t[4], p[4];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) z[i] = fabsf(x[i]) * 0.70710678118654752f;
+  for (int i = 0; i < 4; ++i)
+    z[i] = fmul2(make_float2(fabsf(x[2 * i]), fabsf(x[2 * i + 1])), splat2(0.70710678118654752f));
 #pragma unroll
-  for (int i = 0; i < 8; ++i) t[i] = __fdividef(1.0f, fmaf(0.5f, z[i], 1.0f));
+  for (int i = 0; i < 4; ++i) {
+    const float2 d = fma2(splat2(0.5f), z[i], splat2(1.0f));
+    t[i] = make_float2(__fdividef(1.0f, d.x), __fdividef(1.0f, d.y));
+  }
 #pragma unroll
-  for (int i = 0; i < 8; ++i) p[i] = fmaf(t[i], 0.17087277f, -0.82215223f);
+  for (int i = 0; i < 4; ++i) p[i] = fma2(t[i], splat2(kC[0]), splat2(kC[1]));
 #pragma unroll
-  for (int i = 0; i < 8; ++i) p[i] = fmaf(t[i], p[i], 1.48851587f);
+  for (int c = 2; c < 10; ++c)
 #pragma unroll
-  for (int i = 0; i < 8; ++i) p[i] = fmaf(t[i], p[i], -1.13520398f);
+    for (int i = 0; i < 4; ++i) p[i] = fma2(t[i], p[i], splat2(kC[c]));
 #pragma unroll
-  for (int i = 0; i < 8; ++i) p[i] = fmaf(t[i], p[i], 0.27886807f);
+  for (int i = 0; i < 4; ++i) {
+    // t * exp(p - z^2), exp(v) = 2^(v log2 e)
+    const float2 v = fmul2(fma2(fmul2(z[i], splat2(-1.0f)), z[i], p[i]), splat2(1.4426950408889634f));
+    float e0, e1;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e0) : "f"(v.x));
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e1) : "f"(v.y));
+    p[i] = fmul2(t[i], make_float2(e0, e1));
+  }
 #pragma unroll
-  for (int i = 0; i < 8; ++i) p[i] = fmaf(t[i], p[i], -0.18628806f);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) p[i] = fmaf(t[i], p[i], 0.09678418f);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) p[i] = fmaf(t[i], p[i], 0.37409196f);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) p[i] = fmaf(t[i], p[i], 1.00002368f);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) p[i] = fmaf(t[i], p[i], -1.26551223f);
-#pragma unroll
-  for (int i = 0; i < 8; ++i) p[i] = t[i] * __expf(fmaf(-z[i], z[i], p[i]));
-#pragma unroll
-  for (int i = 0; i < 8; ++i) x[i] = 0.5f * x[i] * (x[i] >= 0.0f ? 2.0f - p[i] : p[i]);
+  for (int i = 0; i < 4; ++i) {
+    // 1 + erf(x / sqrt 2) = 2 - erfc for x >= 0, erfc(|z|) for x < 0
+    const float2 q2 = fma2(p[i], splat2(-1.0f), splat2(2.0f));
+    const float2 q = make_float2(x[2 * i] >= 0.0f ? q2.x : p[i].x, x[2 * i + 1] >= 0.0f ? q2.y : p[i].y);
+    const float2 r = fmul2(fmul2(make_float2(x[2 * i], x[2 * i + 1]), splat2(0.5f)), q);
+    x[2 * i] = r.x;
+    x[2 * i + 1] = r.y;
+  }
 }
 MDLC_DEV void sigmoid8(float (&x)[8]) {
   float e[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) e[i] = expf(-x[i]);
+  for (int i = 0; i < 8; ++i) e[i] = __expf(-x[i]);
 #pragma unroll
-  for (int i = 0; i < 8; ++i) x[i] = 1.0f / (1.0f + e[i]);
+  for (int i = 0; i < 8; ++i) x[i] = __fdividef(1.0f, 1.0f + e[i]);
 }
 
 // Activation fixed at compile time (ACT >= 0) or chosen at run time (ACT == -1).
@@ -409,13 +444,6 @@ MDLC_DEV uint32_t pack_bf16x2(float lo, float hi) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 MDLC_DEV float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }
-// Paired fp32 add (add.rn.f32x2: two IEEE round-to-nearest adds in one
-// instruction) on a float2 kept in a 64-bit register pair.
-MDLC_DEV void fadd2(float2& d, const float2 b) {
-  unsigned long long dd = *reinterpret_cast<unsigned long long*>(&d);
-  asm("add.rn.f32x2 %0, %0, %1;" : "+l"(dd) : "l"(*reinterpret_cast<const unsigned long long*>(&b)));
-  d = *reinterpret_cast<float2*>(&dd);
-}
 // Clamp both halves of a bf16 pair to [lo, hi] (given as bf16 pairs). With
 // bounds exact in bf16, clamping after rounding to bf16 equals rounding after
 // clamping in fp32 (rounding is monotonic); NaN becomes lo, as with

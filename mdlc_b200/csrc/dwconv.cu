@@ -53,16 +53,6 @@ struct DwTmaArgs {
   uint32_t lo2, hi2;                // bf16 output: the clamp bounds as bf16 pairs
 };
 
-// Paired fp32 multiply-add (one fma.rn.f32x2: two IEEE fmas), on float2 kept
-// in a 64-bit register pair.
-MDLC_DEV void ffma2(float2& d, const float2 a, const float2 b) {
-  unsigned long long dd = *reinterpret_cast<unsigned long long*>(&d);
-  asm("fma.rn.f32x2 %0, %1, %2, %0;"
-      : "+l"(dd)
-      : "l"(*reinterpret_cast<const unsigned long long*>(&a)), "l"(*reinterpret_cast<const unsigned long long*>(&b)));
-  d = *reinterpret_cast<float2*>(&dd);
-}
-
 // 4 channels of one pixel from shared memory, as two fp32 pairs
 template <typename T>
 MDLC_DEV void lds4(const uint8_t* p, float2 (&f)[2]);

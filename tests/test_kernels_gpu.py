@@ -133,6 +133,7 @@ EPI_ACTS = [
     (L.ACT_CLIP, (-0.75, 1.5), "Clip"),    # exact, lower bound below zero
     (L.ACT_CLIP, (0.1, 2.0), "Clip"),      # 0.1 is not a bf16 value -> per-element fp32 clamp
     (L.ACT_GELU, (0.0, 6.0), "Gelu"),
+    (L.ACT_SIGMOID, (0.0, 6.0), "Sigmoid"),
 ]
 
 
