@@ -568,6 +568,7 @@ __global__ void __launch_bounds__(threads_for<ESZ>(), (Occ<BN, STAGES, ESZ, AMOD
     uint8_t* stage_ptr0 = smem + L::kE + ew * 2 * kEBuf;
     const bool tma_epi = a.tma_epi;
     int local = 0, chunk_i = 0;
+    int staged_n0[2] = {-1, -1};  // n0 whose parameters each staging buffer holds
     uint32_t res_use0 = 0, res_use1 = 0;  // completed loads per residual buffer (phase parity)
     int res_pending = -1;                 // residual buffer with a load in flight not yet awaited
     uint32_t res_pending_par = 0;
@@ -710,8 +711,15 @@ __global__ void __launch_bounds__(threads_for<ESZ>(), (Occ<BN, STAGES, ESZ, AMOD
       // constant low word | constant high word
       int32_t* sq = reinterpret_cast<int32_t*>(smem + L::kBias) + buf * 5 * BN;
       if (tma_epi) {
-        // stage this tile's epilogue parameters (and the first residual chunk) while the main loop runs
-        if constexpr (ESZ == 2) {
+        // stage this tile's epilogue parameters (and the first residual chunk)
+        // while the main loop runs. A buffer that already holds this n0's
+        // parameters is kept: in a layer whose channels fit one tile (most
+        // memory-bound layers) only the first two tiles load them, so the
+        // parameter loads' latency is off the epilogue's critical path.
+        const bool restage = staged_n0[buf] != n0;  // uniform over the epilogue warps
+        if (restage) staged_n0[buf] = n0;
+        if (!restage) {
+        } else if constexpr (ESZ == 2) {
           for (int i = etid; i < BN; i += 128)
             sbias[i] = (a.bias && n0 + i < a.k) ? __ldg(static_cast<const float*>(a.bias) + n0 + i) : 0.0f;
         } else {
@@ -742,6 +750,8 @@ __global__ void __launch_bounds__(threads_for<ESZ>(), (Occ<BN, STAGES, ESZ, AMOD
           res_pending = sbuf;
           res_pending_par = (sbuf ? res_use1 : res_use0) & 1;
         }
+        // every tile: also bounds the epilogue warps' skew to one tile, so a
+        // restage never overwrites a buffer another warp still reads
         asm volatile("bar.sync 1, 128;" ::: "memory");
       }
       bool ok = true;
@@ -792,17 +802,22 @@ __global__ void __launch_bounds__(threads_for<ESZ>(), (Occ<BN, STAGES, ESZ, AMOD
           // activation is not copied 64 times into the instruction stream.
           constexpr bool kHeavy =
               ESZ == 2 && (ACT == MDLC_ACT_GELU || ACT == MDLC_ACT_SIGMOID || ACT == -1);
+          // columns of this chunk inside the output's channel stride (1..64):
+          // a narrow layer (16 or 24 output channels in a 64-wide tile)
+          // loads, converts and stages only those; the TMA store clips the rest
+          const int valid = a.ks - (n0 + c0) < 64 ? a.ks - (n0 + c0) : 64;  // warp-uniform
           uint32_t v[64];
           if constexpr (!kHeavy) {
             tmem_ld16(taddr + c0, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
-            tmem_ld16(taddr + c0 + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
-            tmem_ld16(taddr + c0 + 32, *reinterpret_cast<uint32_t(*)[16]>(&v[32]));
-            tmem_ld16(taddr + c0 + 48, *reinterpret_cast<uint32_t(*)[16]>(&v[48]));
+            if (valid > 16) tmem_ld16(taddr + c0 + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
+            if (valid > 32) tmem_ld16(taddr + c0 + 32, *reinterpret_cast<uint32_t(*)[16]>(&v[32]));
+            if (valid > 48) tmem_ld16(taddr + c0 + 48, *reinterpret_cast<uint32_t(*)[16]>(&v[48]));
             tmem_ld_wait();
           }
           if constexpr (ESZ == 1) {
 #pragma unroll
             for (int q = 0; q < 4; ++q) {  // 16-column (16-byte) groups
+              if (16 * q >= valid) break;
               uint4* qp = reinterpret_cast<uint4*>(sp + ((q ^ sw) << 4));
               uint4 rr = make_uint4(0, 0, 0, 0);
               if (a.res) rr = *qp;
@@ -960,19 +975,22 @@ __global__ void __launch_bounds__(threads_for<ESZ>(), (Occ<BN, STAGES, ESZ, AMOD
             tmem_ld16(taddr + c0, va);
             tmem_ld_wait();
 #pragma unroll 1
-            for (int j = 0; j < 4; j += 2) {
-              tmem_ld16(taddr + c0 + 16 * (j + 1), vb);
+            for (int j = 0; j < 4 && 16 * j < valid; j += 2) {
+              const bool second = 16 * (j + 1) < valid;
+              if (second) tmem_ld16(taddr + c0 + 16 * (j + 1), vb);
               group(2 * j, va);
-              group(2 * j + 1, va + 8);
+              if (16 * j + 8 < valid) group(2 * j + 1, va + 8);
               tmem_ld_wait();
-              if (j + 2 < 4) tmem_ld16(taddr + c0 + 16 * (j + 2), va);
+              if (!second) break;
+              if (j + 2 < 4 && 16 * (j + 2) < valid) tmem_ld16(taddr + c0 + 16 * (j + 2), va);
               group(2 * j + 2, vb);
-              group(2 * j + 3, vb + 8);
+              if (16 * (j + 1) + 8 < valid) group(2 * j + 3, vb + 8);
               tmem_ld_wait();
             }
           } else {
 #pragma unroll
-            for (int q = 0; q < 8; ++q) group(q, v + 8 * q);
+            for (int q = 0; q < 8; ++q)
+              if (8 * q < valid) group(q, v + 8 * q);
           }
           }
           fence_proxy_async_smem();

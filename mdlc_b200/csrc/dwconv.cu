@@ -135,10 +135,13 @@ __global__ void __launch_bounds__(kDwThreads, 1)
   const int tid = threadIdx.x;
   const int cb_bytes = a.cb_elems * esz;
   const int per_img = a.tiles_x * a.tiles_y;
-  const int per_cb = a.total / a.cblocks;  // tiles of one channel block
+  // tiles are numbered channel block minor and the grid is a multiple of the
+  // block count, so a CTA keeps one channel block (its weights stay in
+  // registers) while the CTAs of the other blocks work on the same pixels at
+  // the same time: the 64-byte DRAM bursts and halo pixels they share are L2 hits
   auto decode = [&](int tile, int& cb, int& img, int& ty, int& tx) {
-    cb = tile / per_cb;
-    int t = tile - cb * per_cb;
+    int t = tile / a.cblocks;
+    cb = tile - t * a.cblocks;
     img = t / per_img;
     t -= img * per_img;
     ty = t / a.tiles_x;
@@ -391,8 +394,12 @@ int conv_dw_tma(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const flo
       a.hi2 = (uint32_t)hb | ((uint32_t)hb << 16);
     }
   }
-  const long long slots = (long long)ctx->num_sms;  // one CTA per SM
-  const unsigned grid = (unsigned)(total < slots ? total : slots);
+  // one CTA per SM, a multiple of the channel block count (see decode)
+  const long long per_block = total / a.cblocks;
+  long long ctas_per_block = ctx->num_sms / a.cblocks;
+  if (ctas_per_block < 1) ctas_per_block = 1;
+  if (ctas_per_block > per_block) ctas_per_block = per_block;
+  const unsigned grid = (unsigned)(ctas_per_block * a.cblocks);
   void (*kern)(const CUtensorMap, const DwTmaArgs);
   const bool gen = a.act_kind == 2;
   if (SH == 1) {

@@ -748,5 +748,11 @@ def lower(graph, shapes: dict, dtype: int, s2d: bool = True) -> Lowered:
             lo.tensors[name].dtype = L.S8
     if s2d:
         space_to_depth_stem(lo)
-        pair_stem_columns(lo)
+        # Pairing buys 128-wide MMAs and fewer, larger loads at the price of
+        # 1.5x the reduction length (4x3 super-pixel taps hold 4x4 useful
+        # ones). bf16 / int8 stems are load- and issue-bound, so they pair; an
+        # fp32 stem runs every MMA three times (3xTF32) and is MMA-bound, so
+        # it keeps the shorter unpaired reduction.
+        if dtype != L.F32:
+            pair_stem_columns(lo)
     return lo
