@@ -176,6 +176,12 @@ def call_work(dev, call):
         e = _esz(d.dtype)
         cls = {0: "maxpool", 1: "avgpool", 2: "gap"}[d.kind]
         return cls, "hbm", d.n * d.h * d.w * d.c_stride * e + d.n * d.oh * d.ow * d.c_stride * e, 0.0
+    if kind == "se":
+        d = call[1]
+        e = _esz(d.dtype)
+        # pooled input, gate output (n x c_stride each) and both fp32 weight matrices
+        nbytes = 2 * d.n * d.c_stride * e + 2 * d.rd * d.c * 4
+        return "se_fc", "hbm", nbytes, 4.0 * d.n * d.rd * d.c
     if kind in ("copy", "softmax"):
         d = call[1]
         e = _esz(d.dtype)
@@ -243,6 +249,8 @@ def launch_times(exe, steps):
                 timed(cls, bound, nbytes, flops, lambda: ctx.copy4d(c[1], c[2], c[3]))
             elif c[0] == "softmax":
                 timed(cls, bound, nbytes, flops, lambda: ctx.softmax(c[1], c[2], c[3]))
+            elif c[0] == "se":
+                timed(cls, bound, nbytes, flops, lambda: ctx.se_fc(*c[1:]))
             else:
                 timed(cls, bound, nbytes, flops, lambda: ctx.eltwise(c[1], c[2], c[3]))
         if len(io) > n_in:

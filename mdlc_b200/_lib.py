@@ -95,6 +95,13 @@ class SoftmaxDesc(C.Structure):
     _fields_ = [("dtype", C.c_int32), ("dims", C.c_int32 * 4), ("cs", C.c_int32), ("axis", C.c_int32)]
 
 
+class SeDesc(C.Structure):
+    _fields_ = [("n", C.c_int32), ("c", C.c_int32), ("c_stride", C.c_int32), ("rd", C.c_int32),
+                ("dtype", C.c_int32), ("act1", C.c_int32), ("act2", C.c_int32),
+                ("alpha1", C.c_float), ("beta1", C.c_float), ("lo1", C.c_float), ("hi1", C.c_float),
+                ("alpha2", C.c_float), ("beta2", C.c_float), ("lo2", C.c_float), ("hi2", C.c_float)]
+
+
 # exported symbol -> (argtypes, restype); the CPU test suite checks every
 # function declared in include/mdlc_b200.h is exported and listed here.
 _P, _I, _S = C.c_void_p, C.c_int, C.c_size_t
@@ -137,6 +144,7 @@ SIGNATURES = {
     "mdlc_nchw_to_s2d": ([_P, _P, _I, _I, _I, _I, _P, _I, _I, C.c_float, _I], C.c_int),
     "mdlc_copy4d": ([_P, C.POINTER(CopyDesc), _P, _P], C.c_int),
     "mdlc_softmax": ([_P, C.POINTER(SoftmaxDesc), _P, _P], C.c_int),
+    "mdlc_se_fc": ([_P, C.POINTER(SeDesc), _P, _P, _P, _P, _P, _P], C.c_int),
     "mdlc_graph_begin": ([_P], C.c_int),
     "mdlc_graph_end": ([_P], C.c_int),
     "mdlc_graph_launch": ([_P], C.c_int),
@@ -310,6 +318,11 @@ class Context:
 
     def softmax(self, desc: SoftmaxDesc, x, y) -> None:
         self.check(self.lib.mdlc_softmax(self.h, C.byref(desc), C.c_void_p(x), C.c_void_p(y)), "softmax")
+
+    def se_fc(self, desc: SeDesc, pooled, w1, b1, w2t, b2, gate) -> None:
+        self.check(self.lib.mdlc_se_fc(self.h, C.byref(desc), C.c_void_p(pooled), C.c_void_p(w1),
+                                       C.c_void_p(b1 or None), C.c_void_p(w2t), C.c_void_p(b2 or None),
+                                       C.c_void_p(gate)), "se_fc")
 
     def to_nhwc(self, x, n, c, h, w, y, cs, dtype, inv_scale=1.0, zp=0) -> None:
         self.check(self.lib.mdlc_nchw_to_nhwc(self.h, C.c_void_p(x), n, c, h, w, C.c_void_p(y), cs, dtype,

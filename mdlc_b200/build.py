@@ -9,14 +9,19 @@ access). ``_lib`` loads it when ``MDLC_B200_LIB=check``.
 
 Each ``csrc/*.cu`` is compiled by nvcc in parallel into ``_build/`` and linked
 into ``mdlc_b200/libmdlc_b200.so`` next to this file, which is where
-:mod:`mdlc_b200._lib` loads it from. Rebuilds only when a source or header is
-newer than the library.
+:mod:`mdlc_b200._lib` loads it from. Incremental by content: each object
+records a digest of its source, every header and the flags, taken before it
+is compiled, and the library the digest of its objects' digests (in
+``manifest.json`` of the build folder), so a file edited while a build runs
+is compiled again by the next build.
 """
 
 from __future__ import annotations
 
 import argparse
 import glob
+import hashlib
+import json
 import os
 import subprocess
 import sys
@@ -46,32 +51,58 @@ def _deps():
         glob.glob(os.path.join(INCLUDE, "*.h"))
 
 
-def up_to_date(lib: str = LIB) -> bool:
+def _digest(*parts: bytes) -> str:
+    h = hashlib.sha256()
+    for p in parts:
+        h.update(len(p).to_bytes(8, "little"))
+        h.update(p)
+    return h.hexdigest()
+
+
+def _read(path: str) -> bytes:
+    with open(path, "rb") as f:
+        return f.read()
+
+
+def _keys(flags: str) -> tuple:
+    """(source basename -> digest, library digest) of the files as they are now."""
+    headers = sorted(p for p in _deps() if not p.endswith(".cu"))
+    hdr = _digest(*[p.encode() + b"\0" + _read(p) for p in headers])
+    keys = {os.path.basename(s): _digest(flags.encode(), hdr.encode(), _read(s)) for s in _sources()}
+    return keys, _digest(*[f"{k}={v}".encode() for k, v in sorted(keys.items())])
+
+
+def _manifest(bdir: str) -> dict:
+    try:
+        with open(os.path.join(bdir, "manifest.json")) as f:
+            return json.load(f)
+    except (OSError, ValueError):
+        return {}
+
+
+def up_to_date(lib: str = LIB, check: bool = False) -> bool:
+    bdir = CHECK_BUILD if check else BUILD
     if not os.path.exists(lib):
         return False
-    t = os.path.getmtime(lib)
-    return all(os.path.getmtime(p) <= t for p in _deps())
+    _, lib_key = _keys(" ".join([*ARCH, *FLAGS, *(("-DMDLC_CHECK",) if check else ())]))
+    return _manifest(bdir).get("__lib__") == lib_key
 
 
 def build(force: bool = False, verbose: bool = False, extra=(), check: bool = False) -> str:
     lib, bdir = (CHECK_LIB, CHECK_BUILD) if check else (LIB, BUILD)
     if check:
         extra = (*extra, "-DMDLC_CHECK")
-    if not force and up_to_date(lib):
-        return lib
     os.makedirs(bdir, exist_ok=True)
-
-    headers = [p for p in _deps() if not p.endswith(".cu")]
-    newest_header = max((os.path.getmtime(p) for p in headers), default=0.0)
-    flags_file = os.path.join(bdir, "flags.txt")
     flags = " ".join([*ARCH, *FLAGS, *extra])
-    same_flags = os.path.exists(flags_file) and open(flags_file).read() == flags
+    keys, lib_key = _keys(flags)          # digests of the inputs as this build reads them
+    manifest = _manifest(bdir)
+    if not force and os.path.exists(lib) and manifest.get("__lib__") == lib_key:
+        return lib
 
     def compile_one(src):
-        obj = os.path.join(bdir, os.path.basename(src) + ".o")
-        # incremental: an object newer than its source and every header is reused
-        if (not force and same_flags and os.path.exists(obj) and
-                os.path.getmtime(obj) >= max(os.path.getmtime(src), newest_header)):
+        name = os.path.basename(src)
+        obj = os.path.join(bdir, name + ".o")
+        if not force and os.path.exists(obj) and manifest.get(name) == keys[name]:
             return obj, ""
         cmd = [NVCC, *ARCH, *FLAGS, *extra, "-c", src, "-o", obj]
         if verbose:
@@ -83,8 +114,6 @@ def build(force: bool = False, verbose: bool = False, extra=(), check: bool = Fa
 
     with ThreadPoolExecutor(max_workers=min(8, os.cpu_count() or 4)) as ex:
         results = list(ex.map(compile_one, _sources()))
-    with open(flags_file, "w") as f:
-        f.write(flags)
     if verbose:
         for _, log in results:
             sys.stderr.write(log)
@@ -95,6 +124,8 @@ def build(force: bool = False, verbose: bool = False, extra=(), check: bool = Fa
     if r.returncode != 0:
         raise RuntimeError(f"link failed:\n{r.stderr}")
     os.replace(tmp, lib)
+    with open(os.path.join(bdir, "manifest.json"), "w") as f:
+        json.dump({**keys, "__lib__": lib_key}, f, indent=1, sort_keys=True)
     return lib
 
 

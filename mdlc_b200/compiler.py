@@ -126,6 +126,12 @@ class _Device:
                 packed = L.pack_weights(desc, wt)
                 self.wbuf[wname] = self.ctx.to_device(packed)
                 self.bbuf[wname] = self.ctx.to_device(bias)
+        # squeeze-excite gates: fp32 FC weights and biases as they are
+        self.sebuf = {}
+        for st in lo.steps:
+            if st.kind == "se":
+                p = st.params
+                self.sebuf[id(st)] = tuple(self.ctx.to_device(p[k]) for k in ("w1", "b1", "w2t", "b2"))
         # elementwise constant operands are read in the tensors' own dtype
         self.cbuf = {name: self.ctx.to_device(_bf16_bits(arr) if lo.dtype == L.BF16 else arr)
                      for name, arr in lo.consts.items()}
@@ -229,6 +235,21 @@ class _Device:
                 for i, v in enumerate((t.n, t.c, t.h, t.w)):
                     d.dims[i] = v
                 calls.append(("softmax", d, self.ptr(st.inputs[0]), self.ptr(st.outputs[0])))
+            elif st.kind == "se":
+                xt, yt = lo.tensors[st.inputs[0]], lo.tensors[st.outputs[0]]
+                p = st.params
+                rd, c = p["w1"].shape
+                d = L.SeDesc(n=xt.n, c=c, c_stride=xt.cs, rd=rd, dtype=xt.dtype)
+                if yt.cs != xt.cs:
+                    raise RuntimeError(f"internal: se step {st.label()} with different channel strides")
+                for i, (act, a) in enumerate(((p["act1"], p["attrs1"]), (p["act2"], p["attrs2"])), 1):
+                    setattr(d, f"act{i}", lowering.ACT_CODES[act])
+                    setattr(d, f"alpha{i}", float(a.get("alpha", 0.2 if act == "HardSigmoid" else 0.01)))
+                    setattr(d, f"beta{i}", float(a.get("beta", 0.5)))
+                    setattr(d, f"lo{i}", -np.inf if a.get("clip_min") is None else float(a["clip_min"]))
+                    setattr(d, f"hi{i}", np.inf if a.get("clip_max") is None else float(a["clip_max"]))
+                w1, b1, w2t, b2 = self.sebuf[id(st)]
+                calls.append(("se", d, self.ptr(st.inputs[0]), w1, b1, w2t, b2, self.ptr(st.outputs[0])))
             elif st.kind == "pool":
                 xt, yt = lo.tensors[st.inputs[0]], lo.tensors[st.outputs[0]]
                 p = st.params
@@ -269,6 +290,8 @@ class _Device:
                 ctx.copy4d(c[1], c[2], c[3])
             elif c[0] == "softmax":
                 ctx.softmax(c[1], c[2], c[3])
+            elif c[0] == "se":
+                ctx.se_fc(*c[1:])
             else:
                 ctx.eltwise(c[1], c[2], c[3])
 
@@ -480,7 +503,9 @@ class Executable:
     def _lowered_for(self, batch):
         if batch not in self._lowered:
             shp = S.infer(self.graph, batch)
-            lo = lowering.lower(self.graph, shp, self.dtype)
+            # a keep_all executable (int8 calibration, debugging) keeps every
+            # activation, so it does not fuse squeeze-excite gates away
+            lo = lowering.lower(self.graph, shp, self.dtype, fuse_se=not self.keep_all)
             for o in lo.outputs:      # dense-conv graph outputs are written as fp32 directly
                 prod = [st for st in lo.steps if o in st.outputs]
                 if prod and prod[0].kind == "conv" and lo.weights[prod[0].params["weight"]][0]["groups"] == 1:

@@ -313,16 +313,11 @@ struct ActParams {
 
 MDLC_DEV float apply_act(float v, const ActParams& p);
 
-// Paired fp32 arithmetic (add / mul / fma .rn.f32x2: two IEEE
+// Paired fp32 arithmetic (mul / fma .rn.f32x2: two IEEE
 // round-to-nearest operations in one instruction) on float2 values kept in
 // 64-bit register pairs.
 MDLC_DEV unsigned long long f2_bits(const float2 v) { return *reinterpret_cast<const unsigned long long*>(&v); }
 MDLC_DEV float2 f2_from(unsigned long long b) { return *reinterpret_cast<float2*>(&b); }
-MDLC_DEV void fadd2(float2& d, const float2 b) {
-  unsigned long long dd = f2_bits(d);
-  asm("add.rn.f32x2 %0, %0, %1;" : "+l"(dd) : "l"(f2_bits(b)));
-  d = f2_from(dd);
-}
 MDLC_DEV float2 fmul2(const float2 a, const float2 b) {
   unsigned long long d;
   asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(f2_bits(a)), "l"(f2_bits(b)));

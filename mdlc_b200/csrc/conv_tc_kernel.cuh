@@ -572,6 +572,7 @@ __global__ void __launch_bounds__(threads_for<ESZ>(), (Occ<BN, STAGES, ESZ, AMOD
     uint32_t res_use0 = 0, res_use1 = 0;  // completed loads per residual buffer (phase parity)
     int res_pending = -1;                 // residual buffer with a load in flight not yet awaited
     uint32_t res_pending_par = 0;
+    bool res_next = false;  // the next tile's first residual chunk was loaded during this tile's last chunk
     volatile int* last_flag = reinterpret_cast<volatile int*>(smem + L::kMisc + 8);
     int lc = 0;  // accumulator slot uses so far (the MMA issuer counts the same way)
     for (int u = blockIdx.x; u < num_units; u += gridDim.x, ++local) {
@@ -705,6 +706,19 @@ __global__ void __launch_bounds__(threads_for<ESZ>(), (Occ<BN, STAGES, ESZ, AMOD
         else
           tma_load_2d(dst, &tmap_r, c, m0 + ew * 32, bar);
       };
+      // the first residual chunk of this CTA's next tile (S == 1 only)
+      const int u_next = u + (int)gridDim.x;
+      auto load_res_next = [&](uint32_t dst, uint32_t bar) {
+        const int t2 = u_next;
+        const int n2 = (t2 % a.num_n_tiles) * BN;
+        if constexpr (AMODE == 4) {
+          int img2, ty2, tx2;
+          halo_tile(t2 / a.num_n_tiles, img2, ty2, tx2);
+          tma_load_4d(dst, &tmap_r, n2, tx2 * kHaloTW, ty2 * kHaloTH + ew * (32 / kHaloTW), img2, bar);
+        } else {
+          tma_load_2d(dst, &tmap_r, n2, (t2 / a.num_n_tiles) * kBM + ew * 32, bar);
+        }
+      };
       float* sbias = reinterpret_cast<float*>(smem + L::kBias) + buf * BN;
       // 8-bit, fp32 form: bias32 | fp32 scale; fixed point: multiplier |
       // residual multiplier | shifts (min(S, 32) | max(S - 32, 0) << 8) |
@@ -740,7 +754,7 @@ __global__ void __launch_bounds__(threads_for<ESZ>(), (Occ<BN, STAGES, ESZ, AMOD
             }
           }
         }
-        if (a.res) {
+        if (a.res && !res_next) {
           const int sbuf = chunk_i & 1;
           if (lane == 0) {
             bulk_wait_read<0>();
@@ -750,6 +764,7 @@ __global__ void __launch_bounds__(threads_for<ESZ>(), (Occ<BN, STAGES, ESZ, AMOD
           res_pending = sbuf;
           res_pending_par = (sbuf ? res_use1 : res_use0) & 1;
         }
+        res_next = false;
         // every tile: also bounds the epilogue warps' skew to one tile, so a
         // restage never overwrites a buffer another warp still reads
         asm volatile("bar.sync 1, 128;" ::: "memory");
@@ -791,6 +806,17 @@ __global__ void __launch_bounds__(threads_for<ESZ>(), (Occ<BN, STAGES, ESZ, AMOD
               }
               res_pending = sbuf ^ 1;
               res_pending_par = (sbuf ^ 1 ? res_use1 : res_use0) & 1;
+            } else if (S == 1 && u_next < num_units) {
+              // last chunk: the next tile's first residual chunk (its chunk 0
+              // uses the other buffer), so its latency hides behind this chunk
+              if (lane == 0) {
+                bulk_wait_read<0>();
+                mbar_arrive_expect_tx(resid(ew, sbuf ^ 1), kEBuf);
+                load_res_next(stage0 + (sbuf ^ 1) * kEBuf, resid(ew, sbuf ^ 1));
+              }
+              res_pending = sbuf ^ 1;
+              res_pending_par = (sbuf ^ 1 ? res_use1 : res_use0) & 1;
+              res_next = true;
             }
           } else {
             if (lane == 0) bulk_wait_read<1>();  // the store issued two chunks ago has read this buffer
@@ -917,8 +943,8 @@ __global__ void __launch_bounds__(threads_for<ESZ>(), (Occ<BN, STAGES, ESZ, AMOD
             }
           } else {
           // one 8-column (16-byte) group: + bias (+ residual), activation, bf16.
-          // Paired fp32 adds; clamp-type activations on the packed bf16 pairs;
-          // padding columns (only in a chunk that reaches past k) zeroed last.
+          // Clamp-type activations on the packed bf16 pairs; padding columns
+          // (only in a chunk that reaches past k) zeroed last.
           constexpr bool kClampAct = ACT == MDLC_ACT_NONE || ACT == MDLC_ACT_RELU || ACT == MDLC_ACT_CLIP;
           const bool full = n0 + c0 + 64 <= a.k;
           auto group = [&](int q, const uint32_t* vv) {
@@ -929,16 +955,14 @@ __global__ void __launch_bounds__(threads_for<ESZ>(), (Occ<BN, STAGES, ESZ, AMOD
                             make_float2(__uint_as_float(vv[2]), __uint_as_float(vv[3])),
                             make_float2(__uint_as_float(vv[4]), __uint_as_float(vv[5])),
                             make_float2(__uint_as_float(vv[6]), __uint_as_float(vv[7]))};
-            fadd2(f2[0], make_float2(b0.x, b0.y));
-            fadd2(f2[1], make_float2(b0.z, b0.w));
-            fadd2(f2[2], make_float2(b1.x, b1.y));
-            fadd2(f2[3], make_float2(b1.z, b1.w));
+            f2[0].x += b0.x; f2[0].y += b0.y; f2[1].x += b0.z; f2[1].y += b0.w;
+            f2[2].x += b1.x; f2[2].y += b1.y; f2[3].x += b1.z; f2[3].y += b1.w;
             if (a.res) {
               const uint4 r = *qp;
-              fadd2(f2[0], make_float2(bf16_lo(r.x), bf16_hi(r.x)));
-              fadd2(f2[1], make_float2(bf16_lo(r.y), bf16_hi(r.y)));
-              fadd2(f2[2], make_float2(bf16_lo(r.z), bf16_hi(r.z)));
-              fadd2(f2[3], make_float2(bf16_lo(r.w), bf16_hi(r.w)));
+              f2[0].x += bf16_lo(r.x); f2[0].y += bf16_hi(r.x);
+              f2[1].x += bf16_lo(r.y); f2[1].y += bf16_hi(r.y);
+              f2[2].x += bf16_lo(r.z); f2[2].y += bf16_hi(r.z);
+              f2[3].x += bf16_lo(r.w); f2[3].y += bf16_hi(r.w);
             }
             uint32_t w[4];
             if (kClampAct && a.act_packed) {

@@ -78,7 +78,7 @@ class TensorSpec:
 
 @dataclass
 class Step:
-    kind: str                      # "conv" | "pool" | "eltwise"
+    kind: str                      # "conv" | "pool" | "eltwise" | "copy" | "softmax" | "se"
     inputs: list                   # activation tensors read
     outputs: list                  # activation tensors written
     nodes: list                    # IR node names covered
@@ -738,7 +738,53 @@ def pair_stem_columns(lo: Lowered) -> None:
         st.params["paired"] = True
 
 
-def lower(graph, shapes: dict, dtype: int, s2d: bool = True) -> Lowered:
+def _is_fc_step(lo: Lowered, st: Step) -> bool:
+    if st.kind != "conv" or st.params.get("residual") or st.params.get("s2d"):
+        return False
+    g = lo.weights[st.params["weight"]][0]
+    return (g["r"], g["s"], g["h"], g["w"], g["oh"], g["ow"], g["groups"]) == (1, 1, 1, 1, 1, 1, 1) \
+        and not g.get("paired")
+
+
+def fuse_squeeze_excite(lo: Lowered) -> None:
+    """Two 1x1 convs on a 1x1 map in a row, the first's output read only by
+    the second and the second's channel count equal to the first's input
+    channels (FC, act, FC, act of a squeeze-excite gate): one "se" step, run by
+    mdlc_se_fc. The weights leave ``lo.weights`` (they are not conv-packed):
+    w1 [rd][c] and w2 transposed, [rd][c], with the biases, go into the step."""
+    readers = {}
+    for st in lo.steps:
+        for t in st.inputs:
+            readers[t] = readers.get(t, 0) + 1
+        if st.params.get("residual"):
+            readers[st.params["residual"]] = readers.get(st.params["residual"], 0) + 1
+    out, i = [], 0
+    while i < len(lo.steps):
+        a = lo.steps[i]
+        b = lo.steps[i + 1] if i + 1 < len(lo.steps) else None
+        if (b is not None and _is_fc_step(lo, a) and _is_fc_step(lo, b) and b.inputs[0] == a.outputs[0]
+                and readers.get(a.outputs[0], 0) == 1 and a.outputs[0] not in lo.outputs
+                and b.outputs[0] not in lo.outputs):
+            ga, wa, ba = lo.weights[a.params["weight"]]
+            gb, wb, bb = lo.weights[b.params["weight"]]
+            c, rd = ga["c"], ga["k"]
+            if gb["c"] == rd and gb["k"] == c and c <= 4096 and rd <= 1024:
+                del lo.weights[a.params["weight"]], lo.weights[b.params["weight"]]
+                out.append(Step("se", [a.inputs[0]], [b.outputs[0]], a.nodes + b.nodes, dict(
+                    w1=np.ascontiguousarray(np.asarray(wa, np.float32).reshape(rd, c)),
+                    b1=np.ascontiguousarray(ba[:rd], np.float32),
+                    w2t=np.ascontiguousarray(np.asarray(wb, np.float32).reshape(c, rd).T),
+                    b2=np.ascontiguousarray(bb[:c], np.float32),
+                    act1=a.params["act"], attrs1=a.params["attrs"], act2=b.params["act"], attrs2=b.params["attrs"],
+                    flops=ga["flops"] + gb["flops"])))
+                i += 2
+                continue
+        out.append(a)
+        i += 1
+    lo.steps = out
+
+
+def lower(graph, shapes: dict, dtype: int, s2d: bool = True, fuse_se: bool = True) -> Lowered:
     """Lower a post-pass graph to backend steps. For 8-bit lowering the graph
     inputs are signed (symmetric int8, zero point 0: padded taps read real
     zeros) and every other activation is unsigned."""
@@ -755,4 +801,6 @@ def lower(graph, shapes: dict, dtype: int, s2d: bool = True) -> Lowered:
         # it keeps the shorter unpaired reduction.
         if dtype != L.F32:
             pair_stem_columns(lo)
+    if fuse_se and dtype in (L.BF16, L.F32):
+        fuse_squeeze_excite(lo)
     return lo

@@ -31,7 +31,8 @@ def test_library_exports_every_declared_function():
 
 STRUCTS = {"mdlc_epilogue": "Epilogue", "mdlc_conv_desc": "ConvDesc", "mdlc_tile_cfg": "TileCfg",
            "mdlc_pool_desc": "PoolDesc", "mdlc_ew_instr": "EwInstr", "mdlc_ew_prog": "EwProg",
-           "mdlc_gemm_desc": "GemmDesc", "mdlc_copy_desc": "CopyDesc", "mdlc_softmax_desc": "SoftmaxDesc"}
+           "mdlc_gemm_desc": "GemmDesc", "mdlc_copy_desc": "CopyDesc", "mdlc_softmax_desc": "SoftmaxDesc",
+           "mdlc_se_desc": "SeDesc"}
 
 
 def test_struct_layouts_match_header(tmp_path):

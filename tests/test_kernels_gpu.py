@@ -818,3 +818,54 @@ def test_dwconv2d_entry_point(ctx, dtype):
     for p in (wp, xd, bd, y1, y2):
         ctx.free(p)
     np.testing.assert_array_equal(r1, r2)
+
+
+SE_CASES = [
+    # n, c, rd, act1, act2
+    (6, 56, 16, L.ACT_RELU, L.ACT_SIGMOID),       # RepViT stage 1 (n not a multiple of 4)
+    (4, 448, 112, L.ACT_RELU, L.ACT_SIGMOID),     # RepViT stage 4
+    (9, 100, 24, L.ACT_RELU, L.ACT_HARD_SIGMOID), # ragged channel stride, MobileNetV3-style gate
+    (3, 2000, 500, L.ACT_NONE, L.ACT_SIGMOID),    # > 48 KB of shared memory
+]
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+@pytest.mark.parametrize("case", SE_CASES, ids=[str(c[:3]) for c in SE_CASES])
+def test_se_fc(ctx, dtype, case):
+    """mdlc_se_fc: FC + act + FC + act on pooled activations against fp32 numpy
+    (the hidden layer stays in fp32; bf16 rounds the input and the gate)."""
+    n, c, rd, act1, act2 = case
+    cs = _rnd8(c)
+    rng = np.random.default_rng(n + c + rd)
+    p = rng.standard_normal((n, c)).astype(np.float32)
+    w1 = (rng.standard_normal((rd, c)) / np.sqrt(c)).astype(np.float32)
+    b1 = (rng.standard_normal(rd) * 0.1).astype(np.float32)
+    w2 = (rng.standard_normal((c, rd)) / np.sqrt(rd)).astype(np.float32)
+    b2 = (rng.standard_normal(c) * 0.1).astype(np.float32)
+    dt = L.BF16 if dtype == "bf16" else L.F32
+    ph = np.zeros((n, cs), np.float32)
+    ph[:, :c] = p
+    pd = ctx.to_device(bf16_bits(ph) if dt == L.BF16 else ph)
+    eb = 2 if dt == L.BF16 else 4
+    gd = ctx.alloc(n * cs * eb)
+    ctx.memset(gd, 0xFF, n * cs * eb)      # poison: padding channels must be written
+    bufs = [ctx.to_device(a) for a in (w1, b1, np.ascontiguousarray(w2.T), b2)]
+    d = L.SeDesc(n=n, c=c, c_stride=cs, rd=rd, dtype=dt, act1=act1, act2=act2, alpha1=0.01, beta1=0.5,
+                 lo1=-np.inf, hi1=np.inf, alpha2=0.2, beta2=0.5, lo2=-np.inf, hi2=np.inf)
+    ctx.se_fc(d, pd, *bufs, gd)
+    ctx.sync()
+    y = ctx.download(gd, (n, cs), np.uint16 if dt == L.BF16 else np.float32)
+    y = from_bf16_bits(y) if dt == L.BF16 else y
+    for b in [pd, gd] + bufs:
+        ctx.free(b)
+    assert np.all(y[:, c:] == 0)
+    acts = {L.ACT_NONE: lambda v: v, L.ACT_RELU: lambda v: np.maximum(v, 0),
+            L.ACT_SIGMOID: lambda v: 1 / (1 + np.exp(-v)),
+            L.ACT_HARD_SIGMOID: lambda v: np.clip(0.2 * v + 0.5, 0, 1)}
+    x = oref.round_bf16(p) if dt == L.BF16 else p
+    h = acts[act1](x.astype(np.float64) @ w1.T.astype(np.float64) + b1)
+    want = acts[act2](h @ w2.T.astype(np.float64) + b2)
+    if dt == L.BF16:
+        np.testing.assert_allclose(y[:, :c], want, rtol=1e-2, atol=4e-3)
+    else:
+        np.testing.assert_allclose(y[:, :c], want, rtol=1e-4, atol=1e-5)

@@ -92,3 +92,31 @@ def test_bf16_constant_bits_round_to_nearest_even():
     want = torch.from_numpy(a).to(torch.bfloat16).view(torch.int16).numpy().view(np.uint16)
     np.testing.assert_array_equal(_bf16_bits(a), want)
     assert _bf16_bits(np.array([np.nan], np.float32))[0] & 0x7FC0 == 0x7FC0
+
+
+def test_squeeze_excite_fused_into_one_step():
+    """RepViT's squeeze-excite gates (ReduceMean -> 1x1 conv + ReLU -> 1x1 conv
+    + Sigmoid -> Mul) lower to pool, one "se" step and the multiply; the FC
+    weights leave the conv weight table; keep_all lowering keeps the two convs."""
+    from mdlc_b200 import builders
+    g = passes.default_pipeline(builders.BUILDERS["repvit"](batch=2, seed=0))
+    shp = S.infer(g, 2)
+    lo = lowering.lower(g, shp, L.BF16)
+    se = [st for st in lo.steps if st.kind == "se"]
+    assert len(se) == 10
+    for st in se:
+        p = st.params
+        rd, c = p["w1"].shape
+        assert p["w2t"].shape == (rd, c) and p["b1"].shape == (rd,) and p["b2"].shape == (c,)
+        assert (p["act1"], p["act2"]) == ("Relu", "Sigmoid")
+        assert not any(n in w for n in st.nodes for w in lo.weights)
+        # the pooled input and the gate keep the same channel stride
+        assert lo.tensors[st.inputs[0]].cs == lo.tensors[st.outputs[0]].cs
+    # the second FC's weight, transposed, is the step's w2t
+    node = {n.name: n for n in g.nodes}[se[0].nodes[1]]
+    rd, c = se[0].params["w1"].shape
+    w2 = np.asarray(g.initializers[node.inputs[1]], np.float32).reshape(c, rd)
+    np.testing.assert_array_equal(se[0].params["w2t"], w2.T)
+    lo_all = lowering.lower(g, shp, L.BF16, fuse_se=False)
+    assert not any(st.kind == "se" for st in lo_all.steps)
+    assert sum(st.kind == "conv" for st in lo_all.steps) == sum(st.kind == "conv" for st in lo.steps) + 20
