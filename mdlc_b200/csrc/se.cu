@@ -1,16 +1,17 @@
 // Squeeze-excite gate: global-average-pooled activations -> FC + act -> FC +
 // act in one kernel (mdlc_se_fc). The two FCs act on one pixel per image, so
 // as tensor-core GEMMs they were two launches of a handful of CTAs each,
-// bounded by launch and load latency; here each block takes four images, so
-// every weight row it reads from L2 serves four dot products, and the hidden
-// layer never leaves shared memory (kept in fp32).
+// bounded by launch and load latency; here each block takes two images, so
+// every weight row it reads from L2 serves two dot products, the loops keep
+// several L2 loads in flight, and the hidden layer never leaves shared memory
+// (kept in fp32).
 #include "common.cuh"
 #include "runtime.h"
 
 namespace mdlc {
 namespace {
 
-constexpr int kSeImgs = 4;       // images per block
+constexpr int kSeImgs = 2;       // images per block (b = 256: 128 blocks)
 constexpr int kSeThreads = 256;
 
 template <typename T>
@@ -43,8 +44,10 @@ __global__ void __launch_bounds__(kSeThreads) se_fc_kernel(const mdlc_se_desc d,
   // FC1: one warp per hidden unit, lanes across the input channels
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int j = warp; j < d.rd; j += kSeThreads / 32) {
-    float acc[kSeImgs] = {0.0f, 0.0f, 0.0f, 0.0f};
+    float acc[kSeImgs] = {};
     const float* wr = w1 + (long long)j * d.c;
+    // unrolled so that several weight loads from L2 are in flight per lane
+#pragma unroll 4
     for (int i = lane; i < d.c; i += 32) {
       const float w = __ldg(wr + i);
 #pragma unroll
@@ -64,11 +67,13 @@ __global__ void __launch_bounds__(kSeThreads) se_fc_kernel(const mdlc_se_desc d,
   __syncthreads();
   // FC2: one thread per output channel, the transposed weights read coalesced
   for (int c = threadIdx.x; c < d.c_stride; c += kSeThreads) {
-    float acc[kSeImgs] = {0.0f, 0.0f, 0.0f, 0.0f};
+    float acc[kSeImgs] = {};
     if (c < d.c) {
       const float bias = b2 ? __ldg(b2 + c) : 0.0f;
 #pragma unroll
       for (int im = 0; im < kSeImgs; ++im) acc[im] = bias;
+      // the loop's L2 loads are independent of the FMAs: unrolled, eight are in flight
+#pragma unroll 8
       for (int j = 0; j < d.rd; ++j) {
         const float w = __ldg(w2t + (long long)j * d.c + c);
 #pragma unroll
