@@ -833,7 +833,7 @@ __global__ void __launch_bounds__(threads_for<ESZ>(), (Occ<BN, STAGES, ESZ, AMOD
           // loads, converts and stages only those; the TMA store clips the rest
           const int valid = a.ks - (n0 + c0) < 64 ? a.ks - (n0 + c0) : 64;  // warp-uniform
           uint32_t v[64];
-          if constexpr (!kHeavy) {
+          if constexpr (!kHeavy && ESZ != 1) {
             tmem_ld16(taddr + c0, *reinterpret_cast<uint32_t(*)[16]>(&v[0]));
             if (valid > 16) tmem_ld16(taddr + c0 + 16, *reinterpret_cast<uint32_t(*)[16]>(&v[16]));
             if (valid > 32) tmem_ld16(taddr + c0 + 32, *reinterpret_cast<uint32_t(*)[16]>(&v[32]));
@@ -841,105 +841,128 @@ __global__ void __launch_bounds__(threads_for<ESZ>(), (Occ<BN, STAGES, ESZ, AMOD
             tmem_ld_wait();
           }
           if constexpr (ESZ == 1) {
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {  // 16-column (16-byte) groups
-              if (16 * q >= valid) break;
+            // one 16-column (16-byte) group of 8-bit outputs from its 16 int32
+            // accumulators vv, in two halves of 8 so that the requantisation's
+            // per-column parameters and 64-bit products stay in registers (two
+            // CTAs per SM leave 96 registers a thread)
+            auto group16 = [&](int q, const uint32_t* vv) {
               uint4* qp = reinterpret_cast<uint4*>(sp + ((q ^ sw) << 4));
               uint4 rr = make_uint4(0, 0, 0, 0);
               if (a.res) rr = *qp;
               const uint32_t rw[4] = {rr.x, rr.y, rr.z, rr.w};
-              // this group's 16 int32 biases and fp32 scales as 128-bit loads
               const int col0 = c0 + 16 * q;
               const bool full = n0 + col0 + 16 <= a.k;  // group-uniform: no pad columns
-              int32_t t[16];
-              if (a.rq_fixed) {
-                // single-rounding fixed point: p = acc * M1 + (bias32 * M1 + 2^(S-1))
-                // [+ (res - zp) * M2] in 64 bits (one wide multiply-add each), then
-                // p >> S as a funnel shift of (hi, lo) by min(S, 32) and an
-                // arithmetic shift by max(S - 32, 0); exact in 32 bits because the
-                // host bounds |p >> S| below 2^30 for every possible 8-bit input
-                int32_t m1[16], m2[16], shp[16];
-                long long cst[16];
+              uint32_t packed[4];
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                  const int4 a4 = *reinterpret_cast<const int4*>(sq + col0 + 4 * j);
-                  const int4 b4 = *reinterpret_cast<const int4*>(sq + BN + col0 + 4 * j);
-                  const int4 c4 = *reinterpret_cast<const int4*>(sq + 2 * BN + col0 + 4 * j);
-                  const int4 l4 = *reinterpret_cast<const int4*>(sq + 3 * BN + col0 + 4 * j);
-                  const int4 h4 = *reinterpret_cast<const int4*>(sq + 4 * BN + col0 + 4 * j);
-                  m1[4 * j] = a4.x; m1[4 * j + 1] = a4.y; m1[4 * j + 2] = a4.z; m1[4 * j + 3] = a4.w;
-                  m2[4 * j] = b4.x; m2[4 * j + 1] = b4.y; m2[4 * j + 2] = b4.z; m2[4 * j + 3] = b4.w;
-                  shp[4 * j] = c4.x; shp[4 * j + 1] = c4.y; shp[4 * j + 2] = c4.z; shp[4 * j + 3] = c4.w;
-                  cst[4 * j] = ((long long)h4.x << 32) | (uint32_t)l4.x;
-                  cst[4 * j + 1] = ((long long)h4.y << 32) | (uint32_t)l4.y;
-                  cst[4 * j + 2] = ((long long)h4.z << 32) | (uint32_t)l4.z;
-                  cst[4 * j + 3] = ((long long)h4.w << 32) | (uint32_t)l4.w;
-                }
-                long long acc64[16];
+              for (int h = 0; h < 2; ++h) {
+                const int cb = col0 + 8 * h;
+                int32_t t[8];
+                if (a.rq_fixed) {
+                  // single-rounding fixed point: p = acc * M1 + (bias32 * M1 + 2^(S-1))
+                  // [+ (res - zp) * M2] in 64 bits (one wide multiply-add each), then
+                  // p >> S as a funnel shift of (hi, lo) by min(S, 32) and an
+                  // arithmetic shift by max(S - 32, 0); exact in 32 bits because the
+                  // host bounds |p >> S| below 2^30 for every possible 8-bit input
+                  long long acc64[8];
 #pragma unroll
-                for (int e = 0; e < 16; ++e) acc64[e] = (long long)(int32_t)v[16 * q + e] * m1[e] + cst[e];
-                if (a.res) {
+                  for (int j = 0; j < 2; ++j) {
+                    const int4 a4 = *reinterpret_cast<const int4*>(sq + cb + 4 * j);
+                    const int4 l4 = *reinterpret_cast<const int4*>(sq + 3 * BN + cb + 4 * j);
+                    const int4 h4 = *reinterpret_cast<const int4*>(sq + 4 * BN + cb + 4 * j);
+                    const int32_t m1[4] = {a4.x, a4.y, a4.z, a4.w};
+                    const int32_t lo[4] = {l4.x, l4.y, l4.z, l4.w}, hi[4] = {h4.x, h4.y, h4.z, h4.w};
 #pragma unroll
-                  for (int e = 0; e < 16; ++e) {
-                    const uint32_t byte = (rw[e >> 2] >> (8 * (e & 3))) & 0xFFu;
-                    const int32_t rq = a.res_signed ? (int32_t)(int8_t)byte : (int32_t)byte;
-                    acc64[e] += (long long)(rq - a.res_zp) * m2[e];
+                    for (int i = 0; i < 4; ++i)
+                      acc64[4 * j + i] = (long long)(int32_t)vv[8 * h + 4 * j + i] * m1[i] +
+                                         (((long long)hi[i] << 32) | (uint32_t)lo[i]);
                   }
+                  if (a.res) {
+#pragma unroll
+                    for (int j = 0; j < 2; ++j) {
+                      const int4 b4 = *reinterpret_cast<const int4*>(sq + BN + cb + 4 * j);
+                      const int32_t m2[4] = {b4.x, b4.y, b4.z, b4.w};
+#pragma unroll
+                      for (int i = 0; i < 4; ++i) {
+                        const int e = 8 * h + 4 * j + i;
+                        const uint32_t byte = (rw[e >> 2] >> (8 * (e & 3))) & 0xFFu;
+                        const int32_t rq = a.res_signed ? (int32_t)(int8_t)byte : (int32_t)byte;
+                        acc64[4 * j + i] += (long long)(rq - a.res_zp) * m2[i];
+                      }
+                    }
+                  }
+#pragma unroll
+                  for (int j = 0; j < 2; ++j) {
+                    const int4 c4 = *reinterpret_cast<const int4*>(sq + 2 * BN + cb + 4 * j);
+                    const int32_t shp[4] = {c4.x, c4.y, c4.z, c4.w};
+#pragma unroll
+                    for (int i = 0; i < 4; ++i) {
+                      const long long p64 = acc64[4 * j + i];
+                      const int32_t r = (int32_t)__funnelshift_rc((uint32_t)(unsigned long long)p64,
+                                                                 (uint32_t)(p64 >> 32), shp[i] & 0xFF) >>
+                                        (shp[i] >> 8);
+                      t[4 * j + i] = min(max(r, a.qlo), a.qhi) + a.out_zp;
+                    }
+                  }
+                } else {
+                  // exact small-integer <-> float conversions without the conversion
+                  // unit: 1.5 * 2^23 in the exponent, value in the low mantissa bits
+                  // (|x| < 2^22; round-to-nearest-even like __float2int_rn)
+                  constexpr float kMagic = 12582912.0f;
+                  constexpr int32_t kMagicBits = 0x4B400000;
+                  const float qlo_f = (float)a.qlo, qhi_f = (float)a.qhi;
+                  float f[8];
+#pragma unroll
+                  for (int j = 0; j < 2; ++j) {
+                    const int4 bb = *reinterpret_cast<const int4*>(sq + cb + 4 * j);
+                    const float4 ss = *reinterpret_cast<const float4*>(sq + BN + cb + 4 * j);
+                    const int32_t bq[4] = {bb.x, bb.y, bb.z, bb.w};
+                    const float sc[4] = {ss.x, ss.y, ss.z, ss.w};
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                      f[4 * j + i] = __fmul_rn(__int2float_rn((int32_t)vv[8 * h + 4 * j + i] + bq[i]), sc[i]);
+                  }
+                  if (a.res) {
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                      const int e = 8 * h + i;
+                      const uint32_t byte = (rw[e >> 2] >> (8 * (e & 3))) & 0xFFu;
+                      const int32_t rq = a.res_signed ? (int32_t)(int8_t)byte : (int32_t)byte;
+                      const float rf = __fsub_rn(__int_as_float(rq - a.res_zp + kMagicBits), kMagic);
+                      f[i] = __fadd_rn(f[i], __fmul_rn(rf, a.res_scale));
+                    }
+                  }
+                  // clamp then round == round then clamp (integer bounds)
+#pragma unroll
+                  for (int i = 0; i < 8; ++i)
+                    t[i] = __float_as_int(__fadd_rn(fminf(fmaxf(f[i], qlo_f), qhi_f), kMagic)) - kMagicBits + a.out_zp;
+                }
+                if (!full) {
+#pragma unroll
+                  for (int i = 0; i < 8; ++i)
+                    if (n0 + cb + i >= a.k) t[i] = 0;
                 }
 #pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                  const int32_t r = (int32_t)__funnelshift_rc((uint32_t)(unsigned long long)acc64[e],
-                                                             (uint32_t)(acc64[e] >> 32), shp[e] & 0xFF) >>
-                                    (shp[e] >> 8);
-                  t[e] = min(max(r, a.qlo), a.qhi) + a.out_zp;
-                }
-              } else {
-              int32_t bq[16];
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const int4 bb = *reinterpret_cast<const int4*>(sq + col0 + 4 * j);
-                bq[4 * j] = bb.x; bq[4 * j + 1] = bb.y; bq[4 * j + 2] = bb.z; bq[4 * j + 3] = bb.w;
+                for (int w = 0; w < 2; ++w)
+                  packed[2 * h + w] = ((uint32_t)t[4 * w] & 0xFFu) | (((uint32_t)t[4 * w + 1] & 0xFFu) << 8) |
+                                      (((uint32_t)t[4 * w + 2] & 0xFFu) << 16) | ((uint32_t)t[4 * w + 3] << 24);
               }
-              float sc[16];
-#pragma unroll
-              for (int j = 0; j < 4; ++j) {
-                const float4 ss = *reinterpret_cast<const float4*>(sq + BN + col0 + 4 * j);
-                sc[4 * j] = ss.x; sc[4 * j + 1] = ss.y; sc[4 * j + 2] = ss.z; sc[4 * j + 3] = ss.w;
-              }
-              // exact small-integer <-> float conversions without the conversion
-              // unit: 1.5 * 2^23 in the exponent, value in the low mantissa bits
-              // (|x| < 2^22; round-to-nearest-even like __float2int_rn)
-              constexpr float kMagic = 12582912.0f;
-              constexpr int32_t kMagicBits = 0x4B400000;
-              const float qlo_f = (float)a.qlo, qhi_f = (float)a.qhi;
-              // each stage over all 16 elements before the next, so their
-              // dependency chains interleave
-              float f[16];
-#pragma unroll
-              for (int e = 0; e < 16; ++e) f[e] = __fmul_rn(__int2float_rn((int32_t)v[16 * q + e] + bq[e]), sc[e]);
-              if (a.res) {
-#pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                  const uint32_t byte = (rw[e >> 2] >> (8 * (e & 3))) & 0xFFu;
-                  const int32_t rq = a.res_signed ? (int32_t)(int8_t)byte : (int32_t)byte;
-                  const float rf = __fsub_rn(__int_as_float(rq - a.res_zp + kMagicBits), kMagic);
-                  f[e] = __fadd_rn(f[e], __fmul_rn(rf, a.res_scale));
-                }
-              }
-              // clamp then round == round then clamp (integer bounds)
-#pragma unroll
-              for (int e = 0; e < 16; ++e)
-                t[e] = __float_as_int(__fadd_rn(fminf(fmaxf(f[e], qlo_f), qhi_f), kMagic)) - kMagicBits + a.out_zp;
-              }
-              if (!full) {
-#pragma unroll
-                for (int e = 0; e < 16; ++e)
-                  if (n0 + col0 + e >= a.k) t[e] = 0;
-              }
-              uint32_t packed[4] = {0, 0, 0, 0};
-#pragma unroll
-              for (int e = 0; e < 16; ++e) packed[e >> 2] |= ((uint32_t)t[e] & 0xFFu) << (8 * (e & 3));
               *qp = make_uint4(packed[0], packed[1], packed[2], packed[3]);
+            };
+            // 16-column loads double-buffered: the next is in flight while the
+            // current group is requantised
+            uint32_t va[16], vb[16];
+            tmem_ld16(taddr + c0, va);
+            tmem_ld_wait();
+#pragma unroll 1
+            for (int q = 0; q < 4 && 16 * q < valid; q += 2) {
+              const bool second = 16 * (q + 1) < valid;
+              if (second) tmem_ld16(taddr + c0 + 16 * (q + 1), vb);
+              group16(q, va);
+              tmem_ld_wait();
+              if (!second) break;
+              if (q + 2 < 4 && 16 * (q + 2) < valid) tmem_ld16(taddr + c0 + 16 * (q + 2), va);
+              group16(q + 1, vb);
+              tmem_ld_wait();
             }
           } else {
           // one 8-column (16-byte) group: + bias (+ residual), activation, bf16.
