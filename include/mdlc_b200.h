@@ -127,7 +127,11 @@ typedef struct {
   int32_t flags;  /* bit 0: gather the A operand with cp.async even when the layer
                      qualifies for TMA loads; bit 1: per-tap TMA loads (im2col mode)
                      instead of the halo band of stride-1 layers; bit 2: load one halo band
-                     per tile for stride-1 layers instead of one load per tap; bits 8-15:
+                     per tile for stride-1 layers instead of one load per tap; bit 3: the
+                     halo band with the whole weight matrix resident in shared memory, one
+                     CTA per SM (bf16, channel stride a multiple of 64, at most 64 output
+                     channels and 9 k-blocks of 128 bytes, e.g. 64 -> 64 3x3; bn and
+                     stages are then chosen by the library; ignored otherwise); bits 8-15:
                      split-K, the reduction cut into that many slices on different CTAs,
                      the last one to finish a tile summing them in slice order (at most
                      8 MiB of fp32 / int32 partials: tiles x slices x 128 x bn x 4 bytes) */

@@ -123,14 +123,25 @@ int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w
   const bool out_tma = (!int8 && d.out_type == MDLC_BF16) || (int8 && out8);
   const int pixel_bytes = d.c_stride * esz;
   const int band_px = pixel_bytes % 128 == 0 ? 128 : (pixel_bytes == 32 || pixel_bytes == 64 ? pixel_bytes : 0);
-  const bool halo = out_tma && band_px && d.stride_h == 1 && d.stride_w == 1 && d.dil_h == 1 && d.dil_w == 1 &&
-                    d.r * d.s > 1 && d.r <= kHaloMaxR && d.s <= kHaloSlots - kHaloTW + 1 && d.oh >= 14 &&
-                    d.ow >= 14 && (!int8 || d.in_zp == 0) && !(cfg && (cfg->flags & 3)) && cfg &&
-                    (cfg->flags & 4) && !fp32;
+  const bool halo_shape = out_tma && band_px && d.stride_h == 1 && d.stride_w == 1 && d.dil_h == 1 &&
+                          d.dil_w == 1 && d.r * d.s > 1 && d.r <= kHaloMaxR && d.s <= kHaloSlots - kHaloTW + 1 &&
+                          d.oh >= 14 && d.ow >= 14 && (!int8 || d.in_zp == 0) && !(cfg && (cfg->flags & 3)) &&
+                          !fp32;
+  // resident weights (flags bit 3): bf16 halo layers with 128-byte channel
+  // blocks whose whole packed weight matrix -- at most 64 output channels and
+  // kResidentKb k-blocks (64 -> 64 3x3: 72 KB) -- stays in shared memory, one
+  // CTA per SM, no split-K
+  const bool resident = halo_shape && cfg && (cfg->flags & 8) && esz == 2 && band_px == 128 &&
+                        d.k_stride <= 64 && num_kb <= kResidentKb && ((cfg->flags >> 8) & 0xFF) <= 1;
+  const bool halo = halo_shape && cfg && ((cfg->flags & 4) || resident);
   const int tiles_x = (d.ow + kHaloTW - 1) / kHaloTW, tiles_y = (d.oh + kHaloTH - 1) / kHaloTH;
 
   int bn = cfg && cfg->bn ? cfg->bn : 0;
   int stages = cfg && cfg->stages ? cfg->stages : 0;
+  if (resident) {
+    bn = 64;
+    stages = kResidentKb;
+  }
   const long long num_m_ll = halo ? (long long)d.n * tiles_x * tiles_y : (M + kBM - 1) / kBM;
   if (num_m_ll > (1ll << 30)) return mdlc_set_error(ctx, MDLC_ERR_INVALID, "conv: too many tiles");
   const int num_m = (int)num_m_ll;
@@ -206,6 +217,7 @@ int conv_tc(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const void* w
   a.halo_rows = kHaloTH + d.r - 1;
   a.band_px = band_px;
   a.cpb = band_px == 128 ? pixel_bytes / 128 : 1;
+  a.b_resident = resident ? 1 : 0;
   a.num_n_tiles = (d.k_stride + bn - 1) / bn;
   a.out_type = d.out_type;
   a.a_signed = d.in_type == MDLC_S8;

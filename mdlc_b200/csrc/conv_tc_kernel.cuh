@@ -62,6 +62,8 @@ constexpr int kHaloTW = 8, kHaloTH = 16, kHaloSlots = 16, kHaloMaxR = 5;
 constexpr int kHaloRowBytes = kHaloSlots * 128;  // band row stride at P = 128
 constexpr int kHaloBytes = (kHaloTH + kHaloMaxR - 1) * kHaloRowBytes;
 constexpr int kHaloStages = 2;
+// resident-weight halo mode: weight k-blocks held in shared memory (one stage each)
+constexpr int kResidentKb = 9;
 static_assert(kHaloTW * kHaloTH == kBM, "a halo tile is one M tile");
 static_assert(kHaloSlots % 8 == 0, "band rows must keep the swizzle phase");
 
@@ -97,6 +99,10 @@ struct TcArgs {
   int act_packed;
   uint32_t act_lo2, act_hi2;
   int tiles_x, tiles_y, halo_rows, cpb;  // halo mode: tile grid per image, band rows, channel blocks
+  // halo mode, one n-tile and num_kb <= STAGES: every weight k-block is loaded
+  // once into its own stage at the start and stays resident for the CTA's
+  // lifetime, so a tile moves only its input band
+  int b_resident;
   int band_px;                           // halo mode: bytes per band pixel slot (32, 64 or 128)
   // split-K: each tile's k-blocks are cut into `split` slices of `kps`; every
   // (tile, slice) unit writes its raw accumulators to `ws` (fp32, or int32 for
@@ -1082,6 +1088,14 @@ __global__ void __launch_bounds__(threads_for<ESZ>(), (Occ<BN, STAGES, ESZ, AMOD
       // k-blocks per band: one per tap (128-byte channel blocks, weight k-block
       // tap * cpb + cb), or every k-block of the filter (whole-pixel bands)
       const int kpb = a.band_px == 128 ? RS : a.num_kb;
+      const bool resident = a.b_resident != 0;
+      if (resident) {
+        // the whole weight matrix, k-block kb in stage kb, once
+        for (int kb = 0; kb < a.num_kb; ++kb) {
+          mbar_arrive_expect_tx(fullB(kb), L::kBBytes);
+          tma_load_2d(sB + kb * L::kBBytes, &tmap_w, kb * KB, 0, fullB(kb));
+        }
+      }
       for (int tile = blockIdx.x; tile < num_tiles && ok; tile += gridDim.x) {
         const int n0 = (tile % a.num_n_tiles) * BN;
         int img, ty, tx;
@@ -1095,7 +1109,7 @@ __global__ void __launch_bounds__(threads_for<ESZ>(), (Occ<BN, STAGES, ESZ, AMOD
           mbar_arrive_expect_tx(hfull(hs), band_bytes);
           tma_load_4d(sA + hs * kHaloBytes, &tmap_x, cb * KB, tx * kHaloTW - a.pl, ty * kHaloTH - a.pt, img,
                       hfull(hs));
-          for (int j = 0; j < kpb; ++j, ++it) {
+          for (int j = 0; j < kpb && !resident; ++j, ++it) {
             const int st = it % STAGES;
             if (!mbar_wait(empty(st), ((it / STAGES) & 1) ^ 1, abort_flag, a.err, a.wait_cycles)) {
               ok = false;
@@ -1108,6 +1122,9 @@ __global__ void __launch_bounds__(threads_for<ESZ>(), (Occ<BN, STAGES, ESZ, AMOD
       }
       if (!ok) {
         // let the loads already issued land before the CTA's shared memory is released
+        if (resident) {
+          for (int kb = 0; kb < a.num_kb; ++kb) mbar_wait(fullB(kb), 0, nullptr, a.err, 2000000ull);
+        }
         for (int q = it - 1; q >= 0 && q >= it - STAGES; --q)
           mbar_wait(fullB(q % STAGES), (q / STAGES) & 1, nullptr, a.err, 2000000ull);
         for (int q = hit - 1; q >= 0 && q >= hit - kHaloStages; --q)
@@ -1163,13 +1180,37 @@ __global__ void __launch_bounds__(threads_for<ESZ>(), (Occ<BN, STAGES, ESZ, AMOD
           const int kpb = P == 128 ? RS : a.num_kb;
           const uint32_t sbo = (uint32_t)(kHaloSlots * P);
           const uint32_t layout = P == 32 ? 6u : (P == 64 ? 4u : 2u);
+          int hty = 0, htx = 0;  // 128-byte blocks: the tap of k-block j, stepped without division
           for (int j = 0; j < kpb; ++j, ++it) {
-            const int st = it % STAGES;
-            if (!mbar_wait(fullB(st), (it / STAGES) & 1, abort_flag, a.err, a.wait_cycles)) {
+            // resident weights: weight k-block (tap, channel block) sits in its own
+            // stage, loaded once (phase 0 completes once; later waits return at once)
+            const int st = a.b_resident ? (P == 128 ? j * a.cpb + cb : j) : it % STAGES;
+            const uint32_t bpar = a.b_resident ? 0u : (uint32_t)(it / STAGES) & 1;
+            if (!mbar_wait(fullB(st), bpar, abort_flag, a.err, a.wait_cycles)) {
               ok = false;
               break;
             }
             const uint32_t bb = sB + st * L::kBBytes;
+            if (P == 128) {
+              // one tap per k-block: the four MMAs read 32-byte slices of the same
+              // band pixels, i.e. descriptors 2 apart in their 16-byte address field
+              const uint64_t ad0 =
+                  umma_desc_k(band + (uint32_t)(hty * kHaloSlots + htx) * 128u, sbo, layout);
+              const uint64_t bd0 = umma_desc_sw128(bb);
+#pragma unroll
+              for (int kq = 0; kq < 4; ++kq) {
+                if constexpr (ESZ == 2)
+                  umma_bf16(d, ad0 + 2u * kq, bd0 + 2u * kq, idesc, (cb | j | kq) != 0);
+                else
+                  umma_i8(d, ad0 + 2u * kq, bd0 + 2u * kq, idesc, (cb | j | kq) != 0);
+              }
+              if (++htx == a.s) {
+                htx = 0;
+                ++hty;
+              }
+              if (!a.b_resident) umma_commit(empty(st));
+              continue;
+            }
 #pragma unroll
             for (int kq = 0; kq < 4; ++kq) {
               // the 32 K bytes of this MMA: tap and byte offset inside the band pixel;
@@ -1186,7 +1227,7 @@ __global__ void __launch_bounds__(threads_for<ESZ>(), (Occ<BN, STAGES, ESZ, AMOD
               else
                 umma_i8(d, ad, bd, idesc, (cb | j | kq) != 0);
             }
-            umma_commit(empty(st));
+            if (!a.b_resident) umma_commit(empty(st));
           }
           if (ok) umma_commit(hempty(hs));  // the band is free once its MMAs have read it
         }

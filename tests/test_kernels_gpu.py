@@ -274,6 +274,38 @@ def test_conv_halo_band_matches_per_tap_paths(ctx, case):
     np.testing.assert_array_equal(per_tap, gather)
     if c <= 64:   # one band per tile: same accumulation order as the per-tap loads
         np.testing.assert_array_equal(halo, per_tap)
+    if c % 64 == 0 and k <= 64 and c * r * r <= 9 * 64:
+        # the weights resident in shared memory: same products in the same order
+        resident = run_conv(ctx, x, wt, b, pad=pad, act=L.ACT_RELU, res=res, flags=8)
+        np.testing.assert_array_equal(resident, halo)
+
+
+RESIDENT_CASES = [
+    # n, c, h, w, k, act, residual   (64 input channels, 3x3, stride 1: the resident-weight halo path)
+    (4, 64, 56, 56, 64, L.ACT_RELU, True),    # ResNet-18 layer1 conv2 shape, several tiles per SM
+    (3, 64, 29, 37, 48, L.ACT_NONE, False),   # ragged tiles, k < 64 (padding columns)
+    (1, 64, 14, 14, 64, L.ACT_CLIP, True),    # fewer tiles than SMs
+    (2, 64, 30, 22, 64, L.ACT_GELU, False),   # heavy epilogue
+]
+
+
+@pytest.mark.parametrize("case", RESIDENT_CASES, ids=[str(c[:5]) for c in RESIDENT_CASES])
+def test_conv_resident_weights(ctx, case):
+    """Tile flags bit 3: the whole weight matrix stays in shared memory and each
+    tile loads only its input band; equal to the per-tap path bit for bit (one
+    channel block: same accumulation order) and to the oracle."""
+    n, c, h, w, k, act, with_res = case
+    rng = np.random.default_rng(400 + n + h + w + k)
+    x = rng.standard_normal((n, c, h, w)).astype(np.float32)
+    wt = (rng.standard_normal((k, c, 3, 3)) * np.sqrt(2.0 / (c * 9))).astype(np.float32)
+    b = (rng.standard_normal(k) * 0.1).astype(np.float32)
+    res = rng.standard_normal((n, k, h, w)).astype(np.float32) if with_res else None
+    clip = (0.0, 6.0)
+    resident = run_conv(ctx, x, wt, b, pad=1, act=act, res=res, flags=8, clip=clip)
+    per_tap = run_conv(ctx, x, wt, b, pad=1, act=act, res=res, flags=2, clip=clip)
+    np.testing.assert_array_equal(resident, per_tap)
+    name = {L.ACT_RELU: "Relu", L.ACT_NONE: None, L.ACT_CLIP: "Clip", L.ACT_GELU: "Gelu"}[act]
+    check(resident, oracle_conv(x, wt, b, pad=1, act=name, res=res, clip=clip), 1e-2)
 
 
 SPLIT_CASES = [
