@@ -2,9 +2,9 @@
 // act in one kernel (mdlc_se_fc). The two FCs act on one pixel per image, so
 // as tensor-core GEMMs they were two launches of a handful of CTAs each,
 // bounded by launch and load latency; here each block takes two images, so
-// every weight row it reads from L2 serves two dot products, the loops keep
-// several L2 loads in flight, and the hidden layer never leaves shared memory
-// (kept in fp32).
+// every weight row it reads from L2 serves two dot products, 32 warps and
+// unrolled loops keep many L2 loads in flight (the loops are latency-bound),
+// and the hidden layer never leaves shared memory (kept in fp32).
 #include "common.cuh"
 #include "runtime.h"
 
@@ -12,7 +12,7 @@ namespace mdlc {
 namespace {
 
 constexpr int kSeImgs = 2;       // images per block (b = 256: 128 blocks)
-constexpr int kSeThreads = 256;
+constexpr int kSeThreads = 1024;  // 32 warps: the FC loops are latency-bound chains of L2 loads
 
 template <typename T>
 MDLC_DEV float se_ld(const T* p);
@@ -41,27 +41,35 @@ __global__ void __launch_bounds__(kSeThreads) se_fc_kernel(const mdlc_se_desc d,
     ps[i] = im < ni ? se_ld<T>(p + (long long)(n0 + im) * d.c_stride + c) : 0.0f;
   }
   __syncthreads();
-  // FC1: one warp per hidden unit, lanes across the input channels
+  // FC1: each warp takes four hidden units at a time, lanes across the input
+  // channels, so every lane has four (x2 unrolled: eight) weight loads in flight
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int j = warp; j < d.rd; j += kSeThreads / 32) {
-    float acc[kSeImgs] = {};
-    const float* wr = w1 + (long long)j * d.c;
-    // unrolled so that several weight loads from L2 are in flight per lane
-#pragma unroll 4
+  for (int j0 = warp * 4; j0 < d.rd; j0 += (kSeThreads / 32) * 4) {
+    const int nr = min(4, d.rd - j0);
+    float acc[4][kSeImgs] = {};
+#pragma unroll 2
     for (int i = lane; i < d.c; i += 32) {
-      const float w = __ldg(wr + i);
+      float w[4];
 #pragma unroll
-      for (int im = 0; im < kSeImgs; ++im) acc[im] = fmaf(w, ps[im * d.c + i], acc[im]);
+      for (int r = 0; r < 4; ++r) w[r] = r < nr ? __ldg(w1 + (long long)(j0 + r) * d.c + i) : 0.0f;
+#pragma unroll
+      for (int r = 0; r < 4; ++r)
+#pragma unroll
+        for (int im = 0; im < kSeImgs; ++im) acc[r][im] = fmaf(w[r], ps[im * d.c + i], acc[r][im]);
     }
 #pragma unroll
-    for (int im = 0; im < kSeImgs; ++im) {
+    for (int r = 0; r < 4; ++r)
 #pragma unroll
-      for (int o = 16; o; o >>= 1) acc[im] += __shfl_xor_sync(0xffffffffu, acc[im], o);
-    }
+      for (int im = 0; im < kSeImgs; ++im) {
+#pragma unroll
+        for (int o = 16; o; o >>= 1) acc[r][im] += __shfl_xor_sync(0xffffffffu, acc[r][im], o);
+      }
     if (lane == 0) {
-      const float bias = b1 ? __ldg(b1 + j) : 0.0f;
+      for (int r = 0; r < nr; ++r) {
+        const float bias = b1 ? __ldg(b1 + j0 + r) : 0.0f;
 #pragma unroll
-      for (int im = 0; im < kSeImgs; ++im) hs[im * d.rd + j] = apply_act(acc[im] + bias, a1);
+        for (int im = 0; im < kSeImgs; ++im) hs[im * d.rd + j0 + r] = apply_act(acc[r][im] + bias, a1);
+      }
     }
   }
   __syncthreads();
@@ -72,8 +80,8 @@ __global__ void __launch_bounds__(kSeThreads) se_fc_kernel(const mdlc_se_desc d,
       const float bias = b2 ? __ldg(b2 + c) : 0.0f;
 #pragma unroll
       for (int im = 0; im < kSeImgs; ++im) acc[im] = bias;
-      // the loop's L2 loads are independent of the FMAs: unrolled, eight are in flight
-#pragma unroll 8
+      // the loop's L2 loads are independent of the FMAs: unrolled, sixteen are in flight
+#pragma unroll 16
       for (int j = 0; j < d.rd; ++j) {
         const float w = __ldg(w2t + (long long)j * d.c + c);
 #pragma unroll
