@@ -9,8 +9,6 @@
 // kernel runs any group whose program fits mdlc_ew_prog.
 #include <cmath>
 
-#include <type_traits>
-
 #include "common.cuh"
 #include "runtime.h"
 
@@ -268,6 +266,9 @@ __global__ void __launch_bounds__(256) gap_kernel(const mdlc_pool_desc d, const 
   if (slice < slices) {
     const char* xb =
         static_cast<const char*>(x) + ((long long)img * hw * d.c_stride + (g0 + gl) * 8) * V8<T>::kBytes;
+    // unrolled: several independent 16-byte loads in flight per thread (the
+    // reduction is latency-bound at one image per block)
+#pragma unroll 4
     for (int p = slice; p < hw; p += slices) {
       float v[8];
       V8<T>::load(xb + (long long)p * d.c_stride * V8<T>::kBytes, v);
@@ -484,123 +485,46 @@ namespace {
 // one unary one after it (the squeeze-excite multiply, a residual add + act
 // not absorbed into a conv). Values stay in registers (the interpreter's
 // register file is indexed at run time and lives in local memory).
-// Raw 8-element vectors kept packed in registers until they are used, so a
-// thread can hold several loads in flight cheaply.
-template <typename T>
-struct Raw8;
-template <>
-struct Raw8<__nv_bfloat16> {
-  uint4 v;
-  MDLC_DEV void load(const void* p) { v = __ldg(reinterpret_cast<const uint4*>(p)); }
-  MDLC_DEV void get(float (&f)[8]) const {
-    f[0] = bf16_lo(v.x); f[1] = bf16_hi(v.x); f[2] = bf16_lo(v.y); f[3] = bf16_hi(v.y);
-    f[4] = bf16_lo(v.z); f[5] = bf16_hi(v.z); f[6] = bf16_lo(v.w); f[7] = bf16_hi(v.w);
-  }
-};
-template <>
-struct Raw8<float> {
-  float4 a, b;
-  MDLC_DEV void load(const void* p) {
-    a = __ldg(reinterpret_cast<const float4*>(p));
-    b = __ldg(reinterpret_cast<const float4*>(p) + 1);
-  }
-  MDLC_DEV void get(float (&f)[8]) const {
-    f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
-  }
-};
-
-constexpr int kEwUnroll = 4;  // 8-element vectors a thread has in flight
-
-// Fast path of the elementwise interpreter for its commonest program: in0
-// full, in1 broadcast per the given mode, one binary instruction and at most
-// one unary one after it (the squeeze-excite multiply, a residual add + act
-// not absorbed into a conv). Values stay in registers (the interpreter's
-// register file is indexed at run time and lives in local memory). Each
-// thread loads kEwUnroll vectors (a grid stride apart, so every load
-// instruction of a warp stays coalesced) before computing any, which keeps
-// enough bytes in flight per SM to stream HBM. IDX32: every vector index fits
-// in 32 bits (cheaper channel-group arithmetic); PAD: the channel stride has
-// padding channels, which are written as zero.
-template <typename T, int BC, bool PAD, bool IDX32>
+template <typename T, int BC>
 __global__ void __launch_bounds__(256) eltwise_binary_kernel(const mdlc_ew_prog p, const void* in0, const void* in1,
                                                              void* out0, int bop, int uop, float u0, float u1,
                                                              long long total) {
-  using I = typename std::conditional<IDX32, int, long long>::type;
-  constexpr int EB = (int)sizeof(T) * 8;  // bytes per vector
-  const I G = (I)(p.c_stride >> 3);
-  const I hwG = (I)p.hw * G;
+  const int G = p.c_stride >> 3;
+  const long long hwG = (long long)p.hw * G;
   float bs = 0.0f;
   if (BC == MDLC_BC_SCALAR)
     bs = (sizeof(T) == 2) ? __bfloat162float(*static_cast<const __nv_bfloat16*>(in1)) : *static_cast<const float*>(in1);
-  const I nthr = (I)gridDim.x * blockDim.x;
-  const I n = (I)total;
-  const char* x0 = static_cast<const char*>(in0);
-  const char* x1 = static_cast<const char*>(in1);
-  char* y0 = static_cast<char*>(out0);
-  for (I base = (I)blockIdx.x * blockDim.x + threadIdx.x; base < n; base += nthr * kEwUnroll) {
-    Raw8<T> ra[kEwUnroll], rb[kEwUnroll];
+  for (long long idx = (long long)blockIdx.x * blockDim.x + threadIdx.x; idx < total;
+       idx += (long long)gridDim.x * blockDim.x) {
+    const int g = (int)(idx % G);
+    float a[8], b[8];
+    V8<T>::load(static_cast<const char*>(in0) + idx * 8 * V8<T>::kBytes, a);
+    if (BC == MDLC_BC_SCALAR) {
 #pragma unroll
-    for (int u = 0; u < kEwUnroll; ++u) {
-      const I idx = base + u * nthr;
-      if (idx < n) {
-        ra[u].load(x0 + (long long)idx * EB);
-        if (BC == MDLC_BC_FULL) rb[u].load(x1 + (long long)idx * EB);
-        else if (BC == MDLC_BC_NC) rb[u].load(x1 + ((long long)(idx / hwG) * G + idx % G) * EB);
-        else if (BC == MDLC_BC_C) rb[u].load(x1 + (long long)(idx % G) * EB);
-      }
+      for (int e = 0; e < 8; ++e) b[e] = bs;
+    } else {
+      const long long off = BC == MDLC_BC_FULL ? idx * 8 : (BC == MDLC_BC_NC ? (idx / hwG) * p.c_stride + g * 8 : g * 8);
+      V8<T>::load(static_cast<const char*>(in1) + off * V8<T>::kBytes, b);
     }
+    float r[8];
 #pragma unroll
-    for (int u = 0; u < kEwUnroll; ++u) {
-      const I idx = base + u * nthr;
-      if (idx >= n) break;
-      float a[8], b[8], r[8];
-      ra[u].get(a);
-      if (BC == MDLC_BC_SCALAR) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) b[e] = bs;
-      } else {
-        rb[u].get(b);
-      }
+    for (int e = 0; e < 8; ++e) {
       switch (bop) {
-        case MDLC_EW_ADD:
-#pragma unroll
-          for (int e = 0; e < 8; ++e) r[e] = a[e] + b[e];
-          break;
-        case MDLC_EW_SUB:
-#pragma unroll
-          for (int e = 0; e < 8; ++e) r[e] = a[e] - b[e];
-          break;
-        case MDLC_EW_MUL:
-#pragma unroll
-          for (int e = 0; e < 8; ++e) r[e] = a[e] * b[e];
-          break;
-        case MDLC_EW_DIV:
-#pragma unroll
-          for (int e = 0; e < 8; ++e) r[e] = a[e] / b[e];
-          break;
-        case MDLC_EW_MAX:
-#pragma unroll
-          for (int e = 0; e < 8; ++e) r[e] = fmaxf(a[e], b[e]);
-          break;
-        default:
-#pragma unroll
-          for (int e = 0; e < 8; ++e) r[e] = fminf(a[e], b[e]);
-          break;
+        case MDLC_EW_ADD: r[e] = a[e] + b[e]; break;
+        case MDLC_EW_SUB: r[e] = a[e] - b[e]; break;
+        case MDLC_EW_MUL: r[e] = a[e] * b[e]; break;
+        case MDLC_EW_DIV: r[e] = a[e] / b[e]; break;
+        case MDLC_EW_MAX: r[e] = fmaxf(a[e], b[e]); break;
+        default: r[e] = fminf(a[e], b[e]); break;
       }
-      if (uop == MDLC_EW_RELU) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) r[e] = fmaxf(r[e], 0.0f);
-      } else if (uop >= 0) {
-#pragma unroll
-        for (int e = 0; e < 8; ++e) r[e] = ew_unary(uop, r[e], u0, u1);
-      }
-      if (PAD) {
-        const int g = (int)(idx % G);
-#pragma unroll
-        for (int e = 0; e < 8; ++e) r[e] = (g * 8 + e < p.c) ? r[e] : 0.0f;
-      }
-      V8<T>::store(y0 + (long long)idx * EB, r);
     }
+    if (uop >= 0) {
+#pragma unroll
+      for (int e = 0; e < 8; ++e) r[e] = ew_unary(uop, r[e], u0, u1);
+    }
+#pragma unroll
+    for (int e = 0; e < 8; ++e) r[e] = (g * 8 + e < p.c) ? r[e] : 0.0f;
+    V8<T>::store(static_cast<char*>(out0) + idx * 8 * V8<T>::kBytes, r);
   }
 }
 
@@ -622,27 +546,21 @@ bool eltwise_fast(mdlc_ctx* ctx, const mdlc_ew_prog* p, const void* const* in, v
     uop = u.op, u0 = u.imm0, u1 = u.imm1, last = u.dst;
   }
   if (p->out_reg[0] != last) return false;
-  // one resident wave: 2 blocks of 256 threads per SM (~100 registers a
-  // thread), each thread kEwUnroll vectors in flight per trip: 64 KB of bf16
-  // loads in flight per SM
-  long long blocks = (total + 256LL * kEwUnroll - 1) / (256LL * kEwUnroll);
-  const long long cap = (long long)ctx->num_sms * 2;
-  const unsigned grid = (unsigned)(blocks < 1 ? 1 : (blocks > cap ? cap : blocks));
-  const bool pad = p->c != p->c_stride;
-  // 32-bit indices: the vector count plus one grid-stride trip stays below 2^31
-  const bool i32 = total + (long long)grid * 256 * kEwUnroll < (1LL << 31);
-  const int mode = p->bcast[1];
-#define MDLC_EW_LAUNCH(BC_)                                                                                  \
-  do {                                                                                                       \
-    auto k = pad ? (i32 ? eltwise_binary_kernel<T, BC_, true, true> : eltwise_binary_kernel<T, BC_, true, false>) \
-                 : (i32 ? eltwise_binary_kernel<T, BC_, false, true> : eltwise_binary_kernel<T, BC_, false, false>); \
-    k<<<grid, 256, 0, ctx->stream>>>(*p, in[0], in[1], out[0], b.op, uop, u0, u1, total);                   \
-  } while (0)
-  if (mode == MDLC_BC_FULL) MDLC_EW_LAUNCH(MDLC_BC_FULL);
-  else if (mode == MDLC_BC_NC) MDLC_EW_LAUNCH(MDLC_BC_NC);
-  else if (mode == MDLC_BC_C) MDLC_EW_LAUNCH(MDLC_BC_C);
-  else MDLC_EW_LAUNCH(MDLC_BC_SCALAR);
-#undef MDLC_EW_LAUNCH
+  const unsigned grid = grid_for(ctx, total);
+  switch (p->bcast[1]) {
+    case MDLC_BC_FULL:
+      eltwise_binary_kernel<T, MDLC_BC_FULL><<<grid, 256, 0, ctx->stream>>>(*p, in[0], in[1], out[0], b.op, uop, u0, u1, total);
+      break;
+    case MDLC_BC_NC:
+      eltwise_binary_kernel<T, MDLC_BC_NC><<<grid, 256, 0, ctx->stream>>>(*p, in[0], in[1], out[0], b.op, uop, u0, u1, total);
+      break;
+    case MDLC_BC_C:
+      eltwise_binary_kernel<T, MDLC_BC_C><<<grid, 256, 0, ctx->stream>>>(*p, in[0], in[1], out[0], b.op, uop, u0, u1, total);
+      break;
+    default:
+      eltwise_binary_kernel<T, MDLC_BC_SCALAR><<<grid, 256, 0, ctx->stream>>>(*p, in[0], in[1], out[0], b.op, uop, u0, u1, total);
+      break;
+  }
   return true;
 }
 
