@@ -247,18 +247,19 @@ __global__ void __launch_bounds__(256) pool_max_u8_kernel(const mdlc_pool_desc d
 }
 
 // ------------------------------------------------------------ global average
-// One CTA per (image, 256-channel block): 32 channel groups x 8 pixel slices,
-// fp32 sums, shared-memory reduction over the slices.
-template <typename T>
 // One block per (image, up to 32 channel groups): the 256 threads split the
 // pixels over however many groups the block holds (a 56-channel tensor keeps
-// every thread busy, not 7 of 32 lanes), then reduce the slices in shared memory.
-__global__ void __launch_bounds__(256) gap_kernel(const mdlc_pool_desc d, const void* x, void* y) {
-  __shared__ float part[256][8];
+// every thread busy, not 7 of 32 lanes), fp32 sums, then reduce the slices in
+// shared memory. (1024 threads per block measured slower: the serial
+// reduction over the slices grows with them.)
+constexpr int kGapThreads = 256;
+template <typename T>
+__global__ void __launch_bounds__(kGapThreads) gap_kernel(const mdlc_pool_desc d, const void* x, void* y) {
+  __shared__ float part[kGapThreads][8];
   const int img = blockIdx.x;
   const int g0 = blockIdx.y * 32;
   const int gb = min(32, (d.c_stride >> 3) - g0);  // channel groups in this block
-  const int slices = 256 / gb;
+  const int slices = kGapThreads / gb;
   const int t = threadIdx.x;
   const int gl = t % gb, slice = t / gb;
   const int hw = d.h * d.w;
@@ -427,9 +428,9 @@ extern "C" int mdlc_pool2d(mdlc_ctx* ctx, const mdlc_pool_desc* d, const void* x
     } else {
       dim3 grid(d->n, (d->c_stride / 8 + 31) / 32);
       if (d->dtype == MDLC_BF16)
-        gap_kernel<__nv_bfloat16><<<grid, 256, 0, ctx->stream>>>(*d, x, y);
+        gap_kernel<__nv_bfloat16><<<grid, kGapThreads, 0, ctx->stream>>>(*d, x, y);
       else if (d->dtype == MDLC_F32)
-        gap_kernel<float><<<grid, 256, 0, ctx->stream>>>(*d, x, y);
+        gap_kernel<float><<<grid, kGapThreads, 0, ctx->stream>>>(*d, x, y);
       else
         return mdlc_set_error(ctx, MDLC_ERR_UNSUPPORTED, "pool: dtype %d", d->dtype);
     }
