@@ -30,10 +30,11 @@ from mdlc_b200 import _lib as L
 
 CONFIGS = ((64, 3), (128, 2), (256, 3), (192, 3), (64, 8), (128, 4))
 # fp32 (3xTF32) keeps hi and lo stages: its own tile set
-CONFIGS_F32 = ((64, 3), (128, 2), (256, 2))
+CONFIGS_F32 = ((64, 3), (64, 4), (128, 2), (128, 3), (256, 2))
 KERNEL_TAG = "conv_tc_v3"
 # resident CTAs per SM of each configuration (shared memory <= 113 KB: two)
-CTAS_PER_SM = {(64, 3): 2, (128, 2): 2, (256, 3): 1, (192, 3): 1, (64, 8): 1, (128, 4): 1, (256, 2): 1}
+CTAS_PER_SM = {(64, 3): 2, (128, 2): 2, (256, 3): 1, (192, 3): 1, (64, 8): 1, (128, 4): 1, (256, 2): 1, (64, 4): 1,
+               (128, 3): 1}
 # Cost-model constants, fitted to B200 measurements of this kernel (b=256
 # ResNet-18 layers, CUDA events): tensor-pipe cycles of one 128 x bn x 16 bf16
 # MMA with operands fresh from the stage ring; the cycles one CTA's issuing

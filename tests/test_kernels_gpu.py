@@ -412,6 +412,40 @@ def test_conv_fp32_3xtf32(ctx, case):
     np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4)   # FP32_REDUCTION tier
 
 
+F32_DEEP_CASES = [
+    # (n, c, h, w, k, r, stride, pad), (bn, stages)
+    ((4, 64, 32, 32, 64, 3, 1, 1), (64, 4)),      # im2col TMA, 64-wide tiles, 4-stage ring
+    ((3, 64, 19, 17, 40, 3, 2, 1), (64, 4)),      # stride 2, ragged output channels
+    ((4, 64, 32, 32, 128, 3, 1, 1), (128, 3)),    # 128-wide tiles, 3-stage ring
+    ((4, 256, 7, 7, 192, 3, 1, 1), (128, 3)),     # deep reduction (2304): promoted accumulator
+    ((4, 128, 20, 20, 256, 1, 1, 0), (128, 3)),   # pointwise 2-D TMA
+    ((3, 96, 11, 13, 64, 1, 1, 0), (64, 4)),
+]
+
+
+@pytest.mark.parametrize("case,cfg", F32_DEEP_CASES, ids=[f"{c}-{t}" for c, t in F32_DEEP_CASES])
+def test_conv_fp32_deep_rings(ctx, case, cfg):
+    """The deeper fp32 stage rings (64, 4) and (128, 3) at the FP32_REDUCTION tier."""
+    n, c, h, w, k, r, st, pad = case
+    rng = np.random.default_rng(6)
+    x = rng.standard_normal((n, c, h, w)).astype(np.float32)
+    wt = (rng.standard_normal((k, c, r, r)) * 0.1).astype(np.float32)
+    b = (rng.standard_normal(k) * 0.1).astype(np.float32)
+    res = rng.standard_normal((n, k, (h + 2 * pad - r) // st + 1, (w + 2 * pad - r) // st + 1)).astype(np.float32)
+    got = run_conv(ctx, x, wt, b, stride=st, pad=pad, dtype="f32", act=L.ACT_RELU, res=res, cfg=cfg)
+    want = oracle_conv(x, wt, b, stride=st, pad=pad, act="Relu", res=res, bf16=False)
+    np.testing.assert_allclose(got, want, rtol=1e-4, atol=1e-4)   # FP32_REDUCTION tier
+
+
+def test_conv_fp32_deep_ring_needs_tma_blocks(ctx):
+    """(64, 4) exists for 128-byte channel blocks only: a gathered layer is refused."""
+    rng = np.random.default_rng(7)
+    x = rng.standard_normal((2, 3, 11, 11)).astype(np.float32)
+    wt = (rng.standard_normal((16, 3, 3, 3)) * 0.1).astype(np.float32)
+    with pytest.raises(L.MdlcError, match="128-byte channel blocks"):
+        run_conv(ctx, x, wt, np.zeros(16, np.float32), pad=1, dtype="f32", cfg=(64, 4))
+
+
 def test_conv_fp32_split_k(ctx):
     """3xTF32 with split-K: fp32 partial sums summed in slice order."""
     n, c, h, w, k, r, st, pad = 1, 512, 7, 7, 512, 3, 1, 1
