@@ -123,7 +123,9 @@ typedef struct {
 /* Tile configuration for the tensor-core implicit GEMM (0 = library default). */
 typedef struct {
   int32_t bn;     /* output channels per CTA: 64, 128, 192 or 256 */
-  int32_t stages; /* shared-memory pipeline depth; built pairs: (64, 3), (128, 2) (two CTAs per SM), (256, 3), (192, 3), (64, 8), (128, 4) */
+  int32_t stages; /* shared-memory pipeline depth; built pairs: (64, 3), (128, 2) (two CTAs per SM), (256, 3), (192, 3), (64, 8), (128, 4);
+                     fp32 (3xTF32): (64, 3), (128, 2), (256, 2), and (64, 4), (128, 3) for layers fed by TMA
+                     in 128-byte channel blocks */
   int32_t flags;  /* bit 0: gather the A operand with cp.async even when the layer
                      qualifies for TMA loads; bit 1: per-tap TMA loads (im2col mode)
                      instead of the halo band of stride-1 layers; bit 2: load one halo band
