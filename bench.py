@@ -179,8 +179,9 @@ def call_work(dev, call):
     if kind == "se":
         d = call[1]
         e = _esz(d.dtype)
-        # pooled input, gate output (n x c_stride each) and both fp32 weight matrices
-        nbytes = 2 * d.n * d.c_stride * e + 2 * d.rd * d.c * 4
+        # input (the pooled map, or with the squeeze fused the activations it
+        # averages), gate output (n x c_stride) and both fp32 weight matrices
+        nbytes = (max(d.hw, 1) + 1) * d.n * d.c_stride * e + 2 * d.rd * d.c * 4
         return "se_fc", "hbm", nbytes, 4.0 * d.n * d.rd * d.c
     if kind in ("copy", "softmax"):
         d = call[1]

@@ -350,22 +350,26 @@ typedef struct {
 } mdlc_softmax_desc;
 int mdlc_softmax(mdlc_ctx* ctx, const mdlc_softmax_desc* desc, const void* x, void* y);
 
-/* Squeeze-excite gate over pooled activations: the two 1x1 convolutions on a
- * 1x1 map that follow a global average pool (FC, act, FC, act), which the
- * reference lowers as two FusedConvAct GEMM launches (emit.py:159-209), in one
- * kernel:
+/* Squeeze-excite gate: a global average pool and the two 1x1 convolutions on
+ * the 1x1 map that follow it (FC, act, FC, act), which the reference runs as a
+ * GlobalAveragePool (runtime/reference.py:134) and two FusedConvAct GEMM
+ * launches (emit.py:159-209), in one kernel:
+ *   p[n, i] = mean over the hw pixels of x[n, :, i]          (hw > 1)
  *   h[n, j] = act1(b1[j] + sum_i w1[j, i] * p[n, i])       j < rd
  *   s[n, i] = act2(b2[i] + sum_j w2t[j, i] * h[n, j])      i < c
- * p and s: [n][c_stride] in dtype (bf16 or fp32; the padding channels of s are
- * written as zero); w1, w2t: [rd][c] fp32 (w2t is the second conv's [c][rd]
- * weight transposed); b1 [rd], b2 [c] fp32 or null. fp32 accumulation, h kept
- * in fp32. c <= 4096, rd <= 1024. */
+ * With hw 0 or 1 the input is the pooled p, [n][c_stride]; with hw > 1 it is
+ * the NHWC activation x, [n][hw][c_stride] (16-byte aligned), averaged in fp32
+ * (kept in fp32, not rounded to dtype). s: [n][c_stride] in dtype (bf16 or
+ * fp32; the padding channels are written as zero); w1, w2t: [rd][c] fp32 (w2t
+ * is the second conv's [c][rd] weight transposed); b1 [rd], b2 [c] fp32 or
+ * null. fp32 accumulation, h kept in fp32. c <= c_stride <= 4096, rd <= 1024. */
 typedef struct {
   int32_t n, c, c_stride, rd;
   int32_t dtype;                  /* MDLC_BF16 or MDLC_F32 */
   int32_t act1, act2;             /* MDLC_ACT_* */
   float alpha1, beta1, lo1, hi1;  /* act1 parameters (leaky / hard-sigmoid / clip) */
   float alpha2, beta2, lo2, hi2;  /* act2 parameters */
+  int32_t hw;                     /* pixels per image of the input: 0 / 1 pooled, > 1 pool fused */
 } mdlc_se_desc;
 int mdlc_se_fc(mdlc_ctx* ctx, const mdlc_se_desc* desc, const void* pooled, const float* w1, const float* b1,
                const float* w2t, const float* b2, void* gate);

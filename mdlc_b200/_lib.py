@@ -99,7 +99,8 @@ class SeDesc(C.Structure):
     _fields_ = [("n", C.c_int32), ("c", C.c_int32), ("c_stride", C.c_int32), ("rd", C.c_int32),
                 ("dtype", C.c_int32), ("act1", C.c_int32), ("act2", C.c_int32),
                 ("alpha1", C.c_float), ("beta1", C.c_float), ("lo1", C.c_float), ("hi1", C.c_float),
-                ("alpha2", C.c_float), ("beta2", C.c_float), ("lo2", C.c_float), ("hi2", C.c_float)]
+                ("alpha2", C.c_float), ("beta2", C.c_float), ("lo2", C.c_float), ("hi2", C.c_float),
+                ("hw", C.c_int32)]
 
 
 # exported symbol -> (argtypes, restype); the CPU test suite checks every

@@ -239,7 +239,8 @@ class _Device:
                 xt, yt = lo.tensors[st.inputs[0]], lo.tensors[st.outputs[0]]
                 p = st.params
                 rd, c = p["w1"].shape
-                d = L.SeDesc(n=xt.n, c=c, c_stride=xt.cs, rd=rd, dtype=xt.dtype)
+                # hw > 1: the step absorbed the global average pool and reads its input
+                d = L.SeDesc(n=xt.n, c=c, c_stride=xt.cs, rd=rd, dtype=xt.dtype, hw=xt.h * xt.w)
                 if yt.cs != xt.cs:
                     raise RuntimeError(f"internal: se step {st.label()} with different channel strides")
                 for i, (act, a) in enumerate(((p["act1"], p["attrs1"]), (p["act2"], p["attrs2"])), 1):

@@ -1,5 +1,9 @@
-// Squeeze-excite gate: global-average-pooled activations -> FC + act -> FC +
-// act in one kernel (mdlc_se_fc). The two FCs act on one pixel per image, so
+// Squeeze-excite gate: global average pool -> FC + act -> FC + act in one
+// kernel (mdlc_se_fc). The pool is either done already (a pooled [n][c]
+// input) or fused: the block averages its images' [hw][c] activations itself
+// (16-byte loads, lanes across 8-channel groups so a warp reads whole pixel
+// rows, pixel slices summed by a tree in shared memory), which saves the
+// pooled tensor's round trip and one launch per gate. The two FCs act on one pixel per image, so
 // as tensor-core GEMMs they were two launches of a handful of CTAs each,
 // bounded by launch and load latency; here each block takes two images, so
 // every weight row it reads from L2 serves two dot products, 32 warps and
@@ -27,6 +31,18 @@ MDLC_DEV void se_st<float>(float* p, float v) { *p = v; }
 template <>
 MDLC_DEV void se_st<__nv_bfloat16>(__nv_bfloat16* p, float v) { *p = __float2bfloat16_rn(v); }
 
+// eight consecutive channels (16 bytes of bf16, 32 of fp32) as fp32
+MDLC_DEV void se_ld8(const __nv_bfloat16* p, float (&f)[8]) {
+  const uint4 u = __ldg(reinterpret_cast<const uint4*>(p));
+  f[0] = bf16_lo(u.x); f[1] = bf16_hi(u.x); f[2] = bf16_lo(u.y); f[3] = bf16_hi(u.y);
+  f[4] = bf16_lo(u.z); f[5] = bf16_hi(u.z); f[6] = bf16_lo(u.w); f[7] = bf16_hi(u.w);
+}
+MDLC_DEV void se_ld8(const float* p, float (&f)[8]) {
+  const float4 a = __ldg(reinterpret_cast<const float4*>(p));
+  const float4 b = __ldg(reinterpret_cast<const float4*>(p) + 1);
+  f[0] = a.x; f[1] = a.y; f[2] = a.z; f[3] = a.w; f[4] = b.x; f[5] = b.y; f[6] = b.z; f[7] = b.w;
+}
+
 template <typename T>
 __global__ void __launch_bounds__(kSeThreads) se_fc_kernel(const mdlc_se_desc d, const T* p, const float* w1,
                                                            const float* b1, const float* w2t, const float* b2,
@@ -36,11 +52,49 @@ __global__ void __launch_bounds__(kSeThreads) se_fc_kernel(const mdlc_se_desc d,
   float* hs = se_smem + kSeImgs * d.c; // [kSeImgs][rd] hidden layer
   const int n0 = blockIdx.x * kSeImgs;
   const int ni = min(kSeImgs, d.n - n0);
-  for (int i = threadIdx.x; i < kSeImgs * d.c; i += kSeThreads) {
-    const int im = i / d.c, c = i - im * d.c;
-    ps[i] = im < ni ? se_ld<T>(p + (long long)(n0 + im) * d.c_stride + c) : 0.0f;
+  if (d.hw > 1) {
+    // fused squeeze: thread t sums channel group t % G over the pixels of slice
+    // t / G (every slices-th pixel), then the slices are added pairwise
+    float* part = hs + kSeImgs * d.rd;  // [8][kSeThreads]: conflict-free columns
+    const int G = d.c_stride >> 3;      // <= 512 groups of 8 channels
+    const int slices = kSeThreads / G;  // >= 2
+    const int g = threadIdx.x % G, sl = threadIdx.x / G;
+    for (int im = 0; im < kSeImgs; ++im) {
+      float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      if (im < ni && sl < slices) {
+        const T* xb = p + (long long)(n0 + im) * d.hw * d.c_stride + g * 8;
+#pragma unroll 4
+        for (int q = sl; q < d.hw; q += slices) {
+          float v[8];
+          se_ld8(xb + (long long)q * d.c_stride, v);
+#pragma unroll
+          for (int e = 0; e < 8; ++e) acc[e] += v[e];
+        }
+      }
+#pragma unroll
+      for (int e = 0; e < 8; ++e) part[e * kSeThreads + threadIdx.x] = acc[e];
+      __syncthreads();
+      for (int st = 1; st < slices; st <<= 1) {
+        if (sl < slices && (sl & (2 * st - 1)) == 0 && sl + st < slices) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) part[e * kSeThreads + threadIdx.x] += part[e * kSeThreads + threadIdx.x + st * G];
+        }
+        __syncthreads();
+      }
+      if (sl == 0) {
+#pragma unroll
+        for (int e = 0; e < 8; ++e)
+          if (g * 8 + e < d.c) ps[im * d.c + g * 8 + e] = part[e * kSeThreads + threadIdx.x] / (float)d.hw;
+      }
+      __syncthreads();
+    }
+  } else {
+    for (int i = threadIdx.x; i < kSeImgs * d.c; i += kSeThreads) {
+      const int im = i / d.c, c = i - im * d.c;
+      ps[i] = im < ni ? se_ld<T>(p + (long long)(n0 + im) * d.c_stride + c) : 0.0f;
+    }
+    __syncthreads();
   }
-  __syncthreads();
   // FC1: each warp takes four hidden units at a time, lanes across the input
   // channels, so every lane has four (x2 unrolled: eight) weight loads in flight
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -103,12 +157,16 @@ extern "C" int mdlc_se_fc(mdlc_ctx* ctx, const mdlc_se_desc* d, const void* pool
                           const float* b1, const float* w2t, const float* b2, void* gate) {
   if (!ctx) return MDLC_ERR_INVALID;
   if (!d || !pooled || !w1 || !w2t || !gate || d->n <= 0 || d->c <= 0 || d->c > 4096 || d->rd <= 0 ||
-      d->rd > 1024 || d->c_stride < d->c || d->c_stride % 8 || (d->dtype != MDLC_BF16 && d->dtype != MDLC_F32))
+      d->rd > 1024 || d->c_stride < d->c || d->c_stride % 8 || d->c_stride > 4096 || d->hw < 0 ||
+      (d->dtype != MDLC_BF16 && d->dtype != MDLC_F32))
     return mdlc_set_error(ctx, MDLC_ERR_INVALID, "se_fc: bad descriptor");
+  if (d->hw > 1 && (reinterpret_cast<uintptr_t>(pooled) & 15))
+    return mdlc_set_error(ctx, MDLC_ERR_INVALID, "se_fc: the activations to pool must be 16-byte aligned");
   cudaSetDevice(ctx->device);
   const ActParams a1{d->act1, d->alpha1, d->beta1, d->lo1, d->hi1};
   const ActParams a2{d->act2, d->alpha2, d->beta2, d->lo2, d->hi2};
-  const int smem = kSeImgs * (d->c + d->rd) * (int)sizeof(float);
+  // pooled inputs and hidden layer, and with the fused squeeze the slice partials
+  const int smem = (kSeImgs * (d->c + d->rd) + (d->hw > 1 ? 8 * kSeThreads : 0)) * (int)sizeof(float);
   const unsigned grid = (unsigned)((d->n + kSeImgs - 1) / kSeImgs);
   cudaError_t e = cudaSuccess;
   if (d->dtype == MDLC_BF16) {

@@ -751,7 +751,9 @@ def fuse_squeeze_excite(lo: Lowered) -> None:
     the second and the second's channel count equal to the first's input
     channels (FC, act, FC, act of a squeeze-excite gate): one "se" step, run by
     mdlc_se_fc. The weights leave ``lo.weights`` (they are not conv-packed):
-    w1 [rd][c] and w2 transposed, [rd][c], with the biases, go into the step."""
+    w1 [rd][c] and w2 transposed, [rd][c], with the biases, go into the step.
+    A global average pool whose output only the gate reads is absorbed too:
+    the step then reads the pool's input and averages it in the same kernel."""
     readers = {}
     for st in lo.steps:
         for t in st.inputs:
@@ -770,7 +772,13 @@ def fuse_squeeze_excite(lo: Lowered) -> None:
             c, rd = ga["c"], ga["k"]
             if gb["c"] == rd and gb["k"] == c and c <= 4096 and rd <= 1024:
                 del lo.weights[a.params["weight"]], lo.weights[b.params["weight"]]
-                out.append(Step("se", [a.inputs[0]], [b.outputs[0]], a.nodes + b.nodes, dict(
+                src, nodes = a.inputs[0], a.nodes + b.nodes
+                g = out[-1] if out else None
+                if (g is not None and g.kind == "pool" and g.params["kind"] == 2 and g.outputs[0] == src
+                        and readers.get(src, 0) == 1 and src not in lo.outputs):
+                    out.pop()
+                    src, nodes = g.inputs[0], g.nodes + nodes
+                out.append(Step("se", [src], [b.outputs[0]], nodes, dict(
                     w1=np.ascontiguousarray(np.asarray(wa, np.float32).reshape(rd, c)),
                     b1=np.ascontiguousarray(ba[:rd], np.float32),
                     w2t=np.ascontiguousarray(np.asarray(wb, np.float32).reshape(c, rd).T),

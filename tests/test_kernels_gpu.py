@@ -935,3 +935,66 @@ def test_se_fc(ctx, dtype, case):
         np.testing.assert_allclose(y[:, :c], want, rtol=1e-2, atol=4e-3)
     else:
         np.testing.assert_allclose(y[:, :c], want, rtol=1e-4, atol=1e-5)
+
+
+SE_POOL_CASES = [
+    # n, c, hw, rd   (the squeeze fused: activations [n][hw][c_stride] in)
+    (5, 56, 56 * 56, 16),     # RepViT stage 1: 7 channel groups, 146 pixel slices (not a power of two)
+    (4, 224, 14 * 14, 56),    # RepViT stage 3: 28 groups, 36 slices
+    (3, 448, 7 * 7, 112),     # RepViT stage 4: 56 groups, 18 slices
+    (2, 100, 9 * 11, 24),     # ragged channel stride (104), odd pixel count
+    (3, 4000, 3 * 3, 1000),   # 500 groups (2 slices), > 48 KB of shared memory
+]
+
+
+@pytest.mark.parametrize("dtype", ["bf16", "f32"])
+@pytest.mark.parametrize("case", SE_POOL_CASES, ids=[str(c) for c in SE_POOL_CASES])
+def test_se_fc_fused_squeeze(ctx, dtype, case):
+    """mdlc_se_fc with hw > 1: the global average pool of the activations and
+    both FCs in one kernel (the mean kept in fp32), against fp32 numpy."""
+    n, c, hw, rd = case
+    cs = _rnd8(c)
+    rng = np.random.default_rng(n + c + hw + rd)
+    x = rng.standard_normal((n, hw, c)).astype(np.float32) + 0.5
+    w1 = (rng.standard_normal((rd, c)) / np.sqrt(c)).astype(np.float32)
+    b1 = (rng.standard_normal(rd) * 0.1).astype(np.float32)
+    w2 = (rng.standard_normal((c, rd)) / np.sqrt(rd)).astype(np.float32)
+    b2 = (rng.standard_normal(c) * 0.1).astype(np.float32)
+    dt = L.BF16 if dtype == "bf16" else L.F32
+    xh = np.zeros((n, hw, cs), np.float32)
+    xh[..., :c] = x
+    xd = ctx.to_device(bf16_bits(xh) if dt == L.BF16 else xh)
+    eb = 2 if dt == L.BF16 else 4
+    gd = ctx.alloc(n * cs * eb)
+    ctx.memset(gd, 0xFF, n * cs * eb)
+    bufs = [ctx.to_device(a) for a in (w1, b1, np.ascontiguousarray(w2.T), b2)]
+    d = L.SeDesc(n=n, c=c, c_stride=cs, rd=rd, dtype=dt, act1=L.ACT_RELU, act2=L.ACT_SIGMOID, alpha1=0.01,
+                 beta1=0.5, lo1=-np.inf, hi1=np.inf, alpha2=0.2, beta2=0.5, lo2=-np.inf, hi2=np.inf, hw=hw)
+    ctx.se_fc(d, xd, *bufs, gd)
+    ctx.sync()
+    y = ctx.download(gd, (n, cs), np.uint16 if dt == L.BF16 else np.float32)
+    y = from_bf16_bits(y) if dt == L.BF16 else y
+    for b in [xd, gd] + bufs:
+        ctx.free(b)
+    assert np.all(y[:, c:] == 0)
+    xr = oref.round_bf16(x) if dt == L.BF16 else x
+    p = xr.astype(np.float64).mean(axis=1)
+    h = np.maximum(p @ w1.T.astype(np.float64) + b1, 0)
+    want = 1 / (1 + np.exp(-(h @ w2.T.astype(np.float64) + b2)))
+    if dt == L.BF16:
+        np.testing.assert_allclose(y[:, :c], want, rtol=1e-2, atol=4e-3)
+    else:
+        np.testing.assert_allclose(y[:, :c], want, rtol=1e-4, atol=1e-5)
+
+
+def test_se_fc_fused_squeeze_needs_alignment(ctx):
+    """The activations to pool are read 16 bytes at a time: a misaligned base is refused."""
+    n, c, hw, rd = 2, 64, 16, 16
+    xd = ctx.alloc(n * hw * c * 2 + 64)
+    gd = ctx.alloc(n * c * 2)
+    bufs = [ctx.to_device(np.zeros(s, np.float32)) for s in (rd * c, rd, rd * c, c)]
+    d = L.SeDesc(n=n, c=c, c_stride=c, rd=rd, dtype=L.BF16, act1=L.ACT_RELU, act2=L.ACT_SIGMOID, hw=hw)
+    with pytest.raises(L.MdlcError, match="16-byte aligned"):
+        ctx.se_fc(d, xd + 2, *bufs, gd)
+    for b in [xd, gd] + bufs:
+        ctx.free(b)

@@ -96,8 +96,9 @@ def test_bf16_constant_bits_round_to_nearest_even():
 
 def test_squeeze_excite_fused_into_one_step():
     """RepViT's squeeze-excite gates (ReduceMean -> 1x1 conv + ReLU -> 1x1 conv
-    + Sigmoid -> Mul) lower to pool, one "se" step and the multiply; the FC
-    weights leave the conv weight table; keep_all lowering keeps the two convs."""
+    + Sigmoid -> Mul) lower to one "se" step (the pool absorbed: it reads the
+    activations themselves) and the multiply; the FC weights leave the conv
+    weight table; keep_all lowering keeps the pool and the two convs."""
     from mdlc_b200 import builders
     g = passes.default_pipeline(builders.BUILDERS["repvit"](batch=2, seed=0))
     shp = S.infer(g, 2)
@@ -110,13 +111,18 @@ def test_squeeze_excite_fused_into_one_step():
         assert p["w2t"].shape == (rd, c) and p["b1"].shape == (rd,) and p["b2"].shape == (c,)
         assert (p["act1"], p["act2"]) == ("Relu", "Sigmoid")
         assert not any(n in w for n in st.nodes for w in lo.weights)
-        # the pooled input and the gate keep the same channel stride
-        assert lo.tensors[st.inputs[0]].cs == lo.tensors[st.outputs[0]].cs
+        # the activations and the gate keep the same channel stride
+        x, y = lo.tensors[st.inputs[0]], lo.tensors[st.outputs[0]]
+        assert x.cs == y.cs and x.h * x.w > 1 and y.h * y.w == 1
+        assert len(st.nodes) == 3
+    # only the head's global average pool is left as a pool step
+    assert sum(st.kind == "pool" and st.params["kind"] == 2 for st in lo.steps) == 1
     # the second FC's weight, transposed, is the step's w2t
-    node = {n.name: n for n in g.nodes}[se[0].nodes[1]]
+    node = {n.name: n for n in g.nodes}[se[0].nodes[-1]]
     rd, c = se[0].params["w1"].shape
     w2 = np.asarray(g.initializers[node.inputs[1]], np.float32).reshape(c, rd)
     np.testing.assert_array_equal(se[0].params["w2t"], w2.T)
     lo_all = lowering.lower(g, shp, L.BF16, fuse_se=False)
     assert not any(st.kind == "se" for st in lo_all.steps)
     assert sum(st.kind == "conv" for st in lo_all.steps) == sum(st.kind == "conv" for st in lo.steps) + 20
+    assert sum(st.kind == "pool" and st.params["kind"] == 2 for st in lo_all.steps) == 11
