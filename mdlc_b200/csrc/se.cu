@@ -63,7 +63,7 @@ __global__ void __launch_bounds__(kSeThreads) se_fc_kernel(const mdlc_se_desc d,
       float acc[8] = {0, 0, 0, 0, 0, 0, 0, 0};
       if (im < ni && sl < slices) {
         const T* xb = p + (long long)(n0 + im) * d.hw * d.c_stride + g * 8;
-#pragma unroll 4
+#pragma unroll 8
         for (int q = sl; q < d.hw; q += slices) {
           float v[8];
           se_ld8(xb + (long long)q * d.c_stride, v);
