@@ -15,6 +15,33 @@
 
 namespace mdlc {
 
+// ------------------------------------------------------------ programmatic dependent launch
+// A kernel started by launch_pdl may begin while the previous kernel in the
+// stream is still running (its launch and prologue overlap that kernel's
+// tail). It must call pdl_wait() before its first global-memory access: the
+// wait returns once the previous grid has completed and its writes are
+// visible (in a kernel launched the ordinary way it returns at once).
+// pdl_trigger() then lets the next kernel in the stream be scheduled; it
+// starts only after every CTA of this grid has triggered or exited.
+MDLC_DEV void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+MDLC_DEV void pdl_trigger() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kern)(KArgs...), dim3 grid, dim3 block, size_t smem, cudaStream_t stream,
+                              Args... args) {
+  cudaLaunchConfig_t lc = {};
+  lc.gridDim = grid;
+  lc.blockDim = block;
+  lc.dynamicSmemBytes = smem;
+  lc.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  lc.attrs = attr;
+  lc.numAttrs = 1;
+  return cudaLaunchKernelEx(&lc, kern, args...);
+}
+
 // ------------------------------------------------------------ error word
 // Each context owns one int in device memory; kernels record the first
 // device-side failure with atomicCAS so the first cause is kept.

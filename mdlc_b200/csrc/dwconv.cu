@@ -123,6 +123,8 @@ MDLC_DEV void store4(const DwTmaArgs& a, T* yp, float2 (&f)[2], bool full, int c
 template <typename T, int SH, bool GEN>
 __global__ void __launch_bounds__(kDwThreads, 1)
     conv_dw3_tma_kernel(const __grid_constant__ CUtensorMap tmap, const DwTmaArgs a) {
+  pdl_wait();  // launched with programmatic serialization: nothing global before this
+  pdl_trigger();
   constexpr int NC = SH == 1 ? 4 : 5;  // input columns under a thread's two output columns
   constexpr int esz = (int)sizeof(T);
   extern __shared__ uint8_t smem_raw[];
@@ -421,9 +423,9 @@ int conv_dw_tma(mdlc_ctx* ctx, const mdlc_conv_desc& d, const void* x, const flo
     if (e != cudaSuccess) return mdlc_cuda_status(ctx, e, "conv_dw3_tma smem attribute");
     attr_set[ctx->device & 63][which] = smem;
   }
-  kern<<<grid, kDwThreads, smem, ctx->stream>>>(tmap, a);
+  const cudaError_t e = launch_pdl(kern, dim3(grid), dim3(kDwThreads), (size_t)smem, ctx->stream, tmap, a);
   mdlc_note_launch(ctx);
-  return mdlc_cuda_status(ctx, cudaGetLastError(), "conv_dw3_tma launch");
+  return mdlc_cuda_status(ctx, e != cudaSuccess ? e : cudaGetLastError(), "conv_dw3_tma launch");
 }
 
 }  // namespace mdlc

@@ -47,6 +47,8 @@ template <typename T>
 __global__ void __launch_bounds__(kSeThreads) se_fc_kernel(const mdlc_se_desc d, const T* p, const float* w1,
                                                            const float* b1, const float* w2t, const float* b2,
                                                            T* s, const ActParams a1, const ActParams a2) {
+  pdl_wait();  // launched with programmatic serialization: nothing global before this
+  pdl_trigger();
   extern __shared__ float se_smem[];
   float* ps = se_smem;                 // [kSeImgs][c] pooled inputs
   float* hs = se_smem + kSeImgs * d.c; // [kSeImgs][rd] hidden layer
@@ -173,16 +175,17 @@ extern "C" int mdlc_se_fc(mdlc_ctx* ctx, const mdlc_se_desc* d, const void* pool
     if (smem > 48 * 1024)
       e = cudaFuncSetAttribute(se_fc_kernel<__nv_bfloat16>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e == cudaSuccess)
-      se_fc_kernel<__nv_bfloat16><<<grid, kSeThreads, smem, ctx->stream>>>(
-          *d, static_cast<const __nv_bfloat16*>(pooled), w1, b1, w2t, b2, static_cast<__nv_bfloat16*>(gate), a1, a2);
+      e = launch_pdl(se_fc_kernel<__nv_bfloat16>, dim3(grid), dim3(kSeThreads), (size_t)smem, ctx->stream, *d,
+                     static_cast<const __nv_bfloat16*>(pooled), w1, b1, w2t, b2, static_cast<__nv_bfloat16*>(gate),
+                     a1, a2);
   } else {
     if (smem > 48 * 1024)
       e = cudaFuncSetAttribute(se_fc_kernel<float>, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     if (e == cudaSuccess)
-      se_fc_kernel<float><<<grid, kSeThreads, smem, ctx->stream>>>(
-          *d, static_cast<const float*>(pooled), w1, b1, w2t, b2, static_cast<float*>(gate), a1, a2);
+      e = launch_pdl(se_fc_kernel<float>, dim3(grid), dim3(kSeThreads), (size_t)smem, ctx->stream, *d,
+                     static_cast<const float*>(pooled), w1, b1, w2t, b2, static_cast<float*>(gate), a1, a2);
   }
-  if (e != cudaSuccess) return mdlc_cuda_status(ctx, e, "se_fc smem attribute");
+  if (e != cudaSuccess) return mdlc_cuda_status(ctx, e, "se_fc launch");
   mdlc_note_launch(ctx);
   return mdlc_cuda_status(ctx, cudaGetLastError(), "se_fc launch");
 }
