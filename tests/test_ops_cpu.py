@@ -126,3 +126,22 @@ def test_squeeze_excite_fused_into_one_step():
     assert not any(st.kind == "se" for st in lo_all.steps)
     assert sum(st.kind == "conv" for st in lo_all.steps) == sum(st.kind == "conv" for st in lo.steps) + 20
     assert sum(st.kind == "pool" and st.params["kind"] == 2 for st in lo_all.steps) == 11
+
+
+def test_squeeze_excite_keeps_a_pool_with_other_readers():
+    """A global average pool whose output another step also reads stays a pool
+    step; the gate then reads the pooled map (mdlc_se_desc.hw == 1)."""
+    from mdlc_b200 import builders
+    g = passes.default_pipeline(builders.BUILDERS["repvit"](batch=2, seed=0))
+    lo = lowering.lower(g, S.infer(g, 2), L.BF16, fuse_se=False)
+    i = next(k for k, st in enumerate(lo.steps) if st.kind == "pool" and st.params["kind"] == 2)
+    pooled = lo.steps[i].outputs[0]
+    extra = lowering.Step("eltwise", [pooled], [pooled + "_copy"], ["extra_reader"], {})
+    lo.steps.insert(i + 3, extra)
+    lowering.fuse_squeeze_excite(lo)
+    first = next(st for st in lo.steps if st.kind == "se")
+    assert first.inputs == [pooled]
+    assert lo.steps[i].kind == "pool" and lo.steps[i].outputs == [pooled]
+    # every other gate still absorbed its pool
+    se = [st for st in lo.steps if st.kind == "se"]
+    assert len(se) == 10 and all(lo.tensors[st.inputs[0]].h > 1 for st in se[1:])
