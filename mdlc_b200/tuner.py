@@ -32,7 +32,8 @@ CONFIGS = ((64, 3), (128, 2), (256, 3), (192, 3), (64, 8), (128, 4))
 # fp32 (3xTF32) keeps hi and lo stages: its own tile set
 CONFIGS_F32 = ((64, 3), (64, 4), (128, 2), (128, 3), (256, 2))
 KERNEL_TAG = "conv_tc_v3"
-# resident CTAs per SM of each configuration (shared memory <= 113 KB: two)
+# resident CTAs per SM of each bf16 / 8-bit configuration (shared memory <= 113 KB:
+# two); every fp32 (3xTF32) configuration runs one (hi, lo and weight stages)
 CTAS_PER_SM = {(64, 3): 2, (128, 2): 2, (256, 3): 1, (192, 3): 1, (64, 8): 1, (128, 4): 1, (256, 2): 1, (64, 4): 1,
                (128, 3): 1}
 # Cost-model constants, fitted to B200 measurements of this kernel (b=256
@@ -113,7 +114,7 @@ def analytical_cost(shape: ConvShape, bn: int, stages: int, num_sms: int = 148) 
     m = shape.n * shape.oh * shape.ow
     tiles = -(-m // 128) * -(-d.k_stride // bn)
     kb = -(-shape.r * shape.s * d.c_stride // (128 // L.ELEM_BYTES[shape.dtype]))
-    occ = CTAS_PER_SM.get((bn, stages), 1)
+    occ = 1 if shape.dtype == L.F32 else CTAS_PER_SM.get((bn, stages), 1)
     per_sm = -(-tiles // num_sms)
     conc = min(occ, per_sm)               # CTAs of this configuration busy on one SM
     issue = 4 * MMA_CYCLES[bn] + (ISSUE_GAP if bn <= 128 else 0.0)

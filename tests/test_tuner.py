@@ -30,6 +30,17 @@ def test_model_prefers_two_ctas_per_sm_for_narrow_layers():
     assert _best(T.ConvShape(256, 512, 7, 7, 512, 3, 3, 1, 1)) == (256, 3)
 
 
+def test_model_fp32_prefers_the_deeper_rings():
+    # 3xTF32 runs one CTA per SM in every configuration, so the model follows the
+    # ring depth, as measured on ResNet-18 fp32 b=256 (layer1 (64, 4), 128- and
+    # 512-channel layers (128, 3))
+    f32 = dict(dtype=L.F32)
+    assert _best(T.ConvShape(256, 64, 56, 56, 64, 3, 3, 1, 1, **f32)) == (64, 4)
+    assert _best(T.ConvShape(256, 128, 28, 28, 128, 3, 3, 1, 1, **f32)) == (128, 3)
+    _, _, ranking = T.tune(T.ConvShape(8, 64, 28, 28, 64, 3, 3, 1, 1, **f32))
+    assert sorted(c for c, _ in ranking) == sorted(T.CONFIGS_F32)
+
+
 def test_model_counts_waves():
     shape = T.ConvShape(1, 512, 7, 7, 512, 3, 3, 1, 1)   # 1 M tile: only N tiles spread the work
     assert T.analytical_cost(shape, 64, 8) < T.analytical_cost(shape, 256, 3)
